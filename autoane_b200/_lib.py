@@ -1,0 +1,76 @@
+"""ctypes binding of libb2p.so (the C ABI declared in include/b2p.h).
+
+Loading fails loudly: there is no CPU or PyTorch fallback for any entry point.
+Signatures are declared once here; `ABI` maps each exported name to its
+(restype, argtypes).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+LIB_PATH = PKG / "libb2p.so"
+HEADER_DIR = ROOT / "include"
+
+vp = C.c_void_p
+i32 = C.c_int
+i64 = C.c_longlong
+u64 = C.c_uint64
+f32 = C.c_float
+fp = C.POINTER(C.c_float)
+ip = C.POINTER(C.c_int)
+u16p = C.POINTER(C.c_uint16)
+u64p = C.POINTER(C.c_uint64)
+szt = C.c_size_t
+cstr = C.c_char_p
+
+# name -> (restype, [argtypes])
+ABI: dict[str, tuple] = {
+    "b2p_init": (i32, [i32]),
+    "b2p_last_error": (cstr, []),
+    "b2p_version": (cstr, []),
+    "b2p_device_status": (i32, [vp]),
+    "b2p_gemm": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+}
+
+
+class B2PError(RuntimeError):
+    """A C-ABI call returned a negative status."""
+
+    def __init__(self, name: str, rc: int, msg: str):
+        super().__init__(f"{name} failed (status {rc}): {msg}")
+        self.rc = rc
+
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Load libb2p.so once and bind every signature. Raises if the library is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(
+            f"{p} is missing: the CUDA library has not been built "
+            "(run `python -m autoane_b200.build` or __graft_entry__.build()); there is no fallback")
+    lib = C.CDLL(str(p))
+    for name, (res, args) in ABI.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def call(name: str, *args):
+    """Call an int-returning entry point and raise B2PError on a negative status."""
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if isinstance(rc, int) and rc < 0:
+        raise B2PError(name, rc, lib.b2p_last_error().decode(errors="replace"))
+    return rc

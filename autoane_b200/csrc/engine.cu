@@ -1,0 +1,190 @@
+// engine.cu — error state, device context, tensor maps and the GEMM dispatcher.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+#include <cudaTypedefs.h>
+#include "engine.cuh"
+
+namespace b2p {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_ctx_mu;
+DeviceCtx g_ctx[64];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+const char* last_error() { return g_last_error.c_str(); }
+
+int ctx_get(DeviceCtx** out) {
+  int dev = 0;
+  B2P_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal %d out of range", dev);
+    return B2P_ERR_ARG;
+  }
+  std::lock_guard<std::mutex> lk(g_ctx_mu);
+  DeviceCtx& c = g_ctx[dev];
+  if (c.device < 0) {
+    int major = 0, minor = 0;
+    B2P_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    B2P_CHECK_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0) {
+      set_error("device %d is sm_%d%d; this library is built for sm_100a (B200) only", dev, major, minor);
+      return B2P_ERR_UNSUPPORTED;
+    }
+    B2P_CHECK_CUDA(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    B2P_CHECK_CUDA(cudaMalloc(&c.status, sizeof(uint32_t)));
+    B2P_CHECK_CUDA(cudaMemset(c.status, 0, sizeof(uint32_t)));
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      B2P_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+      if (q != cudaDriverEntryPointSuccess || !fn) {
+        set_error("cuTensorMapEncodeTiled not available from the driver");
+        return B2P_ERR_CUDA;
+      }
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    c.device = dev;
+  }
+  *out = &c;
+  return B2P_OK;
+}
+
+int check_device_status(cudaStream_t st) {
+  DeviceCtx* c = nullptr;
+  int rc = ctx_get(&c);
+  if (rc) return rc;
+  uint32_t h = 0;
+  B2P_CHECK_CUDA(cudaMemcpyAsync(&h, c->status, sizeof(h), cudaMemcpyDeviceToHost, st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(st));
+  if (h != 0) {
+    B2P_CHECK_CUDA(cudaMemsetAsync(c->status, 0, sizeof(uint32_t), st));
+    set_error("device status %u: a bounded wait inside a kernel expired (1 producer, 2 mma, 3 epilogue)", h);
+    return B2P_ERR_DEVICE;
+  }
+  return B2P_OK;
+}
+
+int make_tmap_kmajor(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint64_t ld, uint32_t box_rows,
+                     bool bf16) {
+  B2P_REQUIRE(base != nullptr, "tensor map over a null pointer");
+  B2P_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15u) == 0, "operand base must be 16-byte aligned");
+  B2P_REQUIRE(k >= 8 && (ld * 2) % 16 == 0 && ld >= k, "K=%llu / ld=%llu: row pitch must be a multiple of 8 elements",
+              (unsigned long long)k, (unsigned long long)ld);
+  B2P_REQUIRE(rows >= 1 && box_rows >= 1 && box_rows <= 256, "bad rows/box");
+  cuuint64_t gdim[2] = {k, rows};
+  cuuint64_t gstride[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return B2P_ERR_CUDA;
+  }
+  return B2P_OK;
+}
+
+int pick_bn(int N, int kind) {
+  if (kind == EPI_SWIGLU) return 256;
+  if (kind == EPI_CE) return 256;
+  const int cands[4] = {256, 192, 160, 128};
+  int best = 256;
+  long long best_pad = -1;
+  for (int i = 0; i < 4; ++i) {
+    const int bn = cands[i];
+    const long long pad = (long long)((N + bn - 1) / bn) * bn - N;
+    if (best_pad < 0 || pad < best_pad) {
+      best_pad = pad;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int BN, int KIND, typename OutT, bool BF16>
+static int launch_t(const void* X, int ldx, const void* W, int ldw, int M, int N, int K, const EpiParams& ep,
+                    cudaStream_t st) {
+  DeviceCtx* c = nullptr;
+  int rc = ctx_get(&c);
+  if (rc) return rc;
+  CUtensorMap tx, tw;
+  if ((rc = make_tmap_kmajor(&tx, X, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, kBM, BF16))) return rc;
+  if ((rc = make_tmap_kmajor(&tw, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BN, BF16))) return rc;
+  using S = GemmSmem<BN>;
+  auto kern = gemm_tc_kernel<BN, KIND, OutT, BF16>;
+  static thread_local int attr_dev_mask = 0;
+  if (!(attr_dev_mask & (1 << (c->device & 31)))) {
+    B2P_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+    attr_dev_mask |= 1 << (c->device & 31);
+  }
+  const long long tiles = (long long)((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = (int)(tiles < c->num_sms ? tiles : c->num_sms);
+  EpiParams e = ep;
+  e.status = c->status;
+  kern<<<grid, kGemmThreads, S::kTotal, st>>>(tx, tw, M, N, K, e);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+template <int KIND, typename OutH, bool BF16>
+static int dispatch_bn(int bn, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                       const EpiParams& ep, cudaStream_t st) {
+  switch (bn) {
+    case 128: return launch_t<128, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
+    case 160: return launch_t<160, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
+    case 192: return launch_t<192, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
+    case 256: return launch_t<256, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
+    default: set_error("unsupported tile width %d", bn); return B2P_ERR_UNSUPPORTED;
+  }
+}
+
+int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                const EpiParams& ep, cudaStream_t st) {
+  B2P_REQUIRE(M > 0 && N > 0 && K > 0, "empty GEMM (M=%d N=%d K=%d)", M, N, K);
+  if (ep.has_lora) {
+    B2P_REQUIRE(ep.lora.rank > 0 && ep.lora.rank <= kMaxRank && ep.lora.rank % 4 == 0,
+                "LoRA rank must be a multiple of 4 in [4, 16] (got %d)", ep.lora.rank);
+    B2P_REQUIRE(ep.lora.group_rows % kBM == 0, "LoRA variant groups must span whole 128-row tiles");
+    for (int s = 1; s < ep.lora.nseg; ++s)
+      B2P_REQUIRE(ep.lora.seg_start[s] % bn == 0, "segment boundary %d not a multiple of tile width %d",
+                  ep.lora.seg_start[s], bn);
+  }
+  if (bf16) {
+    using H = __nv_bfloat16;
+    switch (kind) {
+      case EPI_F32: return dispatch_bn<EPI_F32, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_H16: return dispatch_bn<EPI_H16, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_QKV_ROPE: return launch_t<160, EPI_QKV_ROPE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_RESID: return dispatch_bn<EPI_RESID, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_SWIGLU: return launch_t<256, EPI_SWIGLU, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_CE: return launch_t<256, EPI_CE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
+    }
+  } else {
+    using H = __half;
+    switch (kind) {
+      case EPI_F32: return dispatch_bn<EPI_F32, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_H16: return dispatch_bn<EPI_H16, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_QKV_ROPE: return launch_t<160, EPI_QKV_ROPE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_RESID: return dispatch_bn<EPI_RESID, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_SWIGLU: return launch_t<256, EPI_SWIGLU, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_CE: return launch_t<256, EPI_CE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
+    }
+  }
+  set_error("unknown epilogue kind %d", kind);
+  return B2P_ERR_ARG;
+}
+
+}  // namespace b2p

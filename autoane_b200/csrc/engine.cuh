@@ -1,0 +1,64 @@
+// engine.cuh — host-side plumbing shared by every translation unit of the
+// library: error reporting, the per-device context (stream, status word,
+// SM count), TMA tensor-map encoding and the GEMM launch dispatcher.
+#pragma once
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "gemm.cuh"
+#include "../../include/b2p.h"
+
+namespace b2p {
+
+// Status codes (B2P_OK, B2P_ERR_*) are the macros of include/b2p.h.
+
+void set_error(const char* fmt, ...);
+const char* last_error();
+
+#define B2P_CHECK_CUDA(expr)                                                            \
+  do {                                                                                  \
+    cudaError_t e_ = (expr);                                                            \
+    if (e_ != cudaSuccess) {                                                            \
+      ::b2p::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                       __LINE__);                                                       \
+      return B2P_ERR_CUDA;                                                       \
+    }                                                                                   \
+  } while (0)
+
+#define B2P_REQUIRE(cond, ...)       \
+  do {                               \
+    if (!(cond)) {                   \
+      ::b2p::set_error(__VA_ARGS__); \
+      return B2P_ERR_ARG;     \
+    }                                \
+  } while (0)
+
+struct DeviceCtx {
+  int device = -1;
+  int num_sms = 0;
+  uint32_t* status = nullptr;  // device word written by bounded waits
+};
+
+// Initialise (once per device) and return the context of the current device.
+int ctx_get(DeviceCtx** out);
+
+// Read and clear the device status word; returns B2P_ERR_DEVICE if non-zero.
+int check_device_status(cudaStream_t st);
+
+// 2-D K-major tensor map over a [rows, k] 16-bit matrix (row stride ld elements),
+// box = 64 elements x box_rows rows, 128-byte swizzle, zero fill out of bounds.
+int make_tmap_kmajor(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint64_t ld, uint32_t box_rows,
+                     bool bf16);
+
+// Launch D = X·W^T with the given epilogue. Chooses the compiled tile width
+// `bn` (one of 128, 160, 192, 256).
+int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                const EpiParams& ep, cudaStream_t st);
+
+// Pick the tile width for an N-column output (largest width whose padding
+// waste is minimal; SwiGLU and CE need multiples of 64 / any).
+int pick_bn(int N, int kind);
+
+}  // namespace b2p
