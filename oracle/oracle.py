@@ -1,0 +1,208 @@
+"""ctypes wrapper of oracle/liboracle.so and oracle/_ref/libref_*.so.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline leg of bench.py, as the checker. The product (libb2p.so) never
+calls it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+_lib = None
+
+
+def _f(a):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def _u16(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint16))
+
+
+class Layout(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in
+                ("Aq", "Bq", "Ak", "Bk", "Av", "Bv", "Ao", "Bo", "rms_att", "rms_ffn", "layer_size", "rms_final",
+                 "total")]
+
+
+class _Model(C.Structure):
+    _fields_ = ([(n, C.c_int) for n in ("dim", "hidden", "heads", "kv_heads", "hd", "seq", "nlayers", "vocab",
+                                         "cv", "rank")]
+                + [("rope_theta", C.c_float), ("res_alpha", C.c_float)]
+                + [(n, C.POINTER(C.POINTER(C.c_float))) for n in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")]
+                + [("embed", C.POINTER(C.c_float)), ("cembed", C.POINTER(C.c_float))])
+
+
+class _Taps(C.Structure):
+    _fields_ = [(n, C.POINTER(C.c_float)) for n in ("x_final", "xn_final", "logits", "layer_x")]
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        p = HERE / "liboracle.so"
+        if not p.exists():
+            from . import build as _b  # type: ignore
+            _b.build_oracle()
+        L = C.CDLL(str(p))
+        L.or_xo_next.restype = C.c_uint64
+        L.or_xo_seed.argtypes = [C.c_void_p, C.c_uint64]
+        L.or_xo_next.argtypes = [C.c_void_p]
+        L.or_perturb_buffer.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.c_size_t, C.c_float]
+        L.or_sign_mask.argtypes = [C.c_uint64, C.POINTER(C.c_int64), C.c_int, C.POINTER(C.c_uint32)]
+        L.or_lora_layout.restype = Layout
+        L.or_lora_layout.argtypes = [C.c_int] * 5
+        L.or_perturb_lora.argtypes = [C.POINTER(C.c_float)] + [C.c_int] * 5 + [C.c_uint64, C.c_float]
+        L.or_lora_buffer_sizes.argtypes = [C.c_int] * 5 + [C.POINTER(C.c_int64)]
+        L.or_forward_loss.restype = C.c_float
+        L.or_forward_loss.argtypes = [C.POINTER(_Model), C.POINTER(C.c_float), C.POINTER(C.c_uint16),
+                                      C.POINTER(C.c_uint16), C.POINTER(_Taps)]
+        L.or_mezo_step.argtypes = [C.POINTER(_Model), C.POINTER(C.c_float), C.POINTER(C.c_uint16),
+                                   C.POINTER(C.c_uint16), C.c_uint64, C.c_float, C.c_float,
+                                   C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)]
+        L.or_rope_tables.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_int, C.c_int, C.c_float]
+        L.or_set_threads.argtypes = [C.c_int]
+        L.or_set_threads.restype = C.c_int
+        L.or_cross_entropy.restype = C.c_float
+        L.or_cross_entropy.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_uint16), C.c_int, C.c_int]
+        for n in ("or_rmsnorm",):
+            getattr(L, n).argtypes = [C.POINTER(C.c_float)] * 3 + [C.c_int, C.c_int]
+        L.or_rope_forward.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int, C.c_float]
+        L.or_sdpa_forward.argtypes = [C.POINTER(C.c_float)] * 4 + [C.c_int] * 3
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> int:
+    return lib().or_set_threads(n)
+
+
+# ---------------- PRNG / perturbation ----------------
+def xo_draws(seed: int, n: int) -> list[int]:
+    st = (C.c_uint64 * 4)()
+    lib().or_xo_seed(st, seed)
+    return [lib().or_xo_next(st) for _ in range(n)]
+
+
+def perturb_buffer(seed: int, buf: np.ndarray, scale: float) -> None:
+    """Seed a fresh stream and apply perturb_buffer to one float32 buffer in place."""
+    assert buf.dtype == np.float32 and buf.flags.c_contiguous
+    st = (C.c_uint64 * 4)()
+    lib().or_xo_seed(st, seed)
+    lib().or_perturb_buffer(st, _f(buf), C.c_size_t(buf.size), C.c_float(np.float32(scale)))
+
+
+def sign_mask(seed: int, sizes) -> np.ndarray:
+    sizes = np.ascontiguousarray(sizes, dtype=np.int64)
+    total = int(sizes.sum())
+    out = np.zeros((total + 31) // 32, dtype=np.uint32)
+    lib().or_sign_mask(seed, sizes.ctypes.data_as(C.POINTER(C.c_int64)), len(sizes),
+                       out.ctypes.data_as(C.POINTER(C.c_uint32)))
+    return out
+
+
+def lora_layout(nlayers, dim, q_dim, kv_dim, rank) -> Layout:
+    return lib().or_lora_layout(nlayers, dim, q_dim, kv_dim, rank)
+
+
+def lora_buffer_sizes(nlayers, dim, q_dim, kv_dim, rank) -> np.ndarray:
+    out = np.zeros(10 * nlayers + 1, dtype=np.int64)
+    n = lib().or_lora_buffer_sizes(nlayers, dim, q_dim, kv_dim, rank, out.ctypes.data_as(C.POINTER(C.c_int64)))
+    return out[:n]
+
+
+def perturb_lora(theta: np.ndarray, nlayers, dim, q_dim, kv_dim, rank, seed: int, scale: float) -> None:
+    assert theta.dtype == np.float32 and theta.flags.c_contiguous
+    lib().or_perturb_lora(_f(theta), nlayers, dim, q_dim, kv_dim, rank, seed, np.float32(scale))
+
+
+def rope_tables(seq: int, hd: int, theta: float):
+    c = np.zeros((seq, hd // 2), np.float32)
+    s = np.zeros((seq, hd // 2), np.float32)
+    lib().or_rope_tables(_f(c), _f(s), seq, hd, np.float32(theta))
+    return c, s
+
+
+# ---------------- model ----------------
+@dataclass
+class ModelCfg:
+    dim: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    hd: int
+    seq: int
+    nlayers: int
+    vocab: int
+    rank: int = 8
+    rope_theta: float = 100000.0
+    res_alpha: float = 1.0
+
+    @property
+    def q_dim(self):
+        return self.heads * self.hd
+
+    @property
+    def kv_dim(self):
+        return self.kv_heads * self.hd
+
+
+class OracleModel:
+    """Reference-layout fp32 weights wired into the C oracle."""
+
+    def __init__(self, cfg: ModelCfg, weights: dict, embed: np.ndarray, cembed: np.ndarray):
+        self.cfg = cfg
+        self.w = weights  # name -> list of [out, in] float32 arrays
+        self.embed = np.ascontiguousarray(embed, np.float32)
+        self.cembed = np.ascontiguousarray(cembed, np.float32)
+        self._keep = []
+        m = _Model()
+        for f in ("dim", "hidden", "heads", "kv_heads", "hd", "seq", "nlayers", "vocab", "rank"):
+            setattr(m, f, getattr(cfg, f))
+        m.cv = self.cembed.shape[0]
+        m.rope_theta = cfg.rope_theta
+        m.res_alpha = cfg.res_alpha
+        for n in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3"):
+            arrs = [np.ascontiguousarray(a, np.float32) for a in weights[n]]
+            self._keep.append(arrs)
+            ptrs = (C.POINTER(C.c_float) * cfg.nlayers)(*[_f(a) for a in arrs])
+            self._keep.append(ptrs)
+            setattr(m, n, ptrs)
+        m.embed = _f(self.embed)
+        m.cembed = _f(self.cembed)
+        self.m = m
+
+    def forward_loss(self, theta: np.ndarray, tokens: np.ndarray, ctargets: np.ndarray, taps: dict | None = None):
+        tokens = np.ascontiguousarray(tokens, np.uint16)
+        ctargets = np.ascontiguousarray(ctargets, np.uint16)
+        t = None
+        if taps is not None:
+            t = _Taps()
+            for k, v in taps.items():
+                setattr(t, k, _f(v))
+        return float(lib().or_forward_loss(C.byref(self.m), _f(theta), _u16(tokens), _u16(ctargets),
+                                           C.byref(t) if t is not None else None))
+
+    def mezo_step(self, theta: np.ndarray, tokens, ctargets, seed: int, eps: float, lr: float):
+        lp, lm, g = C.c_float(), C.c_float(), C.c_float()
+        lib().or_mezo_step(C.byref(self.m), _f(theta), _u16(np.ascontiguousarray(tokens, np.uint16)),
+                           _u16(np.ascontiguousarray(ctargets, np.uint16)), seed, np.float32(eps), np.float32(lr),
+                           C.byref(lp), C.byref(lm), C.byref(g))
+        return lp.value, lm.value, g.value
+
+
+# ---------------- reference-compiled library ----------------
+def ref_lib(model: str):
+    """oracle/_ref/libref_<model>.so, or None when it was not built (no reference tree)."""
+    p = HERE / "_ref" / f"libref_{model}.so"
+    if not p.exists():
+        return None
+    L = C.CDLL(str(p))
+    L.ref_cross_entropy.restype = C.c_float
+    L.ref_forward_loss.restype = C.c_float
+    return L

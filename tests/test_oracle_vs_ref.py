@@ -1,0 +1,88 @@
+"""Pin the oracle restatement to the reference's own C, compiled in place from
+the AutoANE tree (oracle/_ref, built by oracle/build.py): cpu_ops.h's rmsnorm,
+rope, SDPA and cross-entropy, and the DO_FORWARD_PASS transcription over them.
+Skipped where oracle/_ref was not built (no reference tree at build time)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import _models as M
+
+F = C.POINTER(C.c_float)
+
+
+def f(a):
+    return a.ctypes.data_as(F)
+
+
+def need(model):
+    lib = O.ref_lib(model)
+    if lib is None:
+        pytest.skip("oracle/_ref not built (reference tree absent at build time)")
+    return lib
+
+
+def test_rmsnorm_rope_sdpa_ce_bit_exact():
+    ref = need("autoresearch")
+    rng = np.random.default_rng(3)
+    d, S, hd, heads = 512, 128, 64, 8
+    x = rng.standard_normal((d, S), dtype=np.float32)
+    w = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    a, b = np.zeros_like(x), np.zeros_like(x)
+    ref.ref_rmsnorm(f(a), f(x), f(w), d, S)
+    O.lib().or_rmsnorm(f(b), f(x), f(w), d, S)
+    assert np.array_equal(a, b)
+    q1, q2 = x.copy(), x.copy()
+    ref.ref_rope_forward(f(q1), S, d, hd)  # autoresearch header: default ROPE_THETA 10000
+    O.lib().or_rope_forward(f(q2), S, d, hd, C.c_float(10000.0))
+    assert np.array_equal(q1, q2)
+    K = rng.standard_normal((d, S), dtype=np.float32)
+    V = rng.standard_normal((d, S), dtype=np.float32)
+    o1, o2 = np.zeros_like(x), np.zeros_like(x)
+    ref.ref_sdpa_forward(f(x), f(K), f(V), f(o1), heads, hd, S)
+    O.lib().or_sdpa_forward(f(x), f(K), f(V), f(o2), heads, hd, S)
+    assert np.array_equal(o1, o2)
+    logits = (3 * rng.standard_normal((S, 777))).astype(np.float32)
+    tg = rng.integers(0, 777, S).astype(np.uint16)
+    dl = np.zeros_like(logits)
+    u16 = tg.ctypes.data_as(C.POINTER(C.c_uint16))
+    l1 = ref.ref_cross_entropy(f(dl), f(logits), u16, 777, S)
+    l2 = O.lib().or_cross_entropy(f(logits), u16, 777, S)
+    assert l1 == l2
+
+
+@pytest.mark.parametrize("model,cfg", [("autoresearch", M.AUTORESEARCH), ("autoresearch_mha", M.AUTORESEARCH_MHA)])
+def test_forward_loss_matches_reference_code(model, cfg):
+    ref = need(model)
+    syn = M.make_model(cfg, n_active=3000, seed=5, b_scale=0.01, rms_jitter=0.05)
+    toks = M.make_tokens(4096, 3000, seed=5)
+    inp, tgt = M.sample_sequence(toks, cfg.seq, syn.full_to_compact, 17)
+    om = O.OracleModel(cfg, syn.weights, syn.embed, syn.cembed)
+    loss_o = om.forward_loss(syn.theta, inp, tgt)
+    L, lay = cfg.nlayers, syn.layout
+    keep = []
+
+    def plist(arrs):
+        p = (F * len(arrs))(*[f(a) for a in arrs])
+        keep.append((arrs, p))
+        return p
+
+    lora, rms = [], []
+    for l in range(L):
+        base = l * lay.layer_size
+        for off in (lay.Aq, lay.Bq, lay.Ak, lay.Bk, lay.Av, lay.Bv, lay.Ao, lay.Bo):
+            lora.append(syn.theta[base + off:])
+        rms += [syn.theta[base + lay.rms_att:], syn.theta[base + lay.rms_ffn:]]
+    lora = [np.ascontiguousarray(a) for a in lora]
+    rms = [np.ascontiguousarray(a) for a in rms]
+    ref.ref_forward_loss.argtypes = [C.POINTER(F)] * 9 + [F, F, F, C.c_int, C.c_int, C.c_float,
+                                                          C.POINTER(C.c_uint16), C.POINTER(C.c_uint16)]
+    rf = np.ascontiguousarray(syn.theta[lay.rms_final:])
+    loss_r = ref.ref_forward_loss(*[plist(syn.weights[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")],
+                                  plist(lora), plist(rms), f(rf), f(syn.embed), f(syn.cembed), syn.cembed.shape[0],
+                                  cfg.rank, C.c_float(cfg.res_alpha), inp.ctypes.data_as(C.POINTER(C.c_uint16)),
+                                  tgt.ctypes.data_as(C.POINTER(C.c_uint16)))
+    assert abs(loss_o - loss_r) < 1e-5, (loss_o, loss_r)
+    assert 7.0 < loss_o < 9.0  # ≈ ln(3000) for a random-init model
