@@ -34,7 +34,33 @@ ABI: dict[str, tuple] = {
     "b2p_version": (cstr, []),
     "b2p_device_status": (i32, [vp]),
     "b2p_gemm": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+    "b2p_model_create": (vp, [vp]),
+    "b2p_model_free": (None, [vp]),
+    "b2p_model_trainable_count": (i64, [vp]),
+    "b2p_model_stream": (vp, [vp]),
+    "b2p_model_set_layer": (i32, [vp, i32, fp, fp, fp, fp, fp, fp, fp]),
+    "b2p_model_set_embedding": (i32, [vp, fp, ip, i32]),
+    "b2p_model_set_trainable": (i32, [vp, vp, i64]),
+    "b2p_model_get_trainable": (i32, [vp, vp, i64]),
+    "b2p_model_eval": (i32, [vp, u16p, u16p, i32, vp, i32, fp]),
+    "b2p_mezo_step": (i32, [vp, u16p, u16p, u64, f32, f32, fp, fp, fp]),
+    "b2p_mezo_eval": (i32, [vp, u16p, u16p, i32, u64p, i32, f32, vp]),
+    "b2p_mezo_update": (i32, [vp, u64p, vp, i32, f32, f32]),
+    "b2p_model_perturb": (i32, [vp, u64p, fp, i32]),
+    "b2p_sign_masks": (i32, [vp, u64p, i32, C.POINTER(C.c_uint32)]),
 }
+
+
+class ModelConfig(C.Structure):
+    """b2p_model_config (include/b2p.h)."""
+    _fields_ = [(n, C.c_int) for n in ("dim", "hidden", "heads", "kv_heads", "head_dim", "seq", "nlayers", "vocab",
+                                        "rank")] + [("rope_theta", C.c_float), ("res_alpha", C.c_float),
+                                                     ("dtype", C.c_int), ("max_groups", C.c_int)]
+
+
+class Variant(C.Structure):
+    """b2p_variant (include/b2p.h)."""
+    _fields_ = [("seed", C.c_uint64), ("mode", C.c_int), ("s1", C.c_float), ("s2", C.c_float)]
 
 
 class B2PError(RuntimeError):

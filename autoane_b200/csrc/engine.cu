@@ -167,7 +167,9 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
     switch (kind) {
       case EPI_F32: return dispatch_bn<EPI_F32, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_H16: return dispatch_bn<EPI_H16, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_QKV_ROPE: return launch_t<160, EPI_QKV_ROPE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_QKV_ROPE:
+        return bn == 128 ? launch_t<128, EPI_QKV_ROPE, H, true>(X, ldx, W, ldw, M, N, K, ep, st)
+                         : launch_t<160, EPI_QKV_ROPE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_RESID: return dispatch_bn<EPI_RESID, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_SWIGLU: return launch_t<256, EPI_SWIGLU, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_CE: return launch_t<256, EPI_CE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
@@ -177,7 +179,9 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
     switch (kind) {
       case EPI_F32: return dispatch_bn<EPI_F32, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_H16: return dispatch_bn<EPI_H16, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_QKV_ROPE: return launch_t<160, EPI_QKV_ROPE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
+      case EPI_QKV_ROPE:
+        return bn == 128 ? launch_t<128, EPI_QKV_ROPE, H, false>(X, ldx, W, ldw, M, N, K, ep, st)
+                         : launch_t<160, EPI_QKV_ROPE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_RESID: return dispatch_bn<EPI_RESID, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_SWIGLU: return launch_t<256, EPI_SWIGLU, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
       case EPI_CE: return launch_t<256, EPI_CE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);

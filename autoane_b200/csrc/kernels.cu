@@ -1,0 +1,573 @@
+// kernels.cu — glue kernels (embedding, RMSNorm + LoRA-down, attention,
+// cross-entropy reduction, perturbation steps, layout conversion).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include "engine.cuh"
+#include "kernels.cuh"
+
+namespace b2p {
+
+template <typename T>
+struct H2;
+template <>
+struct H2<__half> {
+  using V = __half2;
+  static __device__ __forceinline__ float2 to_f2(V v) { return __half22float2(v); }
+  static __device__ __forceinline__ V from_f2(float a, float b) { return __floats2half2_rn(a, b); }
+};
+template <>
+struct H2<__nv_bfloat16> {
+  using V = __nv_bfloat162;
+  static __device__ __forceinline__ float2 to_f2(V v) { return __bfloat1622float2(v); }
+  static __device__ __forceinline__ V from_f2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// embedding gather
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const float* __restrict__ embed, int vocab, int dim, const int32_t* __restrict__ tokens,
+                             const int* __restrict__ group_seq, int seq, int rows, float* __restrict__ x,
+                             uint32_t* status) {
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const int g = row / seq, t = row - g * seq;
+  const int tok = tokens[(long long)group_seq[g] * seq + t];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) atomicCAS(status, 0u, (uint32_t)DEV_BAD_ARGS);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(embed + (long long)tok * dim);
+  float4* dst = reinterpret_cast<float4*>(x + (long long)row * dim);
+  for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+}
+
+int launch_embed(const float* embed, int vocab, int dim, const int32_t* tokens, const int* group_seq, int seq,
+                 int rows, float* x, uint32_t* status, cudaStream_t st) {
+  B2P_REQUIRE(dim % 4 == 0, "dim must be a multiple of 4");
+  embed_kernel<<<rows, 128, 0, st>>>(embed, vocab, dim, tokens, group_seq, seq, rows, x, status);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm (perturbed weight) + LoRA-down (perturbed A), one warp per token row
+// ---------------------------------------------------------------------------
+constexpr int kNormRowsPerBlock = 64;
+constexpr int kNormThreads = 256;
+
+template <int NP, typename T, bool NORM>
+__global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a) {
+  extern __shared__ float sm[];
+  float* s_w = sm;                  // [dim]   perturbed rms weight
+  float* s_a = sm + a.dim;          // [n_a * rank][dim] perturbed LoRA A rows
+  using HV = typename H2<T>::V;
+  const int dim = a.dim;
+  const int row0 = blockIdx.x * kNormRowsPerBlock;
+  const int grp = row0 / a.pc.group_rows;
+  const VariantInfo vi = a.pc.variants[a.pc.group_variant[grp]];
+  const uint32_t* mask = a.pc.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.pc.mask_words;
+  const int nrows_a = a.n_a * a.rank;
+
+  // stage perturbed operands: θ (+ s1 z) (+ s2 z), exactly as perturb_buffer adds them
+  if (NORM) {
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+      const long long p = a.w_off + c;
+      const float th = __ldg(a.pc.theta + p);
+      s_w[c] = vi.mode ? perturb_value(th, mask_bit(mask, p), vi) : th;
+    }
+  }
+  for (int i = threadIdx.x; i < nrows_a * dim; i += blockDim.x) {
+    const int ja = i / dim, c = i - ja * dim;
+    const int m = ja / a.rank, j = ja - m * a.rank;
+    const long long p = a.a_off[m] + (long long)j * dim + c;
+    const float th = __ldg(a.pc.theta + p);
+    s_a[i] = vi.mode ? perturb_value(th, mask_bit(mask, p), vi) : th;
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kNormThreads / 32;
+  for (int r = warp; r < kNormRowsPerBlock; r += kWarps) {
+    const int row = row0 + r;
+    if (row >= a.rows) break;
+    float2 v[NP];
+    if (NORM) {
+      const float2* src = reinterpret_cast<const float2*>(static_cast<const float*>(a.in) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = src[lane + 32 * k];
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
+      ss = warp_sum(ss);
+      const float m = __fmul_rn(ss, 1.0f / (float)dim);
+      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
+      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        const int c = 2 * (lane + 32 * k);
+        v[k].x = __fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]);
+        v[k].y = __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]);
+        dst[lane + 32 * k] = H2<T>::from_f2(v[k].x, v[k].y);
+      }
+    } else {
+      const HV* src = reinterpret_cast<const HV*>(static_cast<const T*>(a.in) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = H2<T>::to_f2(src[lane + 32 * k]);
+    }
+    for (int ja = 0; ja < nrows_a; ++ja) {
+      const float2* arow = reinterpret_cast<const float2*>(s_a + (long long)ja * dim);
+      float p = 0.f;
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        const float2 w = arow[lane + 32 * k];
+        p = fmaf(v[k].x, w.x, p);
+        p = fmaf(v[k].y, w.y, p);
+      }
+      p = warp_sum(p);
+      if (lane == 0) a.U[(long long)row * a.ldu + a.u_col + ja] = p;
+    }
+  }
+}
+
+template <typename T, bool NORM>
+static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
+  const int np = a.dim / 64;
+  const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);
+  const int blocks = (a.rows + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
+#define B2P_NL_CASE(N)                                                                                   \
+  case N: {                                                                                            \
+    auto k = norm_lora_kernel<N, T, NORM>;                                                             \
+    B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));  \
+    k<<<blocks, kNormThreads, smem, st>>>(a);                                                          \
+    break;                                                                                             \
+  }
+  switch (np) {
+    B2P_NL_CASE(4)
+    B2P_NL_CASE(8)
+    B2P_NL_CASE(12)
+    B2P_NL_CASE(15)
+    B2P_NL_CASE(16)
+    B2P_NL_CASE(20)
+    B2P_NL_CASE(24)
+    B2P_NL_CASE(32)
+    B2P_NL_CASE(40)
+    default:
+      set_error("norm/LoRA-down: unsupported width %d (need dim/64 in {4,8,12,15,16,20,24,32,40})", a.dim);
+      return B2P_ERR_UNSUPPORTED;
+  }
+#undef B2P_NL_CASE
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(a.dim % 64 == 0, "dim %d must be a multiple of 64", a.dim);
+  B2P_REQUIRE(a.n_a >= 0 && a.n_a <= 3 && (a.n_a == 0 || a.rank > 0), "bad LoRA-down count");
+  B2P_REQUIRE(a.pc.group_rows % kNormRowsPerBlock == 0, "variant groups must be multiples of %d rows",
+              kNormRowsPerBlock);
+  const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);
+  B2P_REQUIRE(smem <= 227 * 1024, "LoRA-down operands (%zu bytes) exceed shared memory", smem);
+  if (a.norm) return bf16 ? launch_norm_lora_t<__nv_bfloat16, true>(a, st) : launch_norm_lora_t<__half, true>(a, st);
+  return bf16 ? launch_norm_lora_t<__nv_bfloat16, false>(a, st) : launch_norm_lora_t<__half, false>(a, st);
+}
+
+// ---------------------------------------------------------------------------
+// causal GQA attention, head_dim 64, 64-query x 64-key tiles, mma.sync m16n8k16
+// ---------------------------------------------------------------------------
+constexpr int kAttnTile = 64;
+constexpr int kHD = 64;
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [64][64] 16-bit tile
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  auto v = H2<T>::from_f2(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Loads a [64 rows][64 cols] 16-bit tile (row pitch ld elements) into swizzled smem.
+template <typename T>
+__device__ __forceinline__ void load_tile_async(uint32_t s_base, const T* g, long long ld) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int idx = threadIdx.x + i * 128;  // 512 chunks of 16 B
+    const int r = idx >> 3, c = idx & 7;
+    cp_async16(s_base + swz(r, c), g + r * ld + c * 8);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) attn_fwd_kernel(AttnArgs a, float scale_log2) {
+  __shared__ __align__(128) uint8_t s_q[kAttnTile * kHD * 2];
+  __shared__ __align__(128) uint8_t s_k[2][kAttnTile * kHD * 2];
+  __shared__ __align__(128) uint8_t s_v[2][kAttnTile * kHD * 2];
+  const int nqb = a.seq / kAttnTile;
+  const int qb = nqb - 1 - blockIdx.x;  // longest rows first
+  const int h = blockIdx.y, g = blockIdx.z;
+  const int kvh = h / (a.heads / a.kv_heads);
+  const T* base = static_cast<const T*>(a.qkv) + (long long)g * a.seq * a.ld_qkv;
+  const T* gq = base + (long long)qb * kAttnTile * a.ld_qkv + a.q_off + h * kHD;
+  const T* gk = base + a.k_off + kvh * kHD;
+  const T* gv = base + a.v_off + kvh * kHD;
+  const uint32_t sq = smem_u32(s_q), sk0 = smem_u32(s_k[0]), sv0 = smem_u32(s_v[0]);
+  constexpr uint32_t kTileBytes = kAttnTile * kHD * 2;
+
+  load_tile_async<T>(sq, gq, a.ld_qkv);
+  load_tile_async<T>(sk0, gk, a.ld_qkv);
+  load_tile_async<T>(sv0, gv, a.ld_qkv);
+  cp_async_commit();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lg = lane >> 2, lt = lane & 3;
+  const int lm = lane >> 3, lr = lane & 7;
+
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  uint32_t qf[4][4];
+
+  for (int kb = 0; kb <= qb; ++kb) {
+    const int buf = kb & 1;
+    if (kb + 1 <= qb) {
+      load_tile_async<T>(sk0 + (buf ^ 1) * kTileBytes, gk + (long long)(kb + 1) * kAttnTile * a.ld_qkv, a.ld_qkv);
+      load_tile_async<T>(sv0 + (buf ^ 1) * kTileBytes, gv + (long long)(kb + 1) * kAttnTile * a.ld_qkv, a.ld_qkv);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        ldsm_x4(sq + swz(warp * 16 + (lm & 1) * 8 + lr, kk * 2 + (lm >> 1)), qf[kk][0], qf[kk][1], qf[kk][2],
+                qf[kk][3]);
+    }
+    const uint32_t skb = sk0 + buf * kTileBytes, svb = sv0 + buf * kTileBytes;
+    // S = Q K^T  (16 query rows x 64 keys per warp)
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(skb + swz(nt * 16 + (lm >> 1) * 8 + lr, kk * 2 + (lm & 1)), b0, b1, b2, b3);
+        mma16816<T>(s[2 * nt], qf[kk], b0, b1);
+        mma16816<T>(s[2 * nt + 1], qf[kk], b2, b3);
+      }
+    }
+    // scale (log2 domain), causal mask on the diagonal tile, online softmax
+    const int q_row0 = warp * 16 + lg;  // within the tile; second row is +8
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = s[nt][e] * scale_log2;
+        if (kb == qb) {
+          const int key = nt * 8 + 2 * lt + (e & 1);
+          const int qr = q_row0 + ((e >> 1) << 3);
+          if (key > qr) v = -INFINITY;
+        }
+        s[nt][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+    }
+    float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float m_new = fmaxf(m_run[i], mx[i]);
+      corr[i] = exp2f(m_run[i] - m_new);
+      m_run[i] = m_new;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(s[nt][e] - m_run[e >> 1]);
+        s[nt][e] = p;
+        rs[e >> 1] += p;
+      }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 1);
+      rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 2);
+      l_run[i] = l_run[i] * corr[i] + rs[i];
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      o[nt][0] *= corr[0];
+      o[nt][1] *= corr[0];
+      o[nt][2] *= corr[1];
+      o[nt][3] *= corr[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t pa[4];
+      pa[0] = pack_h2<T>(s[2 * kc][0], s[2 * kc][1]);
+      pa[1] = pack_h2<T>(s[2 * kc][2], s[2 * kc][3]);
+      pa[2] = pack_h2<T>(s[2 * kc + 1][0], s[2 * kc + 1][1]);
+      pa[3] = pack_h2<T>(s[2 * kc + 1][2], s[2 * kc + 1][3]);
+#pragma unroll
+      for (int dt = 0; dt < 4; ++dt) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(svb + swz(kc * 16 + (lm & 1) * 8 + lr, dt * 2 + (lm >> 1)), b0, b1, b2, b3);
+        mma16816<T>(o[2 * dt], pa, b0, b1);
+        mma16816<T>(o[2 * dt + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled two iterations later
+  }
+  // normalise and store
+  const float inv0 = 1.0f / l_run[0], inv1 = 1.0f / l_run[1];
+  T* out = static_cast<T*>(a.out) + ((long long)g * a.seq + qb * kAttnTile + warp * 16 + lg) * a.ld_out + h * kHD;
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    const int col = nt * 8 + 2 * lt;
+    *reinterpret_cast<uint32_t*>(out + col) = pack_h2<T>(o[nt][0] * inv0, o[nt][1] * inv0);
+    *reinterpret_cast<uint32_t*>(out + 8LL * a.ld_out + col) = pack_h2<T>(o[nt][2] * inv1, o[nt][3] * inv1);
+  }
+}
+
+int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(a.seq % kAttnTile == 0, "attention needs seq %% 64 == 0 (got %d)", a.seq);
+  B2P_REQUIRE(a.kv_heads > 0 && a.heads % a.kv_heads == 0, "heads must be a multiple of kv_heads");
+  B2P_REQUIRE(a.ld_qkv % 8 == 0 && a.q_off % 8 == 0 && a.k_off % 8 == 0 && a.v_off % 8 == 0 && a.ld_out % 2 == 0,
+              "attention operands must be 16-byte aligned");
+  dim3 grid(a.seq / kAttnTile, a.heads, a.ngroups);
+  const float scale_log2 = (1.0f / sqrtf((float)kHD)) * 1.4426950408889634f;
+  if (bf16)
+    attn_fwd_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a, scale_log2);
+  else
+    attn_fwd_kernel<__half><<<grid, 128, 0, st>>>(a, scale_log2);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+// ---------------------------------------------------------------------------
+// cross-entropy reduction
+// ---------------------------------------------------------------------------
+__global__ void ce_reduce_kernel(const float2* __restrict__ part, int ntiles, const float* __restrict__ tgt_logit,
+                                 int seq, float* __restrict__ row_loss, float* __restrict__ group_loss) {
+  __shared__ float red[256];
+  const int g = blockIdx.x;
+  float acc = 0.f;
+  for (int t = threadIdx.x; t < seq; t += blockDim.x) {
+    const long long row = (long long)g * seq + t;
+    const float2* p = part + row * ntiles;
+    float M = -INFINITY;
+    for (int i = 0; i < ntiles; ++i) M = fmaxf(M, p[i].x);
+    float S = 0.f;
+    for (int i = 0; i < ntiles; ++i) S += p[i].y * expf(p[i].x - M);
+    const float l = -(tgt_logit[row] - M) + logf(S);
+    row_loss[row] = l;
+    acc += l;
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) group_loss[g] = red[0] / (float)seq;
+}
+
+int launch_ce_reduce(const float2* part, int ntiles, const float* tgt_logit, int rows, int seq, float* row_loss,
+                     float* group_loss, cudaStream_t st) {
+  B2P_REQUIRE(rows % seq == 0, "rows must be whole sequences");
+  ce_reduce_kernel<<<rows / seq, 256, 0, st>>>(part, ntiles, tgt_logit, seq, row_loss, group_loss);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+__global__ void variant_loss_kernel(const float* group_loss, int n_var, int n_seq, float* var_loss) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= n_var) return;
+  float s = 0.f;
+  for (int q = 0; q < n_seq; ++q) s += group_loss[v * n_seq + q];
+  var_loss[v] = s / (float)n_seq;
+}
+
+int launch_variant_loss(const float* group_loss, int n_var, int n_seq, float* var_loss, cudaStream_t st) {
+  variant_loss_kernel<<<(n_var + 63) / 64, 64, 0, st>>>(group_loss, n_var, n_seq, var_loss);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+// ---------------------------------------------------------------------------
+// in-place Rademacher steps
+// ---------------------------------------------------------------------------
+__global__ void perturb_kernel(float* __restrict__ theta, long long n, const uint32_t* __restrict__ masks,
+                               long long mask_words, PerturbOps ops, const float* __restrict__ losses) {
+  __shared__ float s_scale[kMaxPerturbOps];
+  if (threadIdx.x < ops.n) {
+    const PerturbOp& op = ops.op[threadIdx.x];
+    float c = op.scale;
+    if (op.from_loss) {
+      const float lp = losses[2 * op.loss_idx], lm = losses[2 * op.loss_idx + 1];
+      const float g = __fdiv_rn(__fsub_rn(lp, lm), __fmul_rn(2.0f, op.eps));  // (L+ - L-) / (2 eps)
+      c = __fmul_rn(-op.lr, g);                                               // update_scale = -lr * g
+      if (op.div != 1.0f) c = __fdiv_rn(c, op.div);
+    }
+    s_scale[threadIdx.x] = c;
+  }
+  __syncthreads();
+  const long long w = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // one 32-parameter word per thread
+  if (w >= mask_words) return;
+  const long long p0 = w * 32;
+  const int cnt = (int)min(32LL, n - p0);
+  float v[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = k < cnt ? theta[p0 + k] : 0.f;
+  for (int o = 0; o < ops.n; ++o) {
+    const uint32_t bits = __ldg(masks + (long long)ops.op[o].slot * mask_words + w);
+    const float c = s_scale[o];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = __fadd_rn(v[k], ((bits >> k) & 1u) ? c : -c);
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k)
+    if (k < cnt) theta[p0 + k] = v[k];
+}
+
+int launch_perturb(float* theta, long long n, const uint32_t* masks, long long mask_words, const PerturbOps& ops,
+                   const float* losses, cudaStream_t st) {
+  B2P_REQUIRE(ops.n >= 0 && ops.n <= kMaxPerturbOps, "too many perturbation ops (%d)", ops.n);
+  if (ops.n == 0) return B2P_OK;
+  const int threads = 128;
+  perturb_kernel<<<(unsigned)((mask_words + threads - 1) / threads), threads, 0, st>>>(theta, n, masks, mask_words,
+                                                                                      ops, losses);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+// ---------------------------------------------------------------------------
+// layout conversion
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void cf_to_tm16_kernel(const float* __restrict__ src, int C, int S, T* __restrict__ dst, int ld) {
+  __shared__ float tile[32][33];
+  const int c0 = blockIdx.y * 32, s0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, s = s0 + threadIdx.x;
+    tile[i][threadIdx.x] = (c < C && s < S) ? src[(long long)c * S + s] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int s = s0 + i, c = c0 + threadIdx.x;
+    if (s < S && c < C) dst[(long long)s * ld + c] = static_cast<T>(tile[threadIdx.x][i]);
+  }
+}
+
+template <typename T, bool F32>
+__global__ void tm_to_cf32_kernel(const void* __restrict__ srcv, int ld, int C, int S, float* __restrict__ dst) {
+  __shared__ float tile[32][33];
+  const int c0 = blockIdx.y * 32, s0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int s = s0 + i, c = c0 + threadIdx.x;
+    float v = 0.f;
+    if (s < S && c < C)
+      v = F32 ? static_cast<const float*>(srcv)[(long long)s * ld + c]
+              : static_cast<float>(static_cast<const T*>(srcv)[(long long)s * ld + c]);
+    tile[i][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, s = s0 + threadIdx.x;
+    if (c < C && s < S) dst[(long long)c * S + s] = tile[threadIdx.x][i];
+  }
+}
+
+int launch_cf_to_tm16(const float* src, int C, int S, void* dst, int ld_dst, bool bf16, cudaStream_t st) {
+  dim3 grid((S + 31) / 32, (C + 31) / 32), block(32, 8);
+  if (bf16)
+    cf_to_tm16_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(src, C, S, static_cast<__nv_bfloat16*>(dst), ld_dst);
+  else
+    cf_to_tm16_kernel<__half><<<grid, block, 0, st>>>(src, C, S, static_cast<__half*>(dst), ld_dst);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int C, int S, float* dst,
+                      cudaStream_t st) {
+  dim3 grid((S + 31) / 32, (C + 31) / 32), block(32, 8);
+  if (src_f32)
+    tm_to_cf32_kernel<float, true><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
+  else if (bf16)
+    tm_to_cf32_kernel<__nv_bfloat16, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
+  else
+    tm_to_cf32_kernel<__half, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+template <typename T>
+__global__ void f32_to_16_kernel(const float* __restrict__ src, T* __restrict__ dst, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = static_cast<T>(src[i]);
+}
+
+int launch_f32_to_16(const float* src, void* dst, long long n, bool bf16, cudaStream_t st) {
+  const long long nb = (n + 255) / 256;
+  const int blocks = (int)(nb < 148 * 16 ? nb : 148 * 16);
+  if (bf16)
+    f32_to_16_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), n);
+  else
+    f32_to_16_kernel<__half><<<blocks, 256, 0, st>>>(src, static_cast<__half*>(dst), n);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+}  // namespace b2p

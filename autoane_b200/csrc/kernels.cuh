@@ -1,0 +1,90 @@
+// kernels.cuh — glue kernels around the projection engine (token-major layout).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "gemm.cuh"
+
+namespace b2p {
+
+// Perturbation context shared by the fused kernels: which variant (θ, θ+εz,
+// θ+εz-2εz) each group of `group_rows` token rows evaluates.
+struct PerturbCtx {
+  const float* theta;
+  const uint32_t* masks;
+  long long mask_words;
+  const VariantInfo* variants;
+  const int* group_variant;
+  int group_rows;
+};
+
+// x[row, :] = embed[token(row), :]  (reference embed_lookup, training/cpu_ops.h:190-197)
+// token(row) = tokens[group_seq[row / seq] * seq + row % seq]
+int launch_embed(const float* embed, int vocab, int dim, const int32_t* tokens, const int* group_seq, int seq,
+                 int rows, float* x, uint32_t* status, cudaStream_t st);
+
+// Per token row: optional RMSNorm with the perturbed weight at theta[w_off]
+// (training/cpu_ops.h:7-22) written as 16-bit xn, then U[row, u_col + i*r + j] =
+// A_i(perturbed)[j, :] · v for the n_a LoRA-down matrices at theta[a_off[i]]
+// (first half of lora_addmm, training/train_mezo.m:698), v = normalised row in fp32
+// (norm) or the 16-bit input row (no norm).
+struct NormLoraArgs {
+  const void* in;       // fp32 [rows, dim] (norm) or 16-bit [rows, dim]
+  void* xn;             // 16-bit [rows, dim] (norm only)
+  int rows, dim;
+  int norm;             // 1: RMSNorm with weight, 0: LoRA-down of the raw 16-bit input
+  long long w_off;      // rms weight offset in theta
+  int n_a;              // number of LoRA-down matrices (0..3)
+  long long a_off[3];
+  int rank;
+  float* U;
+  int ldu, u_col;
+  PerturbCtx pc;
+};
+int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st);
+
+// Causal GQA attention over token-major Q|K|V rows (reference cpu_sdpa_forward,
+// training/cpu_ops.h:321-360, with gqa_tile_kv, training/io.h:439-446):
+// out[row, h*hd + d] for every group of `seq` rows. hd = 64.
+struct AttnArgs {
+  const void* qkv;
+  int ld_qkv, q_off, k_off, v_off;
+  void* out;
+  int ld_out;
+  int seq, heads, kv_heads, ngroups;
+};
+int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st);
+
+// Row losses from the lm-head partials: loss_row = -(logit_tgt - M) + log(Σ s_i e^{m_i - M})
+// (training/cpu_ops.h:108-133); group_loss[g] = mean over the group's rows.
+int launch_ce_reduce(const float2* part, int ntiles, const float* tgt_logit, int rows, int seq, float* row_loss,
+                     float* group_loss, cudaStream_t st);
+// var_loss[v] = mean of group_loss over the n_seq groups of variant v (groups v*n_seq + q).
+int launch_variant_loss(const float* group_loss, int n_var, int n_seq, float* var_loss, cudaStream_t st);
+
+// In-place Rademacher steps on the trainable parameters (perturb_buffer,
+// training/train_mezo.m:122-136), applied in order: θ_i ← fl(θ_i + (z_i ? c : -c)).
+// The scale c of an op is either fixed, or computed on the device from a loss
+// pair as the MeZO update -lr·(L+ - L-)/(2ε) / div (train_mezo.m:2997-3012).
+struct PerturbOp {
+  int slot;          // mask row
+  int from_loss;     // 0: fixed `scale`; 1: from losses[2*loss_idx], losses[2*loss_idx+1]
+  int loss_idx;
+  float scale;
+  float eps, lr, div;
+};
+constexpr int kMaxPerturbOps = 64;
+struct PerturbOps {
+  int n;
+  PerturbOp op[kMaxPerturbOps];
+};
+int launch_perturb(float* theta, long long n, const uint32_t* masks, long long mask_words, const PerturbOps& ops,
+                   const float* losses, cudaStream_t st);
+
+// Layout conversion for the Kern-style boundary: host channel-first fp32 [C, S]
+// <-> device token-major 16-bit / fp32 [S, C].
+int launch_cf_to_tm16(const float* src, int C, int S, void* dst, int ld_dst, bool bf16, cudaStream_t st);
+int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int C, int S, float* dst,
+                      cudaStream_t st);
+int launch_f32_to_16(const float* src, void* dst, long long n, bool bf16, cudaStream_t st);
+
+}  // namespace b2p

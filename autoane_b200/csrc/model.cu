@@ -1,0 +1,705 @@
+// model.cu — device-resident SmolLM2/Llama-style model for the MeZO-LoRA-split
+// path: frozen 16-bit base weights, fp32 master copy of the trainable LoRA/RMS
+// parameters (reference order, train_mezo.m:560-588), device sign masks, and a
+// batched forward over groups of (variant, sequence).
+//
+// One forward evaluates G = n_var * n_seq groups of `seq` token rows at once
+// (group g = v * n_seq + q evaluates sequence q under variant v), so the base
+// projection weights are read once per layer for all ±ε evaluations.
+#include <cmath>
+#include <cstring>
+#include <vector>
+#include "../../include/b2p.h"
+#include "engine.cuh"
+#include "kernels.cuh"
+#include "rng.cuh"
+
+using namespace b2p;
+
+struct b2p_model {
+  b2p_model_config cfg{};
+  int device = 0;
+  bool bf16 = false;
+  cudaStream_t st = nullptr;
+  int q_dim = 0, kv_dim = 0, qkv_dim = 0, ffn2 = 0;
+  // trainable layout (offsets inside a layer block, then rms_final)
+  long long oAq, oBq, oAk, oBk, oAv, oBv, oAo, oBo, oRa, oRf, layer_size, oRfinal, P;
+  // frozen weights (16-bit), per-layer contiguous
+  void *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr, *cembed = nullptr;
+  float* embed = nullptr;
+  int cv = 0;
+  std::vector<char> layer_set;
+  bool embed_set = false;
+  // trainable params + sign masks
+  float* theta = nullptr;
+  uint32_t* masks = nullptr;
+  int max_slots = 0;
+  long long mask_words = 0;
+  SignBuffer* d_bufs = nullptr;
+  int nbufs = 0;
+  uint64_t* d_jumps = nullptr;
+  int njump = 0;
+  long long total_draws = 0;
+  uint64_t* d_seeds = nullptr;
+  // activations
+  int max_groups = 0, max_rows = 0, n_vt = 0;
+  float* x = nullptr;
+  void* xn = nullptr;
+  float* U = nullptr;
+  void* qkv = nullptr;
+  void* attn = nullptr;
+  void* hbuf = nullptr;
+  float2* ce_part = nullptr;
+  float* ce_tgt = nullptr;
+  float* row_loss = nullptr;
+  float* group_loss = nullptr;
+  float* var_loss = nullptr;
+  float* pairs = nullptr;        // [2 * kMaxPerturbOps] loss pairs for updates
+  int qkv_bn = 160;
+  int32_t* d_tok = nullptr;      // [max_seq_in][seq] tokens then targets
+  int32_t* d_row_tgt = nullptr;  // [max_rows]
+  int* d_meta = nullptr;         // group_seq[max_groups] | group_var[max_groups]
+  VariantInfo* d_var = nullptr;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  // pinned host staging
+  int32_t* h_tok = nullptr;
+  int* h_meta = nullptr;
+  VariantInfo* h_var = nullptr;
+  uint64_t* h_seeds = nullptr;
+  float* h_loss = nullptr;
+};
+
+namespace {
+
+constexpr int kU_cols = 32;  // U columns: q, k, v, o LoRA-down (rank <= 8 each)
+
+size_t esz(const b2p_model*) { return 2; }
+
+int model_alloc(b2p_model* m) {
+  const auto& c = m->cfg;
+  const size_t e = esz(m);
+  const size_t L = c.nlayers;
+  B2P_CHECK_CUDA(cudaMalloc(&m->wqkv, L * m->qkv_dim * c.dim * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->wo, L * c.dim * m->q_dim * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->w13, L * 2 * c.hidden * c.dim * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->w2, L * c.dim * c.hidden * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->embed, (size_t)c.vocab * c.dim * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->theta, m->P * 4));
+  B2P_CHECK_CUDA(cudaMemset(m->theta, 0, m->P * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->masks, (size_t)m->max_slots * m->mask_words * 4));
+  B2P_CHECK_CUDA(cudaMemset(m->masks, 0, (size_t)m->max_slots * m->mask_words * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->d_seeds, m->max_slots * 8));
+  const size_t R = m->max_rows;
+  B2P_CHECK_CUDA(cudaMalloc(&m->x, R * c.dim * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->xn, R * std::max(c.dim, m->q_dim) * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->U, R * kU_cols * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->qkv, R * m->qkv_dim * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->attn, R * m->q_dim * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->hbuf, R * c.hidden * e));
+  const int ntiles = (c.vocab + 255) / 256;  // enough for any compact vocabulary
+  B2P_CHECK_CUDA(cudaMalloc(&m->ce_part, R * ntiles * sizeof(float2)));
+  B2P_CHECK_CUDA(cudaMalloc(&m->ce_tgt, R * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->row_loss, R * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->group_loss, m->max_groups * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->var_loss, m->max_groups * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->pairs, 2 * kMaxPerturbOps * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->d_tok, (size_t)2 * m->max_groups * c.seq * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->d_row_tgt, R * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->d_meta, 2 * m->max_groups * sizeof(int)));
+  B2P_CHECK_CUDA(cudaMalloc(&m->d_var, m->max_groups * sizeof(VariantInfo)));
+  B2P_CHECK_CUDA(cudaMalloc(&m->rope_cos, (size_t)c.seq * (c.head_dim / 2) * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->rope_sin, (size_t)c.seq * (c.head_dim / 2) * 4));
+  B2P_CHECK_CUDA(cudaMallocHost(&m->h_tok, (size_t)2 * m->max_groups * c.seq * 4));
+  B2P_CHECK_CUDA(cudaMallocHost(&m->h_meta, 2 * m->max_groups * sizeof(int)));
+  B2P_CHECK_CUDA(cudaMallocHost(&m->h_var, m->max_groups * sizeof(VariantInfo)));
+  B2P_CHECK_CUDA(cudaMallocHost(&m->h_seeds, m->max_slots * 8));
+  B2P_CHECK_CUDA(cudaMallocHost(&m->h_loss, m->max_groups * 4));
+  // RoPE tables with the reference's expressions (training/cpu_ops.h:303-307)
+  const int half = c.head_dim / 2;
+  std::vector<float> cs((size_t)c.seq * half), sn((size_t)c.seq * half);
+  for (int i = 0; i < half; i++) {
+    const float freq = 1.0f / powf(c.rope_theta, 2.0f * i / (float)c.head_dim);
+    for (int p = 0; p < c.seq; p++) {
+      const float ang = p * freq;
+      cs[(size_t)p * half + i] = cosf(ang);
+      sn[(size_t)p * half + i] = sinf(ang);
+    }
+  }
+  B2P_CHECK_CUDA(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  B2P_CHECK_CUDA(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  return B2P_OK;
+}
+
+void model_release(b2p_model* m) {
+  void* dev[] = {m->wqkv, m->wo, m->w13, m->w2, m->cembed, m->embed, m->theta, m->masks, m->d_bufs,
+                 m->d_jumps, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
+                 m->ce_tgt, m->row_loss, m->group_loss, m->var_loss, m->pairs, m->d_tok, m->d_row_tgt, m->d_meta,
+                 m->d_var, m->rope_cos, m->rope_sin};
+  for (void* p : dev)
+    if (p) cudaFree(p);
+  void* host[] = {m->h_tok, m->h_meta, m->h_var, m->h_seeds, m->h_loss};
+  for (void* p : host)
+    if (p) cudaFreeHost(p);
+  if (m->st) cudaStreamDestroy(m->st);
+}
+
+// Convert an fp32 host matrix to 16-bit device storage at dst (row-major, same shape).
+int upload16(b2p_model* m, void* dst, const float* src, size_t n) {
+  float* tmp = nullptr;
+  B2P_CHECK_CUDA(cudaMallocAsync(&tmp, n * 4, m->st));
+  B2P_CHECK_CUDA(cudaMemcpyAsync(tmp, src, n * 4, cudaMemcpyHostToDevice, m->st));
+  int rc = launch_f32_to_16(tmp, dst, (long long)n, m->bf16, m->st);
+  B2P_CHECK_CUDA(cudaFreeAsync(tmp, m->st));
+  if (rc) return rc;
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
+}
+
+PerturbCtx pctx(const b2p_model* m) {
+  PerturbCtx pc;
+  pc.theta = m->theta;
+  pc.masks = m->masks;
+  pc.mask_words = m->mask_words;
+  pc.variants = m->d_var;
+  pc.group_variant = m->d_meta + m->max_groups;
+  pc.group_rows = m->cfg.seq;
+  return pc;
+}
+
+LoraEpi lora_epi(const b2p_model* m) {
+  LoraEpi le;
+  std::memset(&le, 0, sizeof(le));
+  le.theta = m->theta;
+  le.masks = m->masks;
+  le.mask_words = m->mask_words;
+  le.variants = m->d_var;
+  le.group_variant = m->d_meta + m->max_groups;
+  le.group_rows = m->cfg.seq;
+  le.U = m->U;
+  le.ldu = kU_cols;
+  le.rank = m->cfg.rank;
+  return le;
+}
+
+// The batched forward over G groups whose inputs are already staged on the device.
+int run_forward(b2p_model* m, int G) {
+  const auto& c = m->cfg;
+  const int R = G * c.seq;
+  const int D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim, QKV = m->qkv_dim;
+  const size_t e = esz(m);
+  DeviceCtx* ctx = nullptr;
+  int rc = ctx_get(&ctx);
+  if (rc) return rc;
+  const int* group_seq = m->d_meta;
+  const int32_t* tok = m->d_tok;
+  rc = launch_embed(m->embed, c.vocab, D, tok, group_seq, c.seq, R, m->x, ctx->status, m->st);
+  if (rc) return rc;
+  const PerturbCtx pc = pctx(m);
+  for (int l = 0; l < c.nlayers; ++l) {
+    const long long lb = (long long)l * m->layer_size;
+    // RMSNorm(rms_att) + LoRA-down for q, k, v
+    NormLoraArgs na;
+    std::memset(&na, 0, sizeof(na));
+    na.in = m->x;
+    na.xn = m->xn;
+    na.rows = R;
+    na.dim = D;
+    na.norm = 1;
+    na.w_off = lb + m->oRa;
+    na.n_a = 3;
+    na.a_off[0] = lb + m->oAq;
+    na.a_off[1] = lb + m->oAk;
+    na.a_off[2] = lb + m->oAv;
+    na.rank = c.rank;
+    na.U = m->U;
+    na.ldu = kU_cols;
+    na.u_col = 0;
+    na.pc = pc;
+    if ((rc = launch_norm_lora(na, m->bf16, m->st))) return rc;
+    // Q|K|V = xn · Wqkv^T + B·U (perturbed B), RoPE on Q and K
+    EpiParams ep;
+    std::memset(&ep, 0, sizeof(ep));
+    ep.M = R;
+    ep.N = QKV;
+    ep.out = m->qkv;
+    ep.ldo = QKV;
+    ep.has_lora = 1;
+    ep.lora = lora_epi(m);
+    ep.lora.nseg = 3;
+    ep.lora.seg_start[0] = 0;
+    ep.lora.seg_start[1] = QD;
+    ep.lora.seg_start[2] = QD + KVD;
+    ep.lora.seg_start[3] = QKV;
+    ep.lora.seg_boff[0] = lb + m->oBq;
+    ep.lora.seg_boff[1] = lb + m->oBk;
+    ep.lora.seg_boff[2] = lb + m->oBv;
+    ep.lora.seg_ucol[0] = 0;
+    ep.lora.seg_ucol[1] = c.rank;
+    ep.lora.seg_ucol[2] = 2 * c.rank;
+    ep.rope_cos = m->rope_cos;
+    ep.rope_sin = m->rope_sin;
+    ep.rope_cols = QD + KVD;
+    ep.head_dim = c.head_dim;
+    ep.seq_len = c.seq;
+    const char* wqkv = static_cast<const char*>(m->wqkv) + (size_t)l * QKV * D * e;
+    if ((rc = launch_gemm(m->qkv_bn, EPI_QKV_ROPE, m->bf16, m->xn, D, wqkv, D, R, QKV, D, ep, m->st))) return rc;
+    // attention
+    AttnArgs aa;
+    aa.qkv = m->qkv;
+    aa.ld_qkv = QKV;
+    aa.q_off = 0;
+    aa.k_off = QD;
+    aa.v_off = QD + KVD;
+    aa.out = m->attn;
+    aa.ld_out = QD;
+    aa.seq = c.seq;
+    aa.heads = c.heads;
+    aa.kv_heads = c.kv_heads;
+    aa.ngroups = G;
+    if ((rc = launch_attention(aa, m->bf16, m->st))) return rc;
+    // LoRA-down of the attention output for Wo
+    NormLoraArgs nb;
+    std::memset(&nb, 0, sizeof(nb));
+    nb.in = m->attn;
+    nb.rows = R;
+    nb.dim = QD;
+    nb.norm = 0;
+    nb.n_a = 1;
+    nb.a_off[0] = lb + m->oAo;
+    nb.rank = c.rank;
+    nb.U = m->U;
+    nb.ldu = kU_cols;
+    nb.u_col = 3 * c.rank;
+    nb.pc = pc;
+    if ((rc = launch_norm_lora(nb, m->bf16, m->st))) return rc;
+    // x += alpha * (attn · Wo^T + Bo·Uo)
+    EpiParams eo;
+    std::memset(&eo, 0, sizeof(eo));
+    eo.M = R;
+    eo.N = D;
+    eo.out = m->x;
+    eo.ldo = D;
+    eo.alpha = c.res_alpha;
+    eo.has_lora = 1;
+    eo.lora = lora_epi(m);
+    eo.lora.nseg = 1;
+    eo.lora.seg_start[0] = 0;
+    eo.lora.seg_start[1] = D;
+    eo.lora.seg_boff[0] = lb + m->oBo;
+    eo.lora.seg_ucol[0] = 3 * c.rank;
+    const char* wo = static_cast<const char*>(m->wo) + (size_t)l * D * QD * e;
+    if ((rc = launch_gemm(pick_bn(D, EPI_RESID), EPI_RESID, m->bf16, m->attn, QD, wo, QD, R, D, QD, eo, m->st)))
+      return rc;
+    // RMSNorm(rms_ffn)
+    NormLoraArgs nf;
+    std::memset(&nf, 0, sizeof(nf));
+    nf.in = m->x;
+    nf.xn = m->xn;
+    nf.rows = R;
+    nf.dim = D;
+    nf.norm = 1;
+    nf.w_off = lb + m->oRf;
+    nf.n_a = 0;
+    nf.pc = pc;
+    if ((rc = launch_norm_lora(nf, m->bf16, m->st))) return rc;
+    // h = silu(xn·W1^T) * (xn·W3^T)  (W1/W3 rows interleaved in 128-row blocks)
+    EpiParams es;
+    std::memset(&es, 0, sizeof(es));
+    es.M = R;
+    es.N = 2 * H;
+    es.out = m->hbuf;
+    es.ldo = H;
+    const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
+    if ((rc = launch_gemm(256, EPI_SWIGLU, m->bf16, m->xn, D, w13, D, R, 2 * H, D, es, m->st))) return rc;
+    // x += alpha * (h · W2^T)
+    EpiParams e2;
+    std::memset(&e2, 0, sizeof(e2));
+    e2.M = R;
+    e2.N = D;
+    e2.out = m->x;
+    e2.ldo = D;
+    e2.alpha = c.res_alpha;
+    const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
+    if ((rc = launch_gemm(pick_bn(D, EPI_RESID), EPI_RESID, m->bf16, m->hbuf, H, w2, H, R, D, H, e2, m->st)))
+      return rc;
+  }
+  // final RMSNorm + lm-head with fused cross-entropy partials
+  NormLoraArgs nl;
+  std::memset(&nl, 0, sizeof(nl));
+  nl.in = m->x;
+  nl.xn = m->xn;
+  nl.rows = R;
+  nl.dim = D;
+  nl.norm = 1;
+  nl.w_off = m->oRfinal;
+  nl.pc = pc;
+  if ((rc = launch_norm_lora(nl, m->bf16, m->st))) return rc;
+  const int ntiles = (m->cv + 255) / 256;
+  EpiParams ec;
+  std::memset(&ec, 0, sizeof(ec));
+  ec.M = R;
+  ec.N = m->cv;
+  ec.targets = m->d_row_tgt;
+  ec.ce_part = m->ce_part;
+  ec.ce_tgt = m->ce_tgt;
+  ec.n_tiles_n = ntiles;
+  if ((rc = launch_gemm(256, EPI_CE, m->bf16, m->xn, D, m->cembed, D, R, m->cv, D, ec, m->st))) return rc;
+  return launch_ce_reduce(m->ce_part, ntiles, m->ce_tgt, R, c.seq, m->row_loss, m->group_loss, m->st);
+}
+
+__global__ void expand_targets_kernel(const int32_t* seq_tgt, const int* group_seq, int seq, int rows,
+                                      int32_t* row_tgt) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int g = row / seq, t = row - g * seq;
+  row_tgt[row] = seq_tgt[(long long)group_seq[g] * seq + t];
+}
+
+// Stage tokens/targets of n_seq sequences and the group tables for n_var variants.
+int stage_inputs(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, int n_var) {
+  const auto& c = m->cfg;
+  const int G = n_seq * n_var;
+  B2P_REQUIRE(tokens && ctargets, "null token/target buffer");
+  B2P_REQUIRE(n_seq >= 1 && n_var >= 1 && G <= m->max_groups, "groups %d x %d exceed max_groups %d", n_var, n_seq,
+              m->max_groups);
+  const size_t nt = (size_t)n_seq * c.seq;
+  for (size_t i = 0; i < nt; ++i) {
+    B2P_REQUIRE(tokens[i] < c.vocab, "token[%zu]=%d out of range (vocab %d)", i, (int)tokens[i], c.vocab);
+    B2P_REQUIRE(ctargets[i] < m->cv, "target[%zu]=%d out of range (compact vocab %d)", i, (int)ctargets[i], m->cv);
+    m->h_tok[i] = tokens[i];
+    m->h_tok[nt + i] = ctargets[i];
+  }
+  for (int v = 0; v < n_var; ++v)
+    for (int q = 0; q < n_seq; ++q) {
+      m->h_meta[v * n_seq + q] = q;                      // group -> sequence
+      m->h_meta[m->max_groups + v * n_seq + q] = v;      // group -> variant
+    }
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_tok, m->h_tok, 2 * nt * 4, cudaMemcpyHostToDevice, m->st));
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_meta, m->h_meta, 2 * m->max_groups * sizeof(int), cudaMemcpyHostToDevice,
+                                 m->st));
+  expand_targets_kernel<<<(G * c.seq + 255) / 256, 256, 0, m->st>>>(m->d_tok + nt, m->d_meta, c.seq, G * c.seq,
+                                                                     m->d_row_tgt);
+  B2P_CHECK_CUDA(cudaGetLastError());
+  return B2P_OK;
+}
+
+int gen_masks(b2p_model* m, const uint64_t* seeds, int n) {
+  B2P_REQUIRE(n >= 1 && n <= m->max_slots, "seed count %d exceeds mask slots %d", n, m->max_slots);
+  for (int i = 0; i < n; ++i) m->h_seeds[i] = seeds[i];
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_seeds, m->h_seeds, n * 8, cudaMemcpyHostToDevice, m->st));
+  return launch_sign_masks(m->d_bufs, m->nbufs, m->d_jumps, m->njump, m->total_draws, m->mask_words, m->d_seeds, n,
+                           m->masks, m->st);
+}
+
+int ready(const b2p_model* m) {
+  if (!m) {
+    set_error("null model");
+    return B2P_ERR_ARG;
+  }
+  for (int l = 0; l < m->cfg.nlayers; ++l)
+    if (!m->layer_set[l]) {
+      set_error("layer %d weights not set", l);
+      return B2P_ERR_STATE;
+    }
+  if (!m->embed_set) {
+    set_error("embedding not set");
+    return B2P_ERR_STATE;
+  }
+  return B2P_OK;
+}
+
+// Evaluate the given variants (already staged into h_var) and leave per-variant
+// losses in m->var_loss.
+int eval_staged(b2p_model* m, int n_seq, int n_var) {
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_var, m->h_var, n_var * sizeof(VariantInfo), cudaMemcpyHostToDevice, m->st));
+  int rc = run_forward(m, n_seq * n_var);
+  if (rc) return rc;
+  return launch_variant_loss(m->group_loss, n_var, n_seq, m->var_loss, m->st);
+}
+
+int read_losses(b2p_model* m, float* out, int n) {
+  B2P_CHECK_CUDA(cudaMemcpyAsync(out, m->var_loss, n * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+}  // namespace
+
+extern "C" {
+
+b2p_model* b2p_model_create(const b2p_model_config* cfg) {
+  if (!cfg) {
+    set_error("null config");
+    return nullptr;
+  }
+  const auto& c = *cfg;
+  auto bad = [](const char* msg) -> b2p_model* {
+    set_error("%s", msg);
+    return nullptr;
+  };
+  if (c.dim <= 0 || c.dim % 64 || c.hidden <= 0 || c.hidden % 128 || c.head_dim != 64 || c.heads <= 0 ||
+      c.kv_heads <= 0 || c.heads % c.kv_heads || c.seq <= 0 || c.seq % 128 || c.nlayers <= 0 || c.vocab <= 0)
+    return bad("unsupported shape: need dim %% 64 == 0, hidden %% 128 == 0, head_dim 64, seq %% 128 == 0");
+  if (c.rank != 4 && c.rank != 8) return bad("LoRA rank must be 4 or 8");
+  if (c.dtype != B2P_F16 && c.dtype != B2P_BF16) return bad("dtype must be B2P_F16 or B2P_BF16");
+  if (c.max_groups < 1) return bad("max_groups must be >= 1");
+  const int qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
+  if (qd % 128 && qd % 160) return bad("q_dim must be a multiple of 128 or 160");
+  const int qkv_bn = (qd % 160 == 0 && kvd % 160 == 0) ? 160 : ((qd % 128 == 0 && kvd % 128 == 0) ? 128 : 0);
+  if (!qkv_bn) return bad("q_dim and kv_dim need a common Q|K|V tile width (128 or 160)");
+  b2p_model* m = new b2p_model();
+  m->qkv_bn = qkv_bn;
+  m->cfg = c;
+  m->bf16 = c.dtype == B2P_BF16;
+  m->q_dim = qd;
+  m->kv_dim = kvd;
+  m->qkv_dim = qd + 2 * kvd;
+  const long long r = c.rank, D = c.dim, Q = qd, KV = kvd;
+  long long o = 0;
+  m->oAq = o; o += r * D;
+  m->oBq = o; o += Q * r;
+  m->oAk = o; o += r * D;
+  m->oBk = o; o += KV * r;
+  m->oAv = o; o += r * D;
+  m->oBv = o; o += KV * r;
+  m->oAo = o; o += r * Q;
+  m->oBo = o; o += D * r;
+  m->oRa = o; o += D;
+  m->oRf = o; o += D;
+  m->layer_size = o;
+  m->oRfinal = (long long)c.nlayers * o;
+  m->P = m->oRfinal + D;
+  m->mask_words = (m->P + 31) / 32;
+  m->max_groups = c.max_groups;
+  m->max_rows = c.max_groups * c.seq;
+  m->max_slots = kMaxPerturbOps;  // sign-mask rows (64 seeds per call)
+  m->layer_set.assign(c.nlayers, 0);
+  int rc = cudaGetDevice(&m->device) == cudaSuccess ? B2P_OK : B2P_ERR_CUDA;
+  DeviceCtx* ctx = nullptr;
+  if (!rc) rc = ctx_get(&ctx);
+  if (!rc && cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess) {
+    set_error("cudaStreamCreate failed");
+    rc = B2P_ERR_CUDA;
+  }
+  if (!rc) rc = model_alloc(m);
+  if (!rc) {
+    std::vector<long long> sizes;
+    for (int l = 0; l < c.nlayers; ++l) {
+      const long long s[10] = {r * D, Q * r, r * D, KV * r, r * D, KV * r, r * Q, D * r, D, D};
+      sizes.insert(sizes.end(), s, s + 10);
+    }
+    sizes.push_back(D);
+    SignPlan plan = make_sign_plan(sizes);
+    m->nbufs = (int)plan.bufs.size();
+    m->njump = plan.njump;
+    m->total_draws = plan.total_draws;
+    if (cudaMalloc(&m->d_bufs, plan.bufs.size() * sizeof(SignBuffer)) != cudaSuccess ||
+        cudaMalloc(&m->d_jumps, plan.jumps.size() * 8) != cudaSuccess ||
+        cudaMemcpy(m->d_bufs, plan.bufs.data(), plan.bufs.size() * sizeof(SignBuffer), cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaMemcpy(m->d_jumps, plan.jumps.data(), plan.jumps.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess) {
+      set_error("sign-plan upload failed");
+      rc = B2P_ERR_CUDA;
+    }
+  }
+  if (rc) {
+    model_release(m);
+    delete m;
+    return nullptr;
+  }
+  return m;
+}
+
+void b2p_model_free(b2p_model* m) {
+  if (!m) return;
+  cudaStreamSynchronize(m->st);
+  model_release(m);
+  delete m;
+}
+
+long long b2p_model_trainable_count(const b2p_model* m) { return m ? m->P : -1; }
+
+void* b2p_model_stream(b2p_model* m) { return m ? (void*)m->st : nullptr; }
+
+int b2p_model_set_layer(b2p_model* m, int layer, const float* Wq, const float* Wk, const float* Wv, const float* Wo,
+                        const float* W1, const float* W2, const float* W3) {
+  B2P_REQUIRE(m && layer >= 0 && layer < m->cfg.nlayers, "bad model/layer");
+  B2P_REQUIRE(Wq && Wk && Wv && Wo && W1 && W2 && W3, "null weight pointer");
+  const auto& c = m->cfg;
+  const int D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim;
+  const size_t e = esz(m);
+  // stacked [Wq; Wk; Wv] rows (the qkv-fused kernel of training/io.h:182-206)
+  std::vector<float> qkv((size_t)m->qkv_dim * D);
+  std::memcpy(qkv.data(), Wq, (size_t)QD * D * 4);
+  std::memcpy(qkv.data() + (size_t)QD * D, Wk, (size_t)KVD * D * 4);
+  std::memcpy(qkv.data() + (size_t)(QD + KVD) * D, Wv, (size_t)KVD * D * 4);
+  int rc = upload16(m, static_cast<char*>(m->wqkv) + (size_t)layer * m->qkv_dim * D * e, qkv.data(), qkv.size());
+  if (rc) return rc;
+  rc = upload16(m, static_cast<char*>(m->wo) + (size_t)layer * D * QD * e, Wo, (size_t)D * QD);
+  if (rc) return rc;
+  // W1/W3 interleaved in blocks of 128 rows: [W1 b | W3 b] per 256-row tile (SwiGLU epilogue pairs)
+  std::vector<float> w13((size_t)2 * H * D);
+  for (int b = 0; b < H / 128; ++b) {
+    std::memcpy(w13.data() + (size_t)(2 * b) * 128 * D, W1 + (size_t)b * 128 * D, (size_t)128 * D * 4);
+    std::memcpy(w13.data() + (size_t)(2 * b + 1) * 128 * D, W3 + (size_t)b * 128 * D, (size_t)128 * D * 4);
+  }
+  rc = upload16(m, static_cast<char*>(m->w13) + (size_t)layer * 2 * H * D * e, w13.data(), w13.size());
+  if (rc) return rc;
+  rc = upload16(m, static_cast<char*>(m->w2) + (size_t)layer * D * H * e, W2, (size_t)D * H);
+  if (rc) return rc;
+  m->layer_set[layer] = 1;
+  return B2P_OK;
+}
+
+int b2p_model_set_embedding(b2p_model* m, const float* embed, const int32_t* compact_to_full, int cv) {
+  B2P_REQUIRE(m && embed && compact_to_full, "null argument");
+  B2P_REQUIRE(cv >= 1 && cv <= m->cfg.vocab, "compact vocab %d out of range", cv);
+  const auto& c = m->cfg;
+  for (int i = 0; i < cv; ++i)
+    B2P_REQUIRE(compact_to_full[i] >= 0 && compact_to_full[i] < c.vocab, "compact_to_full[%d] out of range", i);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->embed, embed, (size_t)c.vocab * c.dim * 4, cudaMemcpyHostToDevice, m->st));
+  // compact tied embedding (vocab_compact_embed, training/cpu_ops.h:171-176)
+  std::vector<float> ce((size_t)cv * c.dim);
+  for (int i = 0; i < cv; ++i)
+    std::memcpy(ce.data() + (size_t)i * c.dim, embed + (size_t)compact_to_full[i] * c.dim, (size_t)c.dim * 4);
+  if (m->cembed) cudaFree(m->cembed);
+  m->cembed = nullptr;
+  B2P_CHECK_CUDA(cudaMalloc(&m->cembed, (size_t)cv * c.dim * esz(m)));
+  m->cv = cv;
+  int rc = upload16(m, m->cembed, ce.data(), ce.size());
+  if (rc) return rc;
+  m->embed_set = true;
+  return B2P_OK;
+}
+
+int b2p_model_set_trainable(b2p_model* m, const float* theta, long long n) {
+  B2P_REQUIRE(m && theta, "null argument");
+  B2P_REQUIRE(n == m->P, "trainable count %lld != %lld", n, m->P);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->theta, theta, n * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
+}
+
+int b2p_model_get_trainable(b2p_model* m, float* theta, long long n) {
+  B2P_REQUIRE(m && theta, "null argument");
+  B2P_REQUIRE(n == m->P, "trainable count %lld != %lld", n, m->P);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(theta, m->theta, n * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
+}
+
+int b2p_model_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq,
+                   const b2p_variant* vars, int n_var, float* losses) {
+  int rc = ready(m);
+  if (rc) return rc;
+  B2P_REQUIRE(vars && losses, "null variants/losses");
+  if ((rc = stage_inputs(m, tokens, ctargets, n_seq, n_var))) return rc;
+  std::vector<uint64_t> seeds;
+  for (int v = 0; v < n_var; ++v) {
+    B2P_REQUIRE(vars[v].mode >= 0 && vars[v].mode <= 2, "variant mode must be 0, 1 or 2");
+    int slot = 0;
+    if (vars[v].mode) {
+      slot = -1;
+      for (size_t i = 0; i < seeds.size(); ++i)
+        if (seeds[i] == vars[v].seed) slot = (int)i;
+      if (slot < 0) {
+        slot = (int)seeds.size();
+        seeds.push_back(vars[v].seed);
+      }
+    }
+    m->h_var[v] = VariantInfo{slot, vars[v].mode, vars[v].s1, vars[v].s2};
+  }
+  if (!seeds.empty() && (rc = gen_masks(m, seeds.data(), (int)seeds.size()))) return rc;
+  if ((rc = eval_staged(m, n_seq, n_var))) return rc;
+  return read_losses(m, losses, n_var);
+}
+
+int b2p_mezo_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, uint64_t seed, float eps,
+                  float lr, float* loss_plus, float* loss_minus, float* proj_grad) {
+  int rc = ready(m);
+  if (rc) return rc;
+  if ((rc = stage_inputs(m, tokens, ctargets, 1, 2))) return rc;
+  if ((rc = gen_masks(m, &seed, 1))) return rc;
+  const float m2e = -2.0f * eps;
+  m->h_var[0] = VariantInfo{0, 1, eps, 0.f};  // θ + εz
+  m->h_var[1] = VariantInfo{0, 2, eps, m2e};  // (θ + εz) - 2εz
+  if ((rc = eval_staged(m, 1, 2))) return rc;
+  // +ε, -2ε, +ε (restore), then -lr·g with g from the two losses on the device
+  PerturbOps ops;
+  std::memset(&ops, 0, sizeof(ops));
+  ops.n = 4;
+  ops.op[0] = PerturbOp{0, 0, 0, eps, 0.f, 0.f, 1.f};
+  ops.op[1] = PerturbOp{0, 0, 0, m2e, 0.f, 0.f, 1.f};
+  ops.op[2] = PerturbOp{0, 0, 0, eps, 0.f, 0.f, 1.f};
+  ops.op[3] = PerturbOp{0, 1, 0, 0.f, eps, lr, 1.f};
+  if ((rc = launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, m->var_loss, m->st))) return rc;
+  float l2[2];
+  if ((rc = read_losses(m, l2, 2))) return rc;
+  if (loss_plus) *loss_plus = l2[0];
+  if (loss_minus) *loss_minus = l2[1];
+  if (proj_grad) *proj_grad = (l2[0] - l2[1]) / (2.0f * eps);
+  return B2P_OK;
+}
+
+int b2p_mezo_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, const uint64_t* seeds,
+                  int n_seeds, float eps, float* loss_pairs) {
+  int rc = ready(m);
+  if (rc) return rc;
+  B2P_REQUIRE(seeds && loss_pairs && n_seeds >= 1, "bad seeds/loss buffer");
+  B2P_REQUIRE(2 * n_seeds * n_seq <= m->max_groups, "2 x %d seeds x %d sequences exceed max_groups %d", n_seeds,
+              n_seq, m->max_groups);
+  if ((rc = stage_inputs(m, tokens, ctargets, n_seq, 2 * n_seeds))) return rc;
+  if ((rc = gen_masks(m, seeds, n_seeds))) return rc;
+  const float m2e = -2.0f * eps;
+  for (int s = 0; s < n_seeds; ++s) {
+    m->h_var[2 * s] = VariantInfo{s, 1, eps, 0.f};
+    m->h_var[2 * s + 1] = VariantInfo{s, 2, eps, m2e};
+  }
+  if ((rc = eval_staged(m, n_seq, 2 * n_seeds))) return rc;
+  B2P_CHECK_CUDA(cudaMemcpyAsync(loss_pairs, m->var_loss, 2 * n_seeds * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+int b2p_mezo_update(b2p_model* m, const uint64_t* seeds, const float* loss_pairs, int n_seeds, float eps, float lr) {
+  B2P_REQUIRE(m && seeds && loss_pairs, "null argument");
+  B2P_REQUIRE(n_seeds >= 1 && n_seeds <= kMaxPerturbOps && n_seeds <= m->max_slots, "seed count %d out of range",
+              n_seeds);
+  int rc = gen_masks(m, seeds, n_seeds);
+  if (rc) return rc;
+  // loss pairs may live on the host or the device
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->pairs, loss_pairs, 2 * n_seeds * 4, cudaMemcpyDefault, m->st));
+  PerturbOps ops;
+  std::memset(&ops, 0, sizeof(ops));
+  ops.n = n_seeds;
+  for (int s = 0; s < n_seeds; ++s) ops.op[s] = PerturbOp{s, 1, s, 0.f, eps, lr, (float)n_seeds};
+  if ((rc = launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, m->pairs, m->st))) return rc;
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+int b2p_model_perturb(b2p_model* m, const uint64_t* seeds, const float* scales, int n) {
+  B2P_REQUIRE(m && seeds && scales, "null argument");
+  B2P_REQUIRE(n >= 1 && n <= kMaxPerturbOps && n <= m->max_slots, "op count %d out of range", n);
+  int rc = gen_masks(m, seeds, n);
+  if (rc) return rc;
+  PerturbOps ops;
+  std::memset(&ops, 0, sizeof(ops));
+  ops.n = n;
+  for (int s = 0; s < n; ++s) ops.op[s] = PerturbOp{s, 0, 0, scales[s], 0.f, 0.f, 1.f};
+  if ((rc = launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, nullptr, m->st))) return rc;
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
+}
+
+int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_words) {
+  B2P_REQUIRE(m && seeds && out_words, "null argument");
+  int rc = gen_masks(m, seeds, n);
+  if (rc) return rc;
+  B2P_CHECK_CUDA(cudaMemcpyAsync(out_words, m->masks, (size_t)n * m->mask_words * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,52 @@
+// rng.cuh — device generation of the MeZO Rademacher sign stream.
+//
+// The reference draws signs sequentially with xoshiro256+ seeded by splitmix64
+// (training/train_mezo.m:97-136): for each buffer in perturbation order, one
+// 64-bit draw yields the signs of four consecutive parameters (bits 0..3), and a
+// buffer's n%4 tail elements take one draw each (bit 0). perturb_lora_weights
+// (train_mezo.m:560-588) walks the LoRA/RMS buffers in a fixed order, so the
+// sign of parameter i is a pure function of (seed, i).
+//
+// The xoshiro256 state transition is linear over GF(2); T^n is a 256x256 bit
+// matrix. Thread c starts at draw c*kChunkDraws by multiplying the seeded state
+// with J_k = T^(kChunkDraws * 2^k) for the set bits k of c, then draws its chunk
+// sequentially. Output: a bit mask per seed, bit i = 1 when parameter i gets
+// +scale, written with 32-bit word ORs.
+#pragma once
+#include <cstdint>
+#include <vector>
+
+namespace b2p {
+
+constexpr int kChunkDraws = 256;
+
+// One perturbation buffer: `n` parameters starting at parameter `p0`, whose
+// draws start at draw `d0` of the stream.
+struct SignBuffer {
+  long long p0, d0, n;
+};
+
+struct SignPlan {
+  std::vector<SignBuffer> bufs;
+  long long total_params = 0;
+  long long total_draws = 0;
+  int njump = 0;                 // number of jump matrices J_0..J_{njump-1}
+  std::vector<uint64_t> jumps;   // [njump][256 rows][4 words]
+};
+
+// Build the buffer table for the given buffer sizes (perturbation order) and
+// the jump matrices covering its draw count.
+SignPlan make_sign_plan(const std::vector<long long>& sizes);
+
+// Host xoshiro256+ (for tests of the plan itself).
+void host_xo_seed(uint64_t s[4], uint64_t seed);
+uint64_t host_xo_next(uint64_t s[4]);
+
+// Launch: masks[slot][words] = sign bits of seeds[slot] for slot < nseeds.
+// d_bufs / d_jumps are the device copies of plan.bufs / plan.jumps. The mask
+// rows must be zeroed first (done inside, on `st`).
+int launch_sign_masks(const SignBuffer* d_bufs, int nbufs, const uint64_t* d_jumps, int njump,
+                      long long total_draws, long long mask_words, const uint64_t* d_seeds, int nseeds,
+                      uint32_t* d_masks, void* st);
+
+}  // namespace b2p

@@ -1,0 +1,158 @@
+"""Python mirror of the device-resident MeZO-LoRA-split model (include/b2p.h).
+
+Mirrors the reference's host loop vocabulary (training/train_mezo.m): weights in
+LayerWeights layout (fp32 [out, in]), trainable parameters in the
+perturb_lora_weights order, channel-first semantics kept at the boundary, and
+the MeZO step / data-parallel seed evaluation as single calls into libb2p.so.
+Every call runs on the GPU through the C ABI; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+
+F16, BF16 = 0, 1
+
+
+@dataclass
+class Config:
+    dim: int = 960
+    hidden: int = 2560
+    heads: int = 15
+    kv_heads: int = 5
+    head_dim: int = 64
+    seq: int = 256
+    nlayers: int = 32
+    vocab: int = 49152
+    rank: int = 8
+    rope_theta: float = 100000.0
+    res_alpha: float = 1.0
+    dtype: int = F16
+    max_groups: int = 64
+
+    def c(self) -> _lib.ModelConfig:
+        return _lib.ModelConfig(self.dim, self.hidden, self.heads, self.kv_heads, self.head_dim, self.seq,
+                                self.nlayers, self.vocab, self.rank, self.rope_theta, self.res_alpha, self.dtype,
+                                self.max_groups)
+
+
+def _fp(a):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def _u16(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint16))
+
+
+def _u64(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint64))
+
+
+class Model:
+    """A b2p_model on the current CUDA device (call autoane_b200.call('b2p_init', dev) first)."""
+
+    def __init__(self, cfg: Config):
+        self.cfg = cfg
+        self._lib = _lib.load()
+        self._cfg_c = cfg.c()
+        h = self._lib.b2p_model_create(C.byref(self._cfg_c))
+        if not h:
+            raise _lib.B2PError("b2p_model_create", -1, self._lib.b2p_last_error().decode())
+        self.h = C.c_void_p(h)
+        self.P = int(self._lib.b2p_model_trainable_count(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._lib.b2p_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return int(self._lib.b2p_model_stream(self.h) or 0)
+
+    # ---- weights ----
+    def set_layer(self, layer: int, Wq, Wk, Wv, Wo, W1, W2, W3):
+        arrs = [np.ascontiguousarray(a, np.float32) for a in (Wq, Wk, Wv, Wo, W1, W2, W3)]
+        _lib.call("b2p_model_set_layer", self.h, layer, *[_fp(a) for a in arrs])
+
+    def set_embedding(self, embed, compact_to_full):
+        e = np.ascontiguousarray(embed, np.float32)
+        c2f = np.ascontiguousarray(compact_to_full, np.int32)
+        _lib.call("b2p_model_set_embedding", self.h, _fp(e), c2f.ctypes.data_as(C.POINTER(C.c_int)), len(c2f))
+
+    def set_trainable(self, theta):
+        t = np.ascontiguousarray(theta, np.float32)
+        _lib.call("b2p_model_set_trainable", self.h, t.ctypes.data, self.P)
+
+    def get_trainable(self) -> np.ndarray:
+        out = np.empty(self.P, np.float32)
+        _lib.call("b2p_model_get_trainable", self.h, out.ctypes.data, self.P)
+        return out
+
+    # ---- evaluation / MeZO ----
+    def eval(self, tokens, ctargets, variants) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        n_seq = tok.shape[0] if tok.ndim == 2 else 1
+        vs = (_lib.Variant * len(variants))(*[_lib.Variant(int(s), int(m), float(a), float(b))
+                                             for (s, m, a, b) in variants])
+        out = np.empty(len(variants), np.float32)
+        _lib.call("b2p_model_eval", self.h, _u16(tok), _u16(tgt), n_seq, C.cast(vs, C.c_void_p), len(variants),
+                  _fp(out))
+        return out
+
+    def mezo_step(self, tokens, ctargets, seed: int, eps: float, lr: float):
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        lp, lm, g = C.c_float(), C.c_float(), C.c_float()
+        _lib.call("b2p_mezo_step", self.h, _u16(tok), _u16(tgt), seed, eps, lr, C.byref(lp), C.byref(lm),
+                  C.byref(g))
+        return lp.value, lm.value, g.value
+
+    def mezo_eval(self, tokens, ctargets, seeds, eps: float, out=None) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        n_seq = tok.shape[0] if tok.ndim == 2 else 1
+        if out is None:
+            out = np.empty(2 * len(sd), np.float32)
+        ptr = out.ctypes.data if isinstance(out, np.ndarray) else int(out)
+        _lib.call("b2p_mezo_eval", self.h, _u16(tok), _u16(tgt), n_seq, _u64(sd), len(sd), eps, ptr)
+        return out
+
+    def mezo_update(self, seeds, loss_pairs, eps: float, lr: float):
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        ptr = loss_pairs.ctypes.data if isinstance(loss_pairs, np.ndarray) else int(loss_pairs)
+        if isinstance(loss_pairs, np.ndarray):
+            assert loss_pairs.dtype == np.float32 and loss_pairs.size >= 2 * len(sd)
+        _lib.call("b2p_mezo_update", self.h, _u64(sd), ptr, len(sd), eps, lr)
+
+    def perturb(self, seeds, scales):
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        sc = np.ascontiguousarray(scales, np.float32)
+        _lib.call("b2p_model_perturb", self.h, _u64(sd), _fp(sc), len(sd))
+
+    def sign_masks(self, seeds) -> np.ndarray:
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        words = (self.P + 31) // 32
+        out = np.empty((len(sd), words), np.uint32)
+        _lib.call("b2p_sign_masks", self.h, _u64(sd), len(sd), out.ctypes.data_as(C.POINTER(C.c_uint32)))
+        return out
+
+
+def load_synthetic(model: Model, weights: dict, embed, compact_to_full, theta):
+    """Upload reference-layout weights (dict name -> list per layer) into a model."""
+    for l in range(model.cfg.nlayers):
+        model.set_layer(l, *[weights[k][l] for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")])
+    model.set_embedding(embed, compact_to_full)
+    model.set_trainable(theta)

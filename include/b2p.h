@@ -69,6 +69,87 @@ int b2p_device_status(void* stream);
 int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
              void* stream);
 
+/* ======================================================================
+ * Device-resident model: the MeZO-LoRA-split hot path on the GPU.
+ *
+ * Replaces the per-layer compile/stage/eval/read round trips of
+ * DO_FORWARD_PASS (training/train_mezo.m:1528-1699; conv-fused kernels
+ * compiled at train_mezo.m:1296-1327) and the host-side in-place perturbation
+ * of perturb_lora_weights (train_mezo.m:560-588). Base projection weights are
+ * uploaded once and stay frozen (16-bit); the trainable LoRA A/B + RMS weights
+ * live on the device as an fp32 master copy in the reference's perturbation
+ * order; the ±εz perturbation is applied inside the kernels' operand loads.
+ * ====================================================================== */
+typedef struct b2p_model b2p_model;
+
+typedef struct {
+  int dim, hidden, heads, kv_heads, head_dim, seq, nlayers, vocab; /* models/*.h sizes */
+  int rank;          /* LoRA rank (4 or 8), adapters on Wq/Wk/Wv/Wo */
+  float rope_theta;  /* ROPE_THETA (cpu_ops.h:296) */
+  float res_alpha;   /* residual scale (train_mezo.m:1262): 1 for fine-tuning */
+  int dtype;         /* B2P_F16 or B2P_BF16 compute type, fp32 accumulation */
+  int max_groups;    /* max (variant x sequence) forwards evaluated in one call */
+} b2p_model_config;
+
+/* One evaluation point of the trainable parameters θ:
+ *   mode 0: θ;  mode 1: θ + s1·z;  mode 2: (θ + s1·z) + s2·z   (fp32 adds, z = ±1)
+ * with z the Rademacher signs of `seed` (xo_seed/perturb_buffer, train_mezo.m:110-136).
+ * The reference's +ε pass is {seed, 1, ε, 0}; its -ε pass is {seed, 2, ε, -2ε}. */
+typedef struct {
+  uint64_t seed;
+  int mode;
+  float s1, s2;
+} b2p_variant;
+
+/* Allocate a model on the current device (after b2p_init). NULL on error. */
+b2p_model* b2p_model_create(const b2p_model_config* cfg);
+void b2p_model_free(b2p_model* m);
+/* Number of trainable parameters (LoRA A/B + RMS weights; 1,700,800 for SmolLM2-360M r8). */
+long long b2p_model_trainable_count(const b2p_model* m);
+/* The model's CUDA stream (cudaStream_t), for callers that order their own work after it. */
+void* b2p_model_stream(b2p_model* m);
+/* Frozen base weights of one layer, fp32 row-major [out, in] as in LayerWeights
+ * (training/config.h:48-52); converted to the compute dtype on upload.
+ * Replaces compile_qkv_fused_conv1x1_kern / compile_ffn_fused_conv1x1_kern /
+ * compile_conv1x1_kern weight baking (training/io.h:165-230). */
+int b2p_model_set_layer(b2p_model* m, int layer, const float* Wq, const float* Wk, const float* Wv, const float* Wo,
+                        const float* W1, const float* W2, const float* W3);
+/* Full embedding [vocab, dim] (used for the token lookup, cpu_ops.h:190) and the
+ * compact-vocabulary map; the tied lm-head uses the compact rows
+ * (vocab_compact_embed, cpu_ops.h:171). */
+int b2p_model_set_embedding(b2p_model* m, const float* embed, const int32_t* compact_to_full, int cv);
+/* Trainable parameters in perturbation order (per layer Aq,Bq,Ak,Bk,Av,Bv,Ao,Bo,
+ * rms_att,rms_ffn; then rms_final). Host or device pointer. */
+int b2p_model_set_trainable(b2p_model* m, const float* theta, long long n);
+int b2p_model_get_trainable(b2p_model* m, float* theta, long long n);
+
+/* Forward + mean cross-entropy of n_seq sequences (tokens [n_seq][seq] uint16,
+ * compact targets [n_seq][seq]) under each of n_var variants, in one batched
+ * pass. losses[v] = mean over the sequences of the per-token mean CE
+ * (cross_entropy_loss, cpu_ops.h:108-133). Host buffers; synchronous. */
+int b2p_model_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq,
+                   const b2p_variant* vars, int n_var, float* losses);
+
+/* One MeZO-LoRA-split step exactly as train_mezo.m:2938-3012: evaluate θ+εz and
+ * θ-εz (batched), then θ ← ((θ+εz)-2εz)+εz and θ ← θ - lr·g·z with
+ * g = (L+ - L-)/(2ε) computed on the device. Outputs may be NULL. */
+int b2p_mezo_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, uint64_t seed, float eps,
+                  float lr, float* loss_plus, float* loss_minus, float* proj_grad);
+
+/* Data-parallel MeZO, evaluation half: for each of n_seeds seeds, L+ and L- over
+ * the n_seq sequences. loss_pairs[2s] = L+, [2s+1] = L- (host or device pointer). */
+int b2p_mezo_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, const uint64_t* seeds,
+                  int n_seeds, float eps, float* loss_pairs);
+/* Data-parallel MeZO, update half: θ ← θ + c_s·z_s applied in seed order with
+ * c_s = (-lr·(L+_s - L-_s)/(2ε)) / n_seeds (the K-direction averaged update of
+ * train_mezo.m:2751-2768). Every replica given the same arguments ends bit-identical. */
+int b2p_mezo_update(b2p_model* m, const uint64_t* seeds, const float* loss_pairs, int n_seeds, float eps, float lr);
+/* θ ← fl(θ + (z ? c : -c)) for each (seeds[i], scales[i]) in order (perturb_lora_weights). */
+int b2p_model_perturb(b2p_model* m, const uint64_t* seeds, const float* scales, int n);
+/* Sign masks of the perturbation stream: out_words[i][w], bit b of word w = sign of
+ * parameter 32w+b for seeds[i] (1 = +). ceil(P/32) words per seed. */
+int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_words);
+
 #ifdef __cplusplus
 }
 #endif
