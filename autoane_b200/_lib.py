@@ -48,6 +48,11 @@ ABI: dict[str, tuple] = {
     "b2p_mezo_update": (i32, [vp, u64p, vp, i32, f32, f32]),
     "b2p_model_perturb": (i32, [vp, u64p, fp, i32]),
     "b2p_sign_masks": (i32, [vp, u64p, i32, C.POINTER(C.c_uint32)]),
+    "b2p_mezo_eval_device": (i32, [vp, vp, vp, i32, u64p, i32, f32, vp]),
+    "b2p_model_sync": (i32, [vp]),
+    "b2p_model_profile": (i32, [vp, i32]),
+    "b2p_model_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),
+    "b2p_launch_count": (i64, []),
 }
 
 

@@ -1,6 +1,7 @@
 // engine.cu — error state, device context, tensor maps and the GEMM dispatcher.
 #include <cstdarg>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <cudaTypedefs.h>
 #include "engine.cuh"
@@ -12,7 +13,11 @@ thread_local std::string g_last_error;
 std::mutex g_ctx_mu;
 DeviceCtx g_ctx[64];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::atomic<long long> g_launches{0};
 }  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   char buf[1024];
@@ -135,7 +140,7 @@ static int launch_t(const void* X, int ldx, const void* W, int ldw, int M, int N
   EpiParams e = ep;
   e.status = c->status;
   kern<<<grid, kGemmThreads, S::kTotal, st>>>(tx, tw, M, N, K, e);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 

@@ -35,6 +35,16 @@ const char* last_error();
     }                                \
   } while (0)
 
+// Count of kernels this library has launched (all devices, all threads).
+void count_launch();
+long long launch_count();
+
+#define B2P_POST_LAUNCH()                         \
+  do {                                            \
+    ::b2p::count_launch();                        \
+    B2P_CHECK_CUDA(cudaGetLastError());           \
+  } while (0)
+
 struct DeviceCtx {
   int device = -1;
   int num_sms = 0;

@@ -51,7 +51,7 @@ int launch_embed(const float* embed, int vocab, int dim, const int32_t* tokens, 
                  int rows, float* x, uint32_t* status, cudaStream_t st) {
   B2P_REQUIRE(dim % 4 == 0, "dim must be a multiple of 4");
   embed_kernel<<<rows, 128, 0, st>>>(embed, vocab, dim, tokens, group_seq, seq, rows, x, status);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -162,7 +162,7 @@ static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
       return B2P_ERR_UNSUPPORTED;
   }
 #undef B2P_NL_CASE
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -392,7 +392,7 @@ int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st) {
     attn_fwd_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a, scale_log2);
   else
     attn_fwd_kernel<__half><<<grid, 128, 0, st>>>(a, scale_log2);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -428,7 +428,7 @@ int launch_ce_reduce(const float2* part, int ntiles, const float* tgt_logit, int
                      float* group_loss, cudaStream_t st) {
   B2P_REQUIRE(rows % seq == 0, "rows must be whole sequences");
   ce_reduce_kernel<<<rows / seq, 256, 0, st>>>(part, ntiles, tgt_logit, seq, row_loss, group_loss);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -442,7 +442,7 @@ __global__ void variant_loss_kernel(const float* group_loss, int n_var, int n_se
 
 int launch_variant_loss(const float* group_loss, int n_var, int n_seq, float* var_loss, cudaStream_t st) {
   variant_loss_kernel<<<(n_var + 63) / 64, 64, 0, st>>>(group_loss, n_var, n_seq, var_loss);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -489,7 +489,7 @@ int launch_perturb(float* theta, long long n, const uint32_t* masks, long long m
   const int threads = 128;
   perturb_kernel<<<(unsigned)((mask_words + threads - 1) / threads), threads, 0, st>>>(theta, n, masks, mask_words,
                                                                                       ops, losses);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -536,7 +536,7 @@ int launch_cf_to_tm16(const float* src, int C, int S, void* dst, int ld_dst, boo
     cf_to_tm16_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(src, C, S, static_cast<__nv_bfloat16*>(dst), ld_dst);
   else
     cf_to_tm16_kernel<__half><<<grid, block, 0, st>>>(src, C, S, static_cast<__half*>(dst), ld_dst);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -549,7 +549,7 @@ int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int 
     tm_to_cf32_kernel<__nv_bfloat16, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
   else
     tm_to_cf32_kernel<__half, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
@@ -566,7 +566,7 @@ int launch_f32_to_16(const float* src, void* dst, long long n, bool bf16, cudaSt
     f32_to_16_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), n);
   else
     f32_to_16_kernel<__half><<<blocks, 256, 0, st>>>(src, static_cast<__half*>(dst), n);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 

@@ -16,6 +16,14 @@
 
 using namespace b2p;
 
+struct Stager {
+  char* base = nullptr;
+  size_t slot_bytes = 0;
+  int nslots = 0, next = 0;
+  std::vector<cudaEvent_t> ev;
+  std::vector<char> armed;
+};
+
 struct b2p_model {
   b2p_model_config cfg{};
   int device = 0;
@@ -62,12 +70,12 @@ struct b2p_model {
   VariantInfo* d_var = nullptr;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
-  // pinned host staging
-  int32_t* h_tok = nullptr;
-  int* h_meta = nullptr;
-  VariantInfo* h_var = nullptr;
-  uint64_t* h_seeds = nullptr;
-  float* h_loss = nullptr;
+  Stager stg;
+  // optional CUDA-event timing of every projection-GEMM launch
+  bool prof = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<double> prof_flops;
 };
 
 namespace {
@@ -110,11 +118,18 @@ int model_alloc(b2p_model* m) {
   B2P_CHECK_CUDA(cudaMalloc(&m->d_var, m->max_groups * sizeof(VariantInfo)));
   B2P_CHECK_CUDA(cudaMalloc(&m->rope_cos, (size_t)c.seq * (c.head_dim / 2) * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->rope_sin, (size_t)c.seq * (c.head_dim / 2) * 4));
-  B2P_CHECK_CUDA(cudaMallocHost(&m->h_tok, (size_t)2 * m->max_groups * c.seq * 4));
-  B2P_CHECK_CUDA(cudaMallocHost(&m->h_meta, 2 * m->max_groups * sizeof(int)));
-  B2P_CHECK_CUDA(cudaMallocHost(&m->h_var, m->max_groups * sizeof(VariantInfo)));
-  B2P_CHECK_CUDA(cudaMallocHost(&m->h_seeds, m->max_slots * 8));
-  B2P_CHECK_CUDA(cudaMallocHost(&m->h_loss, m->max_groups * 4));
+  {
+    Stager& sg = m->stg;
+    size_t need = std::max<size_t>((size_t)2 * m->max_groups * c.seq * 4, (size_t)2 * m->max_groups * sizeof(int));
+    need = std::max<size_t>(need, (size_t)m->max_groups * sizeof(VariantInfo));
+    need = std::max<size_t>(need, (size_t)m->max_slots * 8);
+    sg.slot_bytes = (need + 255) & ~size_t(255);
+    sg.nslots = 8;
+    B2P_CHECK_CUDA(cudaMallocHost(&sg.base, sg.slot_bytes * sg.nslots));
+    sg.ev.resize(sg.nslots);
+    sg.armed.assign(sg.nslots, 0);
+    for (auto& e : sg.ev) B2P_CHECK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
   // RoPE tables with the reference's expressions (training/cpu_ops.h:303-307)
   const int half = c.head_dim / 2;
   std::vector<float> cs((size_t)c.seq * half), sn((size_t)c.seq * half);
@@ -138,9 +153,11 @@ void model_release(b2p_model* m) {
                  m->d_var, m->rope_cos, m->rope_sin};
   for (void* p : dev)
     if (p) cudaFree(p);
-  void* host[] = {m->h_tok, m->h_meta, m->h_var, m->h_seeds, m->h_loss};
-  for (void* p : host)
-    if (p) cudaFreeHost(p);
+  if (m->stg.base) cudaFreeHost(m->stg.base);
+  for (auto e : m->stg.ev)
+    if (e) cudaEventDestroy(e);
+  for (auto e : m->ev_pool)
+    if (e) cudaEventDestroy(e);
   if (m->st) cudaStreamDestroy(m->st);
 }
 
@@ -182,8 +199,25 @@ LoraEpi lora_epi(const b2p_model* m) {
   return le;
 }
 
+// launch_gemm, bracketed by CUDA events on the model stream when profiling is on.
+int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+         const EpiParams& ep) {
+  if (!m->prof) return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, ep, m->st);
+  while (m->ev_pool.size() < m->ev_used + 2) {
+    cudaEvent_t e;
+    B2P_CHECK_CUDA(cudaEventCreate(&e));
+    m->ev_pool.push_back(e);
+  }
+  B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used], m->st));
+  int rc = launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, ep, m->st);
+  B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used + 1], m->st));
+  m->ev_used += 2;
+  m->prof_flops.push_back(2.0 * M * (double)N * K);
+  return rc;
+}
+
 // The batched forward over G groups whose inputs are already staged on the device.
-int run_forward(b2p_model* m, int G) {
+int run_forward(b2p_model* m, int G, const int32_t* tok) {
   const auto& c = m->cfg;
   const int R = G * c.seq;
   const int D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim, QKV = m->qkv_dim;
@@ -192,7 +226,6 @@ int run_forward(b2p_model* m, int G) {
   int rc = ctx_get(&ctx);
   if (rc) return rc;
   const int* group_seq = m->d_meta;
-  const int32_t* tok = m->d_tok;
   rc = launch_embed(m->embed, c.vocab, D, tok, group_seq, c.seq, R, m->x, ctx->status, m->st);
   if (rc) return rc;
   const PerturbCtx pc = pctx(m);
@@ -243,7 +276,7 @@ int run_forward(b2p_model* m, int G) {
     ep.head_dim = c.head_dim;
     ep.seq_len = c.seq;
     const char* wqkv = static_cast<const char*>(m->wqkv) + (size_t)l * QKV * D * e;
-    if ((rc = launch_gemm(m->qkv_bn, EPI_QKV_ROPE, m->bf16, m->xn, D, wqkv, D, R, QKV, D, ep, m->st))) return rc;
+    if ((rc = gemm(m, m->qkv_bn, EPI_QKV_ROPE, m->xn, D, wqkv, D, R, QKV, D, ep))) return rc;
     // attention
     AttnArgs aa;
     aa.qkv = m->qkv;
@@ -289,7 +322,7 @@ int run_forward(b2p_model* m, int G) {
     eo.lora.seg_boff[0] = lb + m->oBo;
     eo.lora.seg_ucol[0] = 3 * c.rank;
     const char* wo = static_cast<const char*>(m->wo) + (size_t)l * D * QD * e;
-    if ((rc = launch_gemm(pick_bn(D, EPI_RESID), EPI_RESID, m->bf16, m->attn, QD, wo, QD, R, D, QD, eo, m->st)))
+    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->attn, QD, wo, QD, R, D, QD, eo)))
       return rc;
     // RMSNorm(rms_ffn)
     NormLoraArgs nf;
@@ -311,7 +344,7 @@ int run_forward(b2p_model* m, int G) {
     es.out = m->hbuf;
     es.ldo = H;
     const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
-    if ((rc = launch_gemm(256, EPI_SWIGLU, m->bf16, m->xn, D, w13, D, R, 2 * H, D, es, m->st))) return rc;
+    if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, es))) return rc;
     // x += alpha * (h · W2^T)
     EpiParams e2;
     std::memset(&e2, 0, sizeof(e2));
@@ -321,7 +354,7 @@ int run_forward(b2p_model* m, int G) {
     e2.ldo = D;
     e2.alpha = c.res_alpha;
     const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
-    if ((rc = launch_gemm(pick_bn(D, EPI_RESID), EPI_RESID, m->bf16, m->hbuf, H, w2, H, R, D, H, e2, m->st)))
+    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->hbuf, H, w2, H, R, D, H, e2)))
       return rc;
   }
   // final RMSNorm + lm-head with fused cross-entropy partials
@@ -344,50 +377,84 @@ int run_forward(b2p_model* m, int G) {
   ec.ce_part = m->ce_part;
   ec.ce_tgt = m->ce_tgt;
   ec.n_tiles_n = ntiles;
-  if ((rc = launch_gemm(256, EPI_CE, m->bf16, m->xn, D, m->cembed, D, R, m->cv, D, ec, m->st))) return rc;
+  if ((rc = gemm(m, 256, EPI_CE, m->xn, D, m->cembed, D, R, m->cv, D, ec))) return rc;
   return launch_ce_reduce(m->ce_part, ntiles, m->ce_tgt, R, c.seq, m->row_loss, m->group_loss, m->st);
 }
 
-__global__ void expand_targets_kernel(const int32_t* seq_tgt, const int* group_seq, int seq, int rows,
-                                      int32_t* row_tgt) {
+__global__ void expand_targets_kernel(const int32_t* seq_tgt, const int* group_seq, int seq, int rows, int cv,
+                                      int32_t* row_tgt, uint32_t* status) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
   const int g = row / seq, t = row - g * seq;
-  row_tgt[row] = seq_tgt[(long long)group_seq[g] * seq + t];
+  int tg = seq_tgt[(long long)group_seq[g] * seq + t];
+  if (tg < 0 || tg >= cv) {
+    atomicCAS(status, 0u, (uint32_t)DEV_BAD_ARGS);
+    tg = -1;
+  }
+  row_tgt[row] = tg;
 }
 
-// Stage tokens/targets of n_seq sequences and the group tables for n_var variants.
-int stage_inputs(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, int n_var) {
+// Copy a small host buffer to the device through a pinned ring slot. A slot is
+// reused only after the copy that last read it has executed (event fence), so
+// asynchronous calls never see their staging overwritten.
+int stage_copy(b2p_model* m, void* dst, const void* src, size_t bytes) {
+  Stager& s = m->stg;
+  B2P_REQUIRE(bytes <= s.slot_bytes, "staging copy of %zu bytes exceeds slot size %zu", bytes, s.slot_bytes);
+  const int k = s.next;
+  s.next = (s.next + 1) % s.nslots;
+  if (s.armed[k]) B2P_CHECK_CUDA(cudaEventSynchronize(s.ev[k]));
+  char* p = s.base + (size_t)k * s.slot_bytes;
+  std::memcpy(p, src, bytes);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(dst, p, bytes, cudaMemcpyHostToDevice, m->st));
+  B2P_CHECK_CUDA(cudaEventRecord(s.ev[k], m->st));
+  s.armed[k] = 1;
+  return B2P_OK;
+}
+
+// Validate host tokens/targets of n_seq sequences and upload them (int32) to d_tok.
+int stage_tokens(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq) {
   const auto& c = m->cfg;
-  const int G = n_seq * n_var;
   B2P_REQUIRE(tokens && ctargets, "null token/target buffer");
-  B2P_REQUIRE(n_seq >= 1 && n_var >= 1 && G <= m->max_groups, "groups %d x %d exceed max_groups %d", n_var, n_seq,
-              m->max_groups);
+  B2P_REQUIRE(n_seq >= 1 && n_seq <= m->max_groups, "sequence count %d out of range", n_seq);
   const size_t nt = (size_t)n_seq * c.seq;
+  std::vector<int32_t> h(2 * nt);
   for (size_t i = 0; i < nt; ++i) {
     B2P_REQUIRE(tokens[i] < c.vocab, "token[%zu]=%d out of range (vocab %d)", i, (int)tokens[i], c.vocab);
     B2P_REQUIRE(ctargets[i] < m->cv, "target[%zu]=%d out of range (compact vocab %d)", i, (int)ctargets[i], m->cv);
-    m->h_tok[i] = tokens[i];
-    m->h_tok[nt + i] = ctargets[i];
+    h[i] = tokens[i];
+    h[nt + i] = ctargets[i];
   }
+  return stage_copy(m, m->d_tok, h.data(), h.size() * 4);
+}
+
+// Group tables for n_var variants x n_seq sequences, per-row targets, variant table.
+int stage_groups(b2p_model* m, int n_seq, const std::vector<VariantInfo>& vars, const int32_t* d_targets) {
+  const auto& c = m->cfg;
+  const int n_var = (int)vars.size();
+  const int G = n_seq * n_var;
+  B2P_REQUIRE(n_seq >= 1 && n_var >= 1 && G <= m->max_groups, "groups %d x %d exceed max_groups %d", n_var, n_seq,
+              m->max_groups);
+  std::vector<int> meta(2 * m->max_groups, 0);
   for (int v = 0; v < n_var; ++v)
     for (int q = 0; q < n_seq; ++q) {
-      m->h_meta[v * n_seq + q] = q;                      // group -> sequence
-      m->h_meta[m->max_groups + v * n_seq + q] = v;      // group -> variant
+      meta[v * n_seq + q] = q;                  // group -> sequence
+      meta[m->max_groups + v * n_seq + q] = v;  // group -> variant
     }
-  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_tok, m->h_tok, 2 * nt * 4, cudaMemcpyHostToDevice, m->st));
-  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_meta, m->h_meta, 2 * m->max_groups * sizeof(int), cudaMemcpyHostToDevice,
-                                 m->st));
-  expand_targets_kernel<<<(G * c.seq + 255) / 256, 256, 0, m->st>>>(m->d_tok + nt, m->d_meta, c.seq, G * c.seq,
-                                                                     m->d_row_tgt);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  int rc = stage_copy(m, m->d_meta, meta.data(), meta.size() * sizeof(int));
+  if (rc) return rc;
+  if ((rc = stage_copy(m, m->d_var, vars.data(), vars.size() * sizeof(VariantInfo)))) return rc;
+  DeviceCtx* ctx = nullptr;
+  if ((rc = ctx_get(&ctx))) return rc;
+  expand_targets_kernel<<<(G * c.seq + 255) / 256, 256, 0, m->st>>>(d_targets, m->d_meta, c.seq, G * c.seq, m->cv,
+                                                                     m->d_row_tgt, ctx->status);
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
 int gen_masks(b2p_model* m, const uint64_t* seeds, int n) {
   B2P_REQUIRE(n >= 1 && n <= m->max_slots, "seed count %d exceeds mask slots %d", n, m->max_slots);
-  for (int i = 0; i < n; ++i) m->h_seeds[i] = seeds[i];
-  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_seeds, m->h_seeds, n * 8, cudaMemcpyHostToDevice, m->st));
+  int rc = stage_copy(m, m->d_seeds, seeds, (size_t)n * 8);
+  if (rc) return rc;
   return launch_sign_masks(m->d_bufs, m->nbufs, m->d_jumps, m->njump, m->total_draws, m->mask_words, m->d_seeds, n,
                            m->masks, m->st);
 }
@@ -409,17 +476,47 @@ int ready(const b2p_model* m) {
   return B2P_OK;
 }
 
-// Evaluate the given variants (already staged into h_var) and leave per-variant
-// losses in m->var_loss.
-int eval_staged(b2p_model* m, int n_seq, int n_var) {
-  B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_var, m->h_var, n_var * sizeof(VariantInfo), cudaMemcpyHostToDevice, m->st));
-  int rc = run_forward(m, n_seq * n_var);
+// Forward over n_seq sequences (device int32 tokens/targets) x variants; per-variant
+// losses land in m->var_loss. Asynchronous on the model stream.
+int eval_variants(b2p_model* m, const int32_t* d_tokens, const int32_t* d_targets, int n_seq,
+                  const std::vector<VariantInfo>& vars) {
+  int rc = stage_groups(m, n_seq, vars, d_targets);
   if (rc) return rc;
-  return launch_variant_loss(m->group_loss, n_var, n_seq, m->var_loss, m->st);
+  if ((rc = run_forward(m, n_seq * (int)vars.size(), d_tokens))) return rc;
+  return launch_variant_loss(m->group_loss, (int)vars.size(), n_seq, m->var_loss, m->st);
 }
 
-int read_losses(b2p_model* m, float* out, int n) {
-  B2P_CHECK_CUDA(cudaMemcpyAsync(out, m->var_loss, n * 4, cudaMemcpyDefault, m->st));
+// ±ε variants of each seed: index 2s = θ+εz_s, 2s+1 = (θ+εz_s)-2εz_s.
+int eval_pairs(b2p_model* m, const int32_t* d_tokens, const int32_t* d_targets, int n_seq, const uint64_t* seeds,
+               int n_seeds, float eps) {
+  B2P_REQUIRE(seeds && n_seeds >= 1, "no seeds");
+  B2P_REQUIRE(2 * n_seeds * n_seq <= m->max_groups, "2 x %d seeds x %d sequences exceed max_groups %d", n_seeds,
+              n_seq, m->max_groups);
+  int rc = gen_masks(m, seeds, n_seeds);
+  if (rc) return rc;
+  const float m2e = -2.0f * eps;
+  std::vector<VariantInfo> vars(2 * n_seeds);
+  for (int s = 0; s < n_seeds; ++s) {
+    vars[2 * s] = VariantInfo{s, 1, eps, 0.f};
+    vars[2 * s + 1] = VariantInfo{s, 2, eps, m2e};
+  }
+  return eval_variants(m, d_tokens, d_targets, n_seq, vars);
+}
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Copy n floats of var_loss to out; synchronise (and check device status) only
+// when out is host memory.
+int copy_losses(b2p_model* m, float* out, int n) {
+  B2P_CHECK_CUDA(cudaMemcpyAsync(out, m->var_loss, (size_t)n * 4, cudaMemcpyDefault, m->st));
+  if (is_device_ptr(out)) return B2P_OK;
   B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
   return check_device_status(m->st);
 }
@@ -593,9 +690,10 @@ int b2p_model_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctarget
                    const b2p_variant* vars, int n_var, float* losses) {
   int rc = ready(m);
   if (rc) return rc;
-  B2P_REQUIRE(vars && losses, "null variants/losses");
-  if ((rc = stage_inputs(m, tokens, ctargets, n_seq, n_var))) return rc;
+  B2P_REQUIRE(vars && losses && n_var >= 1, "null variants/losses");
+  if ((rc = stage_tokens(m, tokens, ctargets, n_seq))) return rc;
   std::vector<uint64_t> seeds;
+  std::vector<VariantInfo> vi(n_var);
   for (int v = 0; v < n_var; ++v) {
     B2P_REQUIRE(vars[v].mode >= 0 && vars[v].mode <= 2, "variant mode must be 0, 1 or 2");
     int slot = 0;
@@ -608,24 +706,23 @@ int b2p_model_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctarget
         seeds.push_back(vars[v].seed);
       }
     }
-    m->h_var[v] = VariantInfo{slot, vars[v].mode, vars[v].s1, vars[v].s2};
+    vi[v] = VariantInfo{slot, vars[v].mode, vars[v].s1, vars[v].s2};
   }
   if (!seeds.empty() && (rc = gen_masks(m, seeds.data(), (int)seeds.size()))) return rc;
-  if ((rc = eval_staged(m, n_seq, n_var))) return rc;
-  return read_losses(m, losses, n_var);
+  const size_t nt = (size_t)n_seq * m->cfg.seq;
+  if ((rc = eval_variants(m, m->d_tok, m->d_tok + nt, n_seq, vi))) return rc;
+  return copy_losses(m, losses, n_var);
 }
 
 int b2p_mezo_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, uint64_t seed, float eps,
                   float lr, float* loss_plus, float* loss_minus, float* proj_grad) {
   int rc = ready(m);
   if (rc) return rc;
-  if ((rc = stage_inputs(m, tokens, ctargets, 1, 2))) return rc;
-  if ((rc = gen_masks(m, &seed, 1))) return rc;
-  const float m2e = -2.0f * eps;
-  m->h_var[0] = VariantInfo{0, 1, eps, 0.f};  // θ + εz
-  m->h_var[1] = VariantInfo{0, 2, eps, m2e};  // (θ + εz) - 2εz
-  if ((rc = eval_staged(m, 1, 2))) return rc;
+  if ((rc = stage_tokens(m, tokens, ctargets, 1))) return rc;
+  const size_t nt = (size_t)m->cfg.seq;
+  if ((rc = eval_pairs(m, m->d_tok, m->d_tok + nt, 1, &seed, 1, eps))) return rc;
   // +ε, -2ε, +ε (restore), then -lr·g with g from the two losses on the device
+  const float m2e = -2.0f * eps;
   PerturbOps ops;
   std::memset(&ops, 0, sizeof(ops));
   ops.n = 4;
@@ -635,7 +732,7 @@ int b2p_mezo_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets
   ops.op[3] = PerturbOp{0, 1, 0, 0.f, eps, lr, 1.f};
   if ((rc = launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, m->var_loss, m->st))) return rc;
   float l2[2];
-  if ((rc = read_losses(m, l2, 2))) return rc;
+  if ((rc = copy_losses(m, l2, 2))) return rc;
   if (loss_plus) *loss_plus = l2[0];
   if (loss_minus) *loss_minus = l2[1];
   if (proj_grad) *proj_grad = (l2[0] - l2[1]) / (2.0f * eps);
@@ -646,20 +743,20 @@ int b2p_mezo_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets
                   int n_seeds, float eps, float* loss_pairs) {
   int rc = ready(m);
   if (rc) return rc;
-  B2P_REQUIRE(seeds && loss_pairs && n_seeds >= 1, "bad seeds/loss buffer");
-  B2P_REQUIRE(2 * n_seeds * n_seq <= m->max_groups, "2 x %d seeds x %d sequences exceed max_groups %d", n_seeds,
-              n_seq, m->max_groups);
-  if ((rc = stage_inputs(m, tokens, ctargets, n_seq, 2 * n_seeds))) return rc;
-  if ((rc = gen_masks(m, seeds, n_seeds))) return rc;
-  const float m2e = -2.0f * eps;
-  for (int s = 0; s < n_seeds; ++s) {
-    m->h_var[2 * s] = VariantInfo{s, 1, eps, 0.f};
-    m->h_var[2 * s + 1] = VariantInfo{s, 2, eps, m2e};
-  }
-  if ((rc = eval_staged(m, n_seq, 2 * n_seeds))) return rc;
-  B2P_CHECK_CUDA(cudaMemcpyAsync(loss_pairs, m->var_loss, 2 * n_seeds * 4, cudaMemcpyDefault, m->st));
-  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
-  return check_device_status(m->st);
+  B2P_REQUIRE(loss_pairs, "null loss buffer");
+  if ((rc = stage_tokens(m, tokens, ctargets, n_seq))) return rc;
+  const size_t nt = (size_t)n_seq * m->cfg.seq;
+  if ((rc = eval_pairs(m, m->d_tok, m->d_tok + nt, n_seq, seeds, n_seeds, eps))) return rc;
+  return copy_losses(m, loss_pairs, 2 * n_seeds);
+}
+
+int b2p_mezo_eval_device(b2p_model* m, const int32_t* d_tokens, const int32_t* d_targets, int n_seq,
+                         const uint64_t* seeds, int n_seeds, float eps, float* loss_pairs) {
+  int rc = ready(m);
+  if (rc) return rc;
+  B2P_REQUIRE(d_tokens && d_targets && loss_pairs, "null argument");
+  if ((rc = eval_pairs(m, d_tokens, d_targets, n_seq, seeds, n_seeds, eps))) return rc;
+  return copy_losses(m, loss_pairs, 2 * n_seeds);
 }
 
 int b2p_mezo_update(b2p_model* m, const uint64_t* seeds, const float* loss_pairs, int n_seeds, float eps, float lr) {
@@ -668,15 +765,16 @@ int b2p_mezo_update(b2p_model* m, const uint64_t* seeds, const float* loss_pairs
               n_seeds);
   int rc = gen_masks(m, seeds, n_seeds);
   if (rc) return rc;
-  // loss pairs may live on the host or the device
-  B2P_CHECK_CUDA(cudaMemcpyAsync(m->pairs, loss_pairs, 2 * n_seeds * 4, cudaMemcpyDefault, m->st));
+  if (is_device_ptr(loss_pairs)) {
+    B2P_CHECK_CUDA(cudaMemcpyAsync(m->pairs, loss_pairs, (size_t)2 * n_seeds * 4, cudaMemcpyDeviceToDevice, m->st));
+  } else if ((rc = stage_copy(m, m->pairs, loss_pairs, (size_t)2 * n_seeds * 4))) {
+    return rc;
+  }
   PerturbOps ops;
   std::memset(&ops, 0, sizeof(ops));
   ops.n = n_seeds;
   for (int s = 0; s < n_seeds; ++s) ops.op[s] = PerturbOp{s, 1, s, 0.f, eps, lr, (float)n_seeds};
-  if ((rc = launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, m->pairs, m->st))) return rc;
-  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
-  return check_device_status(m->st);
+  return launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, m->pairs, m->st);
 }
 
 int b2p_model_perturb(b2p_model* m, const uint64_t* seeds, const float* scales, int n) {
@@ -688,9 +786,7 @@ int b2p_model_perturb(b2p_model* m, const uint64_t* seeds, const float* scales, 
   std::memset(&ops, 0, sizeof(ops));
   ops.n = n;
   for (int s = 0; s < n; ++s) ops.op[s] = PerturbOp{s, 0, 0, scales[s], 0.f, 0.f, 1.f};
-  if ((rc = launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, nullptr, m->st))) return rc;
-  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
-  return B2P_OK;
+  return launch_perturb(m->theta, m->P, m->masks, m->mask_words, ops, nullptr, m->st);
 }
 
 int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_words) {
@@ -699,7 +795,40 @@ int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_wor
   if (rc) return rc;
   B2P_CHECK_CUDA(cudaMemcpyAsync(out_words, m->masks, (size_t)n * m->mask_words * 4, cudaMemcpyDefault, m->st));
   B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+int b2p_model_sync(b2p_model* m) {
+  B2P_REQUIRE(m, "null model");
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+int b2p_model_profile(b2p_model* m, int enable) {
+  B2P_REQUIRE(m, "null model");
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  m->prof = enable != 0;
+  m->ev_used = 0;
+  m->prof_flops.clear();
   return B2P_OK;
 }
+
+int b2p_model_profile_read(b2p_model* m, double* gemm_ms, double* gemm_flops, long long* gemm_launches) {
+  B2P_REQUIRE(m, "null model");
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  double ms = 0, fl = 0;
+  for (size_t i = 0; i + 1 < m->ev_used; i += 2) {
+    float t = 0;
+    B2P_CHECK_CUDA(cudaEventElapsedTime(&t, m->ev_pool[i], m->ev_pool[i + 1]));
+    ms += t;
+  }
+  for (double f : m->prof_flops) fl += f;
+  if (gemm_ms) *gemm_ms = ms;
+  if (gemm_flops) *gemm_flops = fl;
+  if (gemm_launches) *gemm_launches = (long long)(m->ev_used / 2);
+  return B2P_OK;
+}
+
+long long b2p_launch_count(void) { return launch_count(); }
 
 }  // extern "C"

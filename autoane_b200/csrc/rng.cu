@@ -188,7 +188,7 @@ int launch_sign_masks(const SignBuffer* d_bufs, int nbufs, const uint64_t* d_jum
   dim3 grid((unsigned)((nchunks + threads - 1) / threads), (unsigned)nseeds);
   sign_mask_kernel<<<grid, threads, 0, st>>>(d_bufs, nbufs, d_jumps, njump, total_draws, mask_words, d_seeds,
                                              d_masks);
-  B2P_CHECK_CUDA(cudaGetLastError());
+  B2P_POST_LAUNCH();
   return B2P_OK;
 }
 

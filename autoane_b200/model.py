@@ -130,6 +130,22 @@ class Model:
         _lib.call("b2p_mezo_eval", self.h, _u16(tok), _u16(tgt), n_seq, _u64(sd), len(sd), eps, ptr)
         return out
 
+    def mezo_eval_device(self, d_tokens: int, d_targets: int, n_seq: int, seeds, eps: float, out_ptr: int):
+        """Device-resident inputs (int32 [n_seq, seq] pointers) and a device/host output pointer."""
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        _lib.call("b2p_mezo_eval_device", self.h, d_tokens, d_targets, n_seq, _u64(sd), len(sd), eps, out_ptr)
+
+    def sync(self):
+        _lib.call("b2p_model_sync", self.h)
+
+    def profile(self, enable: bool):
+        _lib.call("b2p_model_profile", self.h, int(enable))
+
+    def profile_read(self):
+        ms, fl, n = C.c_double(), C.c_double(), C.c_longlong()
+        _lib.call("b2p_model_profile_read", self.h, C.byref(ms), C.byref(fl), C.byref(n))
+        return ms.value, fl.value, n.value
+
     def mezo_update(self, seeds, loss_pairs, eps: float, lr: float):
         sd = np.ascontiguousarray(seeds, np.uint64)
         ptr = loss_pairs.ctypes.data if isinstance(loss_pairs, np.ndarray) else int(loss_pairs)

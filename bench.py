@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""MeZO-LoRA-split throughput on SmolLM2-360M shapes, data-parallel over N B200s.
+
+Workload (one "step", every GPU): 8 independent synthetic 256-token sequences,
+4 perturbation seeds of its own, each seed evaluated at θ+εz and θ-εz over all
+8 sequences (64 sequence-forwards per GPU), the per-seed loss pairs all-gathered
+over NCCL, then the same seed-ordered LoRA/RMS update on every replica.
+
+Metric unit: one "seq-step" is one ±ε forward pair over one 256-token sequence,
+i.e. the forward work of one reference MeZO-LoRA-split step (train_mezo.m:2938-3012);
+a step of this workload performs 32 seq-steps per GPU. `value` is the whole-job
+seq-step rate with inputs resident in HBM, timed with CUDA events on the model
+stream; `e2e` is the same rate through the host-buffer C ABI (b2p_mezo_eval /
+b2p_mezo_update), host->device copies and the loss read-back inside the region.
+
+Run:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+(N > 1 under torch.distributed.run, one rank per GPU.)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+DIMS = dict(dim=960, hidden=2560, heads=15, kv_heads=5, head_dim=64, seq=256, nlayers=32, vocab=49152, rank=8,
+            rope_theta=100000.0)
+N_ACTIVE = 16893          # compact vocabulary (ids 0..16892)
+N_TOKENS = 20_000_000     # synthetic token stream
+SEQS_PER_GPU = 8
+SEEDS_PER_GPU = 4
+EPS = np.float32(1e-3)
+LR = np.float32(1e-4)
+REF_STEPS_PER_S = 3.82    # reference best: ANE conv-fused MeZO-LoRA-split r8, M2 Pro (README.md:16)
+
+
+def fwd_flops_per_seq() -> float:
+    """Algorithmic FLOPs of one 256-token forward (projections + lm-head + LoRA + dense attention)."""
+    d = DIMS
+    s, D, H, r = d["seq"], d["dim"], d["hidden"], d["rank"]
+    qd, kvd = d["heads"] * d["head_dim"], d["kv_heads"] * d["head_dim"]
+    proj = 2 * s * (D * (qd + 2 * kvd) + qd * D + 3 * D * H)
+    lora = 2 * s * r * ((3 * D + qd) + (qd + 2 * kvd + D))  # LoRA-down (A·x) + LoRA-up (B·U)
+    attn = 2 * 2 * d["heads"] * s * s * d["head_dim"]
+    head = 2 * s * N_ACTIVE * D
+    return float(d["nlayers"] * (proj + lora + attn) + head)
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def synth_weights(layer: int):
+    rng = np.random.default_rng([42, layer])
+    D, H = DIMS["dim"], DIMS["hidden"]
+    qd, kvd = DIMS["heads"] * DIMS["head_dim"], DIMS["kv_heads"] * DIMS["head_dim"]
+    shapes = [(qd, D), (kvd, D), (kvd, D), (D, qd), (H, D), (D, H), (H, D)]
+    return [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02) for s in shapes]
+
+
+def synth_embed():
+    rng = np.random.default_rng([42, 10_000])
+    return rng.standard_normal((DIMS["vocab"], DIMS["dim"]), dtype=np.float32) * np.float32(0.02)
+
+
+def synth_theta(layout):
+    """LoRA A ~ N(0, 1/r), B = 0, RMS weights 1 (workload definition)."""
+    rng = np.random.default_rng([42, 20_000])
+    L, D, r = DIMS["nlayers"], DIMS["dim"], DIMS["rank"]
+    qd = DIMS["heads"] * DIMS["head_dim"]
+    theta = np.zeros(layout["total"], np.float32)
+    for l in range(L):
+        b = l * layout["layer"]
+        for off, n in ((layout["Aq"], r * D), (layout["Ak"], r * D), (layout["Av"], r * D), (layout["Ao"], r * qd)):
+            theta[b + off:b + off + n] = rng.standard_normal(n, dtype=np.float32) / np.float32(np.sqrt(r))
+        theta[b + layout["rms_att"]:b + layout["rms_att"] + 2 * D] = 1.0
+    theta[layout["rms_final"]:] = 1.0
+    return theta
+
+
+def lora_layout():
+    D, r = DIMS["dim"], DIMS["rank"]
+    qd, kvd = DIMS["heads"] * DIMS["head_dim"], DIMS["kv_heads"] * DIMS["head_dim"]
+    o, lay = 0, {}
+    for name, n in (("Aq", r * D), ("Bq", qd * r), ("Ak", r * D), ("Bk", kvd * r), ("Av", r * D), ("Bv", kvd * r),
+                    ("Ao", r * qd), ("Bo", D * r), ("rms_att", D), ("rms_ffn", D)):
+        lay[name] = o
+        o += n
+    lay["layer"] = o
+    lay["rms_final"] = DIMS["nlayers"] * o
+    lay["total"] = lay["rms_final"] + D
+    return lay
+
+
+def token_stream():
+    return np.random.default_rng([42, 30_000]).integers(0, N_ACTIVE, N_TOKENS, dtype=np.int64).astype(np.uint16)
+
+
+def step_batch(tokens, step: int, rank: int, nseq: int):
+    """nseq sequences at seeded positions of the training split (train_mezo.m:1946-1953 analogue)."""
+    rng = np.random.default_rng([7919, step, rank])
+    train = int(len(tokens) * 0.9)
+    pos = rng.integers(0, train - DIMS["seq"] - 1, nseq)
+    inp = np.stack([tokens[p:p + DIMS["seq"]] for p in pos])
+    tgt = np.stack([tokens[p + 1:p + 1 + DIMS["seq"]] for p in pos])  # compact id == full id here
+    return np.ascontiguousarray(inp), np.ascontiguousarray(tgt)
+
+
+def step_seeds(step: int, world: int):
+    return np.array([step * 1000003 + 42 + k for k in range(SEEDS_PER_GPU * world)], np.uint64)
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [v for v in sm if v > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# --------------------------------------------------------------------------- CPU reference / baseline
+def cpu_reference_rate(max_seconds: float = 20.0, max_steps: int = 6, min_steps: int = 2, weights=None, embed=None):
+    """MeZO-LoRA-split steps/s of the CPU reference path on this host's cores (one step = one seq-step).
+
+    Uses the reference's own cpu_ops.h compiled from the AutoANE sources (oracle/_ref) for the
+    forward when that library was built, otherwise the oracle restatement (oracle/liboracle.so)."""
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    cfg = O.ModelCfg(dim=DIMS["dim"], hidden=DIMS["hidden"], heads=DIMS["heads"], kv_heads=DIMS["kv_heads"],
+                     hd=DIMS["head_dim"], seq=DIMS["seq"], nlayers=DIMS["nlayers"], vocab=DIMS["vocab"],
+                     rank=DIMS["rank"], rope_theta=DIMS["rope_theta"])
+    if weights is None:
+        ws = [synth_weights(l) for l in range(DIMS["nlayers"])]
+        weights = {k: [w[i] for w in ws] for i, k in enumerate(("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3"))}
+    if embed is None:
+        embed = synth_embed()
+    cembed = np.ascontiguousarray(embed[:N_ACTIVE])
+    lay = lora_layout()
+    theta = synth_theta(lay)
+    tokens = token_stream()
+    ref = O.ref_lib("smollm2_360m")
+    kind = "reference" if ref is not None else "port"
+    om = O.OracleModel(cfg, weights, embed, cembed)
+    if ref is not None:
+        step_fn = _ref_step_fn(ref, cfg, weights, embed, cembed, lay)
+    else:
+        def step_fn(th, inp, tgt, seed):
+            om.mezo_step(th, inp, tgt, seed, float(EPS), float(LR))
+    done, t0 = 0, time.perf_counter()
+    while done < max_steps and (done < min_steps or time.perf_counter() - t0 < max_seconds):
+        inp, tgt = step_batch(tokens, done, 0, 1)
+        step_fn(theta, inp[0], tgt[0], int(done * 1000003 + 42))
+        done += 1
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "seq-steps/s", "cores": threads, "kind": kind,
+            "sample": f"{done} MeZO-LoRA-split steps (1 seed, 1x256-token sequence each, +eps/-eps forwards and "
+                      f"update), SmolLM2-360M shapes, fp32, {threads} threads; "
+                      + ("forward = reference training/cpu_ops.h compiled from source + transcribed DO_FORWARD_PASS"
+                         if kind == "reference" else "forward = oracle restatement")}
+
+
+def _ref_step_fn(ref, cfg, weights, embed, cembed, lay):
+    """MeZO step body (train_mezo.m:2938-3012) over the reference-compiled forward (oracle/_ref)."""
+    import ctypes as C
+    from oracle import oracle as O
+    F = C.POINTER(C.c_float)
+    keep = []
+
+    def f(a):
+        return a.ctypes.data_as(F)
+
+    def plist(arrs):
+        p = (F * len(arrs))(*[f(a) for a in arrs])
+        keep.append((arrs, p))
+        return p
+
+    wp = [plist(weights[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")]
+    ref.ref_forward_loss.argtypes = [C.POINTER(F)] * 9 + [F, F, F, C.c_int, C.c_int, C.c_float,
+                                                          C.POINTER(C.c_uint16), C.POINTER(C.c_uint16)]
+
+    def fwd(theta, inp, tgt):
+        lora, rms = [], []
+        for l in range(cfg.nlayers):
+            b = l * lay["layer"]
+            for k in ("Aq", "Bq", "Ak", "Bk", "Av", "Bv", "Ao", "Bo"):
+                lora.append(theta[b + lay[k]:])
+            rms += [theta[b + lay["rms_att"]:], theta[b + lay["rms_ffn"]:]]
+        return ref.ref_forward_loss(*wp, plist(lora), plist(rms), f(theta[lay["rms_final"]:]), f(embed), f(cembed),
+                                    cembed.shape[0], cfg.rank, C.c_float(cfg.res_alpha),
+                                    inp.ctypes.data_as(C.POINTER(C.c_uint16)),
+                                    tgt.ctypes.data_as(C.POINTER(C.c_uint16)))
+
+    def step(theta, inp, tgt, seed):
+        args = (cfg.nlayers, cfg.dim, cfg.q_dim, cfg.kv_dim, cfg.rank, seed)
+        O.perturb_lora(theta, *args, EPS)
+        lp = fwd(theta, inp, tgt)
+        O.perturb_lora(theta, *args, np.float32(-2.0) * EPS)
+        lm = fwd(theta, inp, tgt)
+        O.perturb_lora(theta, *args, EPS)
+        g = np.float32((np.float32(lp) - np.float32(lm)) / (np.float32(2.0) * EPS))
+        O.perturb_lora(theta, *args, np.float32(-LR * g))
+
+    return step
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    # Each timed step is one bounded CPU sample: a single reference MeZO step (one seq-step).
+    # Steps beyond what fits in ~90 s of CPU time are not run; the rate is over the steps timed.
+    r = cpu_reference_rate(max_seconds=90.0, max_steps=max(2, args.steps), min_steps=2)
+    line = {"metric": "MeZO-LoRA steps/s SmolLM2-360M @1/2/4/8 B200; proj-GEMM % of TC peak", "impl": "reference",
+            "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": r["value"] / REF_STEPS_PER_S, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(world) | {"sample": r["sample"]},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(world: int):
+    return {"workload": "DP MeZO-LoRA-split r8, SmolLM2-360M shapes (32L, d960, 15/5 heads, FFN 2560, "
+                        "compact vocab 16893), SEQ 256; per GPU 8 sequences x 4 seeds x (+eps, -eps)",
+            "model": "SmolLM2-360M-shaped (random init)", "global_batch": SEQS_PER_GPU * world, "seq_len": DIMS["seq"],
+            "parallelism": f"dp{world}", "seeds_per_gpu": SEEDS_PER_GPU, "lora_rank": DIMS["rank"],
+            "eps": float(EPS), "lr": float(LR), "seq_steps_per_step": SEQS_PER_GPU * SEEDS_PER_GPU * world,
+            "l2": "inputs larger than L2 (661 MB of 16-bit weights streamed per step)",
+            "vs_baseline_ref": f"{REF_STEPS_PER_S} steps/s, M2 Pro ANE conv-fused (README.md:16)"}
+
+
+# --------------------------------------------------------------------------- B200 arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-profile", action="store_true", help="skip the in-region per-GEMM CUDA events")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from autoane_b200 import _lib
+    from autoane_b200.model import BF16, F16, Config, Model
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    _lib.call("b2p_init", local)
+    cfg = Config(dtype=BF16 if args.dtype == "bf16" else F16, max_groups=2 * SEEDS_PER_GPU * SEQS_PER_GPU,
+                 **{k: DIMS[k] for k in ("dim", "hidden", "heads", "kv_heads", "head_dim", "seq", "nlayers", "vocab",
+                                         "rank", "rope_theta")})
+    model = Model(cfg)
+    keep_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    cpu_w = {k: [] for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")} if keep_cpu else None
+    for l in range(DIMS["nlayers"]):
+        ws = synth_weights(l)
+        model.set_layer(l, *ws)
+        if keep_cpu:
+            for k, w in zip(cpu_w, ws):
+                cpu_w[k].append(w)
+    embed = synth_embed()
+    model.set_embedding(embed, np.arange(N_ACTIVE, dtype=np.int32))
+    lay = lora_layout()
+    model.set_trainable(synth_theta(lay))
+    tokens = token_stream()
+
+    W, K = args.warmup, args.steps
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.ExternalStream(model.stream)
+    # device-resident inputs for every step of the device-timed run
+    batches = [step_batch(tokens, s, rank, SEQS_PER_GPU) for s in range(W + K)]
+    d_tok = torch.tensor(np.stack([b[0] for b in batches]).astype(np.int32), device=dev)
+    d_tgt = torch.tensor(np.stack([b[1] for b in batches]).astype(np.int32), device=dev)
+    torch.cuda.synchronize()
+    pairs = torch.zeros(2 * SEEDS_PER_GPU, device=dev)
+    gathered = torch.zeros(2 * SEEDS_PER_GPU * world, device=dev)
+
+    def dev_step(s):
+        seeds = step_seeds(s, world)
+        local_seeds = seeds[SEEDS_PER_GPU * rank:SEEDS_PER_GPU * (rank + 1)]
+        model.mezo_eval_device(d_tok[s].data_ptr(), d_tgt[s].data_ptr(), SEQS_PER_GPU, local_seeds, float(EPS),
+                               pairs.data_ptr())
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, pairs)
+            model.mezo_update(seeds, gathered.data_ptr(), float(EPS), float(LR))
+        else:
+            model.mezo_update(seeds, pairs.data_ptr(), float(EPS), float(LR))
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    with torch.cuda.stream(stream):
+        for s in range(W):
+            dev_step(s)
+        model.sync()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        try:
+            phys = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+        except (KeyError, ValueError, IndexError):
+            phys = local
+        clocks = ClockSampler(phys)
+        clocks.start()
+        if not args.no_profile:
+            model.profile(True)
+        n_launch0 = int(_lib.load().b2p_launch_count())
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for s in range(W, W + K):
+            dev_step(s)
+        ev1.record(stream)
+        model.sync()
+        torch.cuda.synchronize()
+        n_launch = int(_lib.load().b2p_launch_count()) - n_launch0
+        dev_ms = ev0.elapsed_time(ev1)
+        gemm_ms, gemm_flops, gemm_n = model.profile_read() if not args.no_profile else (0.0, 0.0, 0)
+        model.profile(False)
+        barrier()
+        clk = clocks.stop()
+
+        # e2e: host buffers through the C ABI, every step copies its inputs in and its losses out
+        e_batches = [step_batch(tokens, 10_000 + s, rank, SEQS_PER_GPU) for s in range(K)]
+        host_pairs = np.zeros(2 * SEEDS_PER_GPU, np.float32)
+        model.sync()
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for s in range(K):
+            seeds = step_seeds(10_000 + s, world)
+            inp, tgt = e_batches[s]
+            model.mezo_eval(inp, tgt, seeds[SEEDS_PER_GPU * rank:SEEDS_PER_GPU * (rank + 1)],
+                            float(EPS), out=host_pairs)
+            if world > 1:
+                pairs.copy_(torch.from_numpy(host_pairs))
+                dist.all_gather_into_tensor(gathered, pairs)
+                model.mezo_update(seeds, gathered.data_ptr(), float(EPS), float(LR))
+            else:
+                model.mezo_update(seeds, host_pairs, float(EPS), float(LR))
+        model.sync()
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - t0
+        barrier()
+
+    # max over ranks
+    t = torch.tensor([dev_ms, e2e_s, gemm_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_s, gemm_ms_max = t.tolist()
+    units = SEQS_PER_GPU * SEEDS_PER_GPU * world * K
+    value = units / (dev_ms / 1000.0)
+    e2e_value = units / e2e_s
+
+    roofline = None
+    if gemm_n:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak = peaks.get("bf16_tflops_sustained")
+        peak_src = "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json)"
+        if peak is None:
+            peak, peak_src = 1400.0, "fallback sustained 1.4 PFLOP/s"
+        achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "traffic": gemm_traffic_per_launch(),
+                    "kernel": "gemm_tc_kernel (all projection + lm-head launches)", "launches": gemm_n,
+                    "avg_launch_us": round(1000.0 * gemm_ms / gemm_n, 2), "peak_source": peak_src,
+                    "flops_per_launch_avg": gemm_flops / gemm_n}
+    h2d = 2 * SEQS_PER_GPU * DIMS["seq"] * 4 + 2 * cfg.max_groups * 4 + 2 * SEEDS_PER_GPU * 16 + \
+        SEEDS_PER_GPU * 8 + SEEDS_PER_GPU * world * 8 + (0 if world > 1 else 2 * SEEDS_PER_GPU * 4)
+    d2h = 2 * SEEDS_PER_GPU * 4
+    if rank == 0:
+        cpu = None
+        if keep_cpu:
+            cpu = cpu_reference_rate(weights=cpu_w, embed=embed)
+        line = {"metric": "MeZO-LoRA steps/s SmolLM2-360M @1/2/4/8 B200; proj-GEMM % of TC peak",
+                "value": round(value, 3), "unit": "seq-steps/s", "n_gpus": world, "steps": K, "warmup": W,
+                "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": round(value / REF_STEPS_PER_S, 2), "dtype": args.dtype, "data": "synthetic",
+                "config": workload_config(world) | {
+                    "optimizer_steps_per_s": round(K / (dev_ms / 1000.0), 3),
+                    "tflops_per_gpu": round(2 * SEQS_PER_GPU * SEEDS_PER_GPU * fwd_flops_per_seq() * K /
+                                            (dev_ms / 1000.0) / 1e12, 2)},
+                "e2e": {"value": round(e2e_value, 3), "unit": "seq-steps/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h},
+                "gpu_launches": n_launch, "roofline": roofline, "clocks": clk, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def gemm_traffic_per_launch():
+    """DRAM bytes per projection-GEMM launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "gemm_tc_kernel_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+if __name__ == "__main__":
+    sys.exit(main())

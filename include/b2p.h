@@ -140,6 +140,12 @@ int b2p_mezo_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets
  * the n_seq sequences. loss_pairs[2s] = L+, [2s+1] = L- (host or device pointer). */
 int b2p_mezo_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, const uint64_t* seeds,
                   int n_seeds, float eps, float* loss_pairs);
+/* Same as b2p_mezo_eval with the inputs already resident on the device: d_tokens
+ * and d_targets are int32 [n_seq][seq] device arrays (out-of-range ids are
+ * reported by b2p_model_sync as B2P_ERR_DEVICE). Fully asynchronous when
+ * loss_pairs is device memory, so a collective can follow on the model stream. */
+int b2p_mezo_eval_device(b2p_model* m, const int32_t* d_tokens, const int32_t* d_targets, int n_seq,
+                         const uint64_t* seeds, int n_seeds, float eps, float* loss_pairs);
 /* Data-parallel MeZO, update half: θ ← θ + c_s·z_s applied in seed order with
  * c_s = (-lr·(L+_s - L-_s)/(2ε)) / n_seeds (the K-direction averaged update of
  * train_mezo.m:2751-2768). Every replica given the same arguments ends bit-identical. */
@@ -149,6 +155,19 @@ int b2p_model_perturb(b2p_model* m, const uint64_t* seeds, const float* scales, 
 /* Sign masks of the perturbation stream: out_words[i][w], bit b of word w = sign of
  * parameter 32w+b for seeds[i] (1 = +). ceil(P/32) words per seed. */
 int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_words);
+
+/* Wait for the model stream and report any device-side status (bounded-wait
+ * expiry, out-of-range token). b2p_mezo_update / b2p_model_perturb and the
+ * device-pointer forms of the eval calls are asynchronous; this is their fence. */
+int b2p_model_sync(b2p_model* m);
+/* Time every projection-GEMM launch of subsequent forwards with CUDA events on the
+ * model stream (enable = 1), or stop (0). Enabling clears the record. */
+int b2p_model_profile(b2p_model* m, int enable);
+/* Sum of the recorded GEMM launch durations (ms), their algorithmic FLOPs
+ * (2·M·N·K each) and the launch count since profiling was enabled. */
+int b2p_model_profile_read(b2p_model* m, double* gemm_ms, double* gemm_flops, long long* gemm_launches);
+/* Number of kernels this library has launched in this process. */
+long long b2p_launch_count(void);
 
 #ifdef __cplusplus
 }
