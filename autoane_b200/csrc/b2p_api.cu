@@ -33,10 +33,8 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
   std::memset(&ep, 0, sizeof(ep));
   ep.M = M;
   ep.N = N;
-  ep.out = Y;
-  ep.ldo = ldy;
   const int kind = out_f32 ? EPI_F32 : EPI_H16;
-  return launch_gemm(pick_bn(N, kind), kind, dtype == B2P_BF16, X, K, W, K, M, N, K, ep,
+  return launch_gemm(pick_bn(N, kind), kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, nullptr, ep,
                      static_cast<cudaStream_t>(stream));
 }
 

@@ -80,20 +80,30 @@ int check_device_status(cudaStream_t st) {
   return B2P_OK;
 }
 
-int make_tmap_kmajor(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint64_t ld, uint32_t box_rows,
-                     bool bf16) {
+int make_tmap_2d(CUtensorMap* map, const void* base, TmapType type, uint64_t inner, uint64_t rows, uint64_t ld,
+                 uint32_t box_inner, uint32_t box_rows, int swizzle_bytes) {
+  const uint64_t esz = type == TM_F32 ? 4 : 2;
   B2P_REQUIRE(base != nullptr, "tensor map over a null pointer");
-  B2P_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15u) == 0, "operand base must be 16-byte aligned");
-  B2P_REQUIRE(k >= 8 && (ld * 2) % 16 == 0 && ld >= k, "K=%llu / ld=%llu: row pitch must be a multiple of 8 elements",
-              (unsigned long long)k, (unsigned long long)ld);
-  B2P_REQUIRE(rows >= 1 && box_rows >= 1 && box_rows <= 256, "bad rows/box");
-  cuuint64_t gdim[2] = {k, rows};
-  cuuint64_t gstride[1] = {ld * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  B2P_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15u) == 0, "tensor base must be 16-byte aligned");
+  B2P_REQUIRE(inner >= 1 && (ld * esz) % 16 == 0 && ld >= inner,
+              "inner=%llu / ld=%llu: row pitch must be a multiple of 16 bytes", (unsigned long long)inner,
+              (unsigned long long)ld);
+  B2P_REQUIRE(rows >= 1 && box_rows >= 1 && box_rows <= 256 && box_inner >= 1 && box_inner <= 256, "bad box");
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+  if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  B2P_REQUIRE(swizzle_bytes == 0 || box_inner * esz == (uint64_t)swizzle_bytes,
+              "box inner extent must equal the swizzle span");
+  const CUtensorMapDataType dt = type == TM_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : type == TM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t gdim[2] = {inner, rows};
+  cuuint64_t gstride[1] = {ld * esz};
+  cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estride[2] = {1, 1};
-  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                        const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -119,81 +129,104 @@ int pick_bn(int N, int kind) {
   return best;
 }
 
-template <int BN, int KIND, typename OutT, bool BF16>
-static int launch_t(const void* X, int ldx, const void* W, int ldw, int M, int N, int K, const EpiParams& ep,
-                    cudaStream_t st) {
+template <int BN, int KIND, typename OutT, bool BF16, bool LORA>
+static int launch_t(const void* X, int ldx, const void* W, int ldw, int M, int N, int K, void* out, int ldo,
+                    const void* u16, const EpiParams& ep, cudaStream_t st) {
   DeviceCtx* c = nullptr;
   int rc = ctx_get(&c);
   if (rc) return rc;
-  CUtensorMap tx, tw;
-  if ((rc = make_tmap_kmajor(&tx, X, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, kBM, BF16))) return rc;
-  if ((rc = make_tmap_kmajor(&tw, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, BN, BF16))) return rc;
-  using S = GemmSmem<BN>;
-  auto kern = gemm_tc_kernel<BN, KIND, OutT, BF16>;
-  static thread_local int attr_dev_mask = 0;
-  if (!(attr_dev_mask & (1 << (c->device & 31)))) {
+  const TmapType in_t = BF16 ? TM_BF16 : TM_F16;
+  CUtensorMap tx, tw, to, tu;
+  if ((rc = make_tmap_2d(&tx, X, in_t, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, 64, kBM, 128))) return rc;
+  if ((rc = make_tmap_2d(&tw, W, in_t, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, 64, BN, 128))) return rc;
+  using S = GemmSmem<BN, KIND>;
+  if (S::kStores) {
+    const int ncols = KIND == EPI_SWIGLU ? N / 2 : N;
+    if (S::kOutF32) {
+      if ((rc = make_tmap_2d(&to, out, TM_F32, (uint64_t)ncols, (uint64_t)M, (uint64_t)ldo, 32, 32, 128))) return rc;
+    } else {
+      if ((rc = make_tmap_2d(&to, out, in_t, (uint64_t)ncols, (uint64_t)M, (uint64_t)ldo, 32, 32, 64))) return rc;
+    }
+  } else {
+    to = tx;
+  }
+  if (LORA) {
+    if ((rc = make_tmap_2d(&tu, u16, in_t, (uint64_t)kUCols, (uint64_t)M, (uint64_t)kUCols, 16, kBM, 32))) return rc;
+  } else {
+    tu = tx;
+  }
+  auto kern = gemm_tc_kernel<BN, KIND, OutT, BF16, LORA>;
+  static thread_local uint64_t attr_dev_mask = 0;
+  if (!(attr_dev_mask & (1ull << (c->device & 63)))) {
     B2P_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-    attr_dev_mask |= 1 << (c->device & 31);
+    attr_dev_mask |= 1ull << (c->device & 63);
   }
   const long long tiles = (long long)((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = (int)(tiles < c->num_sms ? tiles : c->num_sms);
   EpiParams e = ep;
   e.status = c->status;
-  kern<<<grid, kGemmThreads, S::kTotal, st>>>(tx, tw, M, N, K, e);
+  kern<<<grid, kGemmThreads, S::kTotal, st>>>(tx, tw, to, tu, M, N, K, e);
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
-template <int KIND, typename OutH, bool BF16>
-static int dispatch_bn(int bn, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
-                       const EpiParams& ep, cudaStream_t st) {
+template <int KIND, typename OutH, bool BF16, bool LORA>
+static int dispatch_bn(int bn, const void* X, int ldx, const void* W, int ldw, int M, int N, int K, void* out,
+                       int ldo, const void* u16, const EpiParams& ep, cudaStream_t st) {
   switch (bn) {
-    case 128: return launch_t<128, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
-    case 160: return launch_t<160, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
-    case 192: return launch_t<192, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
-    case 256: return launch_t<256, KIND, OutH, BF16>(X, ldx, W, ldw, M, N, K, ep, st);
+    case 128: return launch_t<128, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case 160: return launch_t<160, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case 192: return launch_t<192, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case 256: return launch_t<256, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     default: set_error("unsupported tile width %d", bn); return B2P_ERR_UNSUPPORTED;
   }
 }
 
+template <typename H, bool BF16>
+static int dispatch_kind(int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                         void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st) {
+  const bool lora = ep.has_lora != 0;
+  switch (kind) {
+    case EPI_F32:
+      return dispatch_bn<EPI_F32, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case EPI_H16:
+      return dispatch_bn<EPI_H16, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case EPI_QKV_ROPE:
+      if (!lora) break;
+      return bn == 128 ? launch_t<128, EPI_QKV_ROPE, H, BF16, true>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st)
+                       : launch_t<160, EPI_QKV_ROPE, H, BF16, true>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case EPI_RESID:
+      if (lora) return dispatch_bn<EPI_RESID, H, BF16, true>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+      return dispatch_bn<EPI_RESID, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case EPI_SWIGLU:
+      return launch_t<256, EPI_SWIGLU, H, BF16, false>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case EPI_CE:
+      return launch_t<256, EPI_CE, H, BF16, false>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+  }
+  set_error("unsupported epilogue kind %d (LoRA %d)", kind, (int)lora);
+  return B2P_ERR_UNSUPPORTED;
+}
+
 int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
-                const EpiParams& ep, cudaStream_t st) {
+                void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st) {
   B2P_REQUIRE(M > 0 && N > 0 && K > 0, "empty GEMM (M=%d N=%d K=%d)", M, N, K);
   if (ep.has_lora) {
-    B2P_REQUIRE(ep.lora.rank > 0 && ep.lora.rank <= kMaxRank && ep.lora.rank % 4 == 0,
-                "LoRA rank must be a multiple of 4 in [4, 16] (got %d)", ep.lora.rank);
+    B2P_REQUIRE(u16 != nullptr, "LoRA GEMM without a U buffer");
+    B2P_REQUIRE(ep.lora.rank > 0 && ep.lora.rank <= kMaxRank && 32 % ep.lora.rank == 0,
+                "LoRA rank must divide 32 and be <= 16 (got %d)", ep.lora.rank);
     B2P_REQUIRE(ep.lora.group_rows % kBM == 0, "LoRA variant groups must span whole 128-row tiles");
+    for (int s = 0; s < ep.lora.nseg; ++s) {
+      B2P_REQUIRE(ep.lora.seg_boff[s] % ep.lora.rank == 0, "LoRA B offset must be a multiple of the rank");
+      B2P_REQUIRE(ep.lora.seg_ucol[s] % 16 == 0 && ep.lora.seg_ucol[s] + 16 <= kUCols, "bad U column");
+    }
     for (int s = 1; s < ep.lora.nseg; ++s)
       B2P_REQUIRE(ep.lora.seg_start[s] % bn == 0, "segment boundary %d not a multiple of tile width %d",
                   ep.lora.seg_start[s], bn);
   }
-  if (bf16) {
-    using H = __nv_bfloat16;
-    switch (kind) {
-      case EPI_F32: return dispatch_bn<EPI_F32, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_H16: return dispatch_bn<EPI_H16, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_QKV_ROPE:
-        return bn == 128 ? launch_t<128, EPI_QKV_ROPE, H, true>(X, ldx, W, ldw, M, N, K, ep, st)
-                         : launch_t<160, EPI_QKV_ROPE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_RESID: return dispatch_bn<EPI_RESID, H, true>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_SWIGLU: return launch_t<256, EPI_SWIGLU, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_CE: return launch_t<256, EPI_CE, H, true>(X, ldx, W, ldw, M, N, K, ep, st);
-    }
-  } else {
-    using H = __half;
-    switch (kind) {
-      case EPI_F32: return dispatch_bn<EPI_F32, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_H16: return dispatch_bn<EPI_H16, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_QKV_ROPE:
-        return bn == 128 ? launch_t<128, EPI_QKV_ROPE, H, false>(X, ldx, W, ldw, M, N, K, ep, st)
-                         : launch_t<160, EPI_QKV_ROPE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_RESID: return dispatch_bn<EPI_RESID, H, false>(bn, X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_SWIGLU: return launch_t<256, EPI_SWIGLU, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
-      case EPI_CE: return launch_t<256, EPI_CE, H, false>(X, ldx, W, ldw, M, N, K, ep, st);
-    }
-  }
-  set_error("unknown epilogue kind %d", kind);
-  return B2P_ERR_ARG;
+  if (kind != EPI_CE) B2P_REQUIRE(out != nullptr, "GEMM without an output");
+  if (kind == EPI_SWIGLU) B2P_REQUIRE(N % 256 == 0, "SwiGLU needs N %% 256 == 0");
+  if (bf16) return dispatch_kind<__nv_bfloat16, true>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+  return dispatch_kind<__half, false>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
 }
 
 }  // namespace b2p

@@ -57,15 +57,21 @@ int ctx_get(DeviceCtx** out);
 // Read and clear the device status word; returns B2P_ERR_DEVICE if non-zero.
 int check_device_status(cudaStream_t st);
 
-// 2-D K-major tensor map over a [rows, k] 16-bit matrix (row stride ld elements),
-// box = 64 elements x box_rows rows, 128-byte swizzle, zero fill out of bounds.
-int make_tmap_kmajor(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint64_t ld, uint32_t box_rows,
-                     bool bf16);
+// Element type of a tensor map.
+enum TmapType : int { TM_F16 = 0, TM_BF16 = 1, TM_F32 = 2 };
 
-// Launch D = X·W^T with the given epilogue. Chooses the compiled tile width
-// `bn` (one of 128, 160, 192, 256).
+// 2-D tensor map over a row-major [rows, inner] matrix (row pitch ld elements),
+// box = box_inner x box_rows elements, given swizzle (0 none, 32, 64, 128 bytes),
+// zero fill out of bounds.
+int make_tmap_2d(CUtensorMap* map, const void* base, TmapType type, uint64_t inner, uint64_t rows, uint64_t ld,
+                 uint32_t box_inner, uint32_t box_rows, int swizzle_bytes);
+
+// Launch D = X·W^T (+ U·Bv^T with LoRA) with the given epilogue. `bn` is the
+// compiled tile width (128, 160, 192 or 256). `out`/`ldo` is the destination of
+// the stored kinds (fp32 for EPI_F32/EPI_RESID, 16-bit otherwise); `u16` is the
+// [M, 64] 16-bit LoRA-down buffer when ep.has_lora.
 int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
-                const EpiParams& ep, cudaStream_t st);
+                void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
 
 // Pick the tile width for an N-column output (largest width whose padding
 // waste is minimal; SwiGLU and CE need multiples of 64 / any).

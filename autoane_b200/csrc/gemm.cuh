@@ -1,24 +1,34 @@
 // gemm.cuh — the projection tile engine: a persistent, warp-specialised
 // tcgen05 GEMM for sm_100a.
 //
-//   D[M, N] = X[M, K] · W[N, K]^T          (token-major activations X, weights W)
+//   D[M, N] = X[M, K] · W[N, K]^T  (+ U[M, 16] · Bv[N, 16]^T  with LoRA)
 //
 // X rows are tokens (the MMA "M" side, 128-row tiles), W rows are output
 // channels (the "N" side, BN-column tiles). Both operands are K-major 16-bit
 // (fp16 or bf16) and are brought into shared memory by TMA with 128-byte
-// swizzle; the fp32 accumulator lives in TMEM (two BN-column buffers so the
-// epilogue of tile i overlaps the MMAs of tile i+1).
+// swizzle; the fp32 accumulator lives in TMEM (two buffers so the epilogue of
+// tile i overlaps the MMAs of tile i+1).
 //
-// Warp roles (192 threads):
-//   warp 0      TMA producer (one lane)
-//   warp 1      TMEM allocator + UMMA issuer (one lane)
-//   warps 2..5  epilogue: TMEM -> registers -> fused epilogue -> HBM
+// The LoRA-split correction out += B·(A·x) (reference lora_addmm,
+// training/train_mezo.m:694-703) runs on the tensor cores as one extra K=16
+// MMA per tile: U = A·x (per token, 16-bit, zero-padded to 16 columns) is
+// loaded by TMA, and the perturbed B rows of the tile's variant,
+// fl(fl(B + s1·z) + s2·z), are computed on the fly from the fp32 master copy
+// and the sign mask straight into shared memory (never stored to HBM).
+//
+// Warp roles (352 threads):
+//   warp 0       TMA producer (one lane)
+//   warp 1       TMEM allocator + UMMA issuer (one lane)
+//   warp 2       LoRA operand warp (perturbed B tile + U tile TMA), LoRA kernels only
+//   warps 3..10  epilogue: TMEM -> registers -> fused epilogue -> swizzled smem
+//                -> TMA store / TMA reduce-add. Warps w and w+4 share TMEM lane
+//                quarter w%4 and split the tile's 32-column chunks.
 //
 // This is the channel-first projection Y[out,T] = W[out,in]·X[in,T] of the
 // reference (training/train_mezo.m:1533-1538, 1598, 1630-1633, 1669, 1696)
 // stored transposed: the device keeps activations token-major so that every
-// fused epilogue (LoRA-up, RoPE pairs, SiLU·gate pairs, residual, CE row
-// statistics) sees one token row per thread.
+// fused epilogue (RoPE pairs, SiLU·gate pairs, residual, CE row statistics)
+// sees one token row per thread.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -31,14 +41,17 @@ namespace b2p {
 constexpr int kBM = 128;          // token rows per tile (UMMA M)
 constexpr int kBK = 64;           // K elements per pipeline stage (128 B of 16-bit)
 constexpr int kUmmaK = 16;        // K per tcgen05.mma for kind::f16
-constexpr int kGemmThreads = 192;
-constexpr int kMaxRank = 16;
+constexpr int kEpiWarps = 8;
+constexpr int kFirstEpiWarp = 3;
+constexpr int kGemmThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 352
+constexpr int kMaxRank = 16;      // LoRA rank padded to one UMMA K step
+constexpr int kUCols = 64;        // U16 row: 4 projections x 16 columns
 
 enum EpiKind : int {
   EPI_F32 = 0,       // out fp32 [M, ldo] = acc (+ LoRA)
   EPI_H16 = 1,       // out 16-bit [M, ldo] = acc (+ LoRA)
   EPI_QKV_ROPE = 2,  // out 16-bit: acc + LoRA(seg), RoPE on columns < rope_cols
-  EPI_RESID = 3,     // out fp32 x [M, ldo] += alpha * (acc + LoRA)
+  EPI_RESID = 3,     // out fp32 x [M, ldo] += alpha * (acc + LoRA)   (TMA reduce-add)
   EPI_SWIGLU = 4,    // tile = [gate half | up half]; out 16-bit [M, ldo] = silu(gate) * up
   EPI_CE = 5,        // per-row (max, sum exp) partials over the tile's valid columns + target logit
 };
@@ -61,9 +74,7 @@ __device__ __forceinline__ uint32_t mask_bit(const uint32_t* mask, long long idx
   return (__ldg(mask + (idx >> 5)) >> (idx & 31)) & 1u;
 }
 
-// LoRA-up epilogue operands: Y += B_v · U  where U = A_v · x was produced per
-// token by the LoRA-down stage and B_v is the perturbed LoRA B for the tile's
-// variant (reference lora_addmm, training/train_mezo.m:694-703).
+// LoRA operands of a GEMM: U16 tile via TMA, perturbed B from theta.
 struct LoraEpi {
   const float* theta;          // flat trainable parameters (fp32 master copy)
   const uint32_t* masks;       // [slots][mask_words] sign bits, bit i <-> parameter i
@@ -71,19 +82,15 @@ struct LoraEpi {
   const VariantInfo* variants;
   const int* group_variant;    // variant id of each group of `group_rows` token rows
   int group_rows;
-  const float* U;              // [M, ldu] fp32
-  int ldu;
-  int rank;
-  int nseg;                    // column segments sharing one epilogue (1, or 3 for Q|K|V)
+  int rank;                    // 4 or 8 (<= 16)
+  int nseg;                    // column segments (1, or 3 for Q|K|V)
   int seg_start[4];            // seg_start[nseg] == N; every boundary a multiple of BN
-  long long seg_boff[3];       // offset of segment's B [rows, rank] inside theta
-  int seg_ucol[3];             // first U column of the segment
+  long long seg_boff[3];       // offset of segment's B [rows, rank] inside theta (multiple of rank)
+  int seg_ucol[3];             // first U16 column of the segment (multiple of 16)
 };
 
 struct EpiParams {
   int M, N;
-  void* out;
-  int ldo;
   float alpha;
   int has_lora;
   LoraEpi lora;
@@ -95,31 +102,40 @@ struct EpiParams {
   int seq_len;
   // cross-entropy partials
   const int* targets;          // [M] compact target id per token row (-1: none)
-  float2* ce_part;             // [M, n_tiles_n]
+  float2* ce_part;             // [M, 2 * n_tiles_n] (one partial per epilogue column half)
   float* ce_tgt;               // [M]
   int n_tiles_n;
   uint32_t* status;            // device error word
 };
 
-template <int BN>
+template <int BN, int KIND>
 struct GemmSmem {
+  static constexpr bool kOutF32 = (KIND == EPI_F32 || KIND == EPI_RESID);
+  static constexpr bool kStores = (KIND != EPI_CE);
   static constexpr int kAStage = kBM * kBK * 2;  // 16 KB
   static constexpr int kBStage = BN * kBK * 2;
   static constexpr int kStageBytes = kAStage + kBStage;
-  static constexpr int kEpiBytes = BN * kMaxRank * 4;  // perturbed LoRA B tile
+  // per epilogue warp: one 32 x 32 staging box (fp32 128 B rows / 16-bit 64 B rows)
+  static constexpr int kStageOutBytes = kStores ? (kOutF32 ? 4096 : 2048) : 0;
+  static constexpr int kOutBytes = kStageOutBytes * kEpiWarps;
+  static constexpr int kLoraU = kBM * kMaxRank * 2;   // 4 KB
+  static constexpr int kLoraB = BN * kMaxRank * 2;    // BN x 32 B
+  static constexpr int kLoraBytes = 2 * (kLoraU + kLoraB);
   static constexpr int kBudget = 224 * 1024;
-  static constexpr int kStages = ((kBudget - kEpiBytes - 1024) / kStageBytes) > 8
-                                     ? 8
-                                     : ((kBudget - kEpiBytes - 1024) / kStageBytes);
-  static constexpr int kBarOff = kStages * kStageBytes + kEpiBytes;
+  static constexpr int kFree = kBudget - kOutBytes - kLoraBytes - 1024 - 256;
+  static constexpr int kStages = (kFree / kStageBytes) > 8 ? 8 : (kFree / kStageBytes);
+  static constexpr int kOutOff = kStages * kStageBytes;
+  static constexpr int kLoraOff = kOutOff + kOutBytes;
+  static constexpr int kBarOff = kLoraOff + kLoraBytes;
   static constexpr int kTotal = kBarOff + 256 + 1024;  // + barriers + alignment slack
   static constexpr int kAccStride = BN <= 128 ? 128 : 256;  // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = 2 * kAccStride;
   static_assert(kTotal <= 227 * 1024, "shared memory over the 227 KB per-CTA limit");
   static_assert(kStages >= 2, "pipeline needs at least two stages");
+  static_assert(kLoraOff % 1024 == 0 && kOutOff % 1024 == 0, "1 KB alignment of swizzled buffers");
 };
 
-__device__ __forceinline__ float silu_f(float h) { return h / (1.0f + expf(-h)); }
+__device__ __forceinline__ float silu_f(float h) { return __fdividef(h, 1.0f + __expf(-h)); }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -134,37 +150,42 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Store 32 consecutive values of one row as 16-bit, vectorised when the whole
-// chunk is in range.
-template <typename T>
-__device__ __forceinline__ void store_row16(T* dst, const float* v, int nvalid) {
-  if (nvalid >= 32) {
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
+// Write one 32-value row of a 32 x 32 staging box in the TMA swizzle layout:
+// fp32 rows are 128 B (SWIZZLE_128B: chunk c of row r at c ^ (r & 7)),
+// 16-bit rows are 64 B (SWIZZLE_64B: chunk c of row r at c ^ ((r >> 1) & 3)).
+template <bool F32, typename OutT>
+__device__ __forceinline__ void stage_row(uint8_t* box, int r, const float* v) {
+  if (F32) {
+    uint8_t* row = box + r * 128;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
-      w.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
-      w.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
-      w.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
-      d4[q] = w;
-    }
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(row + ((c ^ (r & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   } else {
+    uint8_t* row = box + r * 64;
 #pragma unroll
-    for (int c = 0; c < 32; ++c)
-      if (c < nvalid) dst[c] = static_cast<T>(v[c]);
+    for (int c = 0; c < 4; ++c) {
+      uint4 w;
+      w.x = pack2<OutT>(v[8 * c + 0], v[8 * c + 1]);
+      w.y = pack2<OutT>(v[8 * c + 2], v[8 * c + 3]);
+      w.z = pack2<OutT>(v[8 * c + 4], v[8 * c + 5]);
+      w.w = pack2<OutT>(v[8 * c + 6], v[8 * c + 7]);
+      *reinterpret_cast<uint4*>(row + ((c ^ ((r >> 1) & 3)) << 4)) = w;
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
-template <int BN, int KIND, typename OutT, bool BF16>
+template <int BN, int KIND, typename OutT, bool BF16, bool LORA>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, int M, int N,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmU, int M, int N,
                    int K, EpiParams ep) {
-  using S = GemmSmem<BN>;
+  using S = GemmSmem<BN, KIND>;
   constexpr int STAGES = S::kStages;
+  constexpr int NCHUNK = (KIND == EPI_SWIGLU) ? BN / 64 : BN / 32;  // 32-column output chunks per tile
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
   static_assert(KIND != EPI_SWIGLU || BN % 64 == 0, "SwiGLU tiles hold two halves of 32-column chunks");
 
@@ -172,14 +193,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kAStage;
-  float* sLoraB = reinterpret_cast<float*>(smem + STAGES * S::kStageBytes);
+  uint8_t* sOut = smem + S::kOutOff;
+  uint8_t* sLU = smem + S::kLoraOff;                 // 2 x U tile   [128][16] 16-bit, SW32
+  uint8_t* sLB = sLU + 2 * S::kLoraU;                // 2 x Bv tile  [BN][16]  16-bit, SW32
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* tfull_bar = bars + 2 * STAGES;
-  uint64_t* tempty_bar = bars + 2 * STAGES + 2;
-  uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* lfull_bar = tfull_bar + 4;
+  uint64_t* lempty_bar = tfull_bar + 6;
+  uint64_t* drain_bar = tfull_bar + 8;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tfull_bar + 9);
   volatile uint32_t* abort_flag = tmem_holder + 1;
   volatile uint32_t* epi_abort = tmem_holder + 2;
 
@@ -193,13 +218,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty_bar[a], kEpiWarps);  // one arrive per epilogue warp
+      mbar_init(&lfull_bar[a], 1);
+      mbar_init(&lempty_bar[a], 1);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
+    if (S::kStores) tma_prefetch_desc(&tmOut);
+    if (LORA) tma_prefetch_desc(&tmU);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, S::kTmemCols);
@@ -261,6 +290,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      int lb = 0;
+      uint32_t lphase = 0;
       bool ok = true;
       bool issued_any = false;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -291,6 +322,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (!ok) break;
+        if (LORA) {
+          // += U[128 x 16] · Bv[BN x 16]^T, one K=16 step
+          if (!mbar_wait(&lfull_bar[lb], lphase, abort_flag, ep.status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          umma_f16_ss(d_tmem, sw32_kmajor_desc(smem_u32(sLU + lb * S::kLoraU)),
+                      sw32_kmajor_desc(smem_u32(sLB + lb * S::kLoraB)), idesc, 1u);
+          umma_commit(&lempty_bar[lb]);
+          if (++lb == 2) {
+            lb = 0;
+            lphase ^= 1u;
+          }
+        }
         umma_commit(&tfull_bar[acc]);
         if (++acc == 2) {
           acc = 0;
@@ -303,11 +349,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_wait_drain(drain_bar, 0);
       }
     }
+  } else if (warp == 2) {
+    // ---------------- LoRA operand warp ----------------
+    if (LORA) {
+      int lb = 0;
+      uint32_t lphase = 0;
+      const int rank = ep.lora.rank;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mt = tile / num_n, nt = tile % num_n;
+        const int m0 = mt * kBM, n0 = nt * BN;
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&lempty_bar[lb], lphase ^ 1u, abort_flag, ep.status, DEV_TIMEOUT_PRODUCER);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        int seg = 0;
+        while (seg + 1 < ep.lora.nseg && n0 >= ep.lora.seg_start[seg + 1]) ++seg;
+        const VariantInfo vi = ep.lora.variants[ep.lora.group_variant[m0 / ep.lora.group_rows]];
+        const uint32_t* mask = ep.lora.masks + (long long)(vi.mode ? vi.mask_slot : 0) * ep.lora.mask_words;
+        const int cs = n0 - ep.lora.seg_start[seg];
+        const int seg_rows = ep.lora.seg_start[seg + 1] - ep.lora.seg_start[seg];
+        uint8_t* bt = sLB + lb * S::kLoraB;
+        // one B row (rank values, zero-padded to 16) per lane and pass
+        for (int n = lane; n < BN; n += 32) {
+          float b[kMaxRank];
+#pragma unroll
+          for (int j = 0; j < kMaxRank; ++j) b[j] = 0.f;
+          if (cs + n < seg_rows) {
+            const long long p0 = ep.lora.seg_boff[seg] + (long long)(cs + n) * rank;
+            // rank divides 32 and p0 is a multiple of rank, so the row's signs share one mask word
+            const uint32_t word = vi.mode ? __ldg(mask + (p0 >> 5)) : 0u;
+            const int sh = (int)(p0 & 31);
+#pragma unroll
+            for (int j = 0; j < kMaxRank; ++j)
+              if (j < rank) {
+                const float th = __ldg(ep.lora.theta + p0 + j);
+                b[j] = vi.mode ? perturb_value(th, (word >> (sh + j)) & 1u, vi) : th;
+              }
+          }
+          // SWIZZLE_32B K-major: 32-byte rows, 16-byte chunk c of row n at c ^ ((n >> 2) & 1)
+          uint8_t* rowp = bt + n * 32;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint4 w;
+            w.x = pack2<OutT>(b[8 * c + 0], b[8 * c + 1]);
+            w.y = pack2<OutT>(b[8 * c + 2], b[8 * c + 3]);
+            w.z = pack2<OutT>(b[8 * c + 4], b[8 * c + 5]);
+            w.w = pack2<OutT>(b[8 * c + 6], b[8 * c + 7]);
+            *reinterpret_cast<uint4*>(rowp + ((c ^ ((n >> 2) & 1)) << 4)) = w;
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&lfull_bar[lb], S::kLoraU);
+          tma_load_2d(sLU + lb * S::kLoraU, &tmU, &lfull_bar[lb], ep.lora.seg_ucol[seg], m0);
+        }
+        if (++lb == 2) {
+          lb = 0;
+          lphase ^= 1u;
+        }
+      }
+    }
   } else {
-    // ---------------- Epilogue (warps 2..5) ----------------
+    // ---------------- Epilogue (warps 3..10) ----------------
+    const int ew = warp - kFirstEpiWarp;   // 0..7
     const int lg = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = ew >> 2;              // which interleaved half of the tile's chunks
     const int row_in_tile = lg * 32 + lane;
-    const int et = threadIdx.x - 64;       // 0..127 within the epilogue group
+    const int et = threadIdx.x - kFirstEpiWarp * 32;  // 0..255 within the epilogue group
+    uint8_t* box = sOut + ew * S::kStageOutBytes;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -316,41 +426,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = m0 + row_in_tile;
       const bool row_ok = row < M;
 
-      // ---- stage the perturbed LoRA B tile for this tile's variant ----
-      int seg = 0;
-      float u[kMaxRank];
-      const int rank = ep.has_lora ? ep.lora.rank : 0;
-      if (ep.has_lora) {
-        while (seg + 1 < ep.lora.nseg && n0 >= ep.lora.seg_start[seg + 1]) ++seg;
-        const int grp = m0 / ep.lora.group_rows;
-        const VariantInfo vi = ep.lora.variants[ep.lora.group_variant[grp]];
-        const uint32_t* mask = ep.lora.masks + (long long)(vi.mode ? vi.mask_slot : 0) * ep.lora.mask_words;
-        named_bar_sync(1, 128);  // previous tile done reading sLoraB
-        const int cs = n0 - ep.lora.seg_start[seg];
-        const int seg_rows = ep.lora.seg_start[seg + 1] - ep.lora.seg_start[seg];
-        for (int i = et; i < BN * rank; i += 128) {
-          const int c = i / rank, j = i - c * rank;
-          float b = 0.f;
-          if (cs + c < seg_rows) {
-            const long long pidx = ep.lora.seg_boff[seg] + (long long)(cs + c) * rank + j;
-            const float th = __ldg(ep.lora.theta + pidx);
-            b = vi.mode ? perturb_value(th, mask_bit(mask, pidx), vi) : th;
-          }
-          sLoraB[c * kMaxRank + j] = b;
-        }
-        named_bar_sync(1, 128);
-#pragma unroll
-        for (int j = 0; j < kMaxRank; ++j)
-          u[j] = (j < rank && row_ok) ? __ldg(ep.lora.U + (long long)row * ep.lora.ldu + ep.lora.seg_ucol[seg] + j)
-                                      : 0.f;
-      }
-
       mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, ep.status, DEV_TIMEOUT_EPILOGUE);
-      // All four epilogue warps take the same continue/abort decision, so no
-      // warp is ever left waiting at a named barrier that the others skip.
-      named_bar_sync(2, 128);
+      // All epilogue warps take the same continue/abort decision.
+      named_bar_sync(2, 32 * kEpiWarps);
       if (et == 0) *epi_abort = *abort_flag;
-      named_bar_sync(2, 128);
+      named_bar_sync(2, 32 * kEpiWarps);
       if (*epi_abort) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + acc * S::kAccStride + ((uint32_t)(lg * 32) << 16);
@@ -359,122 +439,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int tgt = -1;
       if (KIND == EPI_CE && row_ok) tgt = ep.targets[row];
 
-      if (KIND == EPI_SWIGLU) {
-        constexpr int HALF = BN / 2;
 #pragma unroll 1
-        for (int c0 = 0; c0 < HALF; c0 += 32) {
+      for (int ch = half; ch < NCHUNK; ch += 2) {
+        float v[32];
+        int col;
+        __syncwarp();
+        if (KIND == EPI_SWIGLU) {
           uint32_t g[32], up[32];
-          __syncwarp();
-          tmem_ld32(t_row + c0, g);
-          tmem_ld32(t_row + HALF + c0, up);
+          tmem_ld32(t_row + ch * 32, g);
+          tmem_ld32(t_row + BN / 2 + ch * 32, up);
           tmem_ld_wait();
-          float* v = reinterpret_cast<float*>(g);
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] = silu_f(__uint_as_float(g[c])) * __uint_as_float(up[c]);
-          const int ocol = nt * HALF + c0;
-          if (row_ok && ocol < ep.N / 2)
-            store_row16<OutT>(reinterpret_cast<OutT*>(ep.out) + (long long)row * ep.ldo + ocol, v,
-                              min(32, ep.N / 2 - ocol));
-        }
-      } else {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+          col = nt * (BN / 2) + ch * 32;
+        } else {
           uint32_t r[32];
-          __syncwarp();
-          tmem_ld32(t_row + c0, r);
+          tmem_ld32(t_row + ch * 32, r);
           tmem_ld_wait();
-          float v[32];
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
-          if (ep.has_lora) {
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const float4* bl = reinterpret_cast<const float4*>(sLoraB + (c0 + c) * kMaxRank);
-              float a = v[c];
-#pragma unroll
-              for (int q = 0; q < kMaxRank / 4; ++q) {
-                if (4 * q < rank) {
-                  const float4 b4 = bl[q];
-                  a = fmaf(b4.x, u[4 * q + 0], a);
-                  a = fmaf(b4.y, u[4 * q + 1], a);
-                  a = fmaf(b4.z, u[4 * q + 2], a);
-                  a = fmaf(b4.w, u[4 * q + 3], a);
-                }
-              }
-              v[c] = a;
-            }
-          }
-          const int col = n0 + c0;
+          col = n0 + ch * 32;
+        }
+        if (KIND == EPI_CE) {
           const int nvalid = min(32, N - col);
-          if (KIND == EPI_CE) {
-            if (row_ok && nvalid > 0) {
-              float cm = -INFINITY;
+          if (row_ok && nvalid > 0) {
+            float cm = -INFINITY;
 #pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (c < nvalid) cm = fmaxf(cm, v[c]);
-              if (cm > ce_m) {
-                ce_s *= expf(ce_m - cm);
-                ce_m = cm;
-              }
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (c < nvalid) ce_s += expf(v[c] - ce_m);
-              if (tgt >= col && tgt < col + nvalid) {
-#pragma unroll
-                for (int c = 0; c < 32; ++c)
-                  if (col + c == tgt) ep.ce_tgt[row] = v[c];
-              }
+            for (int c = 0; c < 32; ++c)
+              if (c < nvalid) cm = fmaxf(cm, v[c]);
+            if (cm > ce_m) {
+              ce_s *= __expf(ce_m - cm);
+              ce_m = cm;
             }
-          } else if (row_ok && nvalid > 0) {
-          if (KIND == EPI_QKV_ROPE && col < ep.rope_cols) {
-            const int pos = row % ep.seq_len;
-            const int half = ep.head_dim >> 1;
-            const float* cs_row = ep.rope_cos + (long long)pos * half;
-            const float* sn_row = ep.rope_sin + (long long)pos * half;
 #pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              const int i = ((col + c) % ep.head_dim) >> 1;
-              const float cs = __ldg(cs_row + i), sn = __ldg(sn_row + i);
-              const float v0 = v[c], v1 = v[c + 1];
-              v[c] = v0 * cs - v1 * sn;
-              v[c + 1] = v0 * sn + v1 * cs;
+            for (int c = 0; c < 32; ++c)
+              if (c < nvalid) ce_s += __expf(v[c] - ce_m);
+            if (tgt >= col && tgt < col + nvalid) {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (col + c == tgt) ep.ce_tgt[row] = v[c];
             }
           }
-          if (KIND == EPI_F32) {
-            float* dst = reinterpret_cast<float*>(ep.out) + (long long)row * ep.ldo + col;
-            if (nvalid >= 32) {
+          continue;
+        }
+        if (KIND == EPI_QKV_ROPE && col < ep.rope_cols) {
+          const int pos = row % ep.seq_len;
+          const int hh = ep.head_dim >> 1;
+          const float* cs_row = ep.rope_cos + (long long)pos * hh;
+          const float* sn_row = ep.rope_sin + (long long)pos * hh;
 #pragma unroll
-              for (int q = 0; q < 8; ++q)
-                reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (c < nvalid) dst[c] = v[c];
-            }
-          } else if (KIND == EPI_RESID) {
-            float* dst = reinterpret_cast<float*>(ep.out) + (long long)row * ep.ldo + col;
-            if (nvalid >= 32) {
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                float4 x = reinterpret_cast<float4*>(dst)[q];
-                x.x = fmaf(ep.alpha, v[4 * q + 0], x.x);
-                x.y = fmaf(ep.alpha, v[4 * q + 1], x.y);
-                x.z = fmaf(ep.alpha, v[4 * q + 2], x.z);
-                x.w = fmaf(ep.alpha, v[4 * q + 3], x.w);
-                reinterpret_cast<float4*>(dst)[q] = x;
-              }
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (c < nvalid) dst[c] = fmaf(ep.alpha, v[c], dst[c]);
-            }
-          } else {  // EPI_H16, EPI_QKV_ROPE
-            store_row16<OutT>(reinterpret_cast<OutT*>(ep.out) + (long long)row * ep.ldo + col, v, nvalid);
+          for (int c = 0; c < 32; c += 2) {
+            const int i = ((col + c) % ep.head_dim) >> 1;
+            const float cs = __ldg(cs_row + i), sn = __ldg(sn_row + i);
+            const float v0 = v[c], v1 = v[c + 1];
+            v[c] = v0 * cs - v1 * sn;
+            v[c + 1] = v0 * sn + v1 * cs;
           }
-          }  // row_ok && nvalid > 0
+        }
+        if (KIND == EPI_RESID) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] *= ep.alpha;
+        }
+        // stage the 32 x 32 box (the previous store must have finished reading it)
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        stage_row<S::kOutF32, OutT>(box, lane, v);
+        fence_proxy_async_smem();
+        __syncwarp();
+        // boxes that start inside the tensor are clipped by TMA; boxes wholly outside are skipped
+        if (lane == 0 && m0 + lg * 32 < M && col < (KIND == EPI_SWIGLU ? N / 2 : N)) {
+          if (KIND == EPI_RESID)
+            tma_reduce_add_2d(&tmOut, box, col, m0 + lg * 32);
+          else
+            tma_store_2d(&tmOut, box, col, m0 + lg * 32);
+          bulk_commit();
         }
       }
-      if (KIND == EPI_CE && row_ok) ep.ce_part[(long long)row * ep.n_tiles_n + nt] = make_float2(ce_m, ce_s);
+      if (KIND == EPI_CE && row_ok)
+        ep.ce_part[(long long)row * (2 * ep.n_tiles_n) + 2 * nt + half] = make_float2(ce_m, ce_s);
 
       tc_fence_before();
       __syncwarp();
@@ -484,6 +526,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (S::kStores && lane == 0) bulk_wait0();  // every store of this warp has completed
   }
 
   tc_fence_before();

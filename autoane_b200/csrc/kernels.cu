@@ -74,20 +74,26 @@ __global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a)
   const uint32_t* mask = a.pc.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.pc.mask_words;
   const int nrows_a = a.n_a * a.rank;
 
-  // stage perturbed operands: θ (+ s1 z) (+ s2 z), exactly as perturb_buffer adds them
-  if (NORM) {
-    for (int c = threadIdx.x; c < dim; c += blockDim.x) {
-      const long long p = a.w_off + c;
-      const float th = __ldg(a.pc.theta + p);
-      s_w[c] = vi.mode ? perturb_value(th, mask_bit(mask, p), vi) : th;
+  // stage perturbed operands: θ (+ s1 z) (+ s2 z), exactly as perturb_buffer adds them;
+  // 4 parameters per load (offsets and widths are multiples of 4, so the four
+  // signs sit in one mask word)
+  auto stage4 = [&](float* dst, long long p) {
+    float4 th = __ldg(reinterpret_cast<const float4*>(a.pc.theta + p));
+    if (vi.mode) {
+      const uint32_t w = __ldg(mask + (p >> 5)) >> (p & 31);
+      th.x = perturb_value(th.x, w & 1u, vi);
+      th.y = perturb_value(th.y, (w >> 1) & 1u, vi);
+      th.z = perturb_value(th.z, (w >> 2) & 1u, vi);
+      th.w = perturb_value(th.w, (w >> 3) & 1u, vi);
     }
-  }
-  for (int i = threadIdx.x; i < nrows_a * dim; i += blockDim.x) {
+    *reinterpret_cast<float4*>(dst) = th;
+  };
+  if (NORM)
+    for (int c = 4 * threadIdx.x; c < dim; c += 4 * blockDim.x) stage4(s_w + c, a.w_off + c);
+  for (int i = 4 * threadIdx.x; i < nrows_a * dim; i += 4 * blockDim.x) {
     const int ja = i / dim, c = i - ja * dim;
     const int m = ja / a.rank, j = ja - m * a.rank;
-    const long long p = a.a_off[m] + (long long)j * dim + c;
-    const float th = __ldg(a.pc.theta + p);
-    s_a[i] = vi.mode ? perturb_value(th, mask_bit(mask, p), vi) : th;
+    stage4(s_a + i, a.a_off[m] + (long long)j * dim + c);
   }
   __syncthreads();
 
@@ -130,7 +136,10 @@ __global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a)
         p = fmaf(v[k].y, w.y, p);
       }
       p = warp_sum(p);
-      if (lane == 0) a.U[(long long)row * a.ldu + a.u_col + ja] = p;
+      if (lane == 0) {
+        const int m = ja / a.rank, j = ja - m * a.rank;
+        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(p);
+      }
     }
   }
 }
@@ -168,7 +177,10 @@ static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
 
 int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st) {
   B2P_REQUIRE(a.dim % 64 == 0, "dim %d must be a multiple of 64", a.dim);
-  B2P_REQUIRE(a.n_a >= 0 && a.n_a <= 3 && (a.n_a == 0 || a.rank > 0), "bad LoRA-down count");
+  B2P_REQUIRE(a.n_a >= 0 && a.n_a <= 3 && (a.n_a == 0 || (a.rank > 0 && a.rank <= 16)), "bad LoRA-down count");
+  B2P_REQUIRE(a.u_col % 16 == 0 && a.u_col + 16 * a.n_a <= kUCols, "LoRA-down columns out of range");
+  B2P_REQUIRE(a.w_off % 4 == 0 && a.a_off[0] % 4 == 0 && a.a_off[1] % 4 == 0 && a.a_off[2] % 4 == 0,
+              "parameter offsets must be multiples of 4");
   B2P_REQUIRE(a.pc.group_rows % kNormRowsPerBlock == 0, "variant groups must be multiples of %d rows",
               kNormRowsPerBlock);
   const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);

@@ -23,10 +23,11 @@ int launch_embed(const float* embed, int vocab, int dim, const int32_t* tokens, 
                  int rows, float* x, uint32_t* status, cudaStream_t st);
 
 // Per token row: optional RMSNorm with the perturbed weight at theta[w_off]
-// (training/cpu_ops.h:7-22) written as 16-bit xn, then U[row, u_col + i*r + j] =
+// (training/cpu_ops.h:7-22) written as 16-bit xn, then U[row, u_col + 16*i + j] =
 // A_i(perturbed)[j, :] · v for the n_a LoRA-down matrices at theta[a_off[i]]
 // (first half of lora_addmm, training/train_mezo.m:698), v = normalised row in fp32
-// (norm) or the 16-bit input row (no norm).
+// (norm) or the 16-bit input row (no norm). U is 16-bit [rows, 64]; columns
+// j >= rank of each 16-column group stay zero (they pad the tensor-core K step).
 struct NormLoraArgs {
   const void* in;       // fp32 [rows, dim] (norm) or 16-bit [rows, dim]
   void* xn;             // 16-bit [rows, dim] (norm only)
@@ -36,8 +37,8 @@ struct NormLoraArgs {
   int n_a;              // number of LoRA-down matrices (0..3)
   long long a_off[3];
   int rank;
-  float* U;
-  int ldu, u_col;
+  void* U;
+  int u_col;
   PerturbCtx pc;
 };
 int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st);

@@ -53,7 +53,7 @@ struct b2p_model {
   int max_groups = 0, max_rows = 0, n_vt = 0;
   float* x = nullptr;
   void* xn = nullptr;
-  float* U = nullptr;
+  void* U = nullptr;             // [max_rows][kUCols] 16-bit LoRA-down results (zero padded)
   void* qkv = nullptr;
   void* attn = nullptr;
   void* hbuf = nullptr;
@@ -80,7 +80,6 @@ struct b2p_model {
 
 namespace {
 
-constexpr int kU_cols = 32;  // U columns: q, k, v, o LoRA-down (rank <= 8 each)
 
 size_t esz(const b2p_model*) { return 2; }
 
@@ -101,12 +100,13 @@ int model_alloc(b2p_model* m) {
   const size_t R = m->max_rows;
   B2P_CHECK_CUDA(cudaMalloc(&m->x, R * c.dim * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->xn, R * std::max(c.dim, m->q_dim) * e));
-  B2P_CHECK_CUDA(cudaMalloc(&m->U, R * kU_cols * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->U, R * kUCols * e));
+  B2P_CHECK_CUDA(cudaMemset(m->U, 0, R * kUCols * e));
   B2P_CHECK_CUDA(cudaMalloc(&m->qkv, R * m->qkv_dim * e));
   B2P_CHECK_CUDA(cudaMalloc(&m->attn, R * m->q_dim * e));
   B2P_CHECK_CUDA(cudaMalloc(&m->hbuf, R * c.hidden * e));
   const int ntiles = (c.vocab + 255) / 256;  // enough for any compact vocabulary
-  B2P_CHECK_CUDA(cudaMalloc(&m->ce_part, R * ntiles * sizeof(float2)));
+  B2P_CHECK_CUDA(cudaMalloc(&m->ce_part, R * 2 * ntiles * sizeof(float2)));
   B2P_CHECK_CUDA(cudaMalloc(&m->ce_tgt, R * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->row_loss, R * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->group_loss, m->max_groups * 4));
@@ -193,23 +193,21 @@ LoraEpi lora_epi(const b2p_model* m) {
   le.variants = m->d_var;
   le.group_variant = m->d_meta + m->max_groups;
   le.group_rows = m->cfg.seq;
-  le.U = m->U;
-  le.ldu = kU_cols;
   le.rank = m->cfg.rank;
   return le;
 }
 
 // launch_gemm, bracketed by CUDA events on the model stream when profiling is on.
 int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
-         const EpiParams& ep) {
-  if (!m->prof) return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, ep, m->st);
+         void* out, int ldo, const EpiParams& ep) {
+  if (!m->prof) return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
   while (m->ev_pool.size() < m->ev_used + 2) {
     cudaEvent_t e;
     B2P_CHECK_CUDA(cudaEventCreate(&e));
     m->ev_pool.push_back(e);
   }
   B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used], m->st));
-  int rc = launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, ep, m->st);
+  int rc = launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
   B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used + 1], m->st));
   m->ev_used += 2;
   m->prof_flops.push_back(2.0 * M * (double)N * K);
@@ -246,8 +244,7 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     na.a_off[2] = lb + m->oAv;
     na.rank = c.rank;
     na.U = m->U;
-    na.ldu = kU_cols;
-    na.u_col = 0;
+    na.u_col = 0;  // q, k, v at U16 columns 0, 16, 32
     na.pc = pc;
     if ((rc = launch_norm_lora(na, m->bf16, m->st))) return rc;
     // Q|K|V = xn · Wqkv^T + B·U (perturbed B), RoPE on Q and K
@@ -255,8 +252,6 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     std::memset(&ep, 0, sizeof(ep));
     ep.M = R;
     ep.N = QKV;
-    ep.out = m->qkv;
-    ep.ldo = QKV;
     ep.has_lora = 1;
     ep.lora = lora_epi(m);
     ep.lora.nseg = 3;
@@ -268,15 +263,15 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     ep.lora.seg_boff[1] = lb + m->oBk;
     ep.lora.seg_boff[2] = lb + m->oBv;
     ep.lora.seg_ucol[0] = 0;
-    ep.lora.seg_ucol[1] = c.rank;
-    ep.lora.seg_ucol[2] = 2 * c.rank;
+    ep.lora.seg_ucol[1] = 16;
+    ep.lora.seg_ucol[2] = 32;
     ep.rope_cos = m->rope_cos;
     ep.rope_sin = m->rope_sin;
     ep.rope_cols = QD + KVD;
     ep.head_dim = c.head_dim;
     ep.seq_len = c.seq;
     const char* wqkv = static_cast<const char*>(m->wqkv) + (size_t)l * QKV * D * e;
-    if ((rc = gemm(m, m->qkv_bn, EPI_QKV_ROPE, m->xn, D, wqkv, D, R, QKV, D, ep))) return rc;
+    if ((rc = gemm(m, m->qkv_bn, EPI_QKV_ROPE, m->xn, D, wqkv, D, R, QKV, D, m->qkv, QKV, ep))) return rc;
     // attention
     AttnArgs aa;
     aa.qkv = m->qkv;
@@ -302,8 +297,7 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     nb.a_off[0] = lb + m->oAo;
     nb.rank = c.rank;
     nb.U = m->U;
-    nb.ldu = kU_cols;
-    nb.u_col = 3 * c.rank;
+    nb.u_col = 48;  // o at U16 column 48
     nb.pc = pc;
     if ((rc = launch_norm_lora(nb, m->bf16, m->st))) return rc;
     // x += alpha * (attn · Wo^T + Bo·Uo)
@@ -311,8 +305,6 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     std::memset(&eo, 0, sizeof(eo));
     eo.M = R;
     eo.N = D;
-    eo.out = m->x;
-    eo.ldo = D;
     eo.alpha = c.res_alpha;
     eo.has_lora = 1;
     eo.lora = lora_epi(m);
@@ -320,9 +312,9 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     eo.lora.seg_start[0] = 0;
     eo.lora.seg_start[1] = D;
     eo.lora.seg_boff[0] = lb + m->oBo;
-    eo.lora.seg_ucol[0] = 3 * c.rank;
+    eo.lora.seg_ucol[0] = 48;
     const char* wo = static_cast<const char*>(m->wo) + (size_t)l * D * QD * e;
-    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->attn, QD, wo, QD, R, D, QD, eo)))
+    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->attn, QD, wo, QD, R, D, QD, m->x, D, eo)))
       return rc;
     // RMSNorm(rms_ffn)
     NormLoraArgs nf;
@@ -341,20 +333,16 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     std::memset(&es, 0, sizeof(es));
     es.M = R;
     es.N = 2 * H;
-    es.out = m->hbuf;
-    es.ldo = H;
     const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
-    if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, es))) return rc;
+    if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, m->hbuf, H, es))) return rc;
     // x += alpha * (h · W2^T)
     EpiParams e2;
     std::memset(&e2, 0, sizeof(e2));
     e2.M = R;
     e2.N = D;
-    e2.out = m->x;
-    e2.ldo = D;
     e2.alpha = c.res_alpha;
     const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
-    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->hbuf, H, w2, H, R, D, H, e2)))
+    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->hbuf, H, w2, H, R, D, H, m->x, D, e2)))
       return rc;
   }
   // final RMSNorm + lm-head with fused cross-entropy partials
@@ -377,8 +365,8 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
   ec.ce_part = m->ce_part;
   ec.ce_tgt = m->ce_tgt;
   ec.n_tiles_n = ntiles;
-  if ((rc = gemm(m, 256, EPI_CE, m->xn, D, m->cembed, D, R, m->cv, D, ec))) return rc;
-  return launch_ce_reduce(m->ce_part, ntiles, m->ce_tgt, R, c.seq, m->row_loss, m->group_loss, m->st);
+  if ((rc = gemm(m, 256, EPI_CE, m->xn, D, m->cembed, D, R, m->cv, D, nullptr, 0, ec))) return rc;
+  return launch_ce_reduce(m->ce_part, 2 * ntiles, m->ce_tgt, R, c.seq, m->row_loss, m->group_loss, m->st);
 }
 
 __global__ void expand_targets_kernel(const int32_t* seq_tgt, const int* group_seq, int seq, int rows, int cv,

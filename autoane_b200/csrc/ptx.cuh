@@ -180,6 +180,43 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// Same for a K-major tile with 32-byte rows (16 16-bit elements = one UMMA K
+// step) and 32-byte swizzle: 8-row core groups 256 B apart, layout 6.
+__device__ __forceinline__ uint64_t sw32_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;             // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(256u >> 4) << 32;      // SBO: 8 rows x 32 B
+  d |= static_cast<uint64_t>(1u) << 46;             // descriptor version for sm_100
+  d |= static_cast<uint64_t>(6u) << 61;             // SWIZZLE_32B
+  return d;
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA stores, tensor-core operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// TMA tiled store / f32 add-reduction of a shared-memory box at (x, y).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Instruction descriptor, kind::f16: f32 accumulator, A and B both f16 or both
 // bf16, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, int M, int N) {
