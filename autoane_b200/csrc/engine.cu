@@ -212,8 +212,10 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
   B2P_REQUIRE(M > 0 && N > 0 && K > 0, "empty GEMM (M=%d N=%d K=%d)", M, N, K);
   if (ep.has_lora) {
     B2P_REQUIRE(u16 != nullptr, "LoRA GEMM without a U buffer");
-    B2P_REQUIRE(ep.lora.rank > 0 && ep.lora.rank <= kMaxRank && 32 % ep.lora.rank == 0,
-                "LoRA rank must divide 32 and be <= 16 (got %d)", ep.lora.rank);
+    B2P_REQUIRE(ep.lora.rank == 4 || ep.lora.rank == 8, "LoRA rank must be 4 or 8 (got %d)", ep.lora.rank);
+    B2P_REQUIRE(ep.lora.n_groups >= (M + ep.lora.group_rows - 1) / ep.lora.group_rows &&
+                    ep.lora.n_groups <= kMaxGroups && ep.lora.n_variants >= 1 && ep.lora.n_variants <= kMaxGroups,
+                "LoRA group/variant tables out of range");
     B2P_REQUIRE(ep.lora.group_rows % kBM == 0, "LoRA variant groups must span whole 128-row tiles");
     for (int s = 0; s < ep.lora.nseg; ++s) {
       B2P_REQUIRE(ep.lora.seg_boff[s] % ep.lora.rank == 0, "LoRA B offset must be a multiple of the rank");
@@ -224,6 +226,9 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
                   ep.lora.seg_start[s], bn);
   }
   if (kind != EPI_CE) B2P_REQUIRE(out != nullptr, "GEMM without an output");
+  if (kind == EPI_QKV_ROPE)
+    B2P_REQUIRE(ep.head_dim == 64 && ep.seq_len % kBM == 0 && ep.rope_cols % 64 == 0,
+                "RoPE epilogue needs head_dim 64, seq %% 128 == 0 and whole heads");
   if (kind == EPI_SWIGLU) B2P_REQUIRE(N % 256 == 0, "SwiGLU needs N %% 256 == 0");
   if (bf16) return dispatch_kind<__nv_bfloat16, true>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
   return dispatch_kind<__half, false>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);

@@ -46,6 +46,7 @@ constexpr int kFirstEpiWarp = 3;
 constexpr int kGemmThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 352
 constexpr int kMaxRank = 16;      // LoRA rank padded to one UMMA K step
 constexpr int kUCols = 64;        // U16 row: 4 projections x 16 columns
+constexpr int kMaxGroups = 256;   // variant groups / variants a LoRA launch may reference
 
 enum EpiKind : int {
   EPI_F32 = 0,       // out fp32 [M, ldo] = acc (+ LoRA)
@@ -82,6 +83,8 @@ struct LoraEpi {
   const VariantInfo* variants;
   const int* group_variant;    // variant id of each group of `group_rows` token rows
   int group_rows;
+  int n_groups;                // entries of group_variant (<= kMaxGroups)
+  int n_variants;              // entries of variants (<= kMaxGroups)
   int rank;                    // 4 or 8 (<= 16)
   int nseg;                    // column segments (1, or 3 for Q|K|V)
   int seg_start[4];            // seg_start[nseg] == N; every boundary a multiple of BN
@@ -122,11 +125,13 @@ struct GemmSmem {
   static constexpr int kLoraB = BN * kMaxRank * 2;    // BN x 32 B
   static constexpr int kLoraBytes = 2 * (kLoraU + kLoraB);
   static constexpr int kBudget = 224 * 1024;
-  static constexpr int kFree = kBudget - kOutBytes - kLoraBytes - 1024 - 256;
+  static constexpr int kFree = kBudget - kOutBytes - kLoraBytes - kMaxGroups * 20 - 1024 - 256;
   static constexpr int kStages = (kFree / kStageBytes) > 8 ? 8 : (kFree / kStageBytes);
   static constexpr int kOutOff = kStages * kStageBytes;
   static constexpr int kLoraOff = kOutOff + kOutBytes;
-  static constexpr int kBarOff = kLoraOff + kLoraBytes;
+  static constexpr int kVarOff = kLoraOff + kLoraBytes;          // group -> variant table, variant infos
+  static constexpr int kVarBytes = kMaxGroups * 4 + kMaxGroups * 16;
+  static constexpr int kBarOff = kVarOff + kVarBytes;
   static constexpr int kTotal = kBarOff + 256 + 1024;  // + barriers + alignment slack
   static constexpr int kAccStride = BN <= 128 ? 128 : 256;  // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = 2 * kAccStride;
@@ -352,50 +357,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 2) {
     // ---------------- LoRA operand warp ----------------
     if (LORA) {
+      int* s_gvar = reinterpret_cast<int*>(smem + S::kVarOff);
+      VariantInfo* s_var = reinterpret_cast<VariantInfo*>(smem + S::kVarOff + kMaxGroups * 4);
+      for (int i = lane; i < ep.lora.n_groups; i += 32) s_gvar[i] = ep.lora.group_variant[i];
+      for (int i = lane; i < ep.lora.n_variants; i += 32) s_var[i] = ep.lora.variants[i];
+      __syncwarp();
+      constexpr int RPL = (BN + 31) / 32;  // B rows per lane
       int lb = 0;
       uint32_t lphase = 0;
       const int rank = ep.lora.rank;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         const int mt = tile / num_n, nt = tile % num_n;
         const int m0 = mt * kBM, n0 = nt * BN;
+        int seg = 0;
+        while (seg + 1 < ep.lora.nseg && n0 >= ep.lora.seg_start[seg + 1]) ++seg;
+        const VariantInfo vi = s_var[s_gvar[m0 / ep.lora.group_rows]];
+        const uint32_t* mask = ep.lora.masks + (long long)(vi.mode ? vi.mask_slot : 0) * ep.lora.mask_words;
+        const int cs = n0 - ep.lora.seg_start[seg];
+        const int seg_rows = ep.lora.seg_start[seg + 1] - ep.lora.seg_start[seg];
+        // issue every load of this tile's B rows before using any (rank divides 32 and each
+        // row starts at a multiple of rank, so a row's signs share one mask word)
+        float4 th[RPL][2];
+        uint32_t mw[RPL];
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+          const int n = lane + 32 * i;
+          const bool ok = n < BN && cs + n < seg_rows;
+          const long long p0 = ep.lora.seg_boff[seg] + (long long)(cs + n) * rank;
+          th[i][0] = ok ? __ldg(reinterpret_cast<const float4*>(ep.lora.theta + p0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          th[i][1] = (ok && rank > 4) ? __ldg(reinterpret_cast<const float4*>(ep.lora.theta + p0 + 4))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+          mw[i] = (ok && vi.mode) ? (__ldg(mask + (p0 >> 5)) >> (p0 & 31)) : 0u;
+        }
         int ok = 1;
         if (lane == 0) ok = mbar_wait(&lempty_bar[lb], lphase ^ 1u, abort_flag, ep.status, DEV_TIMEOUT_PRODUCER);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        int seg = 0;
-        while (seg + 1 < ep.lora.nseg && n0 >= ep.lora.seg_start[seg + 1]) ++seg;
-        const VariantInfo vi = ep.lora.variants[ep.lora.group_variant[m0 / ep.lora.group_rows]];
-        const uint32_t* mask = ep.lora.masks + (long long)(vi.mode ? vi.mask_slot : 0) * ep.lora.mask_words;
-        const int cs = n0 - ep.lora.seg_start[seg];
-        const int seg_rows = ep.lora.seg_start[seg + 1] - ep.lora.seg_start[seg];
         uint8_t* bt = sLB + lb * S::kLoraB;
-        // one B row (rank values, zero-padded to 16) per lane and pass
-        for (int n = lane; n < BN; n += 32) {
-          float b[kMaxRank];
 #pragma unroll
-          for (int j = 0; j < kMaxRank; ++j) b[j] = 0.f;
-          if (cs + n < seg_rows) {
-            const long long p0 = ep.lora.seg_boff[seg] + (long long)(cs + n) * rank;
-            // rank divides 32 and p0 is a multiple of rank, so the row's signs share one mask word
-            const uint32_t word = vi.mode ? __ldg(mask + (p0 >> 5)) : 0u;
-            const int sh = (int)(p0 & 31);
+        for (int i = 0; i < RPL; ++i) {
+          const int n = lane + 32 * i;
+          if (n < BN) {
+            float b[8] = {th[i][0].x, th[i][0].y, th[i][0].z, th[i][0].w,
+                          th[i][1].x, th[i][1].y, th[i][1].z, th[i][1].w};
+            if (vi.mode) {
 #pragma unroll
-            for (int j = 0; j < kMaxRank; ++j)
-              if (j < rank) {
-                const float th = __ldg(ep.lora.theta + p0 + j);
-                b[j] = vi.mode ? perturb_value(th, (word >> (sh + j)) & 1u, vi) : th;
-              }
-          }
-          // SWIZZLE_32B K-major: 32-byte rows, 16-byte chunk c of row n at c ^ ((n >> 2) & 1)
-          uint8_t* rowp = bt + n * 32;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint4 w;
-            w.x = pack2<OutT>(b[8 * c + 0], b[8 * c + 1]);
-            w.y = pack2<OutT>(b[8 * c + 2], b[8 * c + 3]);
-            w.z = pack2<OutT>(b[8 * c + 4], b[8 * c + 5]);
-            w.w = pack2<OutT>(b[8 * c + 6], b[8 * c + 7]);
-            *reinterpret_cast<uint4*>(rowp + ((c ^ ((n >> 2) & 1)) << 4)) = w;
+              for (int j = 0; j < 8; ++j)
+                if (j < rank) b[j] = perturb_value(b[j], (mw[i] >> j) & 1u, vi);
+            }
+            // SWIZZLE_32B K-major: 32-byte rows, 16-byte chunk c of row n at c ^ ((n >> 2) & 1);
+            // K columns 8..15 are the zero padding of the rank
+            uint8_t* rowp = bt + n * 32;
+            uint4 w0, w1;
+            w0.x = pack2<OutT>(b[0], b[1]);
+            w0.y = pack2<OutT>(b[2], b[3]);
+            w0.z = pack2<OutT>(b[4], b[5]);
+            w0.w = pack2<OutT>(b[6], b[7]);
+            w1 = make_uint4(0u, 0u, 0u, 0u);
+            const int sw = (n >> 2) & 1;
+            *reinterpret_cast<uint4*>(rowp + ((0 ^ sw) << 4)) = w0;
+            *reinterpret_cast<uint4*>(rowp + ((1 ^ sw) << 4)) = w1;
           }
         }
         fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
@@ -438,6 +459,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       float ce_m = -INFINITY, ce_s = 0.f;
       int tgt = -1;
       if (KIND == EPI_CE && row_ok) tgt = ep.targets[row];
+      const float* rope_cs_row = nullptr;
+      const float* rope_sn_row = nullptr;
+      if (KIND == EPI_QKV_ROPE) {  // token position: seq_len is a multiple of the 128-row tile
+        const int pos = (m0 % ep.seq_len) + row_in_tile;
+        rope_cs_row = ep.rope_cos + (long long)pos * 32;
+        rope_sn_row = ep.rope_sin + (long long)pos * 32;
+      }
 
 #pragma unroll 1
       for (int ch = half; ch < NCHUNK; ch += 2) {
@@ -483,17 +511,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           continue;
         }
         if (KIND == EPI_QKV_ROPE && col < ep.rope_cols) {
-          const int pos = row % ep.seq_len;
-          const int hh = ep.head_dim >> 1;
-          const float* cs_row = ep.rope_cos + (long long)pos * hh;
-          const float* sn_row = ep.rope_sin + (long long)pos * hh;
+          // head_dim 64: the chunk covers frequency indices (col & 63)/2 .. +15 of one head
+          const float4* cs4 = reinterpret_cast<const float4*>(rope_cs_row + ((col & 63) >> 1));
+          const float4* sn4 = reinterpret_cast<const float4*>(rope_sn_row + ((col & 63) >> 1));
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const int i = ((col + c) % ep.head_dim) >> 1;
-            const float cs = __ldg(cs_row + i), sn = __ldg(sn_row + i);
-            const float v0 = v[c], v1 = v[c + 1];
-            v[c] = v0 * cs - v1 * sn;
-            v[c + 1] = v0 * sn + v1 * cs;
+          for (int q = 0; q < 4; ++q) {
+            const float4 c4 = __ldg(cs4 + q), s4 = __ldg(sn4 + q);
+            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = 8 * q + 2 * e;
+              const float v0 = v[c], v1 = v[c + 1];
+              v[c] = v0 * cs[e] - v1 * sn[e];
+              v[c + 1] = v0 * sn[e] + v1 * cs[e];
+            }
           }
         }
         if (KIND == EPI_RESID) {

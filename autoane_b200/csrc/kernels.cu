@@ -58,143 +58,6 @@ int launch_embed(const float* embed, int vocab, int dim, const int32_t* tokens, 
 // ---------------------------------------------------------------------------
 // RMSNorm (perturbed weight) + LoRA-down (perturbed A), one warp per token row
 // ---------------------------------------------------------------------------
-constexpr int kNormRowsPerBlock = 64;
-constexpr int kNormThreads = 256;
-
-template <int NP, typename T, bool NORM>
-__global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a) {
-  extern __shared__ float sm[];
-  float* s_w = sm;                  // [dim]   perturbed rms weight
-  float* s_a = sm + a.dim;          // [n_a * rank][dim] perturbed LoRA A rows
-  using HV = typename H2<T>::V;
-  const int dim = a.dim;
-  const int row0 = blockIdx.x * kNormRowsPerBlock;
-  const int grp = row0 / a.pc.group_rows;
-  const VariantInfo vi = a.pc.variants[a.pc.group_variant[grp]];
-  const uint32_t* mask = a.pc.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.pc.mask_words;
-  const int nrows_a = a.n_a * a.rank;
-
-  // stage perturbed operands: θ (+ s1 z) (+ s2 z), exactly as perturb_buffer adds them;
-  // 4 parameters per load (offsets and widths are multiples of 4, so the four
-  // signs sit in one mask word)
-  auto stage4 = [&](float* dst, long long p) {
-    float4 th = __ldg(reinterpret_cast<const float4*>(a.pc.theta + p));
-    if (vi.mode) {
-      const uint32_t w = __ldg(mask + (p >> 5)) >> (p & 31);
-      th.x = perturb_value(th.x, w & 1u, vi);
-      th.y = perturb_value(th.y, (w >> 1) & 1u, vi);
-      th.z = perturb_value(th.z, (w >> 2) & 1u, vi);
-      th.w = perturb_value(th.w, (w >> 3) & 1u, vi);
-    }
-    *reinterpret_cast<float4*>(dst) = th;
-  };
-  if (NORM)
-    for (int c = 4 * threadIdx.x; c < dim; c += 4 * blockDim.x) stage4(s_w + c, a.w_off + c);
-  for (int i = 4 * threadIdx.x; i < nrows_a * dim; i += 4 * blockDim.x) {
-    const int ja = i / dim, c = i - ja * dim;
-    const int m = ja / a.rank, j = ja - m * a.rank;
-    stage4(s_a + i, a.a_off[m] + (long long)j * dim + c);
-  }
-  __syncthreads();
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kWarps = kNormThreads / 32;
-  for (int r = warp; r < kNormRowsPerBlock; r += kWarps) {
-    const int row = row0 + r;
-    if (row >= a.rows) break;
-    float2 v[NP];
-    if (NORM) {
-      const float2* src = reinterpret_cast<const float2*>(static_cast<const float*>(a.in) + (long long)row * dim);
-#pragma unroll
-      for (int k = 0; k < NP; ++k) v[k] = src[lane + 32 * k];
-      float ss = 0.f;
-#pragma unroll
-      for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
-      ss = warp_sum(ss);
-      const float m = __fmul_rn(ss, 1.0f / (float)dim);
-      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
-      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
-#pragma unroll
-      for (int k = 0; k < NP; ++k) {
-        const int c = 2 * (lane + 32 * k);
-        v[k].x = __fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]);
-        v[k].y = __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]);
-        dst[lane + 32 * k] = H2<T>::from_f2(v[k].x, v[k].y);
-      }
-    } else {
-      const HV* src = reinterpret_cast<const HV*>(static_cast<const T*>(a.in) + (long long)row * dim);
-#pragma unroll
-      for (int k = 0; k < NP; ++k) v[k] = H2<T>::to_f2(src[lane + 32 * k]);
-    }
-    for (int ja = 0; ja < nrows_a; ++ja) {
-      const float2* arow = reinterpret_cast<const float2*>(s_a + (long long)ja * dim);
-      float p = 0.f;
-#pragma unroll
-      for (int k = 0; k < NP; ++k) {
-        const float2 w = arow[lane + 32 * k];
-        p = fmaf(v[k].x, w.x, p);
-        p = fmaf(v[k].y, w.y, p);
-      }
-      p = warp_sum(p);
-      if (lane == 0) {
-        const int m = ja / a.rank, j = ja - m * a.rank;
-        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(p);
-      }
-    }
-  }
-}
-
-template <typename T, bool NORM>
-static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
-  const int np = a.dim / 64;
-  const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);
-  const int blocks = (a.rows + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
-#define B2P_NL_CASE(N)                                                                                   \
-  case N: {                                                                                            \
-    auto k = norm_lora_kernel<N, T, NORM>;                                                             \
-    B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));  \
-    k<<<blocks, kNormThreads, smem, st>>>(a);                                                          \
-    break;                                                                                             \
-  }
-  switch (np) {
-    B2P_NL_CASE(4)
-    B2P_NL_CASE(8)
-    B2P_NL_CASE(12)
-    B2P_NL_CASE(15)
-    B2P_NL_CASE(16)
-    B2P_NL_CASE(20)
-    B2P_NL_CASE(24)
-    B2P_NL_CASE(32)
-    B2P_NL_CASE(40)
-    default:
-      set_error("norm/LoRA-down: unsupported width %d (need dim/64 in {4,8,12,15,16,20,24,32,40})", a.dim);
-      return B2P_ERR_UNSUPPORTED;
-  }
-#undef B2P_NL_CASE
-  B2P_POST_LAUNCH();
-  return B2P_OK;
-}
-
-int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st) {
-  B2P_REQUIRE(a.dim % 64 == 0, "dim %d must be a multiple of 64", a.dim);
-  B2P_REQUIRE(a.n_a >= 0 && a.n_a <= 3 && (a.n_a == 0 || (a.rank > 0 && a.rank <= 16)), "bad LoRA-down count");
-  B2P_REQUIRE(a.u_col % 16 == 0 && a.u_col + 16 * a.n_a <= kUCols, "LoRA-down columns out of range");
-  B2P_REQUIRE(a.w_off % 4 == 0 && a.a_off[0] % 4 == 0 && a.a_off[1] % 4 == 0 && a.a_off[2] % 4 == 0,
-              "parameter offsets must be multiples of 4");
-  B2P_REQUIRE(a.pc.group_rows % kNormRowsPerBlock == 0, "variant groups must be multiples of %d rows",
-              kNormRowsPerBlock);
-  const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);
-  B2P_REQUIRE(smem <= 227 * 1024, "LoRA-down operands (%zu bytes) exceed shared memory", smem);
-  if (a.norm) return bf16 ? launch_norm_lora_t<__nv_bfloat16, true>(a, st) : launch_norm_lora_t<__half, true>(a, st);
-  return bf16 ? launch_norm_lora_t<__nv_bfloat16, false>(a, st) : launch_norm_lora_t<__half, false>(a, st);
-}
-
-// ---------------------------------------------------------------------------
-// causal GQA attention, head_dim 64, 64-query x 64-key tiles, mma.sync m16n8k16
-// ---------------------------------------------------------------------------
-constexpr int kAttnTile = 64;
-constexpr int kHD = 64;
-
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [64][64] 16-bit tile
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
@@ -240,6 +103,377 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   auto v = H2<T>::from_f2(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+
+
+constexpr int kNormRowsPerBlock = 64;
+constexpr int kNormThreads = 256;
+
+// Sum v[k] over the 32 lanes for k < NV (NV a power of two <= 32); on return
+// lane l holds the total of value (l & (NV - 1)) in v[0]. Lanes exchange
+// halves of their vectors (31 shuffles for NV = 32) instead of reducing each
+// value separately.
+template <int NV>
+__device__ __forceinline__ void transpose_reduce(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= NV; off >>= 1)
+#pragma unroll
+    for (int k = 0; k < NV; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+#pragma unroll
+  for (int h = NV / 2; h >= 1; h >>= 1) {
+    const bool up = (lane & h) != 0;
+#pragma unroll
+    for (int k = 0; k < h; ++k) {
+      const float mine = up ? v[k + h] : v[k];
+      const float other = up ? v[k] : v[k + h];
+      v[k] = mine + __shfl_xor_sync(0xffffffffu, other, h);
+    }
+  }
+}
+
+template <int NA>
+struct PadPow2 {
+  static constexpr int v = NA <= 1 ? 1 : NA <= 2 ? 2 : NA <= 4 ? 4 : NA <= 8 ? 8 : NA <= 16 ? 16 : 32;
+};
+
+template <int NP, typename T, bool NORM, int NA>
+__global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a) {
+  extern __shared__ float sm[];
+  float* s_w = sm;                  // [dim]   perturbed rms weight
+  float* s_a = sm + a.dim;          // [NA][dim] perturbed LoRA A rows
+  using HV = typename H2<T>::V;
+  constexpr int dim = NP * 64;
+  const int row0 = blockIdx.x * kNormRowsPerBlock;
+  const int grp = row0 / a.pc.group_rows;
+  const VariantInfo vi = a.pc.variants[a.pc.group_variant[grp]];
+  const uint32_t* mask = a.pc.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.pc.mask_words;
+
+  // stage perturbed operands: θ (+ s1 z) (+ s2 z), exactly as perturb_buffer adds them.
+  // 4 parameters per load (offsets and widths are multiples of 4, so their signs share
+  // a mask word); 8 loads in flight per thread.
+  constexpr int kUnits = (NORM ? dim / 4 : 0) + NA * dim / 4;
+  for (int u0 = threadIdx.x; u0 < kUnits; u0 += 8 * kNormThreads) {
+    float4 th[8];
+    uint32_t mw[8];
+    long long pidx[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int u = u0 + q * kNormThreads;
+      long long p = 0;
+      if (u < kUnits) {
+        if (NORM && u < dim / 4) {
+          p = a.w_off + 4LL * u;
+        } else {
+          const int i = 4 * (u - (NORM ? dim / 4 : 0));
+          const int ja = i / dim, c = i - ja * dim;
+          const int m = ja / a.rank, j = ja - m * a.rank;
+          p = a.a_off[m] + (long long)j * dim + c;
+        }
+        th[q] = __ldg(reinterpret_cast<const float4*>(a.pc.theta + p));
+        mw[q] = vi.mode ? (__ldg(mask + (p >> 5)) >> (p & 31)) : 0u;
+      }
+      pidx[q] = p;
+    }
+    (void)pidx;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int u = u0 + q * kNormThreads;
+      if (u >= kUnits) break;
+      float4 t = th[q];
+      if (vi.mode) {
+        t.x = perturb_value(t.x, mw[q] & 1u, vi);
+        t.y = perturb_value(t.y, (mw[q] >> 1) & 1u, vi);
+        t.z = perturb_value(t.z, (mw[q] >> 2) & 1u, vi);
+        t.w = perturb_value(t.w, (mw[q] >> 3) & 1u, vi);
+      }
+      float* dst = (NORM && u < dim / 4) ? s_w + 4 * u : s_a + 4 * (u - (NORM ? dim / 4 : 0));
+      *reinterpret_cast<float4*>(dst) = t;
+    }
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kNormThreads / 32;
+  for (int r = warp; r < kNormRowsPerBlock; r += kWarps) {
+    const int row = row0 + r;
+    if (row >= a.rows) break;
+    float2 v[NP];
+    if (NORM) {
+      const float2* src = reinterpret_cast<const float2*>(static_cast<const float*>(a.in) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = src[lane + 32 * k];
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
+      ss = warp_sum(ss);
+      const float m = __fmul_rn(ss, 1.0f / (float)dim);
+      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
+      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        const int c = 2 * (lane + 32 * k);
+        v[k].x = __fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]);
+        v[k].y = __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]);
+        dst[lane + 32 * k] = H2<T>::from_f2(v[k].x, v[k].y);
+      }
+    } else {
+      const HV* src = reinterpret_cast<const HV*>(static_cast<const T*>(a.in) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = H2<T>::to_f2(src[lane + 32 * k]);
+    }
+    if (NA > 0) {
+      constexpr int NV = PadPow2<NA>::v;
+      float acc[32];
+#pragma unroll
+      for (int ja = 0; ja < 32; ++ja) acc[ja] = 0.f;
+#pragma unroll
+      for (int ja = 0; ja < NA; ++ja) {
+        const float2* arow = reinterpret_cast<const float2*>(s_a + ja * dim);
+        float p = 0.f;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+          const float2 w = arow[lane + 32 * k];
+          p = fmaf(v[k].x, w.x, p);
+          p = fmaf(v[k].y, w.y, p);
+        }
+        acc[ja] = p;
+      }
+      transpose_reduce<NV>(acc, lane);
+      if (lane < NA) {
+        const int m = lane / a.rank, j = lane - m * a.rank;
+        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(acc[0]);
+      }
+    }
+  }
+}
+
+// RMSNorm (optional) + LoRA-down on the tensor cores: a 64-row tile of the
+// (normalised) input is kept in shared memory as 16-bit, the perturbed A rows
+// of the tile's variant are staged next to it, and U = X · A^T is computed with
+// mma.sync m16n8k16 (fp32 accumulation), then rounded to 16 bit like the U
+// operand of the LoRA-up tensor-core step that consumes it.
+constexpr int kLdRows = 64;
+
+template <int NP, typename T, bool NORM, int NA>
+__global__ void __launch_bounds__(256, 1) norm_lora_mma_kernel(NormLoraArgs a) {
+  constexpr int dim = NP * 64;
+  constexpr int XS = dim + 8;                 // padded row stride (elements): conflict-free ldmatrix
+  constexpr int NT = (NA + 7) / 8;            // 8-column n-tiles of U
+  extern __shared__ __align__(16) uint8_t smx[];
+  float* s_w = reinterpret_cast<float*>(smx);                                 // [dim] fp32
+  T* s_a = reinterpret_cast<T*>(smx + dim * 4);                               // [NT*8][XS]
+  T* s_x = reinterpret_cast<T*>(smx + dim * 4 + NT * 8 * XS * 2);             // [64][XS]
+  using HV = typename H2<T>::V;
+  const int row0 = blockIdx.x * kLdRows;
+  const int grp = row0 / a.pc.group_rows;
+  const VariantInfo vi = a.pc.variants[a.pc.group_variant[grp]];
+  const uint32_t* mask = a.pc.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.pc.mask_words;
+
+  // ---- stage perturbed rms weight (fp32) and A rows (16-bit; rows >= NA zero) ----
+  constexpr int kWU = NORM ? dim / 4 : 0;
+  constexpr int kUnits = kWU + NT * 8 * dim / 4;
+  for (int u0 = threadIdx.x; u0 < kUnits; u0 += 8 * 256) {
+    float4 th[8];
+    uint32_t mw[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int u = u0 + q * 256;
+      th[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      mw[q] = 0u;
+      if (u >= kUnits) continue;
+      long long p;
+      if (u < kWU) {
+        p = a.w_off + 4LL * u;
+      } else {
+        const int i = 4 * (u - kWU);
+        const int ja = i / dim, c = i - ja * dim;
+        if (ja >= NA) continue;
+        const int m = ja / a.rank, j = ja - m * a.rank;
+        p = a.a_off[m] + (long long)j * dim + c;
+      }
+      th[q] = __ldg(reinterpret_cast<const float4*>(a.pc.theta + p));
+      mw[q] = vi.mode ? (__ldg(mask + (p >> 5)) >> (p & 31)) : 0u;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int u = u0 + q * 256;
+      if (u >= kUnits) break;
+      float4 t = th[q];
+      if (vi.mode) {
+        t.x = perturb_value(t.x, mw[q] & 1u, vi);
+        t.y = perturb_value(t.y, (mw[q] >> 1) & 1u, vi);
+        t.z = perturb_value(t.z, (mw[q] >> 2) & 1u, vi);
+        t.w = perturb_value(t.w, (mw[q] >> 3) & 1u, vi);
+      }
+      if (u < kWU) {
+        *reinterpret_cast<float4*>(s_w + 4 * u) = t;
+      } else {
+        const int i = 4 * (u - kWU);
+        const int ja = i / dim, c = i - ja * dim;
+        HV* d = reinterpret_cast<HV*>(s_a + ja * XS + c);
+        d[0] = H2<T>::from_f2(t.x, t.y);
+        d[1] = H2<T>::from_f2(t.z, t.w);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- 64-row input tile: RMSNorm to HBM + smem, or a copy of the 16-bit rows ----
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (NORM) {
+    // each warp normalises rows warp, warp+8, ...; the next row's loads are in
+    // flight while the current row is reduced and written
+    float2 cur[NP], nxt[NP];
+    auto load_row = [&](float2 (&v)[NP], int r) {
+      const int row = row0 + r;
+      if (row < a.rows) {
+        const float2* src = reinterpret_cast<const float2*>(static_cast<const float*>(a.in) + (long long)row * dim);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) v[k] = src[lane + 32 * k];
+      } else {
+#pragma unroll
+        for (int k = 0; k < NP; ++k) v[k] = make_float2(0.f, 0.f);
+      }
+    };
+    load_row(cur, warp);
+#pragma unroll 1
+    for (int r = warp; r < kLdRows; r += 8) {
+      if (r + 8 < kLdRows) load_row(nxt, r + 8);
+      const int row = row0 + r;
+      HV* sx = reinterpret_cast<HV*>(s_x + r * XS);
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < NP; ++k) ss += cur[k].x * cur[k].x + cur[k].y * cur[k].y;
+      ss = warp_sum(ss);
+      const float m = __fmul_rn(ss, 1.0f / (float)dim);
+      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
+      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        const int c = 2 * (lane + 32 * k);
+        const HV h = H2<T>::from_f2(__fmul_rn(__fmul_rn(cur[k].x, rstd), s_w[c]),
+                                    __fmul_rn(__fmul_rn(cur[k].y, rstd), s_w[c + 1]));
+        if (row < a.rows) dst[lane + 32 * k] = h;
+        sx[lane + 32 * k] = h;
+      }
+#pragma unroll
+      for (int k = 0; k < NP; ++k) cur[k] = nxt[k];
+    }
+  } else {
+    // whole tile in flight at once: 16-byte cp.async per (row, chunk)
+    const uint32_t sxb0 = smem_u32(s_x);
+    for (int i = threadIdx.x; i < kLdRows * (dim / 8); i += 256) {
+      const int r = i / (dim / 8), c8 = i - r * (dim / 8);
+      const int row = row0 + r;
+      const uint32_t dsts = sxb0 + (uint32_t)((r * XS + c8 * 8) * 2);
+      if (row < a.rows) {
+        cp_async16(dsts, static_cast<const T*>(a.in) + (long long)row * dim + c8 * 8);
+      } else {
+        *reinterpret_cast<uint4*>(s_x + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+  }
+  __syncthreads();
+
+  // ---- U[64 x 8NT] = X[64 x dim] · A[8NT x dim]^T  (mma.sync m16n8k16) ----
+  const int mt = warp & 3;
+  const int lm = lane >> 3, lr = lane & 7;
+  const uint32_t sxb = smem_u32(s_x), sab = smem_u32(s_a);
+  for (int nt = warp >> 2; nt < NT; nt += 2) {
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int kk = 0; kk < dim / 16; ++kk) {
+      uint32_t af[4], b0, b1, b2, b3;
+      ldsm_x4(sxb + (uint32_t)(((mt * 16 + (lm & 1) * 8 + lr) * XS + kk * 16 + (lm >> 1) * 8) * 2), af[0], af[1],
+              af[2], af[3]);
+      // x4 over the 8 A rows of the n-tile: k 0-7, k 8-15 (b0, b1); the second pair repeats them
+      ldsm_x4(sab + (uint32_t)(((nt * 8 + lr) * XS + kk * 16 + (lm & 1) * 8) * 2), b0, b1, b2, b3);
+      mma16816<T>(c, af, b0, b1);
+    }
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int rr = mt * 16 + g + ((e >> 1) << 3);
+      const int n = nt * 8 + 2 * t + (e & 1);
+      const int row = row0 + rr;
+      if (n < NA && row < a.rows) {
+        const int m = n / a.rank, j = n - m * a.rank;
+        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(c[e]);
+      }
+    }
+  }
+}
+
+template <int NP, typename T, bool NORM, int NA>
+static int launch_nl_mma(const NormLoraArgs& a, cudaStream_t st) {
+  constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8;
+  const size_t smem = (size_t)dim * 4 + (size_t)NT * 8 * XS * 2 + (size_t)kLdRows * XS * 2;
+  auto k = norm_lora_mma_kernel<NP, T, NORM, NA>;
+  B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<(a.rows + kLdRows - 1) / kLdRows, 256, smem, st>>>(a);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
+template <int NP, typename T, bool NORM, int NA>
+static int launch_nl(const NormLoraArgs& a, size_t smem, int blocks, cudaStream_t st) {
+  auto k = norm_lora_kernel<NP, T, NORM, NA>;
+  B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<blocks, kNormThreads, smem, st>>>(a);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
+template <int NP, typename T, bool NORM>
+static int launch_nl_na(const NormLoraArgs& a, size_t smem, int blocks, cudaStream_t st) {
+  switch (a.n_a * a.rank) {
+    case 0: return launch_nl<NP, T, NORM, 0>(a, smem, blocks, st);
+    case 4: return launch_nl_mma<NP, T, NORM, 4>(a, st);
+    case 8: return launch_nl_mma<NP, T, NORM, 8>(a, st);
+    case 12: return launch_nl_mma<NP, T, NORM, 12>(a, st);
+    case 24: return launch_nl_mma<NP, T, NORM, 24>(a, st);
+    default:
+      set_error("norm/LoRA-down: unsupported LoRA-down row count %d", a.n_a * a.rank);
+      return B2P_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename T, bool NORM>
+static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
+  const int np = a.dim / 64;
+  const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);
+  const int blocks = (a.rows + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
+  switch (np) {
+    case 8: return launch_nl_na<8, T, NORM>(a, smem, blocks, st);
+    case 15: return launch_nl_na<15, T, NORM>(a, smem, blocks, st);
+    case 16: return launch_nl_na<16, T, NORM>(a, smem, blocks, st);
+    case 32: return launch_nl_na<32, T, NORM>(a, smem, blocks, st);
+    default:
+      set_error("norm/LoRA-down: unsupported width %d (need dim in {512, 960, 1024, 2048})", a.dim);
+      return B2P_ERR_UNSUPPORTED;
+  }
+}
+
+int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(a.dim % 64 == 0, "dim %d must be a multiple of 64", a.dim);
+  B2P_REQUIRE(a.n_a >= 0 && a.n_a <= 3 && (a.n_a == 0 || (a.rank > 0 && a.rank <= 16)), "bad LoRA-down count");
+  B2P_REQUIRE(a.u_col % 16 == 0 && a.u_col + 16 * a.n_a <= kUCols, "LoRA-down columns out of range");
+  B2P_REQUIRE(a.w_off % 4 == 0 && a.a_off[0] % 4 == 0 && a.a_off[1] % 4 == 0 && a.a_off[2] % 4 == 0,
+              "parameter offsets must be multiples of 4");
+  B2P_REQUIRE(a.pc.group_rows % kNormRowsPerBlock == 0, "variant groups must be multiples of %d rows",
+              kNormRowsPerBlock);
+  const size_t smem = sizeof(float) * ((size_t)a.dim + (size_t)a.n_a * a.rank * a.dim);
+  B2P_REQUIRE(smem <= 227 * 1024, "LoRA-down operands (%zu bytes) exceed shared memory", smem);
+  if (a.norm) return bf16 ? launch_norm_lora_t<__nv_bfloat16, true>(a, st) : launch_norm_lora_t<__half, true>(a, st);
+  return bf16 ? launch_norm_lora_t<__nv_bfloat16, false>(a, st) : launch_norm_lora_t<__half, false>(a, st);
+}
+
+// ---------------------------------------------------------------------------
+// causal GQA attention, head_dim 64, 64-query x 64-key tiles, mma.sync m16n8k16
+// ---------------------------------------------------------------------------
+constexpr int kAttnTile = 64;
+constexpr int kHD = 64;
 
 // Loads a [64 rows][64 cols] 16-bit tile (row pitch ld elements) into swizzled smem.
 template <typename T>

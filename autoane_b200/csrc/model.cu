@@ -6,6 +6,7 @@
 // One forward evaluates G = n_var * n_seq groups of `seq` token rows at once
 // (group g = v * n_seq + q evaluates sequence q under variant v), so the base
 // projection weights are read once per layer for all ±ε evaluations.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -45,8 +46,9 @@ struct b2p_model {
   long long mask_words = 0;
   SignBuffer* d_bufs = nullptr;
   int nbufs = 0;
-  uint64_t* d_jumps = nullptr;
-  int njump = 0;
+  uint64_t* d_polys = nullptr;
+  long long nchunks = 0;
+  std::vector<uint64_t> slot_seed;  // seeds whose masks the slots currently hold (in slot order)
   long long total_draws = 0;
   uint64_t* d_seeds = nullptr;
   // activations
@@ -64,6 +66,7 @@ struct b2p_model {
   float* var_loss = nullptr;
   float* pairs = nullptr;        // [2 * kMaxPerturbOps] loss pairs for updates
   int qkv_bn = 160;
+  int cur_groups = 0, cur_vars = 0;  // group/variant table sizes of the forward being issued
   int32_t* d_tok = nullptr;      // [max_seq_in][seq] tokens then targets
   int32_t* d_row_tgt = nullptr;  // [max_rows]
   int* d_meta = nullptr;         // group_seq[max_groups] | group_var[max_groups]
@@ -148,7 +151,7 @@ int model_alloc(b2p_model* m) {
 
 void model_release(b2p_model* m) {
   void* dev[] = {m->wqkv, m->wo, m->w13, m->w2, m->cembed, m->embed, m->theta, m->masks, m->d_bufs,
-                 m->d_jumps, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
+                 m->d_polys, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
                  m->ce_tgt, m->row_loss, m->group_loss, m->var_loss, m->pairs, m->d_tok, m->d_row_tgt, m->d_meta,
                  m->d_var, m->rope_cos, m->rope_sin};
   for (void* p : dev)
@@ -193,6 +196,8 @@ LoraEpi lora_epi(const b2p_model* m) {
   le.variants = m->d_var;
   le.group_variant = m->d_meta + m->max_groups;
   le.group_rows = m->cfg.seq;
+  le.n_groups = m->cur_groups;
+  le.n_variants = m->cur_vars;
   le.rank = m->cfg.rank;
   return le;
 }
@@ -428,6 +433,8 @@ int stage_groups(b2p_model* m, int n_seq, const std::vector<VariantInfo>& vars, 
       meta[v * n_seq + q] = q;                  // group -> sequence
       meta[m->max_groups + v * n_seq + q] = v;  // group -> variant
     }
+  m->cur_groups = G;
+  m->cur_vars = n_var;
   int rc = stage_copy(m, m->d_meta, meta.data(), meta.size() * sizeof(int));
   if (rc) return rc;
   if ((rc = stage_copy(m, m->d_var, vars.data(), vars.size() * sizeof(VariantInfo)))) return rc;
@@ -441,10 +448,15 @@ int stage_groups(b2p_model* m, int n_seq, const std::vector<VariantInfo>& vars, 
 
 int gen_masks(b2p_model* m, const uint64_t* seeds, int n) {
   B2P_REQUIRE(n >= 1 && n <= m->max_slots, "seed count %d exceeds mask slots %d", n, m->max_slots);
+  // the slots already hold these seeds' masks (e.g. the update after the evaluation of the same seeds)
+  if ((int)m->slot_seed.size() >= n && std::equal(seeds, seeds + n, m->slot_seed.begin())) return B2P_OK;
   int rc = stage_copy(m, m->d_seeds, seeds, (size_t)n * 8);
   if (rc) return rc;
-  return launch_sign_masks(m->d_bufs, m->nbufs, m->d_jumps, m->njump, m->total_draws, m->mask_words, m->d_seeds, n,
-                           m->masks, m->st);
+  m->slot_seed.assign(seeds, seeds + n);
+  rc = launch_sign_masks(m->d_bufs, m->nbufs, m->d_polys, m->nchunks, m->total_draws, m->mask_words, m->d_seeds, n,
+                         m->masks, m->st);
+  if (rc) m->slot_seed.clear();
+  return rc;
 }
 
 int ready(const b2p_model* m) {
@@ -528,7 +540,7 @@ b2p_model* b2p_model_create(const b2p_model_config* cfg) {
     return bad("unsupported shape: need dim %% 64 == 0, hidden %% 128 == 0, head_dim 64, seq %% 128 == 0");
   if (c.rank != 4 && c.rank != 8) return bad("LoRA rank must be 4 or 8");
   if (c.dtype != B2P_F16 && c.dtype != B2P_BF16) return bad("dtype must be B2P_F16 or B2P_BF16");
-  if (c.max_groups < 1) return bad("max_groups must be >= 1");
+  if (c.max_groups < 1 || c.max_groups > 256) return bad("max_groups must be in [1, 256]");
   const int qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
   if (qd % 128 && qd % 160) return bad("q_dim must be a multiple of 128 or 160");
   const int qkv_bn = (qd % 160 == 0 && kvd % 160 == 0) ? 160 : ((qd % 128 == 0 && kvd % 128 == 0) ? 128 : 0);
@@ -577,13 +589,16 @@ b2p_model* b2p_model_create(const b2p_model_config* cfg) {
     sizes.push_back(D);
     SignPlan plan = make_sign_plan(sizes);
     m->nbufs = (int)plan.bufs.size();
-    m->njump = plan.njump;
+    m->nchunks = plan.nchunks;
     m->total_draws = plan.total_draws;
-    if (cudaMalloc(&m->d_bufs, plan.bufs.size() * sizeof(SignBuffer)) != cudaSuccess ||
-        cudaMalloc(&m->d_jumps, plan.jumps.size() * 8) != cudaSuccess ||
+    if (!plan.valid) {
+      set_error("xoshiro jump polynomial could not be established (Berlekamp-Massey / stepping check failed)");
+      rc = B2P_ERR_STATE;
+    } else if (cudaMalloc(&m->d_bufs, plan.bufs.size() * sizeof(SignBuffer)) != cudaSuccess ||
+        cudaMalloc(&m->d_polys, plan.polys.size() * 8) != cudaSuccess ||
         cudaMemcpy(m->d_bufs, plan.bufs.data(), plan.bufs.size() * sizeof(SignBuffer), cudaMemcpyHostToDevice) !=
             cudaSuccess ||
-        cudaMemcpy(m->d_jumps, plan.jumps.data(), plan.jumps.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpy(m->d_polys, plan.polys.data(), plan.polys.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess) {
       set_error("sign-plan upload failed");
       rc = B2P_ERR_CUDA;
     }

@@ -30,34 +30,68 @@ uint64_t host_xo_next(uint64_t s[4]) {
 }
 
 namespace {
-using Mat = std::vector<uint64_t>;  // 256 rows x 4 words; row i = coefficients of output bit i
+// Polynomials over GF(2) of degree < 256: bit i of word i/64 = coefficient of x^i.
+struct Poly {
+  uint64_t w[4] = {0, 0, 0, 0};
+  bool bit(int i) const { return (w[i >> 6] >> (i & 63)) & 1u; }
+};
 
-inline bool bit_of(const uint64_t* v, int j) { return (v[j >> 6] >> (j & 63)) & 1u; }
-
-// C = A * B over GF(2) (apply B first, then A).
-Mat matmul(const Mat& A, const Mat& B) {
-  Mat C(256 * 4, 0);
-  for (int i = 0; i < 256; ++i) {
-    uint64_t r[4] = {0, 0, 0, 0};
-    for (int j = 0; j < 256; ++j)
-      if (bit_of(&A[i * 4], j))
-        for (int w = 0; w < 4; ++w) r[w] ^= B[j * 4 + w];
-    for (int w = 0; w < 4; ++w) C[i * 4 + w] = r[w];
+// Berlekamp-Massey over GF(2): connection polynomial c (c[0] = 1) of the
+// shortest LFSR generating s, i.e. s[i] = sum_{j=1..L} c[j] s[i-j].
+std::vector<uint8_t> berlekamp_massey(const std::vector<uint8_t>& s) {
+  const int n = (int)s.size();
+  std::vector<uint8_t> C(n + 1, 0), B(n + 1, 0), T;
+  C[0] = B[0] = 1;
+  int L = 0, m = 1;
+  for (int i = 0; i < n; ++i) {
+    uint8_t d = s[i];
+    for (int j = 1; j <= L; ++j) d ^= (uint8_t)(C[j] & s[i - j]);
+    if (!d) {
+      ++m;
+    } else if (2 * L <= i) {
+      T = C;
+      for (int j = 0; j + m <= n; ++j) C[j + m] ^= B[j];
+      L = i + 1 - L;
+      B = T;
+      m = 1;
+    } else {
+      for (int j = 0; j + m <= n; ++j) C[j + m] ^= B[j];
+      ++m;
+    }
   }
+  C.resize(L + 1);
   return C;
 }
 
-// Transition matrix of one xoshiro256 step (state bit b = word b/64, bit b%64).
-Mat transition() {
-  Mat T(256 * 4, 0);
-  for (int j = 0; j < 256; ++j) {
-    uint64_t s[4] = {0, 0, 0, 0};
-    s[j >> 6] = 1ull << (j & 63);
-    host_xo_next(s);
-    for (int i = 0; i < 256; ++i)
-      if (bit_of(s, i)) T[i * 4 + (j >> 6)] |= 1ull << (j & 63);
+// a·x mod P, where P = x^256 + low
+inline void mulx(Poly& a, const Poly& low) {
+  const bool carry = a.bit(255);
+  for (int k = 3; k > 0; --k) a.w[k] = (a.w[k] << 1) | (a.w[k - 1] >> 63);
+  a.w[0] <<= 1;
+  if (carry)
+    for (int k = 0; k < 4; ++k) a.w[k] ^= low.w[k];
+}
+
+// a·b mod P (Horner over the bits of b)
+Poly mulmod(const Poly& a, const Poly& b, const Poly& low) {
+  Poly r;
+  for (int i = 255; i >= 0; --i) {
+    mulx(r, low);
+    if (b.bit(i))
+      for (int k = 0; k < 4; ++k) r.w[k] ^= a.w[k];
   }
-  return T;
+  return r;
+}
+
+// T^n s0 = p_n(T) s0
+void host_jump(const Poly& p, uint64_t s[4]) {
+  uint64_t acc[4] = {0, 0, 0, 0};
+  for (int i = 0; i < 256; ++i) {
+    if (p.bit(i))
+      for (int k = 0; k < 4; ++k) acc[k] ^= s[k];
+    host_xo_next(s);
+  }
+  for (int k = 0; k < 4; ++k) s[k] = acc[k];
 }
 }  // namespace
 
@@ -71,45 +105,70 @@ SignPlan make_sign_plan(const std::vector<long long>& sizes) {
   }
   p.total_params = pp;
   p.total_draws = dd;
-  const long long nchunks = (dd + kChunkDraws - 1) / kChunkDraws;
-  int nj = 1;
-  while ((1ll << nj) < nchunks) ++nj;
-  p.njump = nj;
-  Mat J = transition();
-  for (int k = 0; (1 << k) < kChunkDraws; ++k) J = matmul(J, J);  // T^kChunkDraws
-  p.jumps.reserve((size_t)nj * 1024);
-  for (int k = 0; k < nj; ++k) {
-    p.jumps.insert(p.jumps.end(), J.begin(), J.end());
-    J = matmul(J, J);
+  p.nchunks = (dd + kChunkDraws - 1) / kChunkDraws;
+  if (p.nchunks == 0) p.nchunks = 1;
+
+  // characteristic polynomial from 512 output bits of a nonzero state
+  uint64_t s[4];
+  host_xo_seed(s, 0x5DEECE66DULL);
+  std::vector<uint8_t> bits(512);
+  for (int i = 0; i < 512; ++i) {
+    bits[i] = (uint8_t)(s[0] & 1u);
+    host_xo_next(s);
   }
+  const std::vector<uint8_t> C = berlekamp_massey(bits);
+  const int L = (int)C.size() - 1;
+  if (L != 256) return p;  // valid stays false
+  // P(x) = x^256 + sum_{j=1..256} c_j x^(256-j): low part holds the c_j
+  Poly low;
+  for (int j = 1; j <= 256; ++j)
+    if (C[j]) low.w[(256 - j) >> 6] |= 1ull << ((256 - j) & 63);
+
+  Poly xc;  // x^kChunkDraws mod P
+  xc.w[0] = 1;
+  for (int i = 0; i < kChunkDraws; ++i) mulx(xc, low);
+  p.polys.resize((size_t)p.nchunks * 4);
+  Poly cur;
+  cur.w[0] = 1;  // x^0
+  for (long long c = 0; c < p.nchunks; ++c) {
+    for (int k = 0; k < 4; ++k) p.polys[(size_t)c * 4 + k] = cur.w[k];
+    cur = mulmod(cur, xc, low);
+  }
+  // check the jump against sequential stepping at a few chunk starts
+  const long long checks[4] = {1, 3, p.nchunks / 2, p.nchunks - 1};
+  for (long long c : checks) {
+    if (c <= 0 || c >= p.nchunks) continue;
+    uint64_t a[4], b[4];
+    host_xo_seed(a, 42 + (uint64_t)c);
+    for (int k = 0; k < 4; ++k) b[k] = a[k];
+    Poly pc;
+    for (int k = 0; k < 4; ++k) pc.w[k] = p.polys[(size_t)c * 4 + k];
+    host_jump(pc, a);
+    for (long long i = 0; i < c * kChunkDraws; ++i) host_xo_next(b);
+    for (int k = 0; k < 4; ++k)
+      if (a[k] != b[k]) return p;  // valid stays false
+  }
+  p.valid = true;
   return p;
 }
 
 __device__ __forceinline__ uint64_t dev_rotl(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
 
-__device__ __forceinline__ void apply_jump(uint64_t s[4], const uint64_t* __restrict__ M) {
-  uint64_t o[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    uint64_t acc = 0;
-#pragma unroll 8
-    for (int b = 0; b < 64; ++b) {
-      const ulonglong2 r01 = __ldg(reinterpret_cast<const ulonglong2*>(M + (w * 64 + b) * 4));
-      const ulonglong2 r23 = __ldg(reinterpret_cast<const ulonglong2*>(M + (w * 64 + b) * 4 + 2));
-      const int par = __popcll(r01.x & s[0]) ^ __popcll(r01.y & s[1]) ^ __popcll(r23.x & s[2]) ^
-                      __popcll(r23.y & s[3]);
-      acc |= (uint64_t)(par & 1) << b;
-    }
-    o[w] = acc;
-  }
-#pragma unroll
-  for (int w = 0; w < 4; ++w) s[w] = o[w];
+__device__ __forceinline__ void dev_step(uint64_t s[4]) {
+  const uint64_t t = s[1] << 17;
+  s[2] ^= s[0];
+  s[3] ^= s[1];
+  s[1] ^= s[2];
+  s[0] ^= s[3];
+  s[2] ^= t;
+  s[3] = dev_rotl(s[3], 45);
 }
 
-__global__ void sign_mask_kernel(const SignBuffer* __restrict__ bufs, int nbufs, const uint64_t* __restrict__ jumps,
-                                 int njump, long long total_draws, long long mask_words,
+__global__ void sign_mask_kernel(const SignBuffer* __restrict__ bufs, int nbufs, const uint64_t* __restrict__ polys,
+                                 long long nchunks, long long total_draws, long long mask_words,
                                  const uint64_t* __restrict__ seeds, uint32_t* __restrict__ masks) {
   const long long chunk = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (chunk >= nchunks) return;
   const long long d_begin = chunk * kChunkDraws;
   if (d_begin >= total_draws) return;
   uint32_t* mask = masks + (long long)blockIdx.y * mask_words;
@@ -124,8 +183,25 @@ __global__ void sign_mask_kernel(const SignBuffer* __restrict__ bufs, int nbufs,
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
     s[i] = z ^ (z >> 31);
   }
-  for (int k = 0; k < njump; ++k)
-    if ((chunk >> k) & 1) apply_jump(s, jumps + (size_t)k * 1024);
+  if (chunk > 0) {  // s <- T^(chunk * kChunkDraws) s = sum_i p_i T^i s
+    uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll 1
+    for (int w = 0; w < 4; ++w) {
+      uint64_t pw = __ldg(polys + chunk * 4 + w);
+#pragma unroll 4
+      for (int b = 0; b < 64; ++b) {
+        const uint64_t sel = 0ull - (pw & 1ull);
+        acc[0] ^= s[0] & sel;
+        acc[1] ^= s[1] & sel;
+        acc[2] ^= s[2] & sel;
+        acc[3] ^= s[3] & sel;
+        pw >>= 1;
+        dev_step(s);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s[k] = acc[k];
+  }
 
   // first buffer whose draw range contains d_begin (largest d0 <= d_begin)
   int lo = 0, hi = nbufs - 1;
@@ -140,15 +216,7 @@ __global__ void sign_mask_kernel(const SignBuffer* __restrict__ bufs, int nbufs,
   for (long long d = d_begin; d < d_end; ++d) {
     while (b < nbufs - 1 && d >= bufs[b].d0 + bufs[b].n / 4 + bufs[b].n % 4) ++b;
     const uint64_t r = s[0] + s[3];
-    {
-      const uint64_t t = s[1] << 17;
-      s[2] ^= s[0];
-      s[3] ^= s[1];
-      s[1] ^= s[2];
-      s[0] ^= s[3];
-      s[2] ^= t;
-      s[3] = dev_rotl(s[3], 45);
-    }
+    dev_step(s);
     const long long local = d - bufs[b].d0;
     const long long full = bufs[b].n / 4;
     long long p;
@@ -177,16 +245,15 @@ __global__ void sign_mask_kernel(const SignBuffer* __restrict__ bufs, int nbufs,
   if (cur_word >= 0 && acc) atomicOr(mask + cur_word, acc);
 }
 
-int launch_sign_masks(const SignBuffer* d_bufs, int nbufs, const uint64_t* d_jumps, int njump,
+int launch_sign_masks(const SignBuffer* d_bufs, int nbufs, const uint64_t* d_polys, long long nchunks,
                       long long total_draws, long long mask_words, const uint64_t* d_seeds, int nseeds,
                       uint32_t* d_masks, void* stv) {
   cudaStream_t st = static_cast<cudaStream_t>(stv);
   B2P_REQUIRE(nseeds > 0 && nseeds <= 65535, "seed count %d out of range", nseeds);
   B2P_CHECK_CUDA(cudaMemsetAsync(d_masks, 0, (size_t)nseeds * mask_words * 4, st));
-  const long long nchunks = (total_draws + kChunkDraws - 1) / kChunkDraws;
-  const int threads = 64;
+  const int threads = 128;
   dim3 grid((unsigned)((nchunks + threads - 1) / threads), (unsigned)nseeds);
-  sign_mask_kernel<<<grid, threads, 0, st>>>(d_bufs, nbufs, d_jumps, njump, total_draws, mask_words, d_seeds,
+  sign_mask_kernel<<<grid, threads, 0, st>>>(d_bufs, nbufs, d_polys, nchunks, total_draws, mask_words, d_seeds,
                                              d_masks);
   B2P_POST_LAUNCH();
   return B2P_OK;
