@@ -1,0 +1,51 @@
+"""The C ABI on the host (no GPU work): libb2p.so loads, exports every function
+include/b2p.h declares, and the Python binding covers exactly that set."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from autoane_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "b2p.h"
+
+
+def declared():
+    src = HEADER.read_text()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return set(re.findall(r"\b(b2p_\w+)\s*\(", src))
+
+
+def test_library_exports_every_declared_function():
+    lib = _lib.load()
+    names = declared()
+    assert len(names) >= 20
+    missing = [n for n in sorted(names) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_matches_header():
+    assert set(_lib.ABI) == declared()
+
+
+def test_version_and_error_strings():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.b2p_version()
+    assert isinstance(lib.b2p_last_error(), bytes)
+
+
+def test_struct_layouts_match_header():
+    # b2p_model_config: 9 ints, 2 floats, 2 ints; b2p_variant: u64, int, 2 floats
+    assert C.sizeof(_lib.ModelConfig) == 13 * 4
+    assert C.sizeof(_lib.Variant) == 24
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    saved = _lib._lib
+    try:
+        _lib._lib = None
+        with pytest.raises(RuntimeError, match="no fallback"):
+            _lib.load(tmp_path / "absent.so")
+    finally:
+        _lib._lib = saved
