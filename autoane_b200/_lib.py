@@ -53,6 +53,7 @@ ABI: dict[str, tuple] = {
     "b2p_model_profile": (i32, [vp, i32]),
     "b2p_model_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),
     "b2p_launch_count": (i64, []),
+    "b2p_sign_masks_noalloc": (i32, [C.POINTER(C.c_int64), i32, u64p, i32, vp, vp]),
 }
 
 

@@ -95,6 +95,50 @@ void host_jump(const Poly& p, uint64_t s[4]) {
 }
 }  // namespace
 
+bool jump_polys(long long nchunks, std::vector<uint64_t>& polys) {
+  // characteristic polynomial from 512 output bits of a nonzero state
+  uint64_t s[4];
+  host_xo_seed(s, 0x5DEECE66DULL);
+  std::vector<uint8_t> bits(512);
+  for (int i = 0; i < 512; ++i) {
+    bits[i] = (uint8_t)(s[0] & 1u);
+    host_xo_next(s);
+  }
+  const std::vector<uint8_t> C = berlekamp_massey(bits);
+  const int L = (int)C.size() - 1;
+  if (L != 256) return false;
+  // P(x) = x^256 + sum_{j=1..256} c_j x^(256-j): low part holds the c_j
+  Poly low;
+  for (int j = 1; j <= 256; ++j)
+    if (C[j]) low.w[(256 - j) >> 6] |= 1ull << ((256 - j) & 63);
+
+  Poly xc;  // x^kChunkDraws mod P
+  xc.w[0] = 1;
+  for (int i = 0; i < kChunkDraws; ++i) mulx(xc, low);
+  polys.assign((size_t)nchunks * 4, 0);
+  Poly cur;
+  cur.w[0] = 1;  // x^0
+  for (long long c = 0; c < nchunks; ++c) {
+    for (int k = 0; k < 4; ++k) polys[(size_t)c * 4 + k] = cur.w[k];
+    cur = mulmod(cur, xc, low);
+  }
+  // check the jump against sequential stepping at a few chunk starts
+  const long long checks[4] = {1, 3, nchunks / 2, nchunks - 1};
+  for (long long c : checks) {
+    if (c <= 0 || c >= nchunks) continue;
+    uint64_t a[4], b[4];
+    host_xo_seed(a, 42 + (uint64_t)c);
+    for (int k = 0; k < 4; ++k) b[k] = a[k];
+    Poly pc;
+    for (int k = 0; k < 4; ++k) pc.w[k] = polys[(size_t)c * 4 + k];
+    host_jump(pc, a);
+    for (long long i = 0; i < c * kChunkDraws; ++i) host_xo_next(b);
+    for (int k = 0; k < 4; ++k)
+      if (a[k] != b[k]) return false;
+  }
+  return true;
+}
+
 SignPlan make_sign_plan(const std::vector<long long>& sizes) {
   SignPlan p;
   long long pp = 0, dd = 0;
@@ -108,47 +152,7 @@ SignPlan make_sign_plan(const std::vector<long long>& sizes) {
   p.nchunks = (dd + kChunkDraws - 1) / kChunkDraws;
   if (p.nchunks == 0) p.nchunks = 1;
 
-  // characteristic polynomial from 512 output bits of a nonzero state
-  uint64_t s[4];
-  host_xo_seed(s, 0x5DEECE66DULL);
-  std::vector<uint8_t> bits(512);
-  for (int i = 0; i < 512; ++i) {
-    bits[i] = (uint8_t)(s[0] & 1u);
-    host_xo_next(s);
-  }
-  const std::vector<uint8_t> C = berlekamp_massey(bits);
-  const int L = (int)C.size() - 1;
-  if (L != 256) return p;  // valid stays false
-  // P(x) = x^256 + sum_{j=1..256} c_j x^(256-j): low part holds the c_j
-  Poly low;
-  for (int j = 1; j <= 256; ++j)
-    if (C[j]) low.w[(256 - j) >> 6] |= 1ull << ((256 - j) & 63);
-
-  Poly xc;  // x^kChunkDraws mod P
-  xc.w[0] = 1;
-  for (int i = 0; i < kChunkDraws; ++i) mulx(xc, low);
-  p.polys.resize((size_t)p.nchunks * 4);
-  Poly cur;
-  cur.w[0] = 1;  // x^0
-  for (long long c = 0; c < p.nchunks; ++c) {
-    for (int k = 0; k < 4; ++k) p.polys[(size_t)c * 4 + k] = cur.w[k];
-    cur = mulmod(cur, xc, low);
-  }
-  // check the jump against sequential stepping at a few chunk starts
-  const long long checks[4] = {1, 3, p.nchunks / 2, p.nchunks - 1};
-  for (long long c : checks) {
-    if (c <= 0 || c >= p.nchunks) continue;
-    uint64_t a[4], b[4];
-    host_xo_seed(a, 42 + (uint64_t)c);
-    for (int k = 0; k < 4; ++k) b[k] = a[k];
-    Poly pc;
-    for (int k = 0; k < 4; ++k) pc.w[k] = p.polys[(size_t)c * 4 + k];
-    host_jump(pc, a);
-    for (long long i = 0; i < c * kChunkDraws; ++i) host_xo_next(b);
-    for (int k = 0; k < 4; ++k)
-      if (a[k] != b[k]) return p;  // valid stays false
-  }
-  p.valid = true;
+  p.valid = jump_polys(p.nchunks, p.polys);
   return p;
 }
 

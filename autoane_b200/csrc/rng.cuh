@@ -44,6 +44,10 @@ struct SignPlan {
 // the per-chunk jump polynomials covering its draw count.
 SignPlan make_sign_plan(const std::vector<long long>& sizes);
 
+// Jump polynomials x^(c*kChunkDraws) mod P for chunks c < nchunks ([nchunks][4]
+// words); false if P could not be recovered or the jump disagrees with stepping.
+bool jump_polys(long long nchunks, std::vector<uint64_t>& polys);
+
 // Host xoshiro256+ (for tests of the plan itself).
 void host_xo_seed(uint64_t s[4], uint64_t seed);
 uint64_t host_xo_next(uint64_t s[4]);

@@ -156,6 +156,23 @@ int b2p_model_perturb(b2p_model* m, const uint64_t* seeds, const float* scales, 
  * parameter 32w+b for seeds[i] (1 = +). ceil(P/32) words per seed. */
 int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_words);
 
+/* Allocation-free form of b2p_sign_masks, for callers that cannot allocate device
+ * memory (all device memory owned by another allocator, or a fixed budget).
+ * No counterpart in the reference (it draws signs on the host).
+ * Writes the sign masks of the perturbation stream over an arbitrary buffer
+ * layout into out_words, caller-owned device memory [nseeds][ceil(P/32)]
+ * (P = sum of buffer_sizes). Bit b of word w is the sign of parameter 32w+b
+ * (1 = +), drawn as perturb_buffer draws it (training/train_mezo.m:122-136).
+ * Host inputs: buffer_sizes[nbufs], seeds[nseeds]. Limits: nbufs <= 1024,
+ * nseeds <= 64, at most 524,288 draws per seed; larger inputs are rejected with
+ * B2P_ERR_ARG. Scratch is a fixed 281 KiB __device__ array that every GPU
+ * loading the library keeps until exit. The first call on a device fills it
+ * (synchronous copy); make that call before any stream capture. All calls on a
+ * device share the array, so calls that overlap on the GPU race. Asynchronous
+ * on `stream` otherwise. Calls no cudaMalloc/cudaFree. */
+int b2p_sign_masks_noalloc(const int64_t* buffer_sizes, int nbufs, const uint64_t* seeds, int nseeds,
+                           uint32_t* out_words, void* stream);
+
 /* Wait for the model stream and report any device-side status (bounded-wait
  * expiry, out-of-range token). b2p_mezo_update / b2p_model_perturb and the
  * device-pointer forms of the eval calls are asynchronous; this is their fence. */
