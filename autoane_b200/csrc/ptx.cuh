@@ -92,7 +92,7 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, 2-D, no multicast)
+// TMA (tiled, 2-D, one destination CTA)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
