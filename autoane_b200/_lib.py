@@ -54,6 +54,8 @@ ABI: dict[str, tuple] = {
     "b2p_model_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),
     "b2p_launch_count": (i64, []),
     "b2p_sign_masks_noalloc": (i32, [C.POINTER(C.c_int64), i32, u64p, i32, vp, vp]),
+    "b2p_model_set_option": (i32, [vp, i32, i32]),
+    "b2p_gemm_pair": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
 }
 
 

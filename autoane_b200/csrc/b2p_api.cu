@@ -38,4 +38,20 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
                      static_cast<cudaStream_t>(stream));
 }
 
+int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
+                  void* stream) {
+  B2P_REQUIRE(X && W && Y, "null operand");
+  B2P_REQUIRE(dtype == B2P_F16 || dtype == B2P_BF16, "dtype must be B2P_F16 or B2P_BF16");
+  B2P_REQUIRE(M >= 2 * kBM, "the CTA-pair engine needs M >= %d (got %d)", 2 * kBM, M);
+  B2P_REQUIRE(ldy >= N, "ldy (%d) < N (%d)", ldy, N);
+  B2P_REQUIRE(out_f32 ? (ldy % 4 == 0) : (ldy % 8 == 0), "ldy must keep 16-byte row alignment");
+  B2P_REQUIRE((reinterpret_cast<uintptr_t>(Y) & 15u) == 0, "Y must be 16-byte aligned");
+  EpiParams ep;
+  std::memset(&ep, 0, sizeof(ep));
+  ep.M = M;
+  ep.N = N;
+  return launch_gemm_pair(out_f32 ? EPI_F32 : EPI_H16, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, nullptr, ep,
+                          static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

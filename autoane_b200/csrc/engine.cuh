@@ -73,6 +73,14 @@ int make_tmap_2d(CUtensorMap* map, const void* base, TmapType type, uint64_t inn
 int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                 void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
 
+// The CTA-pair engine (gemm2.cuh): 256-row x 256-column tiles over clusters of
+// two CTAs. pair_supported() tells whether a launch qualifies (M >= 256, LoRA
+// variant groups of whole 256-row tiles, LoRA only on the fused QKV / residual
+// epilogues); launch_gemm_pair() has the same contract as launch_gemm.
+bool pair_supported(int kind, int M, int N, const EpiParams& ep);
+int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                     void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
+
 // Pick the tile width for an N-column output (largest width whose padding
 // waste is minimal; SwiGLU and CE need multiples of 64 / any).
 int pick_bn(int N, int kind);

@@ -67,6 +67,7 @@ struct b2p_model {
   float* pairs = nullptr;        // [2 * kMaxPerturbOps] loss pairs for updates
   int qkv_bn = 160;
   int cur_groups = 0, cur_vars = 0;  // group/variant table sizes of the forward being issued
+  bool use_pair = true;               // CTA-pair GEMMs where they apply (b2p_model_set_option)
   int32_t* d_tok = nullptr;      // [max_seq_in][seq] tokens then targets
   int32_t* d_row_tgt = nullptr;  // [max_rows]
   int* d_meta = nullptr;         // group_seq[max_groups] | group_var[max_groups]
@@ -203,16 +204,23 @@ LoraEpi lora_epi(const b2p_model* m) {
 }
 
 // launch_gemm, bracketed by CUDA events on the model stream when profiling is on.
+int gemm_launch(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                void* out, int ldo, const EpiParams& ep) {
+  if (m->use_pair && pair_supported(kind, M, N, ep))
+    return launch_gemm_pair(kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
+  return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
+}
+
 int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
          void* out, int ldo, const EpiParams& ep) {
-  if (!m->prof) return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
+  if (!m->prof) return gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, ep);
   while (m->ev_pool.size() < m->ev_used + 2) {
     cudaEvent_t e;
     B2P_CHECK_CUDA(cudaEventCreate(&e));
     m->ev_pool.push_back(e);
   }
   B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used], m->st));
-  int rc = launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
+  int rc = gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, ep);
   B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used + 1], m->st));
   m->ev_used += 2;
   m->prof_flops.push_back(2.0 * M * (double)N * K);
@@ -833,5 +841,17 @@ int b2p_model_profile_read(b2p_model* m, double* gemm_ms, double* gemm_flops, lo
 }
 
 long long b2p_launch_count(void) { return launch_count(); }
+
+int b2p_model_set_option(b2p_model* m, int option, int value) {
+  B2P_REQUIRE(m, "null model");
+  switch (option) {
+    case B2P_OPT_PAIR_GEMM:
+      m->use_pair = value != 0;
+      return B2P_OK;
+    default:
+      set_error("unknown model option %d", option);
+      return B2P_ERR_ARG;
+  }
+}
 
 }  // extern "C"

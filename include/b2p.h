@@ -69,6 +69,12 @@ int b2p_device_status(void* stream);
 int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
              void* stream);
 
+/* Same contract as b2p_gemm on the CTA-pair engine: 256 x 256 output tiles
+ * computed by clusters of two CTAs (tcgen05 cta_group::2), each CTA loading its
+ * 128 rows of X and half of the W tile. Requires M >= 256. */
+int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
+                  void* stream);
+
 /* ======================================================================
  * Device-resident model: the MeZO-LoRA-split hot path on the GPU.
  *
@@ -185,6 +191,13 @@ int b2p_model_profile(b2p_model* m, int enable);
 int b2p_model_profile_read(b2p_model* m, double* gemm_ms, double* gemm_flops, long long* gemm_launches);
 /* Number of kernels this library has launched in this process. */
 long long b2p_launch_count(void);
+
+/* Model options. B2P_OPT_PAIR_GEMM (default 1): run the projection GEMMs on the
+ * CTA-pair engine (256 x 256 tiles over two SMs, tcgen05 cta_group::2) where it
+ * applies; 0 forces the single-CTA engine (128-row tiles). Same results either
+ * way up to fp32 summation order. */
+#define B2P_OPT_PAIR_GEMM 1
+int b2p_model_set_option(b2p_model* m, int option, int value);
 
 #ifdef __cplusplus
 }

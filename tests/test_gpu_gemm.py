@@ -40,3 +40,29 @@ def test_gemm_matches_fp32(b2p, M, N, K, dt, out_f32):
     err = (y - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
     tol = 2e-3 if (out_f32 or dt == "f16") else 8e-3
     assert err < tol, f"normwise error {err:.3e} (M={M} N={N} K={K} {dt} out_f32={out_f32})"
+
+
+PAIR_SHAPES = [(256, 960, 960), (512, 1600, 960), (384, 2560, 960), (1024, 16893, 960), (8192, 960, 2560),
+               (300, 100, 64), (16384, 5120, 960)]
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("out_f32", [1, 0])
+def test_pair_gemm_matches_fp32(b2p, M, N, K, dt, out_f32):
+    torch.manual_seed(M * 5 + N * 11 + K)
+    dtype = torch.float16 if dt == "f16" else torch.bfloat16
+    x = torch.randn(M, K, device="cuda").to(dtype)
+    w = (0.02 * torch.randn(N, K, device="cuda")).to(dtype)
+    ref = x.float() @ w.float().t()
+    pad = 4 if out_f32 else 8
+    ldy = (N + pad - 1) // pad * pad
+    y = torch.zeros(M, ldy, device="cuda", dtype=torch.float32 if out_f32 else dtype)
+    _lib.call("b2p_gemm_pair", x.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K, ldy, 0 if dt == "f16" else 1,
+              out_f32, None)
+    torch.cuda.synchronize()
+    _lib.call("b2p_device_status", None)
+    y = y[:, :N].float()
+    err = (y - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
+    tol = 2e-3 if (out_f32 or dt == "f16") else 8e-3
+    assert err < tol, f"normwise error {err:.3e} (M={M} N={N} K={K} {dt} out_f32={out_f32})"

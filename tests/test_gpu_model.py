@@ -144,3 +144,24 @@ def test_full_smollm2_360m_step_matches_oracle(b2p):
     assert abs(lp - rlp) < 1e-3 and abs(lm - rlm) < 1e-3, (lp, lm, rlp, rlm)
     assert 9.0 < lp < 10.5  # ≈ ln(16893) for a random-init model (tests/test_training.sh step-0 band)
     model.close()
+
+
+def test_pair_engine_seq256_matches_oracle_and_single_engine(b2p):
+    """SEQ 256 puts every projection GEMM (with LoRA) on the CTA-pair engine."""
+    cfg = M.small_cfg(nlayers=2, seq=256)
+    syn, om, model, toks = make_pair(cfg, max_groups=8)
+    inp, tgt = seqs(syn, toks, 2, cfg.seq, base=777)
+    seed = 13 * 1000003 + 42
+    vars_ = [(seed, 1, EPS, 0.0), (seed, 2, EPS, np.float32(-2.0) * EPS)]
+    got_pair = model.eval(inp, tgt, vars_)
+    from autoane_b200 import _lib
+    _lib.call("b2p_model_set_option", model.h, 1, 0)
+    got_single = model.eval(inp, tgt, vars_)
+    _lib.call("b2p_model_set_option", model.h, 1, 1)
+    th_p = perturbed(syn.theta, cfg, seed, [EPS])
+    th_m = perturbed(syn.theta, cfg, seed, [EPS, np.float32(-2.0) * EPS])
+    ref = [np.mean([om.forward_loss(t, inp[i], tgt[i]) for i in range(2)]) for t in (th_p, th_m)]
+    for g, s, r in zip(got_pair, got_single, ref):
+        assert abs(g - r) < 1e-3, (got_pair, ref)
+        assert abs(g - s) < 2e-4, (got_pair, got_single)
+    model.close()
