@@ -56,6 +56,21 @@ ABI: dict[str, tuple] = {
     "b2p_sign_masks_noalloc": (i32, [C.POINTER(C.c_int64), i32, u64p, i32, vp, vp]),
     "b2p_model_set_option": (i32, [vp, i32, i32]),
     "b2p_gemm_pair": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+    "b2p_compile": (vp, [vp, C.POINTER(fp)]),
+    "b2p_input_bytes": (szt, [vp, i32]),
+    "b2p_output_bytes": (szt, [vp, i32]),
+    "b2p_write_input": (i32, [vp, i32, vp, szt]),
+    "b2p_write_input_channels": (i32, [vp, i32, i32, i32, fp]),
+    "b2p_eval": (i32, [vp]),
+    "b2p_eval_async": (i32, [vp]),
+    "b2p_read_output": (i32, [vp, i32, fp, szt]),
+    "b2p_read_output_channels": (i32, [vp, i32, i32, i32, fp]),
+    "b2p_free": (None, [vp]),
+    "b2p_kernel_stream": (vp, [vp]),
+    "b2p_set_lora": (i32, [vp, i32, fp, fp, i32]),
+    "b2p_set_perturb": (i32, [vp, u64, f32]),
+    "b2p_compile_count": (i32, []),
+    "b2p_reset_compile_count": (None, []),
 }
 
 
@@ -69,6 +84,15 @@ class ModelConfig(C.Structure):
 class Variant(C.Structure):
     """b2p_variant (include/b2p.h)."""
     _fields_ = [("seed", C.c_uint64), ("mode", C.c_int), ("s1", C.c_float), ("s2", C.c_float)]
+
+
+class OpDesc(C.Structure):
+    """b2p_op_desc (include/b2p.h)."""
+    _fields_ = [(n, C.c_int) for n in ("kind", "ic", "oc", "seq", "q_dim", "kv_dim", "hidden")] + [
+        ("res_alpha", C.c_float), ("dtype", C.c_int), ("n_parts", C.c_int), ("part_oc", C.c_int * 3)]
+
+
+OP_CONV1X1, OP_QKV_FUSED, OP_FFN_FUSED, OP_DYN_MATMUL, OP_LM_HEAD_CE, OP_DX = range(6)
 
 
 class B2PError(RuntimeError):

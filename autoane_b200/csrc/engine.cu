@@ -188,6 +188,7 @@ static int dispatch_kind(int bn, int kind, const void* X, int ldx, const void* W
   const bool lora = ep.has_lora != 0;
   switch (kind) {
     case EPI_F32:
+      if (lora) return dispatch_bn<EPI_F32, H, BF16, true>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       return dispatch_bn<EPI_F32, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case EPI_H16:
       return dispatch_bn<EPI_H16, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);

@@ -786,6 +786,13 @@ int launch_cf_to_tm16(const float* src, int C, int S, void* dst, int ld_dst, boo
   return B2P_OK;
 }
 
+int launch_cf_to_tm32(const float* src, int C, int S, float* dst, int ld_dst, cudaStream_t st) {
+  dim3 grid((S + 31) / 32, (C + 31) / 32), block(32, 8);
+  cf_to_tm16_kernel<float><<<grid, block, 0, st>>>(src, C, S, dst, ld_dst);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
 int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int C, int S, float* dst,
                       cudaStream_t st) {
   dim3 grid((S + 31) / 32, (C + 31) / 32), block(32, 8);

@@ -84,6 +84,7 @@ int launch_perturb(float* theta, long long n, const uint32_t* masks, long long m
 // Layout conversion for the Kern-style boundary: host channel-first fp32 [C, S]
 // <-> device token-major 16-bit / fp32 [S, C].
 int launch_cf_to_tm16(const float* src, int C, int S, void* dst, int ld_dst, bool bf16, cudaStream_t st);
+int launch_cf_to_tm32(const float* src, int C, int S, float* dst, int ld_dst, cudaStream_t st);
 int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int C, int S, float* dst,
                       cudaStream_t st);
 int launch_f32_to_16(const float* src, void* dst, long long n, bool bf16, cudaStream_t st);

@@ -89,7 +89,7 @@ int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, in
 typedef struct b2p_model b2p_model;
 
 typedef struct {
-  int dim, hidden, heads, kv_heads, head_dim, seq, nlayers, vocab; /* models/*.h sizes */
+  int dim, hidden, heads, kv_heads, head_dim, seq, nlayers, vocab; /* sizes of the model header (training/models) */
   int rank;          /* LoRA rank (4 or 8), adapters on Wq/Wk/Wv/Wo */
   float rope_theta;  /* ROPE_THETA (cpu_ops.h:296) */
   float res_alpha;   /* residual scale (train_mezo.m:1262): 1 for fine-tuning */
@@ -198,6 +198,121 @@ long long b2p_launch_count(void);
  * way up to fp32 summation order. */
 #define B2P_OPT_PAIR_GEMM 1
 int b2p_model_set_option(b2p_model* m, int option, int value);
+
+/* ======================================================================
+ * Kern-level boundary: one compiled operator with baked weights and
+ * channel-first fp32 host I/O, the verbs of training/io.h and
+ * bridge/ane_bridge.h without MIL text.
+ *
+ * Op kinds (weights[] in the order listed, each fp32 row-major [out, in]):
+ *   B2P_OP_CONV1X1    {W[oc,ic]}          in0 x[ic,S]            out0 y[oc,S] = W·x
+ *                     (compile_conv1x1_kern, training/io.h:165; gen_conv1x1_mil,
+ *                     training/mil_dynamic.h:17)
+ *   B2P_OP_QKV_FUSED  {Wq,Wk,Wv}          in0 xn[ic,S]           out0 [q+2kv,S] = concat(Wq·xn, Wk·xn, Wv·xn)
+ *                     (compile_qkv_fused_conv1x1_kern, io.h:182; mil_dynamic.h:43)
+ *   B2P_OP_FFN_FUSED  {W1,W3,W2}          in0 xn[ic,S], in1 x[ic,S]
+ *                                         out0 x + alpha·W2·(silu(W1·xn) ⊙ W3·xn)  [ic,S]
+ *                     (compile_ffn_fused_conv1x1_kern, io.h:209; mil_dynamic.h:82; the
+ *                     reference's single [ic, 2S] input surface is in0|in1, see
+ *                     io_write_ffn_fused_conv_input, io.h:232)
+ *   B2P_OP_DYN_MATMUL (none)              in0 act[ic,S], in1 W[ic,oc]
+ *                                         out0 y[oc,S], y[o,s] = sum_d act[d,s]·W[d,o]
+ *                     (gen_dyn_matmul_mil, mil_dynamic.h:157; the weights travel with the
+ *                     input as in io_write_dyn, io.h:79)
+ *   B2P_OP_LM_HEAD_CE {E[oc,ic]}          in0 xn[ic,S], in1 int32 targets[S] in [0, oc)
+ *                                         out0 loss[1] = mean_s CE(E·xn[:,s], target_s)
+ *                     (classifier + cross_entropy_loss, training/train_mezo.m:1695-1698,
+ *                     training/cpu_ops.h:108-133)
+ *   B2P_OP_DX         {W_0..W_{n-1}}      in_i dy_i[part_oc[i],S]
+ *                                         out0 dx[ic,S] = sum_i W_i^T·dy_i
+ *                     (the backward data GEMMs: ffnBwdW2t / ffnBwdW13t / wotBwd /
+ *                     qBwd / kvBwd, training/mil_dynamic.h:414-500, and
+ *                     bp_lora_backward's dX, training/backprop_lora.h:147-288)
+ *
+ * Shape rules: ic and every output width are multiples of 8 (16-byte rows on
+ * the device); S >= 1. Device compute is fp16/bf16 with fp32 accumulation; the
+ * host sees fp32 on both sides.
+ * ====================================================================== */
+#define B2P_OP_CONV1X1 0
+#define B2P_OP_QKV_FUSED 1
+#define B2P_OP_FFN_FUSED 2
+#define B2P_OP_DYN_MATMUL 3
+#define B2P_OP_LM_HEAD_CE 4
+#define B2P_OP_DX 5
+
+typedef struct b2p_op_desc {
+  int kind;          /* B2P_OP_* */
+  int ic;            /* input channels (dim for the fused ops) */
+  int oc;            /* output channels: conv1x1 / dyn_matmul; vocabulary for lm_head_ce */
+  int seq;           /* spatial width S (tokens) */
+  int q_dim, kv_dim; /* qkv_fused */
+  int hidden;        /* ffn_fused */
+  float res_alpha;   /* ffn_fused residual scale (the conv program uses 1) */
+  int dtype;         /* B2P_F16 or B2P_BF16 */
+  int n_parts;       /* dx: number of (W_i, dy_i) pairs, 1..3 */
+  int part_oc[3];    /* dx: output channels of W_i */
+} b2p_op_desc;
+
+typedef struct b2p_kernel b2p_kernel;
+
+/* Compile an operator: validates the descriptor, uploads the weights as 16-bit
+ * device tensors (the copy is baked: later changes to `weights` have no
+ * effect, as with the reference's BLOBFILE constants) and allocates the I/O
+ * buffers. Returns NULL on failure with the reason in b2p_last_error().
+ * Replaces compile_kern_mil_w (io.h:116) / ane_bridge_compile (ane_bridge.h:33). */
+b2p_kernel* b2p_compile(const b2p_op_desc* desc, const float* const* weights);
+
+/* Byte size of input / output `idx` (0 when idx is out of range). */
+size_t b2p_input_bytes(const b2p_kernel* k, int idx);
+size_t b2p_output_bytes(const b2p_kernel* k, int idx);
+
+/* Copy host input `idx` (fp32 [C, S], or int32 targets for lm_head_ce in1) to
+ * the device. `bytes` must equal b2p_input_bytes(k, idx).
+ * Replaces io_write_conv_acts (io.h:102) / ane_bridge_write_input (ane_bridge.h:55). */
+int b2p_write_input(b2p_kernel* k, int idx, const void* data, size_t bytes);
+
+/* Write channels [ch_off, ch_off + channels) of fp32 input `idx`
+ * (io_write_fp16_at, io.h:72). */
+int b2p_write_input_channels(b2p_kernel* k, int idx, int ch_off, int channels, const float* data);
+
+/* Run the operator; returns when the results are ready (ane_eval, io.h:242, which
+ * discards errors; this returns B2P_ERR_DEVICE / B2P_ERR_CUDA instead). */
+int b2p_eval(b2p_kernel* k);
+
+/* Enqueue the operator on the handle's stream and return; b2p_read_output
+ * (or b2p_device_status on the stream) reports errors. */
+int b2p_eval_async(b2p_kernel* k);
+
+/* Copy output `idx` to the host (waits for the handle's stream).
+ * Replaces io_read_dyn (io.h:109) / ane_bridge_read_output (ane_bridge.h:59). */
+int b2p_read_output(b2p_kernel* k, int idx, float* data, size_t bytes);
+
+/* Read channels [ch_off, ch_off + channels) of output `idx` (io_read_fp16, io.h:58). */
+int b2p_read_output_channels(b2p_kernel* k, int idx, int ch_off, int channels, float* data);
+
+/* Release the operator (free_kern, io.h:152 / ane_bridge_free, ane_bridge.h:63). */
+void b2p_free(b2p_kernel* k);
+
+/* The CUDA stream the handle issues on (cudaStream_t). */
+void* b2p_kernel_stream(const b2p_kernel* k);
+
+/* Device-resident LoRA on conv1x1 (part 0) and qkv_fused (parts 0/1/2 = q/k/v):
+ * out_part += B·(A·x) with A fp32 [rank, ic], B fp32 [part_out, rank], rank 4
+ * or 8 (the host-side lora_addmm after the conv read, train_mezo.m:1558-1560,
+ * 1609, moved into the GEMM). Requires ic in {512, 960, 1024, 2048} and S a
+ * multiple of 128. Passing A = B = NULL removes the part's adapter. */
+int b2p_set_lora(b2p_kernel* k, int part, const float* A, const float* B, int rank);
+
+/* Evaluate with the adapters perturbed on the fly: theta' = theta + scale·z,
+ * z the reference's Rademacher stream of `seed` (perturb_buffer,
+ * train_mezo.m:122-136) drawn over the handle's adapters in the order A_0, B_0,
+ * A_1, B_1, ... The stored adapters are not modified. scale 0 turns it off. */
+int b2p_set_perturb(b2p_kernel* k, uint64_t seed, float scale);
+
+/* Operators compiled by this process (ane_bridge_get_compile_count,
+ * ane_bridge.h:66 / g_compile_count, io.h:138), and its reset (ane_bridge.h:69). */
+int b2p_compile_count(void);
+void b2p_reset_compile_count(void);
 
 #ifdef __cplusplus
 }

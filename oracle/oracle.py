@@ -70,6 +70,8 @@ def lib() -> C.CDLL:
         L.or_set_threads.restype = C.c_int
         L.or_cross_entropy.restype = C.c_float
         L.or_cross_entropy.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_uint16), C.c_int, C.c_int]
+        L.or_lora_addmm.argtypes = [C.POINTER(C.c_float)] * 5 + [C.c_int] * 4
+        L.or_sgemm_nn.argtypes = [C.c_int] * 3 + [C.POINTER(C.c_float)] * 3 + [C.c_float]
         for n in ("or_rmsnorm",):
             getattr(L, n).argtypes = [C.POINTER(C.c_float)] * 3 + [C.c_int, C.c_int]
         L.or_rope_forward.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int, C.c_float]
@@ -119,6 +121,38 @@ def lora_buffer_sizes(nlayers, dim, q_dim, kv_dim, rank) -> np.ndarray:
 def perturb_lora(theta: np.ndarray, nlayers, dim, q_dim, kv_dim, rank, seed: int, scale: float) -> None:
     assert theta.dtype == np.float32 and theta.flags.c_contiguous
     lib().or_perturb_lora(_f(theta), nlayers, dim, q_dim, kv_dim, rank, seed, np.float32(scale))
+
+
+def sgemm(A: np.ndarray, B: np.ndarray) -> np.ndarray:
+    """C = A·B in fp32 through cblas_sgemm (the reference's projection call sites)."""
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    M, K = A.shape
+    K2, N = B.shape
+    assert K == K2
+    out = np.zeros((M, N), np.float32)
+    lib().or_sgemm_nn(M, N, K, _f(A), _f(B), _f(out), np.float32(0.0))
+    return out
+
+
+def lora_addmm(out: np.ndarray, A: np.ndarray, B: np.ndarray, x: np.ndarray) -> None:
+    """out[out_dim, S] += B·(A·x) in place (lora_addmm, training/train_mezo.m:694-703)."""
+    assert out.dtype == np.float32 and out.flags.c_contiguous
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    rank, in_dim = A.shape
+    out_dim, S = out.shape
+    tmp = np.zeros((rank, S), np.float32)
+    lib().or_lora_addmm(_f(out), _f(A), _f(B), _f(x), _f(tmp), out_dim, rank, in_dim, S)
+
+
+def cross_entropy(logits_tm: np.ndarray, targets: np.ndarray) -> float:
+    """Mean CE of token-major logits [S, V] (cross_entropy_loss, training/cpu_ops.h:108-133)."""
+    logits_tm = np.ascontiguousarray(logits_tm, np.float32)
+    t = np.ascontiguousarray(targets, np.uint16)
+    S, V = logits_tm.shape
+    return float(lib().or_cross_entropy(_f(logits_tm), _u16(t), V, S))
 
 
 def rope_tables(seq: int, hd: int, theta: float):

@@ -49,3 +49,22 @@ def test_missing_library_fails_loudly(tmp_path):
             _lib.load(tmp_path / "absent.so")
     finally:
         _lib._lib = saved
+
+
+def test_io_shim_header_compiles_as_c(tmp_path):
+    """include/b2p_io.h builds as C11 with warnings as errors (no GPU work)."""
+    import subprocess
+    src = Path(__file__).resolve().parent / "shim" / "conv_fused_site.c"
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", str(HEADER.parent),
+                    str(src)], check=True)
+
+
+def test_kern_compile_without_gpu_fails_loudly():
+    """b2p_compile returns NULL with a reason when no B200 is usable; there is no CPU path."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    from autoane_b200 import kern as KN
+    import numpy as np
+    with pytest.raises(_lib.B2PError):
+        KN.compile_conv1x1_kern(np.zeros((64, 64), np.float32), 64, 64, 128)
