@@ -74,7 +74,8 @@ int check_device_status(cudaStream_t st) {
   B2P_CHECK_CUDA(cudaStreamSynchronize(st));
   if (h != 0) {
     B2P_CHECK_CUDA(cudaMemsetAsync(c->status, 0, sizeof(uint32_t), st));
-    set_error("device status %u: a bounded wait inside a kernel expired (1 producer, 2 mma, 3 epilogue)", h);
+    set_error("device status %u (1-4: a bounded wait inside a kernel expired: producer, mma, epilogue, drain; "
+              "5: an index out of range; 6: a non-finite gradient, the optimizer step was skipped)", h);
     return B2P_ERR_DEVICE;
   }
   return B2P_OK;
@@ -191,6 +192,7 @@ static int dispatch_kind(int bn, int kind, const void* X, int ldx, const void* W
       if (lora) return dispatch_bn<EPI_F32, H, BF16, true>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       return dispatch_bn<EPI_F32, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case EPI_H16:
+      if (lora) return dispatch_bn<EPI_H16, H, BF16, true>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       return dispatch_bn<EPI_H16, H, BF16, false>(bn, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case EPI_QKV_ROPE:
       if (!lora) break;
@@ -203,6 +205,8 @@ static int dispatch_kind(int bn, int kind, const void* X, int ldx, const void* W
       return launch_t<256, EPI_SWIGLU, H, BF16, false>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case EPI_CE:
       return launch_t<256, EPI_CE, H, BF16, false>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+    case EPI_CE_GRAD:
+      return launch_t<256, EPI_CE_GRAD, H, BF16, false>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
   }
   set_error("unsupported epilogue kind %d (LoRA %d)", kind, (int)lora);
   return B2P_ERR_UNSUPPORTED;
@@ -231,6 +235,7 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
     B2P_REQUIRE(ep.head_dim == 64 && ep.seq_len % kBM == 0 && ep.rope_cols % 64 == 0,
                 "RoPE epilogue needs head_dim 64, seq %% 128 == 0 and whole heads");
   if (kind == EPI_SWIGLU) B2P_REQUIRE(N % 256 == 0, "SwiGLU needs N %% 256 == 0");
+  if (kind == EPI_CE_GRAD) B2P_REQUIRE(ep.targets && ep.row_lse, "CE gradient needs targets and row LSE");
   if (bf16) return dispatch_kind<__nv_bfloat16, true>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
   return dispatch_kind<__half, false>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
 }

@@ -95,6 +95,7 @@ int dispatch_pair(int kind, const void* X, int ldx, const void* W, int ldw, int 
 bool pair_supported(int kind, int M, int N, const EpiParams& ep) {
   (void)N;
   if (M < 2 * kBM) return false;
+  if (kind == EPI_CE_GRAD) return false;  // single-CTA engine only
   if (ep.has_lora) {
     if (ep.lora.group_rows % (2 * kBM) != 0) return false;
     if (!(kind == EPI_QKV_ROPE && ep.lora.nseg == 3) && !(kind == EPI_RESID && ep.lora.nseg == 1)) return false;

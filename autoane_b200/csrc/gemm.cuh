@@ -55,6 +55,7 @@ enum EpiKind : int {
   EPI_RESID = 3,     // out fp32 x [M, ldo] += alpha * (acc + LoRA)   (TMA reduce-add)
   EPI_SWIGLU = 4,    // tile = [gate half | up half]; out 16-bit [M, ldo] = silu(gate) * up
   EPI_CE = 5,        // per-row (max, sum exp) partials over the tile's valid columns + target logit
+  EPI_CE_GRAD = 6,   // out 16-bit = alpha * (exp(acc - row_lse[row]) - [col == target[row]])  (dlogits)
 };
 
 // One perturbed evaluation of the trainable parameters: θ, θ+s1·z or
@@ -108,6 +109,7 @@ struct EpiParams {
   float2* ce_part;             // [M, 2 * n_tiles_n] (one partial per epilogue column half)
   float* ce_tgt;               // [M]
   int n_tiles_n;
+  const float* row_lse;        // EPI_CE_GRAD: [M] log-sum-exp of each row's logits
   uint32_t* status;            // device error word
 };
 
@@ -458,7 +460,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
       float ce_m = -INFINITY, ce_s = 0.f;
       int tgt = -1;
-      if (KIND == EPI_CE && row_ok) tgt = ep.targets[row];
+      if ((KIND == EPI_CE || KIND == EPI_CE_GRAD) && row_ok) tgt = ep.targets[row];
+      const float lse = (KIND == EPI_CE_GRAD && row_ok) ? ep.row_lse[row] : 0.f;
       const float* rope_cs_row = nullptr;
       const float* rope_sn_row = nullptr;
       if (KIND == EPI_QKV_ROPE) {  // token position: seq_len is a multiple of the 128-row tile
@@ -530,6 +533,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (KIND == EPI_RESID) {
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] *= ep.alpha;
+        }
+        if (KIND == EPI_CE_GRAD) {
+          // softmax - one-hot (cross_entropy_loss, training/cpu_ops.h:118-130), times the gradient scale
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float p = __expf(v[c] - lse);
+            v[c] = ep.alpha * (col + c == tgt ? p - 1.0f : p);
+          }
         }
         // stage the 32 x 32 box (the previous store must have finished reading it)
         if (lane == 0) bulk_wait_read0();

@@ -1,26 +1,13 @@
 // kernels.cu — glue kernels (embedding, RMSNorm + LoRA-down, attention,
 // cross-entropy reduction, perturbation steps, layout conversion).
+#include <algorithm>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include "engine.cuh"
 #include "kernels.cuh"
+#include "mma.cuh"
 
 namespace b2p {
-
-template <typename T>
-struct H2;
-template <>
-struct H2<__half> {
-  using V = __half2;
-  static __device__ __forceinline__ float2 to_f2(V v) { return __half22float2(v); }
-  static __device__ __forceinline__ V from_f2(float a, float b) { return __floats2half2_rn(a, b); }
-};
-template <>
-struct H2<__nv_bfloat16> {
-  using V = __nv_bfloat162;
-  static __device__ __forceinline__ float2 to_f2(V v) { return __bfloat1622float2(v); }
-  static __device__ __forceinline__ V from_f2(float a, float b) { return __floats2bfloat162_rn(a, b); }
-};
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -58,53 +45,6 @@ int launch_embed(const float* embed, int vocab, int dim, const int32_t* tokens, 
 // ---------------------------------------------------------------------------
 // RMSNorm (perturbed weight) + LoRA-down (perturbed A), one warp per token row
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [64][64] 16-bit tile
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-template <typename T>
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
-template <>
-__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <>
-__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <typename T>
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-  auto v = H2<T>::from_f2(a, b);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-
 constexpr int kNormRowsPerBlock = 64;
 constexpr int kNormThreads = 256;
 
@@ -618,6 +558,11 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnArgs a, float scale_l
   }
   // normalise and store
   const float inv0 = 1.0f / l_run[0], inv1 = 1.0f / l_run[1];
+  if (a.lse && lt == 0) {
+    const long long r0 = (long long)g * a.seq + qb * kAttnTile + warp * 16 + lg;
+    a.lse[r0 * a.heads + h] = m_run[0] + log2f(l_run[0]);
+    a.lse[(r0 + 8) * a.heads + h] = m_run[1] + log2f(l_run[1]);
+  }
   T* out = static_cast<T*>(a.out) + ((long long)g * a.seq + qb * kAttnTile + warp * 16 + lg) * a.ld_out + h * kHD;
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) {
@@ -646,7 +591,8 @@ int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st) {
 // cross-entropy reduction
 // ---------------------------------------------------------------------------
 __global__ void ce_reduce_kernel(const float2* __restrict__ part, int ntiles, const float* __restrict__ tgt_logit,
-                                 int seq, float* __restrict__ row_loss, float* __restrict__ group_loss) {
+                                 int seq, float* __restrict__ row_loss, float* __restrict__ group_loss,
+                                 float* __restrict__ row_lse) {
   __shared__ float red[256];
   const int g = blockIdx.x;
   float acc = 0.f;
@@ -659,6 +605,7 @@ __global__ void ce_reduce_kernel(const float2* __restrict__ part, int ntiles, co
     for (int i = 0; i < ntiles; ++i) S += p[i].y * expf(p[i].x - M);
     const float l = -(tgt_logit[row] - M) + logf(S);
     row_loss[row] = l;
+    if (row_lse) row_lse[row] = M + logf(S);
     acc += l;
   }
   red[threadIdx.x] = acc;
@@ -671,9 +618,9 @@ __global__ void ce_reduce_kernel(const float2* __restrict__ part, int ntiles, co
 }
 
 int launch_ce_reduce(const float2* part, int ntiles, const float* tgt_logit, int rows, int seq, float* row_loss,
-                     float* group_loss, cudaStream_t st) {
+                     float* group_loss, cudaStream_t st, float* row_lse) {
   B2P_REQUIRE(rows % seq == 0, "rows must be whole sequences");
-  ce_reduce_kernel<<<rows / seq, 256, 0, st>>>(part, ntiles, tgt_logit, seq, row_loss, group_loss);
+  ce_reduce_kernel<<<rows / seq, 256, 0, st>>>(part, ntiles, tgt_logit, seq, row_loss, group_loss, row_lse);
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -802,6 +749,42 @@ int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int 
     tm_to_cf32_kernel<__nv_bfloat16, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
   else
     tm_to_cf32_kernel<__half, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
+template <typename T>
+__global__ void swiglu_gate_kernel(const T* __restrict__ h13, int rows, int H, T* __restrict__ gate) {
+  const long long n8 = (long long)rows * H / 8;  // 8 gate columns per thread (never straddle a 128-block)
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const long long e = i * 8;
+    const long long r = e / H;
+    const int c = (int)(e - r * H);
+    const T* src = h13 + r * 2 * H + (c >> 7) * 256 + (c & 127);
+    const uint4 a = *reinterpret_cast<const uint4*>(src);
+    const uint4 b = *reinterpret_cast<const uint4*>(src + 128);
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 h1 = H2<T>::to_f2(*reinterpret_cast<const typename H2<T>::V*>(&av[k]));
+      const float2 h3 = H2<T>::to_f2(*reinterpret_cast<const typename H2<T>::V*>(&bv[k]));
+      o[k] = pack_h2<T>(silu_f(h1.x) * h3.x, silu_f(h1.y) * h3.y);
+    }
+    *reinterpret_cast<uint4*>(gate + e) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+int launch_swiglu_gate(const void* h13, int rows, int H, void* gate, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(H % 128 == 0, "hidden %d must be a multiple of 128", H);
+  const long long n8 = (long long)rows * H / 8;
+  const int blocks = (int)std::min<long long>((n8 + 255) / 256, 148 * 16);
+  if (bf16)
+    swiglu_gate_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(h13), rows, H,
+                                                              static_cast<__nv_bfloat16*>(gate));
+  else
+    swiglu_gate_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(h13), rows, H,
+                                                       static_cast<__half*>(gate));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }

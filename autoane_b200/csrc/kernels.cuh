@@ -52,13 +52,14 @@ struct AttnArgs {
   void* out;
   int ld_out;
   int seq, heads, kv_heads, ngroups;
+  float* lse;  // optional [rows, heads]: each row's log2-domain softmax normaliser (for the backward)
 };
 int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st);
 
 // Row losses from the lm-head partials: loss_row = -(logit_tgt - M) + log(Σ s_i e^{m_i - M})
 // (training/cpu_ops.h:108-133); group_loss[g] = mean over the group's rows.
 int launch_ce_reduce(const float2* part, int ntiles, const float* tgt_logit, int rows, int seq, float* row_loss,
-                     float* group_loss, cudaStream_t st);
+                     float* group_loss, cudaStream_t st, float* row_lse = nullptr);
 // var_loss[v] = mean of group_loss over the n_seq groups of variant v (groups v*n_seq + q).
 int launch_variant_loss(const float* group_loss, int n_var, int n_seq, float* var_loss, cudaStream_t st);
 
@@ -80,6 +81,10 @@ struct PerturbOps {
 };
 int launch_perturb(float* theta, long long n, const uint32_t* masks, long long mask_words, const PerturbOps& ops,
                    const float* losses, cudaStream_t st);
+
+// gate[r, c] = silu(h1) * h3 from the interleaved W1|W3 output h13 [rows, 2H]
+// (h1 of column c at 256*(c/128) + c%128, h3 128 columns later; train_mezo.m:1664-1667).
+int launch_swiglu_gate(const void* h13, int rows, int H, void* gate, bool bf16, cudaStream_t st);
 
 // Layout conversion for the Kern-style boundary: host channel-first fp32 [C, S]
 // <-> device token-major 16-bit / fp32 [S, C].

@@ -10,77 +10,9 @@
 #include <cmath>
 #include <cstring>
 #include <vector>
-#include "../../include/b2p.h"
-#include "engine.cuh"
-#include "kernels.cuh"
-#include "rng.cuh"
+#include "model.cuh"
 
 using namespace b2p;
-
-struct Stager {
-  char* base = nullptr;
-  size_t slot_bytes = 0;
-  int nslots = 0, next = 0;
-  std::vector<cudaEvent_t> ev;
-  std::vector<char> armed;
-};
-
-struct b2p_model {
-  b2p_model_config cfg{};
-  int device = 0;
-  bool bf16 = false;
-  cudaStream_t st = nullptr;
-  int q_dim = 0, kv_dim = 0, qkv_dim = 0, ffn2 = 0;
-  // trainable layout (offsets inside a layer block, then rms_final)
-  long long oAq, oBq, oAk, oBk, oAv, oBv, oAo, oBo, oRa, oRf, layer_size, oRfinal, P;
-  // frozen weights (16-bit), per-layer contiguous
-  void *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr, *cembed = nullptr;
-  float* embed = nullptr;
-  int cv = 0;
-  std::vector<char> layer_set;
-  bool embed_set = false;
-  // trainable params + sign masks
-  float* theta = nullptr;
-  uint32_t* masks = nullptr;
-  int max_slots = 0;
-  long long mask_words = 0;
-  SignBuffer* d_bufs = nullptr;
-  int nbufs = 0;
-  uint64_t* d_polys = nullptr;
-  long long nchunks = 0;
-  std::vector<uint64_t> slot_seed;  // seeds whose masks the slots currently hold (in slot order)
-  long long total_draws = 0;
-  uint64_t* d_seeds = nullptr;
-  // activations
-  int max_groups = 0, max_rows = 0, n_vt = 0;
-  float* x = nullptr;
-  void* xn = nullptr;
-  void* U = nullptr;             // [max_rows][kUCols] 16-bit LoRA-down results (zero padded)
-  void* qkv = nullptr;
-  void* attn = nullptr;
-  void* hbuf = nullptr;
-  float2* ce_part = nullptr;
-  float* ce_tgt = nullptr;
-  float* row_loss = nullptr;
-  float* group_loss = nullptr;
-  float* var_loss = nullptr;
-  float* pairs = nullptr;        // [2 * kMaxPerturbOps] loss pairs for updates
-  int qkv_bn = 160;
-  int cur_groups = 0, cur_vars = 0;  // group/variant table sizes of the forward being issued
-  bool use_pair = true;               // CTA-pair GEMMs where they apply (b2p_model_set_option)
-  int32_t* d_tok = nullptr;      // [max_seq_in][seq] tokens then targets
-  int32_t* d_row_tgt = nullptr;  // [max_rows]
-  int* d_meta = nullptr;         // group_seq[max_groups] | group_var[max_groups]
-  VariantInfo* d_var = nullptr;
-  float* rope_cos = nullptr;
-  float* rope_sin = nullptr;
-  Stager stg;
-  // optional CUDA-event timing of every projection-GEMM launch
-  bool prof = false;
-  std::vector<cudaEvent_t> ev_pool;
-  size_t ev_used = 0;
-  std::vector<double> prof_flops;
-};
 
 namespace {
 
@@ -162,6 +94,8 @@ void model_release(b2p_model* m) {
     if (e) cudaEventDestroy(e);
   for (auto e : m->ev_pool)
     if (e) cudaEventDestroy(e);
+  if (m->p16) p16_release(m->p16);
+  m->p16 = nullptr;
   if (m->st) cudaStreamDestroy(m->st);
 }
 
@@ -205,22 +139,23 @@ LoraEpi lora_epi(const b2p_model* m) {
 
 // launch_gemm, bracketed by CUDA events on the model stream when profiling is on.
 int gemm_launch(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
-                void* out, int ldo, const EpiParams& ep) {
+                void* out, int ldo, const void* u16, const EpiParams& ep) {
   if (m->use_pair && pair_supported(kind, M, N, ep))
-    return launch_gemm_pair(kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
-  return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, m->U, ep, m->st);
+    return launch_gemm_pair(kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, m->st);
+  return launch_gemm(bn, kind, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, m->st);
 }
 
 int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
-         void* out, int ldo, const EpiParams& ep) {
-  if (!m->prof) return gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, ep);
+         void* out, int ldo, const EpiParams& ep, const void* u16 = nullptr) {
+  if (!u16) u16 = m->U;
+  if (!m->prof) return gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep);
   while (m->ev_pool.size() < m->ev_used + 2) {
     cudaEvent_t e;
     B2P_CHECK_CUDA(cudaEventCreate(&e));
     m->ev_pool.push_back(e);
   }
   B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used], m->st));
-  int rc = gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, ep);
+  int rc = gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep);
   B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used + 1], m->st));
   m->ev_used += 2;
   m->prof_flops.push_back(2.0 * M * (double)N * K);
@@ -228,7 +163,11 @@ int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, 
 }
 
 // The batched forward over G groups whose inputs are already staged on the device.
-int run_forward(b2p_model* m, int G, const int32_t* tok) {
+// With `sv`, every activation the backprop-LoRA backward reads is written to its
+// per-layer slab instead of the shared scratch buffers, and the W1/W3 outputs are
+// kept (16-bit GEMM output + a separate gate kernel instead of the fused SwiGLU
+// epilogue).
+int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv = nullptr) {
   const auto& c = m->cfg;
   const int R = G * c.seq;
   const int D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim, QKV = m->qkv_dim;
@@ -240,13 +179,22 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
   rc = launch_embed(m->embed, c.vocab, D, tok, group_seq, c.seq, R, m->x, ctx->status, m->st);
   if (rc) return rc;
   const PerturbCtx pc = pctx(m);
+  auto slab = [R](void* base, int l, size_t row_bytes) -> void* {
+    return static_cast<char*>(base) + (size_t)l * R * row_bytes;
+  };
   for (int l = 0; l < c.nlayers; ++l) {
     const long long lb = (long long)l * m->layer_size;
+    void* xn = sv ? slab(sv->xn, l, D * e) : m->xn;
+    void* U = sv ? slab(sv->U, l, kUCols * e) : m->U;
+    void* qkv = sv ? slab(sv->qkv, l, QKV * e) : m->qkv;
+    void* attn = sv ? slab(sv->attn, l, QD * e) : m->attn;
+    if (sv) B2P_CHECK_CUDA(cudaMemcpyAsync(slab(sv->x_in, l, D * 4), m->x, (size_t)R * D * 4,
+                                           cudaMemcpyDeviceToDevice, m->st));
     // RMSNorm(rms_att) + LoRA-down for q, k, v
     NormLoraArgs na;
     std::memset(&na, 0, sizeof(na));
     na.in = m->x;
-    na.xn = m->xn;
+    na.xn = xn;
     na.rows = R;
     na.dim = D;
     na.norm = 1;
@@ -256,7 +204,7 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     na.a_off[1] = lb + m->oAk;
     na.a_off[2] = lb + m->oAv;
     na.rank = c.rank;
-    na.U = m->U;
+    na.U = U;
     na.u_col = 0;  // q, k, v at U16 columns 0, 16, 32
     na.pc = pc;
     if ((rc = launch_norm_lora(na, m->bf16, m->st))) return rc;
@@ -284,32 +232,34 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     ep.head_dim = c.head_dim;
     ep.seq_len = c.seq;
     const char* wqkv = static_cast<const char*>(m->wqkv) + (size_t)l * QKV * D * e;
-    if ((rc = gemm(m, m->qkv_bn, EPI_QKV_ROPE, m->xn, D, wqkv, D, R, QKV, D, m->qkv, QKV, ep))) return rc;
+    if ((rc = gemm(m, m->qkv_bn, EPI_QKV_ROPE, xn, D, wqkv, D, R, QKV, D, qkv, QKV, ep, U))) return rc;
     // attention
     AttnArgs aa;
-    aa.qkv = m->qkv;
+    std::memset(&aa, 0, sizeof(aa));
+    aa.qkv = qkv;
     aa.ld_qkv = QKV;
     aa.q_off = 0;
     aa.k_off = QD;
     aa.v_off = QD + KVD;
-    aa.out = m->attn;
+    aa.out = attn;
     aa.ld_out = QD;
     aa.seq = c.seq;
     aa.heads = c.heads;
     aa.kv_heads = c.kv_heads;
     aa.ngroups = G;
+    aa.lse = sv ? sv->lse + (size_t)l * R * c.heads : nullptr;
     if ((rc = launch_attention(aa, m->bf16, m->st))) return rc;
     // LoRA-down of the attention output for Wo
     NormLoraArgs nb;
     std::memset(&nb, 0, sizeof(nb));
-    nb.in = m->attn;
+    nb.in = attn;
     nb.rows = R;
     nb.dim = QD;
     nb.norm = 0;
     nb.n_a = 1;
     nb.a_off[0] = lb + m->oAo;
     nb.rank = c.rank;
-    nb.U = m->U;
+    nb.U = U;
     nb.u_col = 48;  // o at U16 column 48
     nb.pc = pc;
     if ((rc = launch_norm_lora(nb, m->bf16, m->st))) return rc;
@@ -327,8 +277,9 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     eo.lora.seg_boff[0] = lb + m->oBo;
     eo.lora.seg_ucol[0] = 48;
     const char* wo = static_cast<const char*>(m->wo) + (size_t)l * D * QD * e;
-    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->attn, QD, wo, QD, R, D, QD, m->x, D, eo)))
-      return rc;
+    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, attn, QD, wo, QD, R, D, QD, m->x, D, eo, U))) return rc;
+    if (sv) B2P_CHECK_CUDA(cudaMemcpyAsync(slab(sv->x_mid, l, D * 4), m->x, (size_t)R * D * 4,
+                                           cudaMemcpyDeviceToDevice, m->st));
     // RMSNorm(rms_ffn)
     NormLoraArgs nf;
     std::memset(&nf, 0, sizeof(nf));
@@ -347,7 +298,13 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
     es.M = R;
     es.N = 2 * H;
     const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
-    if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, m->hbuf, H, es))) return rc;
+    if (sv) {
+      void* h13 = slab(sv->h13, l, (size_t)2 * H * e);
+      if ((rc = gemm(m, 256, EPI_H16, m->xn, D, w13, D, R, 2 * H, D, h13, 2 * H, es))) return rc;
+      if ((rc = launch_swiglu_gate(h13, R, H, m->hbuf, m->bf16, m->st))) return rc;
+    } else {
+      if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, m->hbuf, H, es))) return rc;
+    }
     // x += alpha * (h · W2^T)
     EpiParams e2;
     std::memset(&e2, 0, sizeof(e2));
@@ -359,10 +316,12 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
       return rc;
   }
   // final RMSNorm + lm-head with fused cross-entropy partials
+  if (sv) B2P_CHECK_CUDA(cudaMemcpyAsync(sv->x_final, m->x, (size_t)R * D * 4, cudaMemcpyDeviceToDevice, m->st));
+  void* xnf = sv ? sv->xn_final : m->xn;
   NormLoraArgs nl;
   std::memset(&nl, 0, sizeof(nl));
   nl.in = m->x;
-  nl.xn = m->xn;
+  nl.xn = xnf;
   nl.rows = R;
   nl.dim = D;
   nl.norm = 1;
@@ -378,8 +337,9 @@ int run_forward(b2p_model* m, int G, const int32_t* tok) {
   ec.ce_part = m->ce_part;
   ec.ce_tgt = m->ce_tgt;
   ec.n_tiles_n = ntiles;
-  if ((rc = gemm(m, 256, EPI_CE, m->xn, D, m->cembed, D, R, m->cv, D, nullptr, 0, ec))) return rc;
-  return launch_ce_reduce(m->ce_part, 2 * ntiles, m->ce_tgt, R, c.seq, m->row_loss, m->group_loss, m->st);
+  if ((rc = gemm(m, 256, EPI_CE, xnf, D, m->cembed, D, R, m->cv, D, nullptr, 0, ec))) return rc;
+  return launch_ce_reduce(m->ce_part, 2 * ntiles, m->ce_tgt, R, c.seq, m->row_loss, m->group_loss, m->st,
+                          sv ? sv->row_lse : nullptr);
 }
 
 __global__ void expand_targets_kernel(const int32_t* seq_tgt, const int* group_seq, int seq, int rows, int cv,
@@ -531,6 +491,28 @@ int copy_losses(b2p_model* m, float* out, int n) {
 
 }  // namespace
 
+namespace b2p {
+
+size_t model_esz(const b2p_model* m) { return esz(m); }
+int model_ready(const b2p_model* m) { return ready(m); }
+int model_stage_tokens(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq) {
+  return stage_tokens(m, tokens, ctargets, n_seq);
+}
+int model_stage_groups(b2p_model* m, int n_seq, const std::vector<VariantInfo>& vars, const int32_t* d_targets) {
+  return stage_groups(m, n_seq, vars, d_targets);
+}
+PerturbCtx model_pctx(const b2p_model* m) { return pctx(m); }
+LoraEpi model_lora_epi(const b2p_model* m) { return lora_epi(m); }
+int model_gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+               void* out, int ldo, const void* u16, const EpiParams& ep) {
+  return gemm(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, ep, u16);
+}
+int model_run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv) {
+  return run_forward(m, G, tok, sv);
+}
+
+}  // namespace b2p
+
 extern "C" {
 
 b2p_model* b2p_model_create(const b2p_model_config* cfg) {
@@ -657,6 +639,7 @@ int b2p_model_set_layer(b2p_model* m, int layer, const float* Wq, const float* W
   rc = upload16(m, static_cast<char*>(m->w2) + (size_t)layer * D * H * e, W2, (size_t)D * H);
   if (rc) return rc;
   m->layer_set[layer] = 1;
+  m->weights_version++;
   return B2P_OK;
 }
 
@@ -678,6 +661,7 @@ int b2p_model_set_embedding(b2p_model* m, const float* embed, const int32_t* com
   int rc = upload16(m, m->cembed, ce.data(), ce.size());
   if (rc) return rc;
   m->embed_set = true;
+  m->weights_version++;
   return B2P_OK;
 }
 
@@ -847,6 +831,10 @@ int b2p_model_set_option(b2p_model* m, int option, int value) {
   switch (option) {
     case B2P_OPT_PAIR_GEMM:
       m->use_pair = value != 0;
+      return B2P_OK;
+    case B2P_OPT_GRAD_SCALE_LOG2:
+      B2P_REQUIRE(value >= -30 && value <= 30, "gradient scale exponent %d out of range [-30, 30]", value);
+      m->grad_scale_log2 = value;
       return B2P_OK;
     default:
       set_error("unknown model option %d", option);

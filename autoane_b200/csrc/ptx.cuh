@@ -21,6 +21,7 @@ enum DevErr : uint32_t {
   DEV_TIMEOUT_EPILOGUE = 3,
   DEV_TIMEOUT_DRAIN = 4,
   DEV_BAD_ARGS = 5,
+  DEV_NONFINITE_GRAD = 6,
 };
 
 // Time budget for one mbarrier wait, in nanoseconds of %globaltimer. Every

@@ -16,6 +16,7 @@ import numpy as np
 from . import _lib
 
 F16, BF16 = 0, 1
+OPT_PAIR_GEMM, OPT_GRAD_SCALE_LOG2 = 1, 2
 
 
 @dataclass
@@ -157,6 +158,51 @@ class Model:
         sd = np.ascontiguousarray(seeds, np.uint64)
         sc = np.ascontiguousarray(scales, np.float32)
         _lib.call("b2p_model_perturb", self.h, _u64(sd), _fp(sc), len(sd))
+
+    # ---- backprop-LoRA (P16) ----
+    def p16_grad(self, tokens, ctargets):
+        """Loss and gradient (trainable layout) of n_seq sequences, parameters unchanged."""
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        n_seq = tok.shape[0] if tok.ndim == 2 else 1
+        loss = C.c_float()
+        grad = np.empty(self.P, np.float32)
+        _lib.call("b2p_p16_grad", self.h, _u16(tok), _u16(tgt), n_seq, C.byref(loss), grad.ctypes.data)
+        return loss.value, grad
+
+    def p16_grad_device(self, d_tokens: int, d_targets: int, n_seq: int, d_loss: int = 0):
+        _lib.call("b2p_p16_grad_device", self.h, d_tokens, d_targets, n_seq, d_loss or None)
+
+    def grad_ptr(self) -> int:
+        return int(self._lib.b2p_model_grad(self.h) or 0)
+
+    def adam_step(self, lr: float, b1: float = 0.9, b2: float = 0.95, eps: float = 1e-8, wd: float = 0.0):
+        _lib.call("b2p_adam_step", self.h, lr, b1, b2, eps, wd)
+
+    def adam_state(self):
+        t = C.c_int()
+        m = np.empty(self.P, np.float32)
+        v = np.empty(self.P, np.float32)
+        _lib.call("b2p_adam_state", self.h, 0, C.byref(t), m.ctypes.data, v.ctypes.data)
+        return t.value, m, v
+
+    def set_adam_state(self, t: int, m=None, v=None):
+        tt = C.c_int(t)
+        mm = None if m is None else np.ascontiguousarray(m, np.float32)
+        vv = None if v is None else np.ascontiguousarray(v, np.float32)
+        _lib.call("b2p_adam_state", self.h, 1, C.byref(tt), None if mm is None else mm.ctypes.data,
+                  None if vv is None else vv.ctypes.data)
+
+    def p16_step(self, tokens, ctargets, lr: float) -> float:
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        n_seq = tok.shape[0] if tok.ndim == 2 else 1
+        loss = C.c_float()
+        _lib.call("b2p_p16_step", self.h, _u16(tok), _u16(tgt), n_seq, lr, C.byref(loss))
+        return loss.value
+
+    def set_option(self, option: int, value: int):
+        _lib.call("b2p_model_set_option", self.h, option, value)
 
     def sign_masks(self, seeds) -> np.ndarray:
         sd = np.ascontiguousarray(seeds, np.uint64)

@@ -197,7 +197,54 @@ long long b2p_launch_count(void);
  * applies; 0 forces the single-CTA engine (128-row tiles). Same results either
  * way up to fp32 summation order. */
 #define B2P_OPT_PAIR_GEMM 1
+/* B2P_OPT_GRAD_SCALE_LOG2 (default 0): the backprop-LoRA backward stores
+ * dlogits as 2^value * (softmax - onehot) in the 16-bit compute type; raise it
+ * if gradients underflow, lower it if they overflow (a non-finite gradient
+ * makes the optimizer step a no-op and the call return B2P_ERR_DEVICE). */
+#define B2P_OPT_GRAD_SCALE_LOG2 2
 int b2p_model_set_option(b2p_model* m, int option, int value);
+
+/* ======================================================================
+ * Backprop-LoRA training (the reference's P16 mode, train_mezo.m:1961-2136):
+ * forward with activation saves, backward through the whole network
+ * (bp_lora_backward, training/backprop_lora.h:147-288) with gradients for the
+ * LoRA A/B and RMSNorm weights only, then Adam (cpu_ops.h:62-104).
+ *
+ * The adapters are applied split on frozen base weights, as the conv-fused
+ * P16 forward does; the backward propagates through W + B·A. The loss of
+ * n_seq sequences is the mean of their per-token mean cross-entropies; the
+ * gradient is d(loss)/d(theta) in the layout of b2p_model_set_trainable.
+ * ====================================================================== */
+
+/* Forward + backward of n_seq sequences (host tokens / compact targets,
+ * [n_seq][seq] uint16). `loss` (1 float) and `grad` (trainable-count floats,
+ * host or device) may be NULL. Synchronous. */
+int b2p_p16_grad(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float* loss,
+                 float* grad);
+
+/* Same on device int32 tokens/targets, asynchronous on the model stream; the
+ * loss goes to the device float d_loss (may be NULL). */
+int b2p_p16_grad_device(b2p_model* m, const int32_t* d_tokens, const int32_t* d_targets, int n_seq, float* d_loss);
+
+/* Device pointer of the gradient buffer the last b2p_p16_grad* call wrote
+ * (fp32, trainable-count elements), NULL before the first call. Data-parallel
+ * callers all-reduce it in place (then divide by the rank count) before
+ * b2p_adam_step. */
+void* b2p_model_grad(b2p_model* m);
+
+/* One Adam step on the trainable parameters with the gradient buffer
+ * (adam_update, cpu_ops.h:62-104; per-element operation order of the
+ * reference; the step counter t starts at 1). Asynchronous on the model
+ * stream; a non-finite gradient skips the step and sets the device status. */
+int b2p_adam_step(b2p_model* m, float lr, float b1, float b2, float eps, float wd);
+
+/* Read (set = 0) or write (set = 1) the Adam step count and moment vectors
+ * (trainable-count floats each, host or device; NULL skips a vector). */
+int b2p_adam_state(b2p_model* m, int set, int* t, float* mom, float* vel);
+
+/* One full step as train_mezo.m:1982-2117: b2p_p16_grad, then Adam with
+ * b1 0.9, b2 0.95, eps 1e-8, no weight decay at learning rate lr. */
+int b2p_p16_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float lr, float* loss);
 
 /* ======================================================================
  * Kern-level boundary: one compiled operator with baked weights and

@@ -375,3 +375,334 @@ void or_mezo_step(const or_model* m, float* theta, const uint16_t* tokens, const
   if (loss_minus) *loss_minus = lm;
   if (proj_grad) *proj_grad = g;
 }
+
+/* ================= backprop-LoRA (P16) ================= */
+
+/* rmsnorm_bwd (cpu_ops.h:24-60): dx = rrms (w dy - x dot rrms^2/d); dw += Σ_s dy x rrms */
+void or_rmsnorm_bwd(float* dx, float* dw, const float* dy, const float* x, const float* w, int d, int S) {
+  float* ss = (float*)calloc((size_t)S, sizeof(float));
+  float* rrms = (float*)xmalloc(sizeof(float) * (size_t)S);
+  float* dot = (float*)calloc((size_t)S, sizeof(float));
+  for (int i = 0; i < d; i++)
+    for (int t = 0; t < S; t++) {
+      const float sq = x[(size_t)i * S + t] * x[(size_t)i * S + t];
+      ss[t] = sq + ss[t];
+    }
+  const float invd = 1.0f / d, eps = 1e-5f;
+  for (int t = 0; t < S; t++) {
+    const float m = ss[t] * invd;
+    rrms[t] = 1.0f / sqrtf(m + eps);
+  }
+  for (int i = 0; i < d; i++)
+    for (int t = 0; t < S; t++) {
+      const float p = dy[(size_t)i * S + t] * x[(size_t)i * S + t];
+      const float q = p * w[i];
+      dot[t] = q + dot[t];
+    }
+  for (int t = 0; t < S; t++) {
+    const float r2 = rrms[t] * rrms[t];
+    const float r2d = r2 * invd;
+    dot[t] = dot[t] * r2d;
+  }
+  for (int i = 0; i < d; i++) {
+    float acc = 0.f;
+    for (int t = 0; t < S; t++) {
+      const size_t k = (size_t)i * S + t;
+      const float xd = x[k] * dot[t];
+      const float wd = dy[k] * w[i];
+      const float v = wd - xd;
+      dx[k] = v * rrms[t];
+      const float g = dy[k] * x[k];
+      acc += g * rrms[t];
+    }
+    dw[i] += acc;
+  }
+  free(ss);
+  free(rrms);
+  free(dot);
+}
+
+/* rope_backward_inplace (cpu_ops.h:377-393): rotate pairs by -angle */
+void or_rope_backward(float* dx, int seq, int dim, int hd, float theta) {
+  const int nheads = dim / hd;
+  for (int h = 0; h < nheads; h++)
+    for (int i = 0; i < hd / 2; i++) {
+      const float freq = 1.0f / powf(theta, 2.0f * i / (float)hd);
+      for (int p = 0; p < seq; p++) {
+        const float ang = p * freq;
+        const float c = cosf(ang), s = sinf(ang);
+        const size_t i0 = (size_t)(h * hd + 2 * i) * seq + p;
+        const size_t i1 = (size_t)(h * hd + 2 * i + 1) * seq + p;
+        const float v0 = dx[i0], v1 = dx[i1];
+        dx[i0] = v0 * c + v1 * s;
+        dx[i1] = -v0 * s + v1 * c;
+      }
+    }
+}
+
+/* cpu_sdpa_backward (cpu_ops.h:213-290): recompute causal softmax P per head,
+ * dV = dA·P, dP = dAᵀ·V, dS = (dP - rowsum(dP∘P))∘P/√hd, dQ = K·dSᵀ, dK = Q·dS.
+ * Inputs at HEADS (K, V already tiled); outputs at HEADS. */
+void or_sdpa_backward(const float* Q, const float* Kt, const float* Vt, const float* da, float* dq, float* dk,
+                      float* dv, int heads, int hd, int seq) {
+  const float scale = 1.0f / sqrtf((float)hd);
+  float* P = (float*)xmalloc(sizeof(float) * (size_t)seq * seq);
+  float* dS = (float*)xmalloc(sizeof(float) * (size_t)seq * seq);
+  for (int h = 0; h < heads; h++) {
+    const size_t o = (size_t)h * hd * seq;
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, seq, seq, hd, scale, Q + o, seq, Kt + o, seq, 0.0f, P, seq);
+    for (int s = 0; s < seq; s++) {
+      float* row = P + (size_t)s * seq;
+      for (int j = s + 1; j < seq; j++) row[j] = -1e9f;
+      float maxv = -1e30f;
+      for (int j = 0; j <= s; j++) maxv = fmaxf(maxv, row[j]);
+      float sum = 0;
+      for (int j = 0; j <= s; j++) {
+        row[j] = expf(row[j] - maxv);
+        sum += row[j];
+      }
+      const float inv = 1.0f / (sum + 1e-10f);
+      for (int j = 0; j <= s; j++) row[j] *= inv;
+      for (int j = s + 1; j < seq; j++) row[j] = 0.0f;
+    }
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrNoTrans, hd, seq, seq, 1.0f, da + o, seq, P, seq, 0.0f, dv + o, seq);
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, seq, seq, hd, 1.0f, da + o, seq, Vt + o, seq, 0.0f, dS, seq);
+    for (int s = 0; s < seq; s++) {
+      float* dp = dS + (size_t)s * seq;
+      const float* pr = P + (size_t)s * seq;
+      float dot = 0;
+      for (int j = 0; j < seq; j++) dot += dp[j] * pr[j];
+      for (int j = 0; j < seq; j++) dp[j] = (dp[j] - dot) * pr[j] * scale;
+    }
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, hd, seq, seq, 1.0f, Kt + o, seq, dS, seq, 0.0f, dq + o, seq);
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrNoTrans, hd, seq, seq, 1.0f, Q + o, seq, dS, seq, 0.0f, dk + o, seq);
+  }
+  free(P);
+  free(dS);
+}
+
+/* gqa_reduce_kv (training/io.h:449-459): sum the query heads sharing a KV head */
+static void gqa_reduce(float* out, const float* in, int kv_heads, int ratio, int hd, int seq) {
+  memset(out, 0, sizeof(float) * (size_t)kv_heads * hd * seq);
+  for (int kv = 0; kv < kv_heads; kv++)
+    for (int r = 0; r < ratio; r++) {
+      const float* src = in + (size_t)(kv * ratio + r) * hd * seq;
+      float* dst = out + (size_t)kv * hd * seq;
+      for (size_t i = 0; i < (size_t)hd * seq; i++) dst[i] = src[i] + dst[i];
+    }
+}
+
+/* W_eff = W + B·A (lora_merge_weight, training/config.h:278-283) */
+static float* merged(const float* W, const float* B, const float* A, int out_dim, int rank, int in_dim) {
+  float* M = (float*)xmalloc(sizeof(float) * (size_t)out_dim * in_dim);
+  memcpy(M, W, sizeof(float) * (size_t)out_dim * in_dim);
+  cblas_sgemm(OrRowMajor, OrNoTrans, OrNoTrans, out_dim, in_dim, rank, 1.0f, B, rank, A, in_dim, 1.0f, M, in_dim);
+  return M;
+}
+
+/* dB += dW·Aᵀ ; dA += Bᵀ·dW (lora_grad_project, training/config.h:286-292) */
+static void grad_project(float* dA, float* dB, const float* dW, const float* A, const float* B, int out_dim, int rank,
+                         int in_dim) {
+  cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, out_dim, rank, in_dim, 1.0f, dW, in_dim, A, in_dim, 1.0f, dB, rank);
+  cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, rank, in_dim, out_dim, 1.0f, B, rank, dW, in_dim, 1.0f, dA, in_dim);
+}
+
+/* P16 step body without the optimizer (train_mezo.m:1982-2087 with the conv-fused
+ * forward: frozen base + split LoRA; then bp_lora_backward through W + B·A).
+ * grad (theta layout) is overwritten; returns the loss. */
+float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
+                  float* grad) {
+  const int D = m->dim, H = m->hidden, S = m->seq, QD = m->heads * m->hd, KVD = m->kv_heads * m->hd;
+  const int r = m->rank, NL = m->nlayers, CV = m->cv, ratio = m->heads / m->kv_heads;
+  const or_layout L = or_lora_layout(NL, D, QD, KVD, r);
+  const size_t DS = (size_t)D * S, QS = (size_t)QD * S, KS = (size_t)KVD * S, HS = (size_t)H * S;
+  /* per-layer saves (BP_LayerActs, backprop_lora.h:15-27) */
+  float* x_pre = (float*)xmalloc(sizeof(float) * DS * NL);
+  float* xnorm = (float*)xmalloc(sizeof(float) * DS * NL);
+  float* Qs = (float*)xmalloc(sizeof(float) * QS * NL);
+  float* Ks = (float*)xmalloc(sizeof(float) * KS * NL);
+  float* Vs = (float*)xmalloc(sizeof(float) * KS * NL);
+  float* att = (float*)xmalloc(sizeof(float) * QS * NL);
+  float* x2 = (float*)xmalloc(sizeof(float) * DS * NL);
+  float* h1 = (float*)xmalloc(sizeof(float) * HS * NL);
+  float* h3 = (float*)xmalloc(sizeof(float) * HS * NL);
+  float* x = (float*)xmalloc(sizeof(float) * DS);
+  float* xn = (float*)xmalloc(sizeof(float) * DS);
+  float* Q = (float*)xmalloc(sizeof(float) * QS);
+  float* K = (float*)xmalloc(sizeof(float) * KS);
+  float* Kt = (float*)xmalloc(sizeof(float) * QS);
+  float* Vt = (float*)xmalloc(sizeof(float) * QS);
+  float* o = (float*)xmalloc(sizeof(float) * DS);
+  float* g = (float*)xmalloc(sizeof(float) * HS);
+  float* tmp = (float*)xmalloc(sizeof(float) * (size_t)r * S);
+  float* logits = (float*)xmalloc(sizeof(float) * (size_t)S * CV);
+  for (int t = 0; t < S; t++) {
+    const int tok = tokens[t];
+    if (tok < 0 || tok >= m->vocab) {
+      fprintf(stderr, "oracle: token[%d]=%d out of range\n", t, tok);
+      abort();
+    }
+    for (int d = 0; d < D; d++) x[(size_t)d * S + t] = m->embed[(size_t)tok * D + d];
+  }
+  for (int l = 0; l < NL; l++) {
+    const float* th = theta + (size_t)l * L.layer_size;
+    memcpy(x_pre + DS * l, x, sizeof(float) * DS);
+    or_rmsnorm(xnorm + DS * l, x, th + L.rms_att, D, S);
+    const float* xnl = xnorm + DS * l;
+    float *Ql = Qs + QS * l, *Kl = Ks + KS * l, *Vl = Vs + KS * l;
+    or_sgemm_nn(QD, S, D, m->Wq[l], xnl, Ql, 0.0f);
+    or_sgemm_nn(KVD, S, D, m->Wk[l], xnl, Kl, 0.0f);
+    or_sgemm_nn(KVD, S, D, m->Wv[l], xnl, Vl, 0.0f);
+    or_lora_addmm(Ql, th + L.Aq, th + L.Bq, xnl, tmp, QD, r, D, S);
+    or_lora_addmm(Kl, th + L.Ak, th + L.Bk, xnl, tmp, KVD, r, D, S);
+    or_lora_addmm(Vl, th + L.Av, th + L.Bv, xnl, tmp, KVD, r, D, S);
+    memcpy(Q, Ql, sizeof(float) * QS);
+    memcpy(K, Kl, sizeof(float) * KS);
+    or_rope_forward(Q, S, QD, m->hd, m->rope_theta);
+    or_rope_forward(K, S, KVD, m->hd, m->rope_theta);
+    gqa_tile(Kt, K, m->kv_heads, ratio, m->hd, S);
+    gqa_tile(Vt, Vl, m->kv_heads, ratio, m->hd, S);
+    or_sdpa_forward(Q, Kt, Vt, att + QS * l, m->heads, m->hd, S);
+    or_sgemm_nn(D, S, QD, m->Wo[l], att + QS * l, o, 0.0f);
+    or_lora_addmm(o, th + L.Ao, th + L.Bo, att + QS * l, tmp, D, r, QD, S);
+    resid_add(x, o, m->res_alpha, DS);
+    memcpy(x2 + DS * l, x, sizeof(float) * DS);
+    or_rmsnorm(xn, x, th + L.rms_ffn, D, S);
+    or_sgemm_nn(H, S, D, m->W1[l], xn, h1 + HS * l, 0.0f);
+    or_sgemm_nn(H, S, D, m->W3[l], xn, h3 + HS * l, 0.0f);
+    for (size_t i = 0; i < HS; i++) {
+      const float sv = h1[HS * l + i] / (1.0f + expf(-h1[HS * l + i]));
+      g[i] = sv * h3[HS * l + i];
+    }
+    or_sgemm_nn(D, S, H, m->W2[l], g, o, 0.0f);
+    resid_add(x, o, m->res_alpha, DS);
+  }
+  /* x is x_pre_final; logits and dlogits (cross_entropy_loss, cpu_ops.h:108-133) */
+  or_rmsnorm(xn, x, theta + L.rms_final, D, S);
+  cblas_sgemm(OrRowMajor, OrTrans, OrTrans, S, CV, D, 1.0f, xn, S, m->cembed, D, 0.0f, logits, CV);
+  float total = 0;
+  const float invS = 1.0f / S;
+  for (int t = 0; t < S; t++) {
+    float* row = logits + (size_t)t * CV;
+    float maxv = row[0];
+    for (int v = 1; v < CV; v++) maxv = fmaxf(maxv, row[v]);
+    const float tgt_logit = row[ctargets[t]];
+    float sum = 0;
+    for (int v = 0; v < CV; v++) {
+      row[v] = expf(row[v] + (-maxv));
+      sum += row[v];
+    }
+    const float inv = 1.0f / sum;
+    for (int v = 0; v < CV; v++) row[v] *= inv;
+    total += -(tgt_logit - maxv) + logf(sum);
+    row[ctargets[t]] -= 1.0f;
+    for (int v = 0; v < CV; v++) row[v] *= invS;
+  }
+  const float loss = total / S;
+  /* ---- backward (bp_lora_backward, backprop_lora.h:147-288) ---- */
+  memset(grad, 0, sizeof(float) * (size_t)L.total);
+  float* dy = (float*)xmalloc(sizeof(float) * DS);
+  float* dxr = (float*)xmalloc(sizeof(float) * DS);
+  float* dx2 = (float*)xmalloc(sizeof(float) * DS);
+  float* dx2s = (float*)xmalloc(sizeof(float) * DS);
+  float* dsl = (float*)xmalloc(sizeof(float) * HS);
+  float* dh1 = (float*)xmalloc(sizeof(float) * HS);
+  float* dh3 = (float*)xmalloc(sizeof(float) * HS);
+  float* da = (float*)xmalloc(sizeof(float) * QS);
+  float* dqf = (float*)xmalloc(sizeof(float) * QS);
+  float* dkf = (float*)xmalloc(sizeof(float) * QS);
+  float* dvf = (float*)xmalloc(sizeof(float) * QS);
+  float* dk = (float*)xmalloc(sizeof(float) * KS);
+  float* dv = (float*)xmalloc(sizeof(float) * KS);
+  float* dW = (float*)xmalloc(sizeof(float) * (size_t)(QD > D ? QD : D) * (QD > D ? QD : D));
+  cblas_sgemm(OrRowMajor, OrTrans, OrTrans, D, S, CV, 1.0f, m->cembed, D, logits, CV, 0.0f, dy, S);
+  memset(dxr, 0, sizeof(float) * DS);
+  or_rmsnorm_bwd(dxr, grad + L.rms_final, dy, x, theta + L.rms_final, D, S);
+  memcpy(dy, dxr, sizeof(float) * DS);
+  const float alpha = m->res_alpha;
+  for (int l = NL - 1; l >= 0; l--) {
+    const float* th = theta + (size_t)l * L.layer_size;
+    float* gl = grad + (size_t)l * L.layer_size;
+    for (size_t i = 0; i < DS; i++) dx2s[i] = dy[i] * alpha; /* dffn */
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, H, S, D, 1.0f, m->W2[l], H, dx2s, S, 0.0f, dsl, S);
+    for (size_t i = 0; i < HS; i++) {
+      const float a1 = h1[HS * l + i], a3 = h3[HS * l + i];
+      const float sig = 1.0f / (1.0f + expf(-a1));
+      dh3[i] = dsl[i] * (a1 * sig);
+      dh1[i] = (dsl[i] * a3) * (sig * (1.0f + a1 * (1.0f - sig)));
+    }
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, H, 1.0f, m->W1[l], D, dh1, S, 0.0f, dxr, S);
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, H, 1.0f, m->W3[l], D, dh3, S, 1.0f, dxr, S);
+    memset(dx2, 0, sizeof(float) * DS);
+    or_rmsnorm_bwd(dx2, gl + L.rms_ffn, dxr, x2 + DS * l, th + L.rms_ffn, D, S);
+    for (size_t i = 0; i < DS; i++) dx2[i] += dy[i];
+    for (size_t i = 0; i < DS; i++) dx2s[i] = dx2[i] * alpha;
+    float* Wo_e = merged(m->Wo[l], th + L.Bo, th + L.Ao, D, r, QD);
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, QD, S, D, 1.0f, Wo_e, QD, dx2s, S, 0.0f, da, S);
+    free(Wo_e);
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, D, QD, S, 1.0f, dx2s, S, att + QS * l, S, 0.0f, dW, QD);
+    grad_project(gl + L.Ao, gl + L.Bo, dW, th + L.Ao, th + L.Bo, D, r, QD);
+    memcpy(Q, Qs + QS * l, sizeof(float) * QS);
+    memcpy(K, Ks + KS * l, sizeof(float) * KS);
+    or_rope_forward(Q, S, QD, m->hd, m->rope_theta);
+    or_rope_forward(K, S, KVD, m->hd, m->rope_theta);
+    gqa_tile(Kt, K, m->kv_heads, ratio, m->hd, S);
+    gqa_tile(Vt, Vs + KS * l, m->kv_heads, ratio, m->hd, S);
+    or_sdpa_backward(Q, Kt, Vt, da, dqf, dkf, dvf, m->heads, m->hd, S);
+    gqa_reduce(dk, dkf, m->kv_heads, ratio, m->hd, S);
+    gqa_reduce(dv, dvf, m->kv_heads, ratio, m->hd, S);
+    or_rope_backward(dqf, S, QD, m->hd, m->rope_theta);
+    or_rope_backward(dk, S, KVD, m->hd, m->rope_theta);
+    const float* xnl = xnorm + DS * l;
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, QD, D, S, 1.0f, dqf, S, xnl, S, 0.0f, dW, D);
+    grad_project(gl + L.Aq, gl + L.Bq, dW, th + L.Aq, th + L.Bq, QD, r, D);
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, KVD, D, S, 1.0f, dk, S, xnl, S, 0.0f, dW, D);
+    grad_project(gl + L.Ak, gl + L.Bk, dW, th + L.Ak, th + L.Bk, KVD, r, D);
+    cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, KVD, D, S, 1.0f, dv, S, xnl, S, 0.0f, dW, D);
+    grad_project(gl + L.Av, gl + L.Bv, dW, th + L.Av, th + L.Bv, KVD, r, D);
+    float* Wq_e = merged(m->Wq[l], th + L.Bq, th + L.Aq, QD, r, D);
+    float* Wk_e = merged(m->Wk[l], th + L.Bk, th + L.Ak, KVD, r, D);
+    float* Wv_e = merged(m->Wv[l], th + L.Bv, th + L.Av, KVD, r, D);
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, QD, 1.0f, Wq_e, D, dqf, S, 0.0f, dxr, S);
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, KVD, 1.0f, Wk_e, D, dk, S, 1.0f, dxr, S);
+    cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, KVD, 1.0f, Wv_e, D, dv, S, 1.0f, dxr, S);
+    free(Wq_e);
+    free(Wk_e);
+    free(Wv_e);
+    memset(dy, 0, sizeof(float) * DS);
+    or_rmsnorm_bwd(dy, gl + L.rms_att, dxr, x_pre + DS * l, th + L.rms_att, D, S);
+    for (size_t i = 0; i < DS; i++) dy[i] = dy[i] + dx2[i];
+  }
+  free(x_pre); free(xnorm); free(Qs); free(Ks); free(Vs); free(att); free(x2); free(h1); free(h3);
+  free(x); free(xn); free(Q); free(K); free(Kt); free(Vt); free(o); free(g); free(tmp); free(logits);
+  free(dy); free(dxr); free(dx2); free(dx2s); free(dsl); free(dh1); free(dh3); free(da); free(dqf); free(dkf);
+  free(dvf); free(dk); free(dv); free(dW);
+  return loss;
+}
+
+/* adam_update (cpu_ops.h:62-104), one rounding per vectorised operation */
+void or_adam(float* w, const float* g, float* m, float* v, size_t n, int t, float lr, float b1, float b2, float eps,
+             float wd) {
+  const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
+  const float bc1 = 1.0f - powf(b1, (float)t), bc2 = 1.0f - powf(b2, (float)t);
+  const float ibc1 = 1.0f / bc1, ibc2 = 1.0f / bc2, neg_lr = -lr;
+  for (size_t i = 0; i < n; i++) {
+    const float m1 = m[i] * b1;
+    const float gm = g[i] * omb1;
+    m[i] = gm + m1;
+    const float g2 = g[i] * g[i];
+    const float v1 = v[i] * b2;
+    const float gv = g2 * omb2;
+    v[i] = gv + v1;
+    const float mh = m[i] * ibc1;
+    const float vh = v[i] * ibc2;
+    const float den = sqrtf(vh) + eps;
+    float u = mh / den;
+    if (wd > 0.0f) {
+      const float ww = w[i] * wd;
+      u = ww + u;
+    }
+    const float step = u * neg_lr;
+    w[i] = step + w[i];
+  }
+}

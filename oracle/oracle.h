@@ -97,6 +97,19 @@ void or_mezo_step(const or_model* m, float* theta, const uint16_t* tokens, const
 /* BLAS thread count control (OpenBLAS); returns the count in effect. */
 int or_set_threads(int n);
 
+/* ---- backprop-LoRA (P16): train_mezo.m:1982-2117, backprop_lora.h:147-288 ---- */
+void or_rmsnorm_bwd(float* dx, float* dw, const float* dy, const float* x, const float* w, int d, int S); /* :24-60 */
+void or_rope_backward(float* dx, int seq, int dim, int hd, float theta);                               /* :377-393 */
+void or_sdpa_backward(const float* Q, const float* Kt, const float* Vt, const float* da, float* dq, float* dk,
+                      float* dv, int heads, int hd, int seq);                                         /* :213-290 */
+/* Loss and gradient (theta layout, overwritten) of one sequence: forward on frozen
+ * base weights + split LoRA (conv-fused P16), backward through W + B·A. */
+float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
+                  float* grad);
+/* adam_update (cpu_ops.h:62-104) over n elements, step t >= 1 */
+void or_adam(float* w, const float* g, float* m, float* v, size_t n, int t, float lr, float b1, float b2, float eps,
+             float wd);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,10 @@ def lib() -> C.CDLL:
         L.or_cross_entropy.restype = C.c_float
         L.or_cross_entropy.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_uint16), C.c_int, C.c_int]
         L.or_lora_addmm.argtypes = [C.POINTER(C.c_float)] * 5 + [C.c_int] * 4
+        L.or_p16_grad.restype = C.c_float
+        L.or_p16_grad.argtypes = [C.POINTER(_Model), C.POINTER(C.c_float), C.POINTER(C.c_uint16),
+                                  C.POINTER(C.c_uint16), C.POINTER(C.c_float)]
+        L.or_adam.argtypes = [C.POINTER(C.c_float)] * 4 + [C.c_size_t, C.c_int] + [C.c_float] * 5
         L.or_sgemm_nn.argtypes = [C.c_int] * 3 + [C.POINTER(C.c_float)] * 3 + [C.c_float]
         for n in ("or_rmsnorm",):
             getattr(L, n).argtypes = [C.POINTER(C.c_float)] * 3 + [C.c_int, C.c_int]
@@ -222,12 +226,29 @@ class OracleModel:
         return float(lib().or_forward_loss(C.byref(self.m), _f(theta), _u16(tokens), _u16(ctargets),
                                            C.byref(t) if t is not None else None))
 
+    def p16_grad(self, theta: np.ndarray, tokens, ctargets):
+        """(loss, gradient in theta layout) of one sequence (backprop-LoRA, P16)."""
+        grad = np.zeros_like(theta)
+        loss = lib().or_p16_grad(C.byref(self.m), _f(np.ascontiguousarray(theta, np.float32)),
+                                 _u16(np.ascontiguousarray(tokens, np.uint16)),
+                                 _u16(np.ascontiguousarray(ctargets, np.uint16)), _f(grad))
+        return float(loss), grad
+
     def mezo_step(self, theta: np.ndarray, tokens, ctargets, seed: int, eps: float, lr: float):
         lp, lm, g = C.c_float(), C.c_float(), C.c_float()
         lib().or_mezo_step(C.byref(self.m), _f(theta), _u16(np.ascontiguousarray(tokens, np.uint16)),
                            _u16(np.ascontiguousarray(ctargets, np.uint16)), seed, np.float32(eps), np.float32(lr),
                            C.byref(lp), C.byref(lm), C.byref(g))
         return lp.value, lm.value, g.value
+
+
+def adam(w: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray, t: int, lr: float, b1: float = 0.9,
+         b2: float = 0.95, eps: float = 1e-8, wd: float = 0.0) -> None:
+    """adam_update (training/cpu_ops.h:62-104) in place on w, m, v."""
+    for a in (w, g, m, v):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    lib().or_adam(_f(w), _f(g), _f(m), _f(v), w.size, t, np.float32(lr), np.float32(b1), np.float32(b2),
+                  np.float32(eps), np.float32(wd))
 
 
 # ---------------- reference-compiled library ----------------
@@ -239,4 +260,5 @@ def ref_lib(model: str):
     L = C.CDLL(str(p))
     L.ref_cross_entropy.restype = C.c_float
     L.ref_forward_loss.restype = C.c_float
+    L.ref_p16_grad.restype = C.c_float
     return L

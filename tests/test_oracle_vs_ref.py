@@ -86,3 +86,79 @@ def test_forward_loss_matches_reference_code(model, cfg):
                                   tgt.ctypes.data_as(C.POINTER(C.c_uint16)))
     assert abs(loss_o - loss_r) < 1e-5, (loss_o, loss_r)
     assert 7.0 < loss_o < 9.0  # ≈ ln(3000) for a random-init model
+
+
+def _theta_lists(syn, L):
+    lay = syn.layout
+    lora, rms = [], []
+    for l in range(L):
+        base = l * lay.layer_size
+        for off in (lay.Aq, lay.Bq, lay.Ak, lay.Bk, lay.Av, lay.Bv, lay.Ao, lay.Bo):
+            lora.append(syn.theta[base + off:])
+        rms += [syn.theta[base + lay.rms_att:], syn.theta[base + lay.rms_ffn:]]
+    return [np.ascontiguousarray(a) for a in lora], [np.ascontiguousarray(a) for a in rms]
+
+
+@pytest.mark.parametrize("model,cfg", [("autoresearch", M.AUTORESEARCH), ("autoresearch_mha", M.AUTORESEARCH_MHA)])
+def test_p16_gradient_matches_reference_backward(model, cfg):
+    """or_p16_grad against the reference's bp_lora_backward (backprop_lora.h:147-288) compiled in place."""
+    ref = need(model)
+    syn = M.make_model(cfg, n_active=3000, seed=11, b_scale=0.02, rms_jitter=0.05)
+    toks = M.make_tokens(4096, 3000, seed=11)
+    inp, tgt = M.sample_sequence(toks, cfg.seq, syn.full_to_compact, 23)
+    om = O.OracleModel(cfg, syn.weights, syn.embed, syn.cembed)
+    loss_o, grad_o = om.p16_grad(syn.theta, inp, tgt)
+    L, lay, r, D = cfg.nlayers, syn.layout, cfg.rank, cfg.dim
+    keep = []
+
+    def plist(arrs):
+        p = (F * len(arrs))(*[f(a) for a in arrs])
+        keep.append((arrs, p))
+        return p
+
+    lora, rms = _theta_lists(syn, L)
+    sizes = [r * D, cfg.q_dim * r, r * D, cfg.kv_dim * r, r * D, cfg.kv_dim * r, r * cfg.q_dim, D * r]
+    glora = [np.zeros(sizes[k % 8], np.float32) for k in range(8 * L)]
+    grms = [np.zeros(D, np.float32) for _ in range(2 * L)]
+    grf = np.zeros(D, np.float32)
+    rf = np.ascontiguousarray(syn.theta[lay.rms_final:])
+    ref.ref_p16_grad.argtypes = [C.POINTER(F)] * 9 + [F, F, F, C.c_int, C.c_int, C.c_float,
+                                                      C.POINTER(C.c_uint16), C.POINTER(C.c_uint16),
+                                                      C.POINTER(F), C.POINTER(F), F]
+    loss_r = ref.ref_p16_grad(*[plist(syn.weights[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")],
+                              plist(lora), plist(rms), f(rf), f(syn.embed), f(syn.cembed), syn.cembed.shape[0], r,
+                              C.c_float(cfg.res_alpha), inp.ctypes.data_as(C.POINTER(C.c_uint16)),
+                              tgt.ctypes.data_as(C.POINTER(C.c_uint16)), plist(glora), plist(grms), f(grf))
+    assert abs(loss_o - loss_r) < 1e-5, (loss_o, loss_r)
+    grad_r = np.zeros_like(grad_o)
+    offs = (lay.Aq, lay.Bq, lay.Ak, lay.Bk, lay.Av, lay.Bv, lay.Ao, lay.Bo)
+    for l in range(L):
+        base = l * lay.layer_size
+        for k, off in enumerate(offs):
+            grad_r[base + off: base + off + sizes[k]] = glora[8 * l + k]
+        grad_r[base + lay.rms_att: base + lay.rms_att + D] = grms[2 * l]
+        grad_r[base + lay.rms_ffn: base + lay.rms_ffn + D] = grms[2 * l + 1]
+    grad_r[lay.rms_final: lay.rms_final + D] = grf
+    # same fp32 arithmetic through the same BLAS; only summation order differs
+    err = np.abs(grad_o - grad_r).max()
+    assert err <= 1e-4 * np.abs(grad_r).max(), (err, np.abs(grad_r).max())
+    assert np.abs(grad_r).max() > 0
+
+
+def test_adam_matches_reference_bit_exact():
+    ref = need("autoresearch")
+    rng = np.random.default_rng(4)
+    n = 10007
+    w0 = rng.standard_normal(n).astype(np.float32)
+    m0 = (0.01 * rng.standard_normal(n)).astype(np.float32)
+    v0 = (0.001 * rng.random(n)).astype(np.float32)
+    for t in (1, 2, 37):
+        g = (0.1 * rng.standard_normal(n)).astype(np.float32)
+        w1, m1, v1 = w0.copy(), m0.copy(), v0.copy()
+        w2, m2, v2 = w0.copy(), m0.copy(), v0.copy()
+        ref.ref_adam(f(w1), f(g), f(m1), f(v1), C.c_size_t(n), t, C.c_float(3e-4), C.c_float(0.9),
+                     C.c_float(0.95), C.c_float(1e-8), C.c_float(0.0))
+        O.adam(w2, g, m2, v2, t, 3e-4)
+        assert np.array_equal(w1.view(np.uint32), w2.view(np.uint32))
+        assert np.array_equal(m1.view(np.uint32), m2.view(np.uint32))
+        assert np.array_equal(v1.view(np.uint32), v2.view(np.uint32))
