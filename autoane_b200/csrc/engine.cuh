@@ -37,6 +37,8 @@ const char* last_error();
 
 // Count of kernels this library has launched (all devices, all threads).
 void count_launch();
+// Adjust the count by n (kernels recorded into a CUDA graph run once per replay).
+void count_launches(long long n);
 long long launch_count();
 
 #define B2P_POST_LAUNCH()                         \

@@ -154,9 +154,13 @@ int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, 
     B2P_CHECK_CUDA(cudaEventCreate(&e));
     m->ev_pool.push_back(e);
   }
-  B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used], m->st));
+  // inside a stream capture the records must become event-record nodes of the graph
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  B2P_CHECK_CUDA(cudaStreamIsCapturing(m->st, &cap));
+  const unsigned flags = cap == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+  B2P_CHECK_CUDA(cudaEventRecordWithFlags(m->ev_pool[m->ev_used], m->st, flags));
   int rc = gemm_launch(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep);
-  B2P_CHECK_CUDA(cudaEventRecord(m->ev_pool[m->ev_used + 1], m->st));
+  B2P_CHECK_CUDA(cudaEventRecordWithFlags(m->ev_pool[m->ev_used + 1], m->st, flags));
   m->ev_used += 2;
   m->prof_flops.push_back(2.0 * M * (double)N * K);
   return rc;
@@ -805,6 +809,7 @@ int b2p_model_profile(b2p_model* m, int enable) {
   m->prof = enable != 0;
   m->ev_used = 0;
   m->prof_flops.clear();
+  m->prof_epoch++;
   return B2P_OK;
 }
 
@@ -831,6 +836,9 @@ int b2p_model_set_option(b2p_model* m, int option, int value) {
   switch (option) {
     case B2P_OPT_PAIR_GEMM:
       m->use_pair = value != 0;
+      return B2P_OK;
+    case B2P_OPT_GRAPHS:
+      m->graphs = value != 0;
       return B2P_OK;
     case B2P_OPT_GRAD_SCALE_LOG2:
       B2P_REQUIRE(value >= -30 && value <= 30, "gradient scale exponent %d out of range [-30, 30]", value);

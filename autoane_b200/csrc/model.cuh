@@ -86,6 +86,8 @@ struct b2p_model {
   b2p::P16State* p16 = nullptr;
   int grad_scale_log2 = 0;  // B2P_OPT_GRAD_SCALE_LOG2
   int weights_version = 0;  // bumped by every frozen-weight upload
+  int prof_epoch = 0;       // bumped by every b2p_model_profile call
+  bool graphs = true;       // B2P_OPT_GRAPHS
 };
 
 

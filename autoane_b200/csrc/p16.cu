@@ -36,13 +36,15 @@ struct WgradJob {
   long long ldx;
   int ncols;
   int ucol;
-  const void* U;  // [R][64]
+  const void* U;  // [R][ldu]
+  long long ldu;
   float* out;
   int a_layout;
   int pad;
 };
 constexpr int kMaxWgradJobs = 8;
-constexpr int kRmsRows = 64;  // rows per block of the RMSNorm backward
+constexpr int kWgradSplit = 8;  // row chunks per weight gradient (partials summed in chunk order)
+constexpr int kRmsRows = 16;  // rows per block of the RMSNorm backward (2 per warp)
 
 struct P16State {
   int rows = 0;
@@ -52,9 +54,10 @@ struct P16State {
   ForwardSaves sv;
   void* dlogits = nullptr;
   float *dy = nullptr, *dy2 = nullptr, *dxf = nullptr, *dsilu = nullptr;
-  void *d16 = nullptr, *dh13 = nullptr, *da = nullptr, *dqkv = nullptr, *ub_o = nullptr, *ub_qkv = nullptr;
+  void *d16 = nullptr, *dh13 = nullptr, *da = nullptr, *dqkv = nullptr, *ub_o = nullptr;
   float* dvec = nullptr;
   float* rms_part = nullptr;
+  float* wgrad_part = nullptr;
   float* a_oT = nullptr;
   void *bblk_qkv = nullptr, *bblk_o = nullptr;
   float* grad = nullptr;
@@ -63,6 +66,15 @@ struct P16State {
   uint32_t* flag = nullptr;
   WgradJob* d_jobs = nullptr;
   int* d_rms_off = nullptr;
+  int gen = 0;  // bumped whenever a buffer a captured graph points into is reallocated
+  // the captured forward + backward (CUDA graph), replayed while its key matches
+  struct Graph {
+    const void* tok = nullptr;
+    int n_seq = 0, gen = -1, scale_log2 = 0, prof_epoch = -1;
+    bool pair = true;
+    cudaGraphExec_t exec = nullptr;
+    long long launches = 0;
+  } graph;
 };
 
 namespace {
@@ -75,11 +87,11 @@ void free_ptrs(std::initializer_list<void*> ps) {
 void release_rows(P16State* s) {
   const ForwardSaves& v = s->sv;
   free_ptrs({v.x_in, v.x_mid, v.xn, v.U, v.qkv, v.attn, v.lse, v.h13, v.x_final, v.xn_final, v.row_lse, s->dlogits,
-             s->dy, s->dy2, s->dxf, s->dsilu, s->d16, s->dh13, s->da, s->dqkv, s->ub_o, s->ub_qkv, s->dvec,
-             s->rms_part});
+             s->dy, s->dy2, s->dxf, s->dsilu, s->d16, s->dh13, s->da, s->dqkv, s->ub_o, s->dvec,
+             s->rms_part, s->wgrad_part});
   s->sv = ForwardSaves();
-  s->dlogits = s->d16 = s->dh13 = s->da = s->dqkv = s->ub_o = s->ub_qkv = nullptr;
-  s->dy = s->dy2 = s->dxf = s->dsilu = s->dvec = s->rms_part = nullptr;
+  s->dlogits = s->d16 = s->dh13 = s->da = s->dqkv = s->ub_o = nullptr;
+  s->dy = s->dy2 = s->dxf = s->dsilu = s->dvec = s->rms_part = s->wgrad_part = nullptr;
   s->rows = 0;
 }
 
@@ -190,9 +202,8 @@ int swiglu_bwd(const float* dsilu, const void* h13, int rows, int H, void* dh13,
 // RMSNorm backward (rmsnorm_bwd, training/cpu_ops.h:24-60), one warp per row:
 //   rrms = 1/sqrt(sum x^2 / d + 1e-5); dot = sum_i w_i g_i x_i * rrms^2 / d
 //   dx_i = (w_i g_i - x_i dot) * rrms (+ resid_i);  dw_i += g_i x_i rrms
-// g may first receive the LoRA input-gradient sum_p U'_p · A_p (the A^T·(B^T·dY)
-// half of dX through W_eff, train-time form of backprop_lora.h:258-266).
-// dw partials are summed per block of kRmsRows rows into part[block][d].
+// kRmsRows rows per block (2 per warp); the dw partials of a block go to
+// part[block][d] and are summed in block order by rms_part_reduce_kernel.
 // ---------------------------------------------------------------------------
 struct RmsBwdArgs {
   const float* g;
@@ -204,30 +215,17 @@ struct RmsBwdArgs {
   float alpha16;
   float* part;         // [blocks][D]
   int rows;
-  // LoRA input-gradient term
-  int n_a;             // 0 or 3
-  const void* U;       // [rows][64], part p at columns 16p .. 16p + rank
-  const float* A[3];   // [rank][D] each
-  int rank;
 };
 
 template <typename T, int CPL>
 __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
   constexpr int D = CPL * 32;
-  extern __shared__ float smem[];
-  float* s_red = smem;             // [8][D]
-  float* s_a = smem + 8 * D;       // [n_a * rank][D]
+  __shared__ float s_red[8][D];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nA = a.n_a * a.rank;
-  for (int i = threadIdx.x; i < nA * D; i += blockDim.x) {
-    const int p = i / (a.rank * D), rem = i - p * a.rank * D;
-    s_a[i] = a.A[p][rem];
-  }
-  __syncthreads();
   float wv[CPL], acc[CPL];
 #pragma unroll
   for (int k = 0; k < CPL; ++k) {
-    wv[k] = a.w[lane + 32 * k];
+    wv[k] = __ldg(a.w + lane + 32 * k);
     acc[k] = 0.f;
   }
   const float invd = 1.0f / (float)D;
@@ -242,16 +240,6 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
     for (int k = 0; k < CPL; ++k) {
       gv[k] = gr[lane + 32 * k];
       xv[k] = xr[lane + 32 * k];
-    }
-    if (nA) {
-      const T* ur = static_cast<const T*>(a.U) + (long long)row * 64;
-      for (int p = 0; p < a.n_a; ++p)
-        for (int j = 0; j < a.rank; ++j) {
-          const float u = static_cast<float>(ur[16 * p + j]);
-          const float* arow = s_a + (p * a.rank + j) * D;
-#pragma unroll
-          for (int k = 0; k < CPL; ++k) gv[k] += u * arow[lane + 32 * k];
-        }
     }
     float ss = 0.f, dot = 0.f;
 #pragma unroll
@@ -283,12 +271,12 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
     }
   }
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) s_red[warp * D + lane + 32 * k] = acc[k];
+  for (int k = 0; k < CPL; ++k) s_red[warp][lane + 32 * k] = acc[k];
   __syncthreads();
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += s_red[w * D + c];
+    for (int w = 0; w < 8; ++w) s += s_red[w][c];
     a.part[(long long)blockIdx.x * D + c] = s;
   }
 }
@@ -296,25 +284,17 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
 template <typename T>
 int rms_bwd_t(const RmsBwdArgs& a, int D, cudaStream_t st) {
   const int blocks = (a.rows + kRmsRows - 1) / kRmsRows;
-  const size_t smem = sizeof(float) * ((size_t)8 * D + (size_t)a.n_a * a.rank * D);
-  auto go = [&](auto kern) -> int {
-    B2P_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<blocks, 256, smem, st>>>(a);
-    B2P_POST_LAUNCH();
-    return B2P_OK;
-  };
   switch (D) {
-    case 512: return go(rms_bwd_kernel<T, 16>);
-    case 960: return go(rms_bwd_kernel<T, 30>);
-    case 1024: return go(rms_bwd_kernel<T, 32>);
-    case 2048: return go(rms_bwd_kernel<T, 64>);
+    case 512: rms_bwd_kernel<T, 16><<<blocks, 256, 0, st>>>(a); break;
+    case 960: rms_bwd_kernel<T, 30><<<blocks, 256, 0, st>>>(a); break;
+    case 1024: rms_bwd_kernel<T, 32><<<blocks, 256, 0, st>>>(a); break;
+    default: set_error("RMSNorm backward: unsupported width %d", D); return B2P_ERR_UNSUPPORTED;
   }
-  set_error("RMSNorm backward: unsupported width %d", D);
-  return B2P_ERR_UNSUPPORTED;
+  B2P_POST_LAUNCH();
+  return B2P_OK;
 }
 
 int rms_bwd(const RmsBwdArgs& a, int D, bool bf16, cudaStream_t st) {
-  B2P_REQUIRE(a.n_a == 0 || (a.n_a == 3 && a.rank >= 1 && a.rank <= 8), "bad LoRA term");
   return bf16 ? rms_bwd_t<__nv_bfloat16>(a, D, st) : rms_bwd_t<__half>(a, D, st);
 }
 
@@ -332,34 +312,38 @@ __global__ void rms_part_reduce_kernel(const float* __restrict__ part, int nvec,
 
 // ---------------------------------------------------------------------------
 // factored LoRA weight gradients (lora_grad_project, training/config.h:286-292,
-// without forming dW): one block per (job, 64-column tile), all rows.
+// without forming dW): one block per (64-column tile, job, row chunk) writes
+// part[job][chunk][c][j] = sum_{t in chunk} X[t, c] * U[t, j]; a second kernel
+// sums the chunks in order, scales and stores in the A or B layout.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restrict__ jobs, int rows, int rank,
-                                                        float scale) {
+                                                        float* __restrict__ part, int max_cols) {
   __shared__ __align__(16) T s_x[64][64];
   __shared__ float s_u[64][8];
   const WgradJob jb = jobs[blockIdx.y];
   const int c0 = blockIdx.x * 64;
   if (c0 >= jb.ncols) return;
+  const int chunk_rows = (rows + kWgradSplit - 1) / kWgradSplit;
+  const int r_begin = blockIdx.z * chunk_rows, r_end = min(rows, r_begin + chunk_rows);
   const int tid = threadIdx.x;
   const int c = tid & 63, jg = tid >> 6;  // 4 groups of output columns j
   const int jpt = rank / 4;               // 2 for rank 8, 1 for rank 4
   const T* X = static_cast<const T*>(jb.X);
   const T* U = static_cast<const T*>(jb.U);
   float acc0 = 0.f, acc1 = 0.f;
-  for (int t0 = 0; t0 < rows; t0 += 64) {
-    // X tile: 64 rows x 64 columns (8 chunks of 16 B per row); columns past ncols read as 0
+  for (int t0 = r_begin; t0 < r_end; t0 += 64) {
     for (int i = tid; i < 64 * 8; i += 256) {
       const int r = i >> 3, ch = i & 7;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (t0 + r < rows && c0 + ch * 8 < jb.ncols)
+      if (t0 + r < r_end && c0 + ch * 8 < jb.ncols)
         v = *reinterpret_cast<const uint4*>(X + (long long)(t0 + r) * jb.ldx + c0 + ch * 8);
       *reinterpret_cast<uint4*>(&s_x[r][ch * 8]) = v;
     }
     for (int i = tid; i < 64 * 8; i += 256) {
       const int r = i >> 3, j = i & 7;
-      s_u[r][j] = (t0 + r < rows && j < rank) ? static_cast<float>(U[(long long)(t0 + r) * 64 + jb.ucol + j]) : 0.f;
+      s_u[r][j] =
+          (t0 + r < r_end && j < rank) ? static_cast<float>(U[(long long)(t0 + r) * jb.ldu + jb.ucol + j]) : 0.f;
     }
     __syncthreads();
     const int j0 = jg * jpt;
@@ -374,23 +358,36 @@ __global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restr
   const int col = c0 + c;
   if (col >= jb.ncols) return;
   const int j0 = jg * jpt;
-  if (jb.a_layout) {
-    jb.out[(long long)j0 * jb.ncols + col] = acc0 * scale;
-    if (jpt == 2) jb.out[(long long)(j0 + 1) * jb.ncols + col] = acc1 * scale;
-  } else {
-    jb.out[(long long)col * rank + j0] = acc0 * scale;
-    if (jpt == 2) jb.out[(long long)col * rank + j0 + 1] = acc1 * scale;
-  }
+  float* p = part + ((long long)(blockIdx.y * kWgradSplit + blockIdx.z) * max_cols + col) * 8;
+  p[j0] = acc0;
+  if (jpt == 2) p[j0 + 1] = acc1;
 }
 
-int lora_wgrad(const WgradJob* d_jobs, int njobs, int max_cols, int rows, int rank, float scale, bool bf16,
-               cudaStream_t st) {
-  B2P_REQUIRE(rank == 4 || rank == 8, "LoRA rank must be 4 or 8");
-  dim3 grid((max_cols + 63) / 64, njobs);
-  if (bf16)
-    lora_wgrad_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(d_jobs, rows, rank, scale);
+__global__ void lora_wgrad_reduce_kernel(const WgradJob* __restrict__ jobs, int rank, const float* __restrict__ part,
+                                         int max_cols, float scale) {
+  const WgradJob jb = jobs[blockIdx.y];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (col, j)
+  if (i >= jb.ncols * rank) return;
+  const int col = i / rank, j = i - col * rank;
+  float s = 0.f;
+  for (int z = 0; z < kWgradSplit; ++z) s += part[((long long)(blockIdx.y * kWgradSplit + z) * max_cols + col) * 8 + j];
+  if (jb.a_layout)
+    jb.out[(long long)j * jb.ncols + col] = s * scale;
   else
-    lora_wgrad_kernel<__half><<<grid, 256, 0, st>>>(d_jobs, rows, rank, scale);
+    jb.out[(long long)col * rank + j] = s * scale;
+}
+
+int lora_wgrad(const WgradJob* d_jobs, int njobs, int max_cols, int rows, int rank, float scale, float* part,
+               bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(rank == 4 || rank == 8, "LoRA rank must be 4 or 8");
+  dim3 grid((max_cols + 63) / 64, njobs, kWgradSplit);
+  if (bf16)
+    lora_wgrad_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(d_jobs, rows, rank, part, max_cols);
+  else
+    lora_wgrad_kernel<__half><<<grid, 256, 0, st>>>(d_jobs, rows, rank, part, max_cols);
+  B2P_POST_LAUNCH();
+  dim3 g2((max_cols * rank + 255) / 256, njobs);
+  lora_wgrad_reduce_kernel<<<g2, 256, 0, st>>>(d_jobs, rank, part, max_cols, scale);
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -403,17 +400,20 @@ int lora_wgrad(const WgradJob* d_jobs, int njobs, int max_cols, int rows, int ra
 // ---------------------------------------------------------------------------
 struct LoraTArgs {
   const float* theta;
-  long long layer_size, oBq, oBk, oBv, oBo, oAo;
+  long long layer_size, oBq, oBk, oBv, oBo, oAo, oAq, oAk, oAv;
   int L, D, QD, KVD, rank;
   void* bblk_qkv;
   void* bblk_o;
   float* a_oT;
+  void* wqkvT;   // [L][D][ldw]: columns QKV + 16p + j receive A_p[j, :] (the LoRA K-extension)
+  int ldw;
 };
 
 template <typename T>
 __global__ void lora_t_kernel(LoraTArgs a) {
   const int QKV = a.QD + 2 * a.KVD;
-  const long long per_layer = (long long)QKV * a.rank + (long long)a.D * a.rank + (long long)a.QD * a.rank;
+  const long long per_layer = (long long)QKV * a.rank + (long long)a.D * a.rank + (long long)a.QD * a.rank +
+                              3LL * a.rank * a.D;
   const long long n = per_layer * a.L;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int l = (int)(i / per_layer);
@@ -437,8 +437,19 @@ __global__ void lora_t_kernel(LoraTArgs a) {
       continue;
     }
     k -= (long long)a.D * a.rank;
-    const int col = (int)(k / a.rank), j = (int)(k % a.rank);
-    a.a_oT[((long long)l * a.QD + col) * a.rank + j] = th[a.oAo + (long long)j * a.QD + col];
+    if (k < (long long)a.QD * a.rank) {
+      const int col = (int)(k / a.rank), j = (int)(k % a.rank);
+      a.a_oT[((long long)l * a.QD + col) * a.rank + j] = th[a.oAo + (long long)j * a.QD + col];
+      continue;
+    }
+    k -= (long long)a.QD * a.rank;
+    // A_q, A_k, A_v rows as extra K columns of W_qkv^T: dX = dQKV·W_qkv + U'·A
+    const int p = (int)(k / ((long long)a.rank * a.D));
+    const long long rem = k - (long long)p * a.rank * a.D;
+    const int j = (int)(rem / a.D), d = (int)(rem % a.D);
+    const long long aoff = p == 0 ? a.oAq : (p == 1 ? a.oAk : a.oAv);
+    static_cast<T*>(a.wqkvT)[((long long)l * a.D + d) * a.ldw + QKV + 16 * p + j] =
+        static_cast<T>(th[aoff + (long long)j * a.D + d]);
   }
 }
 
@@ -511,7 +522,8 @@ struct AttnBwdArgs {
   int ld_o;
   const float* lse; // [rows][heads]
   float* dvec;      // [rows][heads]
-  void* dqkv;       // [rows][ld] dQ | dK | dV, same column layout as qkv
+  void* dqkv;       // [rows][ld_d] dQ | dK | dV, same column offsets as qkv
+  int ld_d;
   const float* rope_cos;
   const float* rope_sin;  // [seq][32]
   int seq, heads, kv_heads, ngroups;
@@ -674,7 +686,7 @@ __global__ void __launch_bounds__(128) attn_bwd_dq_kernel(AttnBwdArgs a) {
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int pos = qb * kAT + q0 + 8 * half;
-    T* out = static_cast<T*>(a.dqkv) + (row_base + pos) * a.ld + a.q_off + h * kAHD;
+    T* out = static_cast<T*>(a.dqkv) + (row_base + pos) * a.ld_d + a.q_off + h * kAHD;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       float d0 = dq[nt][2 * half], d1 = dq[nt][2 * half + 1];
@@ -816,8 +828,8 @@ __global__ void __launch_bounds__(128) attn_bwd_dkdv_kernel(AttnBwdArgs a) {
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int pos = kb * kAT + k0 + 8 * half;
-    T* ok = static_cast<T*>(a.dqkv) + (row_base + pos) * a.ld + a.k_off + kvh * kAHD;
-    T* ov = static_cast<T*>(a.dqkv) + (row_base + pos) * a.ld + a.v_off + kvh * kAHD;
+    T* ok = static_cast<T*>(a.dqkv) + (row_base + pos) * a.ld_d + a.k_off + kvh * kAHD;
+    T* ov = static_cast<T*>(a.dqkv) + (row_base + pos) * a.ld_d + a.v_off + kvh * kAHD;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       float d0 = dk[nt][2 * half], d1 = dk[nt][2 * half + 1];
@@ -832,7 +844,8 @@ int attention_backward(const AttnBwdArgs& a0, bool bf16, cudaStream_t st) {
   AttnBwdArgs a = a0;
   B2P_REQUIRE(a.seq % kAT == 0, "attention backward needs seq %% 64 == 0 (got %d)", a.seq);
   B2P_REQUIRE(a.kv_heads > 0 && a.heads % a.kv_heads == 0, "heads must be a multiple of kv_heads");
-  B2P_REQUIRE(a.ld % 8 == 0 && a.q_off % 8 == 0 && a.k_off % 8 == 0 && a.v_off % 8 == 0 && a.ld_o % 8 == 0,
+  B2P_REQUIRE(a.ld % 8 == 0 && a.ld_d % 2 == 0 && a.q_off % 8 == 0 && a.k_off % 8 == 0 && a.v_off % 8 == 0 &&
+                  a.ld_o % 8 == 0,
               "attention operands must be 16-byte aligned");
   a.scale = 1.0f / sqrtf((float)kAHD);
   a.scale_log2 = a.scale * 1.4426950408889634f;
@@ -876,7 +889,8 @@ int ensure_model_state(b2p_model* m) {
   const size_t e = model_esz(m);
   P16State* s = new P16State();
   m->p16 = s;
-  P16_ALLOC(s->wqkvT, L * D * QKV * e);
+  P16_ALLOC(s->wqkvT, L * D * (QKV + kUCols) * e);
+  B2P_CHECK_CUDA(cudaMemset(s->wqkvT, 0, L * D * (QKV + kUCols) * e));
   P16_ALLOC(s->woT, L * QD * D * e);
   P16_ALLOC(s->w13T, L * D * 2 * H * e);
   P16_ALLOC(s->w2T, L * H * D * e);
@@ -917,6 +931,7 @@ int ensure_weights(b2p_model* m) {
     s->cembedT = nullptr;
     P16_ALLOC(s->cembedT, (size_t)D * cv_pad * e);
     s->cv_pad = cv_pad;
+    s->gen++;
     release_rows(s);  // dlogits rows depend on the padded vocabulary
   }
   B2P_CHECK_CUDA(cudaMemsetAsync(s->cembedT, 0, (size_t)D * cv_pad * e, m->st));
@@ -927,7 +942,8 @@ int ensure_weights(b2p_model* m) {
     const char* wo = static_cast<const char*>(m->wo) + (size_t)l * D * QD * e;
     const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
     const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
-    if ((rc = transpose16(wqkv, QKV, D, D, static_cast<char*>(s->wqkvT) + (size_t)l * D * QKV * e, QKV, bf, m->st)))
+    if ((rc = transpose16(wqkv, QKV, D, D, static_cast<char*>(s->wqkvT) + (size_t)l * D * (QKV + kUCols) * e,
+                          QKV + kUCols, bf, m->st)))
       return rc;
     if ((rc = transpose16(wo, D, QD, QD, static_cast<char*>(s->woT) + (size_t)l * QD * D * e, D, bf, m->st)))
       return rc;
@@ -946,6 +962,7 @@ int ensure_rows(b2p_model* m, int R) {
   P16State* s = m->p16;
   if (s->rows == R) return B2P_OK;
   release_rows(s);
+  s->gen++;
   const auto& c = m->cfg;
   const size_t L = c.nlayers, D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim, QKV = m->qkv_dim;
   const size_t e = model_esz(m), Rz = R, heads = c.heads;
@@ -971,14 +988,14 @@ int ensure_rows(b2p_model* m, int R) {
   P16_ALLOC(s->d16, Rz * D * e);
   P16_ALLOC(s->dh13, Rz * 2 * H * e);
   P16_ALLOC(s->da, Rz * QD * e);
-  P16_ALLOC(s->dqkv, Rz * QKV * e);
+  P16_ALLOC(s->dqkv, Rz * (QKV + kUCols) * e);
+  B2P_CHECK_CUDA(cudaMemset(s->dqkv, 0, Rz * (QKV + kUCols) * e));
   P16_ALLOC(s->ub_o, Rz * kUCols * e);
-  P16_ALLOC(s->ub_qkv, Rz * kUCols * e);
   B2P_CHECK_CUDA(cudaMemset(s->ub_o, 0, Rz * kUCols * e));
-  B2P_CHECK_CUDA(cudaMemset(s->ub_qkv, 0, Rz * kUCols * e));
   P16_ALLOC(s->dvec, Rz * heads * 4);
   const size_t nblk = (Rz + kRmsRows - 1) / kRmsRows;
   P16_ALLOC(s->rms_part, (2 * L + 1) * nblk * D * 4);
+  P16_ALLOC(s->wgrad_part, (size_t)kMaxWgradJobs * kWgradSplit * std::max(D, QD) * 8 * 4);
   s->rows = R;
   // weight-gradient jobs of every layer (fixed once the buffers are)
   std::vector<WgradJob> jobs(L * kMaxWgradJobs);
@@ -991,15 +1008,17 @@ int ensure_rows(b2p_model* m, int R) {
     const void* Ul = at(v.U, l, kUCols);
     const void* xnl = at(v.xn, l, D);
     const char* dq = static_cast<const char*>(s->dqkv);
+    const long long ldq = QKV + kUCols;
+    const void* up = dq + QKV * e;  // U'_{q,k,v} = dQKV · B, columns QKV.. of dqkv
     WgradJob* j = &jobs[l * kMaxWgradJobs];
-    j[0] = {s->d16, (long long)D, (int)D, 48, Ul, g + m->oBo, 0, 0};                       // dB_o
-    j[1] = {at(v.attn, l, QD), (long long)QD, (int)QD, 0, s->ub_o, g + m->oAo, 1, 0};        // dA_o
-    j[2] = {dq, (long long)QKV, (int)QD, 0, Ul, g + m->oBq, 0, 0};                           // dB_q
-    j[3] = {dq + QD * e, (long long)QKV, (int)KVD, 16, Ul, g + m->oBk, 0, 0};                // dB_k
-    j[4] = {dq + (QD + KVD) * e, (long long)QKV, (int)KVD, 32, Ul, g + m->oBv, 0, 0};        // dB_v
-    j[5] = {xnl, (long long)D, (int)D, 0, s->ub_qkv, g + m->oAq, 1, 0};                      // dA_q
-    j[6] = {xnl, (long long)D, (int)D, 16, s->ub_qkv, g + m->oAk, 1, 0};                     // dA_k
-    j[7] = {xnl, (long long)D, (int)D, 32, s->ub_qkv, g + m->oAv, 1, 0};                     // dA_v
+    j[0] = {s->d16, (long long)D, (int)D, 48, Ul, kUCols, g + m->oBo, 0, 0};                 // dB_o
+    j[1] = {at(v.attn, l, QD), (long long)QD, (int)QD, 0, s->ub_o, kUCols, g + m->oAo, 1, 0};  // dA_o
+    j[2] = {dq, ldq, (int)QD, 0, Ul, kUCols, g + m->oBq, 0, 0};                               // dB_q
+    j[3] = {dq + QD * e, ldq, (int)KVD, 16, Ul, kUCols, g + m->oBk, 0, 0};                    // dB_k
+    j[4] = {dq + (QD + KVD) * e, ldq, (int)KVD, 32, Ul, kUCols, g + m->oBv, 0, 0};            // dB_v
+    j[5] = {xnl, (long long)D, (int)D, 0, up, ldq, g + m->oAq, 1, 0};                          // dA_q
+    j[6] = {xnl, (long long)D, (int)D, 16, up, ldq, g + m->oAk, 1, 0};                         // dA_k
+    j[7] = {xnl, (long long)D, (int)D, 32, up, ldq, g + m->oAv, 1, 0};                         // dA_v
   }
   B2P_CHECK_CUDA(cudaMemcpy(s->d_jobs, jobs.data(), jobs.size() * sizeof(WgradJob), cudaMemcpyHostToDevice));
   return B2P_OK;
@@ -1007,23 +1026,80 @@ int ensure_rows(b2p_model* m, int R) {
 
 // Forward with saves + cross-entropy + backward; gradients (theta layout) in s->grad,
 // the mean loss in m->var_loss[0]. Tokens/targets already staged at d_tok / d_tgt.
+int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq);
+
 int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq) {
   int rc;
   if ((rc = model_ready(m))) return rc;
   const auto& c = m->cfg;
-  const int L = c.nlayers, D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim, QKV = m->qkv_dim;
-  const int R = n_seq * c.seq, r = c.rank;
-  const size_t e = model_esz(m);
-  const bool bf = m->bf16;
+  const int R = n_seq * c.seq;
   B2P_REQUIRE(c.rank == 4 || c.rank == 8, "backprop-LoRA needs rank 4 or 8");
   if ((rc = ensure_model_state(m))) return rc;
   P16State* s = m->p16;
   if ((rc = ensure_weights(m))) return rc;
   if ((rc = ensure_rows(m, R))) return rc;
-  const ForwardSaves& v = s->sv;
-  // forward (θ unperturbed) with saves
+  // group/variant tables and per-row targets (host-staged, outside any graph)
   std::vector<VariantInfo> vars(1, VariantInfo{0, 0, 0.f, 0.f});
   if ((rc = model_stage_groups(m, n_seq, vars, d_tgt))) return rc;
+  if (!m->graphs) return p16_kernels(m, d_tok, n_seq);
+  // the graph reads tokens from the model's own buffer, so any caller buffer can feed a replay
+  if (d_tok != m->d_tok) {
+    B2P_CHECK_CUDA(cudaMemcpyAsync(m->d_tok, d_tok, (size_t)n_seq * c.seq * sizeof(int32_t),
+                                   cudaMemcpyDeviceToDevice, m->st));
+    d_tok = m->d_tok;
+  }
+  // With profiling on, the graph also holds the per-GEMM event records; a replay
+  // re-records them, so b2p_model_profile_read reports the latest step.
+  P16State::Graph& gr = s->graph;
+  const bool hit = gr.exec && gr.tok == d_tok && gr.n_seq == n_seq && gr.gen == s->gen &&
+                   gr.scale_log2 == m->grad_scale_log2 && gr.pair == m->use_pair && gr.prof_epoch == m->prof_epoch;
+  if (!hit) {
+    if (gr.exec) cudaGraphExecDestroy(gr.exec);
+    gr.exec = nullptr;
+    const long long n0 = launch_count();
+    B2P_CHECK_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeRelaxed));
+    rc = p16_kernels(m, d_tok, n_seq);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+    const long long captured = launch_count() - n0;
+    count_launches(-captured);  // recorded, not run: counted on every replay instead
+    if (rc || ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      if (!rc) set_error("graph capture of the backprop-LoRA step failed: %s", cudaGetErrorString(ce));
+      return rc ? rc : B2P_ERR_CUDA;
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&gr.exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+      gr.exec = nullptr;
+      set_error("cudaGraphInstantiate failed: %s", cudaGetErrorString(ie));
+      return B2P_ERR_CUDA;
+    }
+    gr.tok = d_tok;
+    gr.n_seq = n_seq;
+    gr.gen = s->gen;
+    gr.scale_log2 = m->grad_scale_log2;
+    gr.pair = m->use_pair;
+    gr.prof_epoch = m->prof_epoch;
+    gr.launches = captured;
+  }
+  B2P_CHECK_CUDA(cudaGraphLaunch(gr.exec, m->st));
+  count_launches(gr.launches);
+  return B2P_OK;
+}
+
+// Every device operation of the backprop-LoRA gradient after the host staging:
+// forward with saves, loss, backward, gradient assembly (capturable).
+int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
+  int rc;
+  const auto& c = m->cfg;
+  const int L = c.nlayers, D = c.dim, H = c.hidden, QD = m->q_dim, KVD = m->kv_dim, QKV = m->qkv_dim;
+  const int R = n_seq * c.seq, r = c.rank;
+  const size_t e = model_esz(m);
+  const bool bf = m->bf16;
+  P16State* s = m->p16;
+  const ForwardSaves& v = s->sv;
   if ((rc = model_run_forward(m, n_seq, d_tok, &v))) return rc;
   if ((rc = launch_variant_loss(m->group_loss, 1, n_seq, m->var_loss, m->st))) return rc;
 
@@ -1032,10 +1108,13 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
   lt.theta = m->theta;
   lt.layer_size = m->layer_size;
   lt.oBq = m->oBq; lt.oBk = m->oBk; lt.oBv = m->oBv; lt.oBo = m->oBo; lt.oAo = m->oAo;
+  lt.oAq = m->oAq; lt.oAk = m->oAk; lt.oAv = m->oAv;
   lt.L = L; lt.D = D; lt.QD = QD; lt.KVD = KVD; lt.rank = r;
   lt.bblk_qkv = s->bblk_qkv;
   lt.bblk_o = s->bblk_o;
   lt.a_oT = s->a_oT;
+  lt.wqkvT = s->wqkvT;
+  lt.ldw = QKV + kUCols;
   if (bf) lora_t_kernel<__nv_bfloat16><<<148 * 4, 256, 0, m->st>>>(lt);
   else lora_t_kernel<__half><<<148 * 4, 256, 0, m->st>>>(lt);
   B2P_POST_LAUNCH();
@@ -1146,6 +1225,7 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
     ab.lse = v.lse + (size_t)l * R * c.heads;
     ab.dvec = s->dvec;
     ab.dqkv = s->dqkv;
+    ab.ld_d = QKV + kUCols;
     ab.rope_cos = m->rope_cos;
     ab.rope_sin = m->rope_sin;
     ab.seq = c.seq;
@@ -1153,20 +1233,22 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
     ab.kv_heads = c.kv_heads;
     ab.ngroups = n_seq;
     if ((rc = attention_backward(ab, bf, m->st))) return rc;
-    // U'_{q,k,v} = d{q,k,v} · B_{q,k,v}; dx_attn = dQKV · Wqkv (+ A^T U' inside the norm backward)
+    // U'_{q,k,v} = d{q,k,v} · B_{q,k,v} into the 64 extra columns of dqkv; then
+    // dx_attn = [dQKV | U'] · [W_qkv ; A_qkv]  (base data gradient + A^T (B^T dY) in one GEMM)
+    const int QKVp = QKV + kUCols;
     EpiParams p4;
     std::memset(&p4, 0, sizeof(p4));
     p4.M = R;
     p4.N = kUCols;
-    if ((rc = model_gemm(m, 128, EPI_H16, s->dqkv, QKV, static_cast<char*>(s->bblk_qkv) + (size_t)l * 64 * QKV * e,
-                         QKV, R, kUCols, QKV, s->ub_qkv, kUCols, nullptr, p4)))
+    if ((rc = model_gemm(m, 128, EPI_H16, s->dqkv, QKVp, static_cast<char*>(s->bblk_qkv) + (size_t)l * 64 * QKV * e,
+                         QKV, R, kUCols, QKV, static_cast<char*>(s->dqkv) + (size_t)QKV * e, QKVp, nullptr, p4)))
       return rc;
     EpiParams p5;
     std::memset(&p5, 0, sizeof(p5));
     p5.M = R;
     p5.N = D;
-    if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dqkv, QKV,
-                         static_cast<char*>(s->wqkvT) + (size_t)l * D * QKV * e, QKV, R, D, QKV, s->dxf, D, nullptr,
+    if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dqkv, QKVp,
+                         static_cast<char*>(s->wqkvT) + (size_t)l * D * QKVp * e, QKVp, R, D, QKVp, s->dxf, D, nullptr,
                          p5)))
       return rc;
     // RMSNorm1 backward + skip: dy = rmsnorm_bwd(dx_attn) + dx2
@@ -1178,16 +1260,10 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
     ra.out = cur;
     ra.part = part(2 * l);
     ra.rows = R;
-    ra.n_a = 3;
-    ra.U = s->ub_qkv;
-    ra.A[0] = m->theta + lb + m->oAq;
-    ra.A[1] = m->theta + lb + m->oAk;
-    ra.A[2] = m->theta + lb + m->oAv;
-    ra.rank = r;
     if ((rc = rms_bwd(ra, D, bf, m->st))) return rc;
     // factored LoRA weight gradients of the layer
     if ((rc = lora_wgrad(s->d_jobs + (size_t)l * kMaxWgradJobs, kMaxWgradJobs, std::max(D, QD), R, r, inv_lambda,
-                         bf, m->st)))
+                         s->wgrad_part, bf, m->st)))
       return rc;
   }
   const int nvec = 2 * L + 1;
@@ -1235,6 +1311,7 @@ int adam_step(b2p_model* m, float lr, float b1, float b2, float eps, float wd) {
 
 void p16_release(P16State* s) {
   if (!s) return;
+  if (s->graph.exec) cudaGraphExecDestroy(s->graph.exec);
   release_rows(s);
   free_ptrs({s->wqkvT, s->woT, s->w13T, s->w2T, s->cembedT, s->a_oT, s->bblk_qkv, s->bblk_o, s->grad, s->adam_m,
              s->adam_v, s->flag, s->d_jobs, s->d_rms_off});

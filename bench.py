@@ -289,9 +289,17 @@ def main():
     ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true", help="skip the in-region per-GEMM CUDA events")
+    ap.add_argument("--p16-seqs", type=int, default=P16_SEQS_PER_GPU, help="sequences per GPU per P16 step")
+    ap.add_argument("--workload", choices=["mezo", "p16", "gemm"], default="mezo",
+                    help="mezo: the headline DP MeZO-LoRA-split step; p16: DP backprop-LoRA step; "
+                         "gemm: projection-GEMM sweep (one line per shape)")
     args = ap.parse_args()
+    if args.workload == "gemm":
+        return run_gemm_sweep(args)
     if args.impl == "reference":
-        return run_reference(args)
+        return run_reference(args) if args.workload == "mezo" else run_reference_p16(args)
+    if args.workload == "p16":
+        return run_p16(args)
 
     import torch
     import torch.distributed as dist
@@ -445,6 +453,340 @@ def main():
     model.close()
     if world > 1:
         dist.destroy_process_group()
+    return 0
+
+
+# --------------------------------------------------------------------------- backprop-LoRA (P16) workload
+P16_SEQS_PER_GPU = 8
+P16_LR = 3e-4
+REF_P16_MS = 612.0  # reference P16 CPU step (fwd 234 + bwd 360 + opt 18 ms, results/p16_backprop_lora_cpu_200steps.txt)
+
+
+def p16_flops_per_seq() -> float:
+    """Algorithmic FLOPs of one P16 sequence step: forward + dX of the 7 projections + classifier backward
+    (logit recompute + dy) + attention backward (4 dense T^2 matmuls + score recompute) + factored dA/dB."""
+    d = DIMS
+    s, D, H, r, L = d["seq"], d["dim"], d["hidden"], d["rank"], d["nlayers"]
+    qd, kvd = d["heads"] * d["head_dim"], d["kv_heads"] * d["head_dim"]
+    proj = 2 * s * (D * (qd + 2 * kvd) + qd * D + 3 * D * H)
+    attn_mm = 2 * d["heads"] * s * s * d["head_dim"]
+    head = 2 * s * N_ACTIVE * D
+    lora_grad = 2 * s * r * 2 * ((qd + 2 * kvd) + D + 3 * D + qd)
+    bwd = L * (proj + 5 * attn_mm + lora_grad) + 2 * head
+    return fwd_flops_per_seq() + float(bwd)
+
+
+def p16_config(world: int, nseq: int = P16_SEQS_PER_GPU):
+    return {"workload": f"DP backprop-LoRA (P16) r8, SmolLM2-360M shapes, SEQ 256; per GPU {nseq} sequences, "
+                        "forward + full backward + NCCL all-reduce of the LoRA/RMS gradient + Adam",
+            "model": "SmolLM2-360M-shaped (random init)", "global_batch": nseq * world,
+            "seq_len": DIMS["seq"], "parallelism": f"dp{world}", "lora_rank": DIMS["rank"], "lr": P16_LR,
+            "adam": "b1 0.9, b2 0.95, eps 1e-8, wd 0", "l2": "inputs larger than L2 (1.3 GB of weights per step)",
+            "gflop_per_seq_step": round(p16_flops_per_seq() / 1e9, 2)}
+
+
+def run_p16(args):
+    import torch
+    import torch.distributed as dist
+    from autoane_b200 import _lib
+    from autoane_b200.model import BF16, F16, Config, Model
+
+    rank, world, local = env_rank()
+    NSEQ = args.p16_seqs
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    _lib.call("b2p_init", local)
+    cfg = Config(dtype=BF16 if args.dtype == "bf16" else F16, max_groups=NSEQ,
+                 **{k: DIMS[k] for k in ("dim", "hidden", "heads", "kv_heads", "head_dim", "seq", "nlayers", "vocab",
+                                         "rank", "rope_theta")})
+    model = Model(cfg)
+    for l in range(DIMS["nlayers"]):
+        model.set_layer(l, *synth_weights(l))
+    embed = synth_embed()
+    model.set_embedding(embed, np.arange(N_ACTIVE, dtype=np.int32))
+    model.set_trainable(synth_theta(lora_layout()))
+    tokens = token_stream()
+    W, K = args.warmup, args.steps
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.ExternalStream(model.stream)
+    batches = [step_batch(tokens, s, rank, NSEQ) for s in range(W + K)]
+    d_tok = torch.tensor(np.stack([b[0] for b in batches]).astype(np.int32), device=dev)
+    d_tgt = torch.tensor(np.stack([b[1] for b in batches]).astype(np.int32), device=dev)
+    d_loss = torch.zeros(1, device=dev)
+    torch.cuda.synchronize()
+
+    def grad_tensor():
+        class _G:  # the model's device gradient buffer as a torch tensor (no copy)
+            __cuda_array_interface__ = {"shape": (model.P,), "typestr": "<f4", "data": (model.grad_ptr(), False),
+                                        "version": 3, "stream": None}
+        return torch.as_tensor(_G(), device=dev)
+
+    grad = None
+
+    def allreduce():
+        if world > 1:
+            dist.all_reduce(grad)
+            grad.mul_(1.0 / world)
+
+    def dev_step(s):
+        nonlocal grad
+        model.p16_grad_device(d_tok[s].data_ptr(), d_tgt[s].data_ptr(), NSEQ, d_loss.data_ptr())
+        if grad is None:
+            grad = grad_tensor()
+        allreduce()
+        model.adam_step(P16_LR)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    with torch.cuda.stream(stream):
+        for s in range(W):
+            dev_step(s)
+        model.sync()
+        torch.cuda.synchronize()
+        barrier()
+        try:
+            phys = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+        except (KeyError, ValueError, IndexError):
+            phys = local
+        clocks = ClockSampler(phys)
+        clocks.start()
+        n_launch0 = int(_lib.load().b2p_launch_count())
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for s in range(W, W + K):
+            dev_step(s)
+        ev1.record(stream)
+        model.sync()
+        torch.cuda.synchronize()
+        n_launch = int(_lib.load().b2p_launch_count()) - n_launch0
+        dev_ms = ev0.elapsed_time(ev1)
+        barrier()
+        clk = clocks.stop()
+        # per-GEMM CUDA events of one more step (its graph holds the event records; not in the timed region)
+        gemm_ms, gemm_flops, gemm_n = 0.0, 0.0, 0
+        if not args.no_profile:
+            model.profile(True)
+            dev_step(W + K - 1)
+            dev_step(W + K - 1)
+            model.sync()
+            gemm_ms, gemm_flops, gemm_n = model.profile_read()
+            model.profile(False)
+            barrier()
+        # e2e through the host-buffer C ABI: tokens in, loss out, every step
+        e_batches = [step_batch(tokens, 20_000 + s, rank, NSEQ) for s in range(K)]
+        model.sync()
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        last = 0.0
+        for s in range(K):
+            inp, tgt = e_batches[s]
+            if world > 1:
+                last, _ = model.p16_grad(inp, tgt)
+                allreduce()
+                model.adam_step(P16_LR)
+            else:
+                last = model.p16_step(inp, tgt, P16_LR)
+        model.sync()
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - t0
+        barrier()
+    t = torch.tensor([dev_ms, e2e_s, gemm_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_s, gemm_ms = t.tolist()
+    units = NSEQ * world * K
+    value = units / (dev_ms / 1000.0)
+    roofline = None
+    if gemm_n:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak = peaks.get("bf16_tflops_sustained", 1400.0)
+        achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "traffic": None,
+                    "kernel": "tcgen05 GEMMs (forward + data-gradient launches) of the last step (CUDA graph)",
+                    "launches": gemm_n,
+                    "avg_launch_us": round(1000.0 * gemm_ms / gemm_n, 2),
+                    "peak_source": "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json)"}
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_reference_p16_rate()
+        line = {"metric": "backprop-LoRA (P16) seq-steps/s SmolLM2-360M", "value": round(value, 3),
+                "unit": "seq-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 4),
+                "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": round(value / (1000.0 / REF_P16_MS), 2), "dtype": args.dtype, "data": "synthetic",
+                "config": p16_config(world, NSEQ) | {
+                    "tflops_per_gpu": round(NSEQ * p16_flops_per_seq() * K / (dev_ms / 1000.0) / 1e12, 2),
+                    "last_e2e_loss": round(float(last), 5)},
+                "e2e": {"value": round(units / e2e_s, 3), "unit": "seq-steps/s",
+                        "h2d_bytes_per_step": 2 * NSEQ * DIMS["seq"] * 4 + 2 * cfg.max_groups * 4 + 16,
+                        "d2h_bytes_per_step": 4},
+                "gpu_launches": n_launch, "roofline": roofline, "clocks": clk, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def _ref_p16_fn():
+    """(callable running one reference P16 gradient step on SmolLM2 shapes, threads) or None."""
+    from oracle import oracle as O
+    import ctypes as C
+    ref = O.ref_lib("smollm2_360m")
+    if ref is None:
+        return None
+    rng = np.random.default_rng(0)
+    L, D, H = DIMS["nlayers"], DIMS["dim"], DIMS["hidden"]
+    qd, kvd, r = DIMS["heads"] * 64, DIMS["kv_heads"] * 64, DIMS["rank"]
+    F = C.POINTER(C.c_float)
+    keep = []
+
+    def f(a):
+        return a.ctypes.data_as(F)
+
+    def plist(arrs):
+        p = (F * len(arrs))(*[f(a) for a in arrs])
+        keep.append((arrs, p))
+        return p
+    ws = [synth_weights(l) for l in range(L)]
+    Wl = [plist([w[i] for w in ws]) for i in range(7)]
+    sizes = [r * D, qd * r, r * D, kvd * r, r * D, kvd * r, r * qd, D * r]
+    lora = [(0.1 * rng.standard_normal(sizes[k % 8])).astype(np.float32) for k in range(8 * L)]
+    rms = [np.ones(D, np.float32) for _ in range(2 * L)]
+    rf = np.ones(D, np.float32)
+    embed = synth_embed()
+    cembed = np.ascontiguousarray(embed[:N_ACTIVE])
+    glora = [np.zeros(sizes[k % 8], np.float32) for k in range(8 * L)]
+    grms = [np.zeros(D, np.float32) for _ in range(2 * L)]
+    grf = np.zeros(D, np.float32)
+    tokens = token_stream()
+    inp, tgt = step_batch(tokens, 0, 0, 1)
+    inp, tgt = np.ascontiguousarray(inp[0], np.uint16), np.ascontiguousarray(tgt[0], np.uint16)
+    ref.ref_p16_grad.argtypes = [C.POINTER(F)] * 9 + [F, F, F, C.c_int, C.c_int, C.c_float,
+                                                      C.POINTER(C.c_uint16), C.POINTER(C.c_uint16),
+                                                      C.POINTER(F), C.POINTER(F), F]
+    args = (*Wl, plist(lora), plist(rms), f(rf), f(embed), f(cembed), N_ACTIVE, r, C.c_float(1.0),
+            inp.ctypes.data_as(C.POINTER(C.c_uint16)), tgt.ctypes.data_as(C.POINTER(C.c_uint16)), plist(glora),
+            plist(grms), f(grf))
+    mom = [np.zeros(a.size, np.float32) for a in lora]
+    vel = [np.zeros(a.size, np.float32) for a in lora]
+
+    def step():
+        _ = keep  # the arrays behind the pointer lists must outlive the calls
+        ref.ref_p16_grad(*args)
+        for k in range(8 * L):  # the reference's Adam on every LoRA buffer (train_mezo.m:2099-2106)
+            ref.ref_adam(f(lora[k]), f(glora[k]), f(mom[k]), f(vel[k]), C.c_size_t(lora[k].size), 1,
+                         C.c_float(P16_LR), C.c_float(0.9), C.c_float(0.95), C.c_float(1e-8), C.c_float(0.0))
+    return step, O.set_threads(os.cpu_count() or 1)
+
+
+def cpu_reference_p16_rate(max_seconds: float = 30.0):
+    got = _ref_p16_fn()
+    if got is None:
+        return None
+    step, threads = got
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        step()
+        n += 1
+        if time.perf_counter() - t0 > max_seconds / 2 or n >= 3:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": "seq-steps/s", "cores": threads, "kind": "reference",
+            "sample": f"{n} P16 steps (batch 1, SEQ 256) of the reference's forward transcription + compiled "
+                      "bp_lora_backward + adam_update, OpenBLAS"}
+
+
+def run_reference_p16(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    r = cpu_reference_p16_rate(max_seconds=max(30.0, 10.0 * args.steps))
+    if r is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_smollm2_360m.so was not built"}))
+        return 0
+    print(json.dumps({"impl": "reference", "metric": "backprop-LoRA (P16) seq-steps/s SmolLM2-360M",
+                      "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
+                      "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "dtype": "f32",
+                      "data": "synthetic", "config": p16_config(world), "cpu_baseline": r,
+                      "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- projection-GEMM sweep
+GEMM_SHAPES = {"Wq": (960, 960), "Wk/Wv": (320, 960), "Wo": (960, 960), "W1/W3": (2560, 960), "W2": (960, 2560),
+               "lm_head": (49152, 960), "lm_head_compact": (16893, 960)}
+
+
+def run_gemm_sweep(args):
+    """Y[T, M] = X[T, K] · W[M, K]^T on the tcgen05 engine for every (shape, T) of the projection sweep;
+    one JSON line per case with TFLOP/s and the HBM/tensor roofline of that shape."""
+    import torch
+    from autoane_b200 import _lib
+    _, _, local = env_rank()
+    torch.cuda.set_device(local)
+    _lib.call("b2p_init", local)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tc = peaks.get("bf16_tflops", 1590.0)
+    bw = peaks.get("hbm_gbs", 6650.0)
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    code = 1 if args.dtype == "bf16" else 0
+    dev = torch.device("cuda", local)
+    flush = None
+    del flush
+    for name, (M, K) in GEMM_SHAPES.items():
+        for T in (128, 256, 1024, 8192):
+            # enough operand copies that one pass over them exceeds L2 (126 MB): every launch reads from HBM
+            per = 2 * (T * K + M * K) + 4 * T * ((M + 3) // 4 * 4)
+            ncopy = max(2, min(64, -(-(256 << 20) // per)))
+            xs = [torch.randn(T, K, device=dev).to(dt) for _ in range(ncopy)]
+            ws = [(0.02 * torch.randn(M, K, device=dev)).to(dt) for _ in range(ncopy)]
+            ys = [torch.empty(T, (M + 3) // 4 * 4, device=dev, dtype=torch.float32) for _ in range(ncopy)]
+            fn = "b2p_gemm_pair" if T >= 256 else "b2p_gemm"
+
+            def run(i):
+                st = torch.cuda.current_stream().cuda_stream
+                _lib.call(fn, xs[i].data_ptr(), ws[i].data_ptr(), ys[i].data_ptr(), T, M, K, ys[i].shape[1], code, 1,
+                          st)
+            for i in range(ncopy):
+                run(i)
+            torch.cuda.synchronize()
+            # back-to-back launches over the rotating copies, recorded once into a CUDA graph so the
+            # host's per-call cost stays out of the timed region
+            reps = max(ncopy, 8 * max(5, args.steps))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(reps):
+                    run(i % ncopy)
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            del graph
+            flops = 2.0 * M * K * T
+            byts = 2.0 * M * K + 2.0 * K * T + 4.0 * M * T
+            roof = min(tc, bw * 1e9 * flops / byts / 1e12)
+            ach = flops / (ms / 1000.0) / 1e12
+            print(json.dumps({"metric": "projection GEMM TFLOP/s", "shape": name, "M": M, "K": K, "T": T,
+                              "dtype": args.dtype, "value": round(ach, 2), "unit": "TFLOP/s", "us": round(ms * 1e3, 2),
+                              "roofline_tflops": round(roof, 1), "frac_of_roofline": round(ach / roof, 3),
+                              "bound": "tensor" if roof >= tc else "hbm", "engine": fn,
+                              "l2": f"operands rotate over {ncopy} copies (> 256 MB) so every launch reads HBM",
+                              "timing": f"{reps} back-to-back launches in one CUDA graph, CUDA events"}),
+                  flush=True)
+            del xs, ws, ys
     return 0
 
 

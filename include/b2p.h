@@ -202,6 +202,10 @@ long long b2p_launch_count(void);
  * if gradients underflow, lower it if they overflow (a non-finite gradient
  * makes the optimizer step a no-op and the call return B2P_ERR_DEVICE). */
 #define B2P_OPT_GRAD_SCALE_LOG2 2
+/* B2P_OPT_GRAPHS (default 1): the backprop-LoRA gradient pass is recorded once
+ * into a CUDA graph per (token buffer, batch size, buffers) and replayed; 0 issues
+ * every kernel from the host instead. */
+#define B2P_OPT_GRAPHS 3
 int b2p_model_set_option(b2p_model* m, int option, int value);
 
 /* ======================================================================
