@@ -44,7 +44,9 @@ struct WgradJob {
 };
 constexpr int kMaxWgradJobs = 8;
 constexpr int kWgradSplit = 8;  // row chunks per weight gradient (partials summed in chunk order)
-constexpr int kRmsRows = 16;  // rows per block of the RMSNorm backward (2 per warp)
+constexpr int kRmsTeam = 128;   // threads per row of the RMSNorm backward
+constexpr int kRmsTeams = 4;    // rows in flight per block
+constexpr int kRmsBlocks = 296; // blocks (dw partial rows) per RMSNorm backward launch, 2 per SM
 
 struct P16State {
   int rows = 0;
@@ -202,8 +204,8 @@ int swiglu_bwd(const float* dsilu, const void* h13, int rows, int H, void* dh13,
 // RMSNorm backward (rmsnorm_bwd, training/cpu_ops.h:24-60), one warp per row:
 //   rrms = 1/sqrt(sum x^2 / d + 1e-5); dot = sum_i w_i g_i x_i * rrms^2 / d
 //   dx_i = (w_i g_i - x_i dot) * rrms (+ resid_i);  dw_i += g_i x_i rrms
-// kRmsRows rows per block (2 per warp); the dw partials of a block go to
-// part[block][d] and are summed in block order by rms_part_reduce_kernel.
+// The dw partials of a block go to part[block][d] and are summed in block order
+// by rms_part_reduce_kernel.
 // ---------------------------------------------------------------------------
 struct RmsBwdArgs {
   const float* g;
@@ -217,77 +219,109 @@ struct RmsBwdArgs {
   int rows;
 };
 
-template <typename T, int CPL>
-__global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
-  constexpr int D = CPL * 32;
-  __shared__ float s_red[8][D];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float wv[CPL], acc[CPL];
+// A team of 128 threads owns one row at a time (float4 chunks c4 = tt + 128k);
+// kRmsTeams teams per block walk the rows grid-stride, so each block's dw partial
+// covers a fixed, deterministic row set.
+template <typename T, int NCH>
+__global__ void __launch_bounds__(kRmsTeam * kRmsTeams) rms_bwd_kernel(RmsBwdArgs a, int D) {
+  __shared__ float s_red[kRmsTeams][2][4][2];  // [team][row parity][warp][ss, dot]
+  __shared__ float4 s_acc[kRmsTeams][kRmsTeam * NCH];
+  const int team = threadIdx.x / kRmsTeam, tt = threadIdx.x % kRmsTeam;
+  const int wit = tt >> 5, lane = tt & 31;
+  const int nc4 = D / 4;
+  const float4* w4 = reinterpret_cast<const float4*>(a.w);
+  float4 wv[NCH], acc[NCH];
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) {
-    wv[k] = __ldg(a.w + lane + 32 * k);
-    acc[k] = 0.f;
+  for (int k = 0; k < NCH; ++k) {
+    const int c4 = tt + kRmsTeam * k;
+    wv[k] = c4 < nc4 ? __ldg(w4 + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const float invd = 1.0f / (float)D;
-  const int row0 = blockIdx.x * kRmsRows;
-  for (int rr = warp; rr < kRmsRows; rr += 8) {
-    const int row = row0 + rr;
-    if (row >= a.rows) break;
-    const float* gr = a.g + (long long)row * D;
-    const float* xr = a.x + (long long)row * D;
-    float gv[CPL], xv[CPL];
-#pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      gv[k] = gr[lane + 32 * k];
-      xv[k] = xr[lane + 32 * k];
-    }
+  int parity = 0;
+  for (int row = blockIdx.x * kRmsTeams + team; row < a.rows; row += gridDim.x * kRmsTeams) {
+    const float4* g4 = reinterpret_cast<const float4*>(a.g + (long long)row * D);
+    const float4* x4 = reinterpret_cast<const float4*>(a.x + (long long)row * D);
+    float4 gv[NCH], xv[NCH];
     float ss = 0.f, dot = 0.f;
 #pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      ss += xv[k] * xv[k];
-      dot += (wv[k] * gv[k]) * xv[k];
+    for (int k = 0; k < NCH; ++k) {
+      const int c4 = tt + kRmsTeam * k;
+      gv[k] = c4 < nc4 ? g4[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[k] = c4 < nc4 ? x4[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y + xv[k].z * xv[k].z + xv[k].w * xv[k].w;
+      dot += (wv[k].x * gv[k].x) * xv[k].x + (wv[k].y * gv[k].y) * xv[k].y + (wv[k].z * gv[k].z) * xv[k].z +
+             (wv[k].w * gv[k].w) * xv[k].w;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       ss += __shfl_xor_sync(0xffffffffu, ss, o);
       dot += __shfl_xor_sync(0xffffffffu, dot, o);
     }
+    if (lane == 0) {
+      s_red[team][parity][wit][0] = ss;
+      s_red[team][parity][wit][1] = dot;
+    }
+    named_bar_sync(1 + team, kRmsTeam);
+    ss = s_red[team][parity][0][0] + s_red[team][parity][1][0] + s_red[team][parity][2][0] + s_red[team][parity][3][0];
+    dot = s_red[team][parity][0][1] + s_red[team][parity][1][1] + s_red[team][parity][2][1] + s_red[team][parity][3][1];
+    parity ^= 1;
     const float rrms = 1.0f / sqrtf(ss * invd + 1e-5f);
     const float dots = dot * (rrms * rrms * invd);
-    float* orow = a.out + (long long)row * D;
-    const float* rrow = a.resid ? a.resid + (long long)row * D : nullptr;
+    float4* o4 = reinterpret_cast<float4*>(a.out + (long long)row * D);
+    const float4* r4 = a.resid ? reinterpret_cast<const float4*>(a.resid + (long long)row * D) : nullptr;
 #pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      float dx = (wv[k] * gv[k] - xv[k] * dots) * rrms;
-      if (rrow) dx += rrow[lane + 32 * k];
-      orow[lane + 32 * k] = dx;
-      acc[k] += (gv[k] * xv[k]) * rrms;
-      gv[k] = dx;
-    }
-    if (a.out16) {
-      T* o16 = static_cast<T*>(a.out16) + (long long)row * D;
-#pragma unroll
-      for (int k = 0; k < CPL; ++k) o16[lane + 32 * k] = static_cast<T>(gv[k] * a.alpha16);
+    for (int k = 0; k < NCH; ++k) {
+      const int c4 = tt + kRmsTeam * k;
+      if (c4 >= nc4) continue;
+      float4 d;
+      d.x = (wv[k].x * gv[k].x - xv[k].x * dots) * rrms;
+      d.y = (wv[k].y * gv[k].y - xv[k].y * dots) * rrms;
+      d.z = (wv[k].z * gv[k].z - xv[k].z * dots) * rrms;
+      d.w = (wv[k].w * gv[k].w - xv[k].w * dots) * rrms;
+      if (r4) {
+        const float4 r = r4[c4];
+        d.x += r.x; d.y += r.y; d.z += r.z; d.w += r.w;
+      }
+      o4[c4] = d;
+      acc[k].x += (gv[k].x * xv[k].x) * rrms;
+      acc[k].y += (gv[k].y * xv[k].y) * rrms;
+      acc[k].z += (gv[k].z * xv[k].z) * rrms;
+      acc[k].w += (gv[k].w * xv[k].w) * rrms;
+      if (a.out16) {
+        uint2 h;
+        h.x = pack_h2<T>(d.x * a.alpha16, d.y * a.alpha16);
+        h.y = pack_h2<T>(d.z * a.alpha16, d.w * a.alpha16);
+        *reinterpret_cast<uint2*>(static_cast<T*>(a.out16) + (long long)row * D + 4 * c4) = h;
+      }
     }
   }
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) s_red[warp][lane + 32 * k] = acc[k];
+  for (int k = 0; k < NCH; ++k) s_acc[team][tt + kRmsTeam * k] = acc[k];
   __syncthreads();
-  for (int c = threadIdx.x; c < D; c += blockDim.x) {
-    float s = 0.f;
+  float4* p4 = reinterpret_cast<float4*>(a.part + (long long)blockIdx.x * D);
+  for (int c4 = threadIdx.x; c4 < nc4; c4 += blockDim.x) {
+    float4 t = s_acc[0][c4];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += s_red[w][c];
-    a.part[(long long)blockIdx.x * D + c] = s;
+    for (int m = 1; m < kRmsTeams; ++m) {
+      const float4 u = s_acc[m][c4];
+      t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+    }
+    p4[c4] = t;
   }
 }
 
+int rms_blocks(int rows) { return std::min(kRmsBlocks, (rows + kRmsTeams - 1) / kRmsTeams); }
+
 template <typename T>
 int rms_bwd_t(const RmsBwdArgs& a, int D, cudaStream_t st) {
-  const int blocks = (a.rows + kRmsRows - 1) / kRmsRows;
-  switch (D) {
-    case 512: rms_bwd_kernel<T, 16><<<blocks, 256, 0, st>>>(a); break;
-    case 960: rms_bwd_kernel<T, 30><<<blocks, 256, 0, st>>>(a); break;
-    case 1024: rms_bwd_kernel<T, 32><<<blocks, 256, 0, st>>>(a); break;
+  const int blocks = rms_blocks(a.rows);
+  const int nch = (D / 4 + kRmsTeam - 1) / kRmsTeam;
+  switch (nch) {
+    case 1: rms_bwd_kernel<T, 1><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
+    case 2: rms_bwd_kernel<T, 2><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
+    case 3: rms_bwd_kernel<T, 3><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
+    case 4: rms_bwd_kernel<T, 4><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
     default: set_error("RMSNorm backward: unsupported width %d", D); return B2P_ERR_UNSUPPORTED;
   }
   B2P_POST_LAUNCH();
@@ -295,6 +329,7 @@ int rms_bwd_t(const RmsBwdArgs& a, int D, cudaStream_t st) {
 }
 
 int rms_bwd(const RmsBwdArgs& a, int D, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(D % 4 == 0 && D <= 4 * kRmsTeam * 4, "RMSNorm backward: width %d must be a multiple of 4, <= 2048", D);
   return bf16 ? rms_bwd_t<__nv_bfloat16>(a, D, st) : rms_bwd_t<__half>(a, D, st);
 }
 
@@ -316,22 +351,28 @@ __global__ void rms_part_reduce_kernel(const float* __restrict__ part, int nvec,
 // part[job][chunk][c][j] = sum_{t in chunk} X[t, c] * U[t, j]; a second kernel
 // sums the chunks in order, scales and stores in the A or B layout.
 // ---------------------------------------------------------------------------
+// 256 threads: column group cg = tid % 16 (4 columns) x row group rg = tid / 16;
+// each thread accumulates 4 columns x 8 rank outputs over its rows of the tile.
 template <typename T>
 __global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restrict__ jobs, int rows, int rank,
                                                         float* __restrict__ part, int max_cols) {
   __shared__ __align__(16) T s_x[64][64];
-  __shared__ float s_u[64][8];
+  __shared__ __align__(16) float s_u[64][8];
+  __shared__ float s_sum[16][64 * 8 + 4];
   const WgradJob jb = jobs[blockIdx.y];
   const int c0 = blockIdx.x * 64;
   if (c0 >= jb.ncols) return;
   const int chunk_rows = (rows + kWgradSplit - 1) / kWgradSplit;
   const int r_begin = blockIdx.z * chunk_rows, r_end = min(rows, r_begin + chunk_rows);
   const int tid = threadIdx.x;
-  const int c = tid & 63, jg = tid >> 6;  // 4 groups of output columns j
-  const int jpt = rank / 4;               // 2 for rank 8, 1 for rank 4
+  const int cg = tid & 15, rg = tid >> 4;
   const T* X = static_cast<const T*>(jb.X);
   const T* U = static_cast<const T*>(jb.U);
-  float acc0 = 0.f, acc1 = 0.f;
+  float acc[4][8];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[a][j] = 0.f;
   for (int t0 = r_begin; t0 < r_end; t0 += 64) {
     for (int i = tid; i < 64 * 8; i += 256) {
       const int r = i >> 3, ch = i & 7;
@@ -346,21 +387,38 @@ __global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restr
           (t0 + r < r_end && j < rank) ? static_cast<float>(U[(long long)(t0 + r) * jb.ldu + jb.ucol + j]) : 0.f;
     }
     __syncthreads();
-    const int j0 = jg * jpt;
-#pragma unroll 8
-    for (int t = 0; t < 64; ++t) {
-      const float xv = static_cast<float>(s_x[t][c]);
-      acc0 += xv * s_u[t][j0];
-      if (jpt == 2) acc1 += xv * s_u[t][j0 + 1];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int t = rg + 16 * q;
+      const uint2 xr = *reinterpret_cast<const uint2*>(&s_x[t][cg * 4]);
+      const float2 x01 = H2<T>::to_f2(*reinterpret_cast<const typename H2<T>::V*>(&xr.x));
+      const float2 x23 = H2<T>::to_f2(*reinterpret_cast<const typename H2<T>::V*>(&xr.y));
+      const float4 ua = *reinterpret_cast<const float4*>(&s_u[t][0]);
+      const float4 ub = *reinterpret_cast<const float4*>(&s_u[t][4]);
+      const float xs[4] = {x01.x, x01.y, x23.x, x23.y};
+      const float us[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[a][j] += xs[a] * us[j];
     }
     __syncthreads();
   }
-  const int col = c0 + c;
-  if (col >= jb.ncols) return;
-  const int j0 = jg * jpt;
-  float* p = part + ((long long)(blockIdx.y * kWgradSplit + blockIdx.z) * max_cols + col) * 8;
-  p[j0] = acc0;
-  if (jpt == 2) p[j0 + 1] = acc1;
+  // sum the 16 row groups in order
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s_sum[rg][(cg * 4 + a) * 8 + j] = acc[a][j];
+  __syncthreads();
+  float* p = part + (long long)(blockIdx.y * kWgradSplit + blockIdx.z) * max_cols * 8;
+  for (int o = tid; o < 64 * 8; o += 256) {
+    const int col = c0 + o / 8;
+    if (col >= jb.ncols) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) sum += s_sum[g][o];
+    p[(long long)col * 8 + (o & 7)] = sum;
+  }
 }
 
 __global__ void lora_wgrad_reduce_kernel(const WgradJob* __restrict__ jobs, int rank, const float* __restrict__ part,
@@ -993,7 +1051,7 @@ int ensure_rows(b2p_model* m, int R) {
   P16_ALLOC(s->ub_o, Rz * kUCols * e);
   B2P_CHECK_CUDA(cudaMemset(s->ub_o, 0, Rz * kUCols * e));
   P16_ALLOC(s->dvec, Rz * heads * 4);
-  const size_t nblk = (Rz + kRmsRows - 1) / kRmsRows;
+  const size_t nblk = rms_blocks(R);
   P16_ALLOC(s->rms_part, (2 * L + 1) * nblk * D * 4);
   P16_ALLOC(s->wgrad_part, (size_t)kMaxWgradJobs * kWgradSplit * std::max(D, QD) * 8 * 4);
   s->rows = R;
@@ -1140,7 +1198,7 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
   if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dlogits, s->cv_pad, s->cembedT, s->cv_pad, R, D, s->cv_pad,
                        s->dxf, D, nullptr, ef)))
     return rc;
-  const int nblk = (R + kRmsRows - 1) / kRmsRows;
+  const int nblk = rms_blocks(R);
   auto part = [&](int idx) { return s->rms_part + (size_t)idx * nblk * D; };
   RmsBwdArgs ra;
   std::memset(&ra, 0, sizeof(ra));
