@@ -91,7 +91,12 @@ __global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a)
   // 4 parameters per load (offsets and widths are multiples of 4, so their signs share
   // a mask word); 8 loads in flight per thread.
   constexpr int kUnits = (NORM ? dim / 4 : 0) + NA * dim / 4;
-  for (int u0 = threadIdx.x; u0 < kUnits; u0 += 8 * kNormThreads) {
+  const bool prepped = NA == 0 && a.w_prep != nullptr;  // rms weight already perturbed for this variant
+  if (prepped) {
+    const float4* wp = reinterpret_cast<const float4*>(a.w_prep + (long long)a.pc.group_variant[grp] * a.w_prep_vstride);
+    for (int i = threadIdx.x; i < dim / 4; i += kNormThreads) reinterpret_cast<float4*>(s_w)[i] = __ldg(wp + i);
+  }
+  for (int u0 = threadIdx.x; !prepped && u0 < kUnits; u0 += 8 * kNormThreads) {
     float4 th[8];
     uint32_t mw[8];
     long long pidx[8];
@@ -191,27 +196,46 @@ __global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a)
 // of the tile's variant are staged next to it, and U = X · A^T is computed with
 // mma.sync m16n8k16 (fp32 accumulation), then rounded to 16 bit like the U
 // operand of the LoRA-up tensor-core step that consumes it.
-constexpr int kLdRows = 64;
+constexpr int kLdRows = 32;
 
 template <int NP, typename T, bool NORM, int NA>
-__global__ void __launch_bounds__(256, 1) norm_lora_mma_kernel(NormLoraArgs a) {
+__global__ void __launch_bounds__(256, 2) norm_lora_mma_kernel(NormLoraArgs a) {
   constexpr int dim = NP * 64;
   constexpr int XS = dim + 8;                 // padded row stride (elements): conflict-free ldmatrix
   constexpr int NT = (NA + 7) / 8;            // 8-column n-tiles of U
   extern __shared__ __align__(16) uint8_t smx[];
   float* s_w = reinterpret_cast<float*>(smx);                                 // [dim] fp32
   T* s_a = reinterpret_cast<T*>(smx + dim * 4);                               // [NT*8][XS]
-  T* s_x = reinterpret_cast<T*>(smx + dim * 4 + NT * 8 * XS * 2);             // [64][XS]
+  T* s_x = reinterpret_cast<T*>(smx + dim * 4 + NT * 8 * XS * 2);             // [kLdRows][XS]
   using HV = typename H2<T>::V;
   const int row0 = blockIdx.x * kLdRows;
   const int grp = row0 / a.pc.group_rows;
-  const VariantInfo vi = a.pc.variants[a.pc.group_variant[grp]];
+  const int var = a.pc.group_variant[grp];
+  const VariantInfo vi = a.pc.variants[var];
   const uint32_t* mask = a.pc.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.pc.mask_words;
 
-  // ---- stage perturbed rms weight (fp32) and A rows (16-bit; rows >= NA zero) ----
+  if (a.a_prep) {
+    // ---- prepared operands: 16-bit A rows and fp32 rms weight of this variant, by cp.async ----
+    const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
+    const uint32_t sab = smem_u32(s_a);
+    for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 256) {
+      const int r = i / (dim / 8), c8 = i - r * (dim / 8);
+      if (r < NA)
+        cp_async16(sab + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
+      else
+        *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (NORM) {
+      const float* wp = a.w_prep + (long long)var * a.w_prep_vstride;
+      const uint32_t swb = smem_u32(s_w);
+      for (int i = threadIdx.x; i < dim / 4; i += 256) cp_async16(swb + 16u * i, wp + 4 * i);
+    }
+    cp_async_commit();
+  }
+  // ---- otherwise stage perturbed rms weight (fp32) and A rows (16-bit; rows >= NA zero) from theta ----
   constexpr int kWU = NORM ? dim / 4 : 0;
   constexpr int kUnits = kWU + NT * 8 * dim / 4;
-  for (int u0 = threadIdx.x; u0 < kUnits; u0 += 8 * 256) {
+  for (int u0 = threadIdx.x; !a.a_prep && u0 < kUnits; u0 += 8 * 256) {
     float4 th[8];
     uint32_t mw[8];
 #pragma unroll
@@ -255,9 +279,10 @@ __global__ void __launch_bounds__(256, 1) norm_lora_mma_kernel(NormLoraArgs a) {
       }
     }
   }
+  if (a.a_prep) cp_async_wait<0>();
   __syncthreads();
 
-  // ---- 64-row input tile: RMSNorm to HBM + smem, or a copy of the 16-bit rows ----
+  // ---- input tile: RMSNorm to HBM + smem, or a copy of the 16-bit rows ----
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (NORM) {
     // each warp normalises rows warp, warp+8, ...; the next row's loads are in
@@ -316,11 +341,12 @@ __global__ void __launch_bounds__(256, 1) norm_lora_mma_kernel(NormLoraArgs a) {
   }
   __syncthreads();
 
-  // ---- U[64 x 8NT] = X[64 x dim] · A[8NT x dim]^T  (mma.sync m16n8k16) ----
-  const int mt = warp & 3;
+  // ---- U[rows x 8NT] = X[rows x dim] · A[8NT x dim]^T  (mma.sync m16n8k16), one (m16, n8) task per warp ----
+  constexpr int MT = kLdRows / 16;
   const int lm = lane >> 3, lr = lane & 7;
   const uint32_t sxb = smem_u32(s_x), sab = smem_u32(s_a);
-  for (int nt = warp >> 2; nt < NT; nt += 2) {
+  for (int task = warp; task < MT * NT; task += 8) {
+    const int mt = task % MT, nt = task / MT;
     float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int kk = 0; kk < dim / 16; ++kk) {
@@ -749,6 +775,72 @@ int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int 
     tm_to_cf32_kernel<__nv_bfloat16, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
   else
     tm_to_cf32_kernel<__half, false><<<grid, block, 0, st>>>(src, ld_src, C, S, dst);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
+template <typename T>
+__global__ void lora_prep_kernel(LoraPrepArgs a) {
+  const int r = a.rank;
+  const long long per_a = 4LL * r * a.ld;             // A elements per (layer, variant)
+  const long long per_w = 2LL * a.dim;                // rms elements per (layer, variant)
+  const long long n_a = (long long)a.nlayers * a.n_var * per_a;
+  const long long n_w = (long long)a.nlayers * a.n_var * per_w + (long long)a.n_var * a.dim;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_a + n_w;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long p;
+    int v;
+    bool valid = true;
+    if (i < n_a) {
+      const long long lv = i / per_a, e = i - lv * per_a;
+      const int l = (int)(lv / a.n_var);
+      v = (int)(lv - (long long)l * a.n_var);
+      const int row = (int)(e / a.ld), c = (int)(e - (long long)row * a.ld);
+      const int m = row / r, j = row - m * r;
+      const int width = m < 3 ? a.dim : a.q_dim;
+      const long long off = m == 0 ? a.oAq : (m == 1 ? a.oAk : (m == 2 ? a.oAv : a.oAo));
+      valid = c < width;
+      p = (long long)l * a.layer_size + off + (long long)j * width + c;
+      float val = 0.f;
+      if (valid) {
+        const VariantInfo vi = a.variants[v];
+        const uint32_t* mask = a.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.mask_words;
+        const uint32_t bit = vi.mode ? (__ldg(mask + (p >> 5)) >> (p & 31)) & 1u : 0u;
+        val = perturb_value(__ldg(a.theta + p), bit, vi);
+      }
+      static_cast<T*>(a.a_out)[i] = static_cast<T>(val);
+      continue;
+    }
+    const long long k = i - n_a;
+    float* dst;
+    const long long nl = (long long)a.nlayers * a.n_var * per_w;
+    if (k < nl) {
+      const long long lv = k / per_w, e = k - lv * per_w;
+      const int l = (int)(lv / a.n_var);
+      v = (int)(lv - (long long)l * a.n_var);
+      const int which = (int)(e / a.dim), c = (int)(e - (long long)which * a.dim);
+      p = (long long)l * a.layer_size + (which ? a.oRf : a.oRa) + c;
+      dst = a.w_out + k;
+    } else {
+      const long long e = k - nl;
+      v = (int)(e / a.dim);
+      p = a.oRfinal + (e - (long long)v * a.dim);
+      dst = a.w_final + e;
+    }
+    const VariantInfo vi = a.variants[v];
+    const uint32_t* mask = a.masks + (long long)(vi.mode ? vi.mask_slot : 0) * a.mask_words;
+    const uint32_t bit = vi.mode ? (__ldg(mask + (p >> 5)) >> (p & 31)) & 1u : 0u;
+    *dst = perturb_value(__ldg(a.theta + p), bit, vi);
+  }
+}
+
+int launch_lora_prep(const LoraPrepArgs& a, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(a.n_var >= 1 && a.rank >= 1 && a.rank <= 8 && a.ld >= a.dim && a.ld >= a.q_dim && a.ld % 8 == 0,
+              "bad LoRA prep shape");
+  if (bf16)
+    lora_prep_kernel<__nv_bfloat16><<<148 * 8, 256, 0, st>>>(a);
+  else
+    lora_prep_kernel<__half><<<148 * 8, 256, 0, st>>>(a);
   B2P_POST_LAUNCH();
   return B2P_OK;
 }

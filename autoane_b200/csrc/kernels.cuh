@@ -40,8 +40,33 @@ struct NormLoraArgs {
   void* U;
   int u_col;
   PerturbCtx pc;
+  // Prepared operands (launch_lora_prep): when a_prep is set, the variant's perturbed
+  // A rows are read from a_prep + variant * a_prep_vstride (16-bit, n_a*rank rows of
+  // a_prep_ld elements) and the perturbed rms weight from w_prep + variant * w_prep_vstride.
+  const void* a_prep;
+  long long a_prep_vstride;
+  int a_prep_ld;
+  const float* w_prep;
+  long long w_prep_vstride;
 };
 int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st);
+
+// Per-variant perturbed LoRA-down operands of every layer, made once per forward:
+//   a_out[l][v][4r][ld]: rows 0..3r-1 = A_q, A_k, A_v (dim columns), rows 3r..4r-1 = A_o (q_dim columns), 16-bit
+//   w_out[l][v][2][dim]: rms_att, rms_ffn (fp32); w_final[v][dim]: rms_final
+// each parameter as perturb_value(theta, sign bit of the variant's seed).
+struct LoraPrepArgs {
+  const float* theta;
+  const uint32_t* masks;
+  long long mask_words;
+  const VariantInfo* variants;
+  int n_var, nlayers, dim, q_dim, rank, ld;
+  long long layer_size, oAq, oAk, oAv, oAo, oRa, oRf, oRfinal;
+  void* a_out;
+  float* w_out;
+  float* w_final;
+};
+int launch_lora_prep(const LoraPrepArgs& a, bool bf16, cudaStream_t st);
 
 // Causal GQA attention over token-major Q|K|V rows (reference cpu_sdpa_forward,
 // training/cpu_ops.h:321-360, with gqa_tile_kv, training/io.h:439-446):

@@ -52,6 +52,10 @@ int model_alloc(b2p_model* m) {
   B2P_CHECK_CUDA(cudaMalloc(&m->d_row_tgt, R * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->d_meta, 2 * m->max_groups * sizeof(int)));
   B2P_CHECK_CUDA(cudaMalloc(&m->d_var, m->max_groups * sizeof(VariantInfo)));
+  m->prep_ld = (std::max(c.dim, m->q_dim) + 7) / 8 * 8;
+  B2P_CHECK_CUDA(cudaMalloc(&m->prep_a, (size_t)c.nlayers * m->max_groups * 4 * c.rank * m->prep_ld * e));
+  B2P_CHECK_CUDA(cudaMalloc(&m->prep_w, (size_t)c.nlayers * m->max_groups * 2 * c.dim * 4));
+  B2P_CHECK_CUDA(cudaMalloc(&m->prep_wf, (size_t)m->max_groups * c.dim * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->rope_cos, (size_t)c.seq * (c.head_dim / 2) * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->rope_sin, (size_t)c.seq * (c.head_dim / 2) * 4));
   {
@@ -86,7 +90,7 @@ void model_release(b2p_model* m) {
   void* dev[] = {m->wqkv, m->wo, m->w13, m->w2, m->cembed, m->embed, m->theta, m->masks, m->d_bufs,
                  m->d_polys, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
                  m->ce_tgt, m->row_loss, m->group_loss, m->var_loss, m->pairs, m->d_tok, m->d_row_tgt, m->d_meta,
-                 m->d_var, m->rope_cos, m->rope_sin};
+                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (m->stg.base) cudaFreeHost(m->stg.base);
@@ -183,6 +187,30 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
   rc = launch_embed(m->embed, c.vocab, D, tok, group_seq, c.seq, R, m->x, ctx->status, m->st);
   if (rc) return rc;
   const PerturbCtx pc = pctx(m);
+  // every variant's perturbed LoRA-down operands and rms weights, once for all layers
+  const int nv = m->cur_vars;
+  LoraPrepArgs lp;
+  lp.theta = m->theta;
+  lp.masks = m->masks;
+  lp.mask_words = m->mask_words;
+  lp.variants = m->d_var;
+  lp.n_var = nv;
+  lp.nlayers = c.nlayers;
+  lp.dim = D;
+  lp.q_dim = QD;
+  lp.rank = c.rank;
+  lp.ld = m->prep_ld;
+  lp.layer_size = m->layer_size;
+  lp.oAq = m->oAq; lp.oAk = m->oAk; lp.oAv = m->oAv; lp.oAo = m->oAo;
+  lp.oRa = m->oRa; lp.oRf = m->oRf; lp.oRfinal = m->oRfinal;
+  lp.a_out = m->prep_a;
+  lp.w_out = m->prep_w;
+  lp.w_final = m->prep_wf;
+  if ((rc = launch_lora_prep(lp, m->bf16, m->st))) return rc;
+  const long long a_vstride = 4LL * c.rank * m->prep_ld;
+  auto prep_a = [&](int l, int row) -> const void* {
+    return static_cast<const char*>(m->prep_a) + ((size_t)l * nv * a_vstride + (size_t)row * m->prep_ld) * e;
+  };
   auto slab = [R](void* base, int l, size_t row_bytes) -> void* {
     return static_cast<char*>(base) + (size_t)l * R * row_bytes;
   };
@@ -211,6 +239,11 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     na.U = U;
     na.u_col = 0;  // q, k, v at U16 columns 0, 16, 32
     na.pc = pc;
+    na.a_prep = prep_a(l, 0);
+    na.a_prep_vstride = a_vstride;
+    na.a_prep_ld = m->prep_ld;
+    na.w_prep = m->prep_w + (size_t)l * nv * 2 * D;
+    na.w_prep_vstride = 2LL * D;
     if ((rc = launch_norm_lora(na, m->bf16, m->st))) return rc;
     // Q|K|V = xn · Wqkv^T + B·U (perturbed B), RoPE on Q and K
     EpiParams ep;
@@ -266,6 +299,9 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     nb.U = U;
     nb.u_col = 48;  // o at U16 column 48
     nb.pc = pc;
+    nb.a_prep = prep_a(l, 3 * c.rank);
+    nb.a_prep_vstride = a_vstride;
+    nb.a_prep_ld = m->prep_ld;
     if ((rc = launch_norm_lora(nb, m->bf16, m->st))) return rc;
     // x += alpha * (attn · Wo^T + Bo·Uo)
     EpiParams eo;
@@ -295,6 +331,8 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     nf.w_off = lb + m->oRf;
     nf.n_a = 0;
     nf.pc = pc;
+    nf.w_prep = m->prep_w + (size_t)l * nv * 2 * D + D;
+    nf.w_prep_vstride = 2LL * D;
     if ((rc = launch_norm_lora(nf, m->bf16, m->st))) return rc;
     // h = silu(xn·W1^T) * (xn·W3^T)  (W1/W3 rows interleaved in 128-row blocks)
     EpiParams es;
@@ -331,6 +369,8 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
   nl.norm = 1;
   nl.w_off = m->oRfinal;
   nl.pc = pc;
+  nl.w_prep = m->prep_wf;
+  nl.w_prep_vstride = D;
   if ((rc = launch_norm_lora(nl, m->bf16, m->st))) return rc;
   const int ntiles = (m->cv + 255) / 256;
   EpiParams ec;

@@ -74,6 +74,10 @@ struct b2p_model {
   int32_t* d_row_tgt = nullptr;  // [max_rows]
   int* d_meta = nullptr;         // group_seq[max_groups] | group_var[max_groups]
   b2p::VariantInfo* d_var = nullptr;
+  void* prep_a = nullptr;         // [L][max_groups][4r][prep_ld] perturbed A rows per variant (16-bit)
+  float* prep_w = nullptr;        // [L][max_groups][2][dim] perturbed rms_att / rms_ffn per variant
+  float* prep_wf = nullptr;       // [max_groups][dim] perturbed rms_final per variant
+  int prep_ld = 0;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
   Stager stg;
