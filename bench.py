@@ -428,7 +428,7 @@ def main():
         achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
         roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                     "frac": round(achieved / peak, 4), "traffic": gemm_traffic_per_launch(),
-                    "kernel": "gemm_tc_kernel (all projection + lm-head launches)", "launches": gemm_n,
+                    "kernel": "gemm_pair_kernel (all projection + lm-head launches)", "launches": gemm_n,
                     "avg_launch_us": round(1000.0 * gemm_ms / gemm_n, 2), "peak_source": peak_src,
                     "flops_per_launch_avg": gemm_flops / gemm_n}
     h2d = 2 * SEQS_PER_GPU * DIMS["seq"] * 4 + 2 * cfg.max_groups * 4 + 2 * SEEDS_PER_GPU * 16 + \
@@ -792,7 +792,7 @@ def run_gemm_sweep(args):
 
 def gemm_traffic_per_launch():
     """DRAM bytes per projection-GEMM launch from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "gemm_tc_kernel_traffic.txt"
+    p = ROOT / "profiles" / "gemm_pair_kernel_traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
