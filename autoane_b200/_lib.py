@@ -62,6 +62,11 @@ ABI: dict[str, tuple] = {
     "b2p_adam_step": (i32, [vp, f32, f32, f32, f32, f32]),
     "b2p_adam_state": (i32, [vp, i32, ip, vp, vp]),
     "b2p_p16_step": (i32, [vp, u16p, u16p, i32, f32, fp]),
+    "b2p_full_grad": (i32, [vp, u16p, u16p, i32, fp]),
+    "b2p_full_update": (i32, [vp, f32, f32, f32, fp]),
+    "b2p_full_step": (i32, [vp, u16p, u16p, i32, f32, f32, f32, fp, fp]),
+    "b2p_full_weight_count": (i64, [vp]),
+    "b2p_full_read": (i32, [vp, i32, vp, i64]),
     "b2p_compile": (vp, [vp, C.POINTER(fp)]),
     "b2p_input_bytes": (szt, [vp, i32]),
     "b2p_output_bytes": (szt, [vp, i32]),

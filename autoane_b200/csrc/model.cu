@@ -90,7 +90,7 @@ void model_release(b2p_model* m) {
   void* dev[] = {m->wqkv, m->wo, m->w13, m->w2, m->cembed, m->embed, m->theta, m->masks, m->d_bufs,
                  m->d_polys, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
                  m->ce_tgt, m->row_loss, m->group_loss, m->var_loss, m->pairs, m->d_tok, m->d_row_tgt, m->d_meta,
-                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf};
+                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf, m->d_c2f};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (m->stg.base) cudaFreeHost(m->stg.base);
@@ -324,7 +324,8 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     NormLoraArgs nf;
     std::memset(&nf, 0, sizeof(nf));
     nf.in = m->x;
-    nf.xn = m->xn;
+    void* xn2 = (sv && sv->xn2) ? slab(sv->xn2, l, D * e) : m->xn;
+    nf.xn = xn2;
     nf.rows = R;
     nf.dim = D;
     nf.norm = 1;
@@ -342,7 +343,7 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
     if (sv) {
       void* h13 = slab(sv->h13, l, (size_t)2 * H * e);
-      if ((rc = gemm(m, 256, EPI_H16, m->xn, D, w13, D, R, 2 * H, D, h13, 2 * H, es))) return rc;
+      if ((rc = gemm(m, 256, EPI_H16, xn2, D, w13, D, R, 2 * H, D, h13, 2 * H, es))) return rc;
       if ((rc = launch_swiglu_gate(h13, R, H, m->hbuf, m->bf16, m->st))) return rc;
     } else {
       if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, m->hbuf, H, es))) return rc;
@@ -702,6 +703,10 @@ int b2p_model_set_embedding(b2p_model* m, const float* embed, const int32_t* com
   m->cembed = nullptr;
   B2P_CHECK_CUDA(cudaMalloc(&m->cembed, (size_t)cv * c.dim * esz(m)));
   m->cv = cv;
+  if (m->d_c2f) cudaFree(m->d_c2f);
+  m->d_c2f = nullptr;
+  B2P_CHECK_CUDA(cudaMalloc(&m->d_c2f, (size_t)cv * sizeof(int32_t)));
+  B2P_CHECK_CUDA(cudaMemcpy(m->d_c2f, compact_to_full, (size_t)cv * sizeof(int32_t), cudaMemcpyHostToDevice));
   int rc = upload16(m, m->cembed, ce.data(), ce.size());
   if (rc) return rc;
   m->embed_set = true;

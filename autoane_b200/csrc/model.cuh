@@ -78,6 +78,7 @@ struct b2p_model {
   float* prep_w = nullptr;        // [L][max_groups][2][dim] perturbed rms_att / rms_ffn per variant
   float* prep_wf = nullptr;       // [max_groups][dim] perturbed rms_final per variant
   int prep_ld = 0;
+  int32_t* d_c2f = nullptr;       // [cv] compact -> full vocabulary id (device copy)
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
   Stager stg;
@@ -118,6 +119,7 @@ struct ForwardSaves {
   void* attn = nullptr;      // [L][R][q] attention output
   float* lse = nullptr;      // [L][R][heads] attention row normalisers (log2 domain)
   void* h13 = nullptr;       // [L][R][2H] W1|W3 outputs, interleaved in 128-column blocks
+  void* xn2 = nullptr;       // [L][R][D] normalised FFN input (16-bit; kept for the W1/W3 weight gradients)
   float* x_final = nullptr;  // [R][D] input of the final norm
   void* xn_final = nullptr;  // [R][D]
   float* row_lse = nullptr;  // [R] lm-head log-sum-exp per row

@@ -54,7 +54,7 @@ struct P16State {
   int cv_pad = 0;
   void *wqkvT = nullptr, *woT = nullptr, *w13T = nullptr, *w2T = nullptr, *cembedT = nullptr;
   ForwardSaves sv;
-  void* dlogits = nullptr;
+  void* dlogits = nullptr;  // (full mode also keeps sv.xn2)
   float *dy = nullptr, *dy2 = nullptr, *dxf = nullptr, *dsilu = nullptr;
   void *d16 = nullptr, *dh13 = nullptr, *da = nullptr, *dqkv = nullptr, *ub_o = nullptr;
   float* dvec = nullptr;
@@ -69,6 +69,18 @@ struct P16State {
   WgradJob* d_jobs = nullptr;
   int* d_rms_off = nullptr;
   int gen = 0;  // bumped whenever a buffer a captured graph points into is reallocated
+  // full backprop (train.m): fp32 masters of every projection weight, laid out as the 16-bit
+  // copies ([all layers' Wq|Wk|Wv] [all Wo] [all W1|W3 interleaved] [all W2]), their gradients,
+  // Adam moments, embedding gradients and scratch
+  bool full = false;
+  float *mw = nullptr, *gw = nullptr, *am_w = nullptr, *av_w = nullptr;
+  long long n_w = 0, o_qkv = 0, o_o = 0, o_13 = 0, o_2 = 0;
+  float *g_embed = nullptr, *g_cembed = nullptr, *am_e = nullptr, *av_e = nullptr;
+  void *tA = nullptr, *tB = nullptr, *gate = nullptr;
+  int32_t* d_seg = nullptr;  // [1 + rows + 1 + rows]: segment count, starts, row order (rows grouped by token)
+  long long* d_nseg = nullptr;  // norm / Adam segment tables: [3 + 2L+1] offsets then lengths
+  float* norm_part = nullptr;  // [kNormBlocks]; then norm, clip scale
+  int full_t = 0;
   // the captured forward + backward (CUDA graph), replayed while its key matches
   struct Graph {
     const void* tok = nullptr;
@@ -88,6 +100,9 @@ void free_ptrs(std::initializer_list<void*> ps) {
 
 void release_rows(P16State* s) {
   const ForwardSaves& v = s->sv;
+  free_ptrs({s->tA, s->tB, s->gate, s->d_seg, v.xn2});
+  s->tA = s->tB = s->gate = nullptr;
+  s->d_seg = nullptr;
   free_ptrs({v.x_in, v.x_mid, v.xn, v.U, v.qkv, v.attn, v.lse, v.h13, v.x_final, v.xn_final, v.row_lse, s->dlogits,
              s->dy, s->dy2, s->dxf, s->dsilu, s->d16, s->dh13, s->da, s->dqkv, s->ub_o, s->dvec,
              s->rms_part, s->wgrad_part});
@@ -1054,6 +1069,14 @@ int ensure_rows(b2p_model* m, int R) {
   const size_t nblk = rms_blocks(R);
   P16_ALLOC(s->rms_part, (2 * L + 1) * nblk * D * 4);
   P16_ALLOC(s->wgrad_part, (size_t)kMaxWgradJobs * kWgradSplit * std::max(D, QD) * 8 * 4);
+  if (s->full) {
+    const size_t rows_t = std::max<size_t>(std::max<size_t>(QKV, 2 * H), (size_t)s->cv_pad);
+    P16_ALLOC(s->tA, rows_t * Rz * e);
+    P16_ALLOC(s->tB, std::max(std::max(D, H), QD) * Rz * e);
+    P16_ALLOC(s->gate, Rz * H * e);
+    P16_ALLOC(v.xn2, L * Rz * D * e);
+    P16_ALLOC(s->d_seg, (2 * Rz + 2) * sizeof(int32_t));
+  }
   s->rows = R;
   // weight-gradient jobs of every layer (fixed once the buffers are)
   std::vector<WgradJob> jobs(L * kMaxWgradJobs);
@@ -1084,6 +1107,124 @@ int ensure_rows(b2p_model* m, int R) {
 
 // Forward with saves + cross-entropy + backward; gradients (theta layout) in s->grad,
 // the mean loss in m->var_loss[0]. Tokens/targets already staged at d_tok / d_tgt.
+// ---------------------------------------------------------------------------
+// full-backprop helpers (train.m)
+// ---------------------------------------------------------------------------
+// g_embed[tok, :] += scale * (sum of the dx rows of the token, in sequence order)
+// (embed_backward, training/cpu_ops.h:199-207), one block per distinct token.
+__global__ void embed_scatter_kernel(const float* __restrict__ dx, int D, const int32_t* __restrict__ seg, int rows,
+                                     const int32_t* __restrict__ tokens, float* __restrict__ g_embed, float scale) {
+  // seg[0] = number of segments, seg[1 .. rows + 1] their starts, seg[rows + 2 ..] the row order
+  const int sgi = blockIdx.x;
+  if (sgi >= seg[0]) return;
+  const int32_t* order = seg + rows + 2;
+  const int b = seg[1 + sgi], e = seg[2 + sgi];
+  const int tok = tokens[order[b]];
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
+    for (int i = b; i < e; ++i) acc += dx[(long long)order[i] * D + c];
+    g_embed[(long long)tok * D + c] += acc * scale;
+  }
+}
+
+// g_embed[c2f[v], :] += g_cembed[v, :]  (vocab_scatter_grads, training/cpu_ops.h:176-182)
+__global__ void cembed_scatter_kernel(const float* __restrict__ g_cembed, const int32_t* __restrict__ c2f, int cv,
+                                      int D, float* __restrict__ g_embed) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)cv * D) return;
+  const int v = (int)(i / D), c = (int)(i - (long long)v * D);
+  g_embed[(long long)c2f[v] * D + c] += g_cembed[i];
+}
+
+// squared-norm partials over segments (offset, length) of one buffer
+constexpr int kNormBlocks = 296;
+
+__global__ void sqnorm_kernel(const float* __restrict__ base, const long long* seg_off, const long long* seg_len,
+                              int nseg, float* __restrict__ part) {
+  __shared__ float red[256];
+  float acc = 0.f;
+  for (int sg = 0; sg < nseg; ++sg)
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < seg_len[sg];
+         j += (long long)gridDim.x * blockDim.x) {
+      const float g = base[seg_off[sg] + j];
+      acc += g * g;
+    }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int st = blockDim.x / 2; st > 0; st >>= 1) {
+    if (threadIdx.x < st) red[threadIdx.x] += red[threadIdx.x + st];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = red[0];
+}
+
+// norm = sqrt(sum of partials in block order); scale = clip / norm if clip > 0 and norm > clip,
+// else 1 (train.m:1344-1401); a non-finite norm sets *flag, which turns the optimizer step off
+__global__ void clip_scale_kernel(float* part, int nblk, float clip, uint32_t* flag, uint32_t* status) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float s = 0.f;
+  for (int i = 0; i < nblk; ++i) s += part[i];
+  const float norm = sqrtf(s);
+  part[nblk] = norm;
+  part[nblk + 1] = (clip > 0.f && norm > clip) ? clip / norm : 1.0f;
+  if (!isfinite(norm)) {
+    *flag = 1u;
+    atomicCAS(status, 0u, (uint32_t)DEV_NONFINITE_GRAD);
+  }
+}
+
+template <typename T>
+__global__ void f16_to_f32_kernel(const T* __restrict__ src, float* __restrict__ dst, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = static_cast<float>(src[i]);
+}
+
+// Adam over segments (offset, length) of one parameter/gradient/moment layout, gradients first
+// multiplied by *gscale (the clip factor; the reference scales the gradients in place first)
+struct AdamSegArgs {
+  float* w;
+  const float* g;
+  float* m;
+  float* v;
+  const long long* seg_off;
+  const long long* seg_len;
+  int nseg;
+  const float* gscale;
+  float b1, omb1, b2, omb2, ibc1, ibc2, eps, neg_lr, wd;
+  const uint32_t* flag;
+};
+
+__global__ void adam_seg_kernel(AdamSegArgs a) {
+  if (*a.flag) return;
+  const float gs = a.gscale ? *a.gscale : 1.0f;
+  for (int sg = 0; sg < a.nseg; ++sg) {
+    const long long off = a.seg_off[sg], len = a.seg_len[sg];
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < len; j += (long long)gridDim.x * blockDim.x) {
+      const long long i = off + j;
+      const float g = a.gscale ? __fmul_rn(a.g[i], gs) : a.g[i];
+      const float m = __fadd_rn(__fmul_rn(g, a.omb1), __fmul_rn(a.m[i], a.b1));
+      const float v = __fadd_rn(__fmul_rn(__fmul_rn(g, g), a.omb2), __fmul_rn(a.v[i], a.b2));
+      a.m[i] = m;
+      a.v[i] = v;
+      const float mh = __fmul_rn(m, a.ibc1);
+      const float vh = __fmul_rn(v, a.ibc2);
+      float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), a.eps));
+      if (a.wd > 0.f) u = __fadd_rn(__fmul_rn(a.w[i], a.wd), u);
+      a.w[i] = __fadd_rn(__fmul_rn(u, a.neg_lr), a.w[i]);
+    }
+  }
+}
+
+// 16-bit compact tied embedding from the fp32 full embedding (vocab_compact_embed, cpu_ops.h:171-176)
+template <typename T>
+__global__ void cembed_refresh_kernel(const float* __restrict__ embed, const int32_t* __restrict__ c2f, int cv, int D,
+                                      T* __restrict__ cembed) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)cv * D) return;
+  const int v = (int)(i / D), c = (int)(i - (long long)v * D);
+  cembed[i] = static_cast<T>(embed[(long long)c2f[v] * D + c]);
+}
+
 int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq);
 
 int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq) {
@@ -1198,6 +1339,27 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
   if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dlogits, s->cv_pad, s->cembedT, s->cv_pad, R, D, s->cv_pad,
                        s->dxf, D, nullptr, ef)))
     return rc;
+  // full backprop: dW[out, in] += (1/lambda) * dY^T X over the R token rows, as a GEMM of the
+  // transposed 16-bit operands (K = R) accumulated into the fp32 gradient by the reduce-add epilogue
+  auto wgrad_gemm = [&](const void* dY, int ld_dy, int n_out, const void* X, int ld_x, int n_in, float* out) -> int {
+    int rc2;
+    if ((rc2 = transpose16(dY, R, n_out, ld_dy, s->tA, R, bf, m->st))) return rc2;
+    if ((rc2 = transpose16(X, R, n_in, ld_x, s->tB, R, bf, m->st))) return rc2;
+    EpiParams ew;
+    std::memset(&ew, 0, sizeof(ew));
+    ew.M = n_out;
+    ew.N = n_in;
+    ew.alpha = inv_lambda;
+    return model_gemm(m, pick_bn(n_in, EPI_RESID), EPI_RESID, s->tA, R, s->tB, R, n_out, n_in, R, out, n_in, nullptr,
+                      ew);
+  };
+  if (s->full) {
+    B2P_CHECK_CUDA(cudaMemsetAsync(s->gw, 0, (size_t)s->n_w * 4, m->st));
+    B2P_CHECK_CUDA(cudaMemsetAsync(s->g_embed, 0, (size_t)c.vocab * D * 4, m->st));
+    B2P_CHECK_CUDA(cudaMemsetAsync(s->g_cembed, 0, (size_t)m->cv * D * 4, m->st));
+    // classifier: g_cembed[CV, D] = dlogits^T · xn_final  (train.m:938-941)
+    if ((rc = wgrad_gemm(s->dlogits, s->cv_pad, m->cv, v.xn_final, D, D, s->g_cembed))) return rc;
+  }
   const int nblk = rms_blocks(R);
   auto part = [&](int idx) { return s->rms_part + (size_t)idx * nblk * D; };
   RmsBwdArgs ra;
@@ -1226,6 +1388,13 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
                          static_cast<char*>(s->w2T) + (size_t)l * H * D * e, D, R, H, D, s->dsilu, H, nullptr, p0)))
       return rc;
     if ((rc = swiglu_bwd(s->dsilu, slab(v.h13, l, 2 * H), R, H, s->dh13, bf, m->st))) return rc;
+    if (s->full) {
+      // dW2 = dffn^T · silu_out and dW1|W3 = [dh1|dh3]^T · x2norm  (train.m:1027-1034)
+      if ((rc = launch_swiglu_gate(slab(v.h13, l, 2 * H), R, H, s->gate, bf, m->st))) return rc;
+      if ((rc = wgrad_gemm(s->d16, D, D, s->gate, H, H, s->gw + s->o_2 + (size_t)l * D * H))) return rc;
+      if ((rc = wgrad_gemm(s->dh13, 2 * H, 2 * H, slab(v.xn2, l, D), D, D, s->gw + s->o_13 + (size_t)l * 2 * H * D)))
+        return rc;
+    }
     EpiParams p1;
     std::memset(&p1, 0, sizeof(p1));
     p1.M = R;
@@ -1246,6 +1415,9 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
     ra.part = part(2 * l + 1);
     ra.rows = R;
     if ((rc = rms_bwd(ra, D, bf, m->st))) return rc;
+    // dWo = (alpha dx2)^T · attn_out  (train.m:1067-1070)
+    if (s->full && (rc = wgrad_gemm(s->d16, D, D, slab(v.attn, l, QD), QD, QD, s->gw + s->o_o + (size_t)l * D * QD)))
+      return rc;
     // Wo: U'_o = dx2s · B_o; da = dx2s · Wo + U'_o · A_o
     EpiParams p2;
     std::memset(&p2, 0, sizeof(p2));
@@ -1291,6 +1463,10 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
     ab.kv_heads = c.kv_heads;
     ab.ngroups = n_seq;
     if ((rc = attention_backward(ab, bf, m->st))) return rc;
+    // dWq|dWk|dWv = dQKV^T · xnorm  (train.m:1143-1151)
+    if (s->full && (rc = wgrad_gemm(s->dqkv, QKV + kUCols, QKV, slab(v.xn, l, D), D, D,
+                                    s->gw + s->o_qkv + (size_t)l * QKV * D)))
+      return rc;
     // U'_{q,k,v} = d{q,k,v} · B_{q,k,v} into the 64 extra columns of dqkv; then
     // dx_attn = [dQKV | U'] · [W_qkv ; A_qkv]  (base data gradient + A^T (B^T dY) in one GEMM)
     const int QKVp = QKV + kUCols;
@@ -1319,10 +1495,18 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
     ra.part = part(2 * l);
     ra.rows = R;
     if ((rc = rms_bwd(ra, D, bf, m->st))) return rc;
-    // factored LoRA weight gradients of the layer
-    if ((rc = lora_wgrad(s->d_jobs + (size_t)l * kMaxWgradJobs, kMaxWgradJobs, std::max(D, QD), R, r, inv_lambda,
-                         s->wgrad_part, bf, m->st)))
+    // factored LoRA weight gradients of the layer (the adapters are not trained in full mode)
+    if (!s->full && (rc = lora_wgrad(s->d_jobs + (size_t)l * kMaxWgradJobs, kMaxWgradJobs, std::max(D, QD), R, r,
+                                     inv_lambda, s->wgrad_part, bf, m->st)))
       return rc;
+  }
+  if (s->full) {
+    // embedding: rows of dx grouped by token (embed_backward), then the classifier rows
+    embed_scatter_kernel<<<R, 256, 0, m->st>>>(cur, D, s->d_seg, R, d_tok, s->g_embed, inv_lambda);
+    B2P_POST_LAUNCH();
+    cembed_scatter_kernel<<<(int)(((long long)m->cv * D + 255) / 256), 256, 0, m->st>>>(s->g_cembed, m->d_c2f, m->cv,
+                                                                                      D, s->g_embed);
+    B2P_POST_LAUNCH();
   }
   const int nvec = 2 * L + 1;
   rms_part_reduce_kernel<<<(nvec * D + 255) / 256, 256, 0, m->st>>>(s->rms_part, nvec, nblk, D, s->d_rms_off,
@@ -1365,6 +1549,158 @@ int adam_step(b2p_model* m, float lr, float b1, float b2, float eps, float wd) {
   return B2P_OK;
 }
 
+// Switch the state to full backprop: fp32 masters up-converted from the current 16-bit
+// weights (the masters start from what the forward computes with), gradients, moments.
+int ensure_full(b2p_model* m) {
+  P16State* s = m->p16;
+  if (s->full && s->mw) return B2P_OK;
+  const auto& c = m->cfg;
+  const long long L = c.nlayers, D = c.dim, H = c.hidden, QD = m->q_dim, QKV = m->qkv_dim;
+  const long long n_qkv = L * QKV * D, n_o = L * D * QD, n_13 = L * 2 * H * D, n_2 = L * D * H;
+  s->o_qkv = 0;
+  s->o_o = n_qkv;
+  s->o_13 = s->o_o + n_o;
+  s->o_2 = s->o_13 + n_13;
+  s->n_w = s->o_2 + n_2;
+  const size_t nw = (size_t)s->n_w, ne = (size_t)c.vocab * D;
+  P16_ALLOC(s->mw, nw * 4);
+  P16_ALLOC(s->gw, nw * 4);
+  P16_ALLOC(s->am_w, nw * 4);
+  P16_ALLOC(s->av_w, nw * 4);
+  P16_ALLOC(s->g_embed, ne * 4);
+  P16_ALLOC(s->g_cembed, ne * 4);
+  P16_ALLOC(s->am_e, ne * 4);
+  P16_ALLOC(s->av_e, ne * 4);
+  P16_ALLOC(s->norm_part, (3 * kNormBlocks + 2) * 4);
+  B2P_CHECK_CUDA(cudaMemset(s->am_w, 0, nw * 4));
+  B2P_CHECK_CUDA(cudaMemset(s->av_w, 0, nw * 4));
+  B2P_CHECK_CUDA(cudaMemset(s->am_e, 0, ne * 4));
+  B2P_CHECK_CUDA(cudaMemset(s->av_e, 0, ne * 4));
+  // segment table: [0] weights, [1] embedding, [2 ..] rms vectors (rms_att|rms_ffn per layer, rms_final)
+  const int nrs = (int)L + 1;
+  std::vector<long long> off(2 + nrs), len(2 + nrs);
+  off[0] = 0; len[0] = s->n_w;
+  off[1] = 0; len[1] = (long long)ne;
+  for (int l = 0; l < (int)L; ++l) {
+    off[2 + l] = (long long)l * m->layer_size + m->oRa;  // rms_att and rms_ffn are adjacent
+    len[2 + l] = 2 * D;
+  }
+  off[2 + L] = m->oRfinal;
+  len[2 + L] = D;
+  P16_ALLOC(s->d_nseg, 2 * off.size() * sizeof(long long));
+  B2P_CHECK_CUDA(cudaMemcpy(s->d_nseg, off.data(), off.size() * 8, cudaMemcpyHostToDevice));
+  B2P_CHECK_CUDA(cudaMemcpy(s->d_nseg + off.size(), len.data(), len.size() * 8, cudaMemcpyHostToDevice));
+  const bool bf = m->bf16;
+  auto up = [&](const void* src, float* dst, long long n) -> int {
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 16);
+    if (bf)
+      f16_to_f32_kernel<__nv_bfloat16><<<blocks, 256, 0, m->st>>>(static_cast<const __nv_bfloat16*>(src), dst, n);
+    else
+      f16_to_f32_kernel<__half><<<blocks, 256, 0, m->st>>>(static_cast<const __half*>(src), dst, n);
+    B2P_POST_LAUNCH();
+    return B2P_OK;
+  };
+  int rc;
+  if ((rc = up(m->wqkv, s->mw + s->o_qkv, n_qkv)) || (rc = up(m->wo, s->mw + s->o_o, n_o)) ||
+      (rc = up(m->w13, s->mw + s->o_13, n_13)) || (rc = up(m->w2, s->mw + s->o_2, n_2)))
+    return rc;
+  s->full = true;
+  s->full_t = 0;
+  release_rows(s);  // the row buffers gain the full-mode scratch
+  s->gen++;
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
+}
+
+// Host tokens -> staged tokens/targets, the per-token row segments, then the gradient pass.
+int full_grad(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq) {
+  int rc = model_ready(m);
+  if (rc) return rc;
+  if ((rc = ensure_model_state(m))) return rc;
+  if ((rc = ensure_full(m))) return rc;
+  if ((rc = ensure_weights(m))) return rc;
+  const int R = n_seq * m->cfg.seq;
+  if ((rc = ensure_rows(m, R))) return rc;
+  if ((rc = model_stage_tokens(m, tokens, ctargets, n_seq))) return rc;
+  // rows grouped by token, each group in sequence order (deterministic embedding scatter)
+  std::vector<int32_t> idx(R);
+  for (int i = 0; i < R; ++i) idx[i] = i;
+  std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return tokens[a] < tokens[b]; });
+  std::vector<int32_t> seg(2 * (size_t)R + 2, 0);
+  int nseg = 0;
+  for (int i = 0; i < R; ++i)
+    if (i == 0 || tokens[idx[i]] != tokens[idx[i - 1]]) seg[1 + nseg++] = i;
+  seg[1 + nseg] = R;
+  seg[0] = nseg;
+  std::copy(idx.begin(), idx.end(), seg.begin() + R + 2);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(m->p16->d_seg, seg.data(), seg.size() * 4, cudaMemcpyHostToDevice, m->st));
+  return p16_grad(m, m->d_tok, m->d_tok + (size_t)n_seq * m->cfg.seq, n_seq);
+}
+
+// Global-norm clip and AdamW over weights (wd), embedding (wd) and rms weights (no wd),
+// train.m:1309-1517; then the 16-bit weights, compact embedding and transposes follow.
+int full_update(b2p_model* m, float lr, float wd, float clip) {
+  B2P_REQUIRE(m && m->p16 && m->p16->full, "no full-backprop gradient: run b2p_full_grad first");
+  P16State* s = m->p16;
+  DeviceCtx* ctx = nullptr;
+  int rc = ctx_get(&ctx);
+  if (rc) return rc;
+  const auto& c = m->cfg;
+  const long long* soff = s->d_nseg;
+  const long long* slen = s->d_nseg + (c.nlayers + 3);
+  const int nrs = c.nlayers + 1;
+  B2P_CHECK_CUDA(cudaMemsetAsync(s->flag, 0, 4, m->st));
+  sqnorm_kernel<<<kNormBlocks, 256, 0, m->st>>>(s->gw, soff, slen, 1, s->norm_part);
+  B2P_POST_LAUNCH();
+  sqnorm_kernel<<<kNormBlocks, 256, 0, m->st>>>(s->g_embed, soff + 1, slen + 1, 1, s->norm_part + kNormBlocks);
+  B2P_POST_LAUNCH();
+  sqnorm_kernel<<<kNormBlocks, 256, 0, m->st>>>(s->grad, soff + 2, slen + 2, nrs, s->norm_part + 2 * kNormBlocks);
+  B2P_POST_LAUNCH();
+  clip_scale_kernel<<<1, 32, 0, m->st>>>(s->norm_part, 3 * kNormBlocks, clip, s->flag, ctx->status);
+  B2P_POST_LAUNCH();
+  s->full_t++;
+  const float b1 = 0.9f, b2 = 0.95f, eps = 1e-8f;  // train.m:266
+  const float bc1 = 1.0f - powf(b1, (float)s->full_t), bc2 = 1.0f - powf(b2, (float)s->full_t);
+  AdamSegArgs a;
+  a.gscale = s->norm_part + 3 * kNormBlocks + 1;
+  a.b1 = b1;
+  a.omb1 = 1.0f - b1;
+  a.b2 = b2;
+  a.omb2 = 1.0f - b2;
+  a.ibc1 = 1.0f / bc1;
+  a.ibc2 = 1.0f / bc2;
+  a.eps = eps;
+  a.neg_lr = -lr;
+  a.flag = s->flag;
+  auto run = [&](float* w, const float* g, float* mo, float* ve, const long long* o, const long long* n, int ns,
+                 float wdv) -> int {
+    a.w = w; a.g = g; a.m = mo; a.v = ve; a.seg_off = o; a.seg_len = n; a.nseg = ns; a.wd = wdv;
+    adam_seg_kernel<<<148 * 8, 256, 0, m->st>>>(a);
+    B2P_POST_LAUNCH();
+    return B2P_OK;
+  };
+  if ((rc = run(s->mw, s->gw, s->am_w, s->av_w, soff, slen, 1, wd))) return rc;
+  if ((rc = run(m->embed, s->g_embed, s->am_e, s->av_e, soff + 1, slen + 1, 1, wd))) return rc;
+  if ((rc = run(m->theta, s->grad, s->adam_m, s->adam_v, soff + 2, slen + 2, nrs, 0.0f))) return rc;
+  // refresh the compute copies
+  const long long n_qkv = s->o_o - s->o_qkv, n_o = s->o_13 - s->o_o, n_13 = s->o_2 - s->o_13, n_2 = s->n_w - s->o_2;
+  if ((rc = launch_f32_to_16(s->mw + s->o_qkv, m->wqkv, n_qkv, m->bf16, m->st)) ||
+      (rc = launch_f32_to_16(s->mw + s->o_o, m->wo, n_o, m->bf16, m->st)) ||
+      (rc = launch_f32_to_16(s->mw + s->o_13, m->w13, n_13, m->bf16, m->st)) ||
+      (rc = launch_f32_to_16(s->mw + s->o_2, m->w2, n_2, m->bf16, m->st)))
+    return rc;
+  const long long ncv = (long long)m->cv * c.dim;
+  if (m->bf16)
+    cembed_refresh_kernel<__nv_bfloat16><<<(int)((ncv + 255) / 256), 256, 0, m->st>>>(
+        m->embed, m->d_c2f, m->cv, c.dim, static_cast<__nv_bfloat16*>(m->cembed));
+  else
+    cembed_refresh_kernel<__half><<<(int)((ncv + 255) / 256), 256, 0, m->st>>>(m->embed, m->d_c2f, m->cv, c.dim,
+                                                                              static_cast<__half*>(m->cembed));
+  B2P_POST_LAUNCH();
+  m->weights_version++;  // the transposed copies are rebuilt before the next backward
+  return B2P_OK;
+}
+
 }  // namespace
 
 void p16_release(P16State* s) {
@@ -1372,7 +1708,8 @@ void p16_release(P16State* s) {
   if (s->graph.exec) cudaGraphExecDestroy(s->graph.exec);
   release_rows(s);
   free_ptrs({s->wqkvT, s->woT, s->w13T, s->w2T, s->cembedT, s->a_oT, s->bblk_qkv, s->bblk_o, s->grad, s->adam_m,
-             s->adam_v, s->flag, s->d_jobs, s->d_rms_off});
+             s->adam_v, s->flag, s->d_jobs, s->d_rms_off, s->mw, s->gw, s->am_w, s->av_w, s->g_embed, s->g_cembed,
+             s->am_e, s->av_e, s->norm_part, s->d_nseg});
   delete s;
 }
 
@@ -1439,6 +1776,67 @@ int b2p_p16_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets,
   if (loss) B2P_CHECK_CUDA(cudaMemcpyAsync(loss, m->var_loss, 4, cudaMemcpyDeviceToHost, m->st));
   B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
   return check_device_status(m->st);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int b2p_full_grad(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float* loss) {
+  int rc = full_grad(m, tokens, ctargets, n_seq);
+  if (rc) return rc;
+  if (loss) B2P_CHECK_CUDA(cudaMemcpyAsync(loss, m->var_loss, 4, cudaMemcpyDeviceToHost, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+int b2p_full_update(b2p_model* m, float lr, float wd, float clip, float* grad_norm) {
+  int rc = full_update(m, lr, wd, clip);
+  if (rc) return rc;
+  if (grad_norm)
+    B2P_CHECK_CUDA(cudaMemcpyAsync(grad_norm, m->p16->norm_part + 3 * kNormBlocks, 4, cudaMemcpyDeviceToHost, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+int b2p_full_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float lr, float wd,
+                  float clip, float* loss, float* grad_norm) {
+  int rc = full_grad(m, tokens, ctargets, n_seq);
+  if (rc) return rc;
+  if ((rc = full_update(m, lr, wd, clip))) return rc;
+  if (loss) B2P_CHECK_CUDA(cudaMemcpyAsync(loss, m->var_loss, 4, cudaMemcpyDeviceToHost, m->st));
+  if (grad_norm)
+    B2P_CHECK_CUDA(cudaMemcpyAsync(grad_norm, m->p16->norm_part + 3 * kNormBlocks, 4, cudaMemcpyDeviceToHost, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
+long long b2p_full_weight_count(b2p_model* m) {
+  if (!m || ensure_model_state(m) || ensure_full(m)) return -1;
+  return m->p16->n_w;
+}
+
+int b2p_full_read(b2p_model* m, int what, float* out, long long n) {
+  B2P_REQUIRE(m && out, "null argument");
+  int rc = ensure_model_state(m);
+  if (rc) return rc;
+  if ((rc = ensure_full(m))) return rc;
+  P16State* s = m->p16;
+  const long long ne = (long long)m->cfg.vocab * m->cfg.dim;
+  const void* src = nullptr;
+  long long cnt = 0;
+  switch (what) {
+    case B2P_FULL_WEIGHTS: src = s->mw; cnt = s->n_w; break;
+    case B2P_FULL_WEIGHT_GRADS: src = s->gw; cnt = s->n_w; break;
+    case B2P_FULL_EMBED: src = m->embed; cnt = ne; break;
+    case B2P_FULL_EMBED_GRAD: src = s->g_embed; cnt = ne; break;
+    case B2P_FULL_TRAINABLE_GRAD: src = s->grad; cnt = m->P; break;
+    default: set_error("unknown quantity %d", what); return B2P_ERR_ARG;
+  }
+  B2P_REQUIRE(n == cnt, "quantity %d has %lld floats, got %lld", what, cnt, n);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(out, src, (size_t)cnt * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return B2P_OK;
 }
 
 }  // extern "C"

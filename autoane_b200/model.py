@@ -201,6 +201,56 @@ class Model:
         _lib.call("b2p_p16_step", self.h, _u16(tok), _u16(tgt), n_seq, lr, C.byref(loss))
         return loss.value
 
+    # ---- full backprop (train.m) ----
+    FULL_WEIGHTS, FULL_WEIGHT_GRADS, FULL_EMBED, FULL_EMBED_GRAD, FULL_TRAINABLE_GRAD = range(5)
+
+    def full_grad(self, tokens, ctargets) -> float:
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        n_seq = tok.shape[0] if tok.ndim == 2 else 1
+        loss = C.c_float()
+        _lib.call("b2p_full_grad", self.h, _u16(tok), _u16(tgt), n_seq, C.byref(loss))
+        return loss.value
+
+    def full_update(self, lr: float, wd: float = 0.1, clip: float = 1.0) -> float:
+        norm = C.c_float()
+        _lib.call("b2p_full_update", self.h, lr, wd, clip, C.byref(norm))
+        return norm.value
+
+    def full_step(self, tokens, ctargets, lr: float, wd: float = 0.1, clip: float = 1.0):
+        tok = np.ascontiguousarray(tokens, np.uint16)
+        tgt = np.ascontiguousarray(ctargets, np.uint16)
+        n_seq = tok.shape[0] if tok.ndim == 2 else 1
+        loss, norm = C.c_float(), C.c_float()
+        _lib.call("b2p_full_step", self.h, _u16(tok), _u16(tgt), n_seq, lr, wd, clip, C.byref(loss), C.byref(norm))
+        return loss.value, norm.value
+
+    def full_read(self, what: int) -> np.ndarray:
+        c = self.cfg
+        n = {self.FULL_WEIGHTS: None, self.FULL_WEIGHT_GRADS: None, self.FULL_EMBED: c.vocab * c.dim,
+             self.FULL_EMBED_GRAD: c.vocab * c.dim, self.FULL_TRAINABLE_GRAD: self.P}[what]
+        if n is None:
+            n = int(self._lib.b2p_full_weight_count(self.h))
+        out = np.empty(n, np.float32)
+        _lib.call("b2p_full_read", self.h, what, out.ctypes.data, n)
+        return out
+
+    def split_full_weights(self, flat: np.ndarray) -> dict:
+        """Device full-mode layout -> per-layer reference matrices (Wq, Wk, Wv, Wo, W1, W2, W3)."""
+        c = self.cfg
+        L, D, H = c.nlayers, c.dim, c.hidden
+        QD, KVD = c.heads * c.head_dim, c.kv_heads * c.head_dim
+        QKV = QD + 2 * KVD
+        o = 0
+        qkv = flat[o:o + L * QKV * D].reshape(L, QKV, D); o += L * QKV * D
+        wo = flat[o:o + L * D * QD].reshape(L, D, QD); o += L * D * QD
+        w13 = flat[o:o + L * 2 * H * D].reshape(L, H // 128, 2, 128, D); o += L * 2 * H * D
+        w2 = flat[o:o + L * D * H].reshape(L, D, H)
+        return {"Wq": [qkv[l, :QD] for l in range(L)], "Wk": [qkv[l, QD:QD + KVD] for l in range(L)],
+                "Wv": [qkv[l, QD + KVD:] for l in range(L)], "Wo": [wo[l] for l in range(L)],
+                "W1": [w13[l, :, 0].reshape(H, D) for l in range(L)], "W2": [w2[l] for l in range(L)],
+                "W3": [w13[l, :, 1].reshape(H, D) for l in range(L)]}
+
     def set_option(self, option: int, value: int):
         _lib.call("b2p_model_set_option", self.h, option, value)
 

@@ -251,6 +251,45 @@ int b2p_adam_state(b2p_model* m, int set, int* t, float* mom, float* vel);
 int b2p_p16_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float lr, float* loss);
 
 /* ======================================================================
+ * Full backprop (training/train.m:686-1520): every projection weight, the RMS
+ * weights and the tied embedding are trained. The first call switches the
+ * model to full mode: fp32 master copies of the projection weights are made
+ * from the current 16-bit weights and kept on the device. The LoRA adapters
+ * are left alone (keep their B at zero so they do not change the forward).
+ * ====================================================================== */
+
+/* Forward + backward of n_seq sequences: dX through every layer and dW of
+ * Wq/Wk/Wv/Wo/W1/W2/W3, the RMS weights and the embedding (the classifier rows
+ * scattered into it, vocab_scatter_grads, cpu_ops.h:176). Synchronous. */
+int b2p_full_grad(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float* loss);
+
+/* Global-norm clipping to `clip` (0: off) and AdamW (b1 0.9, b2 0.95, eps 1e-8;
+ * weight decay wd on projection weights and embedding, none on RMS weights),
+ * train.m:1309-1517; then the 16-bit weights the forward uses are refreshed.
+ * grad_norm (may be NULL) receives the pre-clip norm. */
+int b2p_full_update(b2p_model* m, float lr, float wd, float clip, float* grad_norm);
+
+/* b2p_full_grad followed by b2p_full_update. */
+int b2p_full_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq, float lr, float wd,
+                  float clip, float* loss, float* grad_norm);
+
+/* Number of fp32 projection-weight masters (switches the model to full mode). */
+long long b2p_full_weight_count(b2p_model* m);
+
+/* Copy a full-mode quantity to `out` (host or device, n floats):
+ *   B2P_FULL_WEIGHTS / B2P_FULL_WEIGHT_GRADS: b2p_full_weight_count floats, laid out as
+ *     [every layer's stacked Wq;Wk;Wv] [every Wo] [every W1/W3, interleaved in 128-row
+ *     blocks] [every W2], each matrix row-major [out, in];
+ *   B2P_FULL_EMBED / B2P_FULL_EMBED_GRAD: [vocab, dim];
+ *   B2P_FULL_TRAINABLE_GRAD: trainable-count floats, RMS entries meaningful. */
+#define B2P_FULL_WEIGHTS 0
+#define B2P_FULL_WEIGHT_GRADS 1
+#define B2P_FULL_EMBED 2
+#define B2P_FULL_EMBED_GRAD 3
+#define B2P_FULL_TRAINABLE_GRAD 4
+int b2p_full_read(b2p_model* m, int what, float* out, long long n);
+
+/* ======================================================================
  * Kern-level boundary: one compiled operator with baked weights and
  * channel-first fp32 host I/O, the verbs of training/io.h and
  * bridge/ane_bridge.h without MIL text.

@@ -507,11 +507,13 @@ static void grad_project(float* dA, float* dB, const float* dW, const float* A, 
   cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, rank, in_dim, out_dim, 1.0f, B, rank, dW, in_dim, 1.0f, dA, in_dim);
 }
 
-/* P16 step body without the optimizer (train_mezo.m:1982-2087 with the conv-fused
- * forward: frozen base + split LoRA; then bp_lora_backward through W + B·A).
- * grad (theta layout) is overwritten; returns the loss. */
-float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
-                  float* grad) {
+/* Shared forward-with-saves + backward. grad (theta layout) is overwritten with the
+ * LoRA A/B and RMS gradients. With dw != NULL it also receives every projection's
+ * dW (train.m:1027-1151; per layer Wq, Wk, Wv, Wo, W1, W2, W3, each [out, in]), and
+ * gembed [vocab, dim] the embedding gradient: embed_backward rows, then the
+ * classifier gradient scattered through c2f (NULL: identity). Returns the loss. */
+static float backprop(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
+                      float* grad, float* dw, float* gembed, const int32_t* c2f) {
   const int D = m->dim, H = m->hidden, S = m->seq, QD = m->heads * m->hd, KVD = m->kv_heads * m->hd;
   const int r = m->rank, NL = m->nlayers, CV = m->cv, ratio = m->heads / m->kv_heads;
   const or_layout L = or_lora_layout(NL, D, QD, KVD, r);
@@ -526,6 +528,7 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
   float* x2 = (float*)xmalloc(sizeof(float) * DS * NL);
   float* h1 = (float*)xmalloc(sizeof(float) * HS * NL);
   float* h3 = (float*)xmalloc(sizeof(float) * HS * NL);
+  float* x2n = dw ? (float*)xmalloc(sizeof(float) * DS * NL) : NULL;
   float* x = (float*)xmalloc(sizeof(float) * DS);
   float* xn = (float*)xmalloc(sizeof(float) * DS);
   float* Q = (float*)xmalloc(sizeof(float) * QS);
@@ -568,6 +571,7 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
     resid_add(x, o, m->res_alpha, DS);
     memcpy(x2 + DS * l, x, sizeof(float) * DS);
     or_rmsnorm(xn, x, th + L.rms_ffn, D, S);
+    if (x2n) memcpy(x2n + DS * l, xn, sizeof(float) * DS);
     or_sgemm_nn(H, S, D, m->W1[l], xn, h1 + HS * l, 0.0f);
     or_sgemm_nn(H, S, D, m->W3[l], xn, h3 + HS * l, 0.0f);
     for (size_t i = 0; i < HS; i++) {
@@ -580,6 +584,11 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
   /* x is x_pre_final; logits and dlogits (cross_entropy_loss, cpu_ops.h:108-133) */
   or_rmsnorm(xn, x, theta + L.rms_final, D, S);
   cblas_sgemm(OrRowMajor, OrTrans, OrTrans, S, CV, D, 1.0f, xn, S, m->cembed, D, 0.0f, logits, CV);
+  float* xn_final = NULL;
+  if (dw) {
+    xn_final = (float*)xmalloc(sizeof(float) * DS);
+    memcpy(xn_final, xn, sizeof(float) * DS);
+  }
   float total = 0;
   const float invS = 1.0f / S;
   for (int t = 0; t < S; t++) {
@@ -620,9 +629,18 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
   or_rmsnorm_bwd(dxr, grad + L.rms_final, dy, x, theta + L.rms_final, D, S);
   memcpy(dy, dxr, sizeof(float) * DS);
   const float alpha = m->res_alpha;
+  const size_t per_l = (size_t)QD * D + 2 * (size_t)KVD * D + (size_t)D * QD + 3 * (size_t)H * D;
+  float* gate = dw ? (float*)xmalloc(sizeof(float) * HS) : NULL;
   for (int l = NL - 1; l >= 0; l--) {
     const float* th = theta + (size_t)l * L.layer_size;
     float* gl = grad + (size_t)l * L.layer_size;
+    float* dWq = dw ? dw + per_l * l : NULL;
+    float* dWk = dw ? dWq + (size_t)QD * D : NULL;
+    float* dWv = dw ? dWk + (size_t)KVD * D : NULL;
+    float* dWo = dw ? dWv + (size_t)KVD * D : NULL;
+    float* dW1 = dw ? dWo + (size_t)D * QD : NULL;
+    float* dW2 = dw ? dW1 + (size_t)H * D : NULL;
+    float* dW3 = dw ? dW2 + (size_t)D * H : NULL;
     for (size_t i = 0; i < DS; i++) dx2s[i] = dy[i] * alpha; /* dffn */
     cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, H, S, D, 1.0f, m->W2[l], H, dx2s, S, 0.0f, dsl, S);
     for (size_t i = 0; i < HS; i++) {
@@ -630,6 +648,16 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
       const float sig = 1.0f / (1.0f + expf(-a1));
       dh3[i] = dsl[i] * (a1 * sig);
       dh1[i] = (dsl[i] * a3) * (sig * (1.0f + a1 * (1.0f - sig)));
+    }
+    if (dw) {
+      /* dW2 = dffn · silu_outᵀ; dW1 = dh1 · x2normᵀ; dW3 = dh3 · x2normᵀ (train.m:1027-1034) */
+      for (size_t i = 0; i < HS; i++) {
+        const float sv = h1[HS * l + i] / (1.0f + expf(-h1[HS * l + i]));
+        gate[i] = sv * h3[HS * l + i];
+      }
+      cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, D, H, S, 1.0f, dx2s, S, gate, S, 0.0f, dW2, H);
+      cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, H, D, S, 1.0f, dh1, S, x2n + DS * l, S, 0.0f, dW1, D);
+      cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, H, D, S, 1.0f, dh3, S, x2n + DS * l, S, 0.0f, dW3, D);
     }
     cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, H, 1.0f, m->W1[l], D, dh1, S, 0.0f, dxr, S);
     cblas_sgemm(OrRowMajor, OrTrans, OrNoTrans, D, S, H, 1.0f, m->W3[l], D, dh3, S, 1.0f, dxr, S);
@@ -642,6 +670,7 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
     free(Wo_e);
     cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, D, QD, S, 1.0f, dx2s, S, att + QS * l, S, 0.0f, dW, QD);
     grad_project(gl + L.Ao, gl + L.Bo, dW, th + L.Ao, th + L.Bo, D, r, QD);
+    if (dw) memcpy(dWo, dW, sizeof(float) * (size_t)D * QD);
     memcpy(Q, Qs + QS * l, sizeof(float) * QS);
     memcpy(K, Ks + KS * l, sizeof(float) * KS);
     or_rope_forward(Q, S, QD, m->hd, m->rope_theta);
@@ -656,10 +685,13 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
     const float* xnl = xnorm + DS * l;
     cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, QD, D, S, 1.0f, dqf, S, xnl, S, 0.0f, dW, D);
     grad_project(gl + L.Aq, gl + L.Bq, dW, th + L.Aq, th + L.Bq, QD, r, D);
+    if (dw) memcpy(dWq, dW, sizeof(float) * (size_t)QD * D);
     cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, KVD, D, S, 1.0f, dk, S, xnl, S, 0.0f, dW, D);
     grad_project(gl + L.Ak, gl + L.Bk, dW, th + L.Ak, th + L.Bk, KVD, r, D);
+    if (dw) memcpy(dWk, dW, sizeof(float) * (size_t)KVD * D);
     cblas_sgemm(OrRowMajor, OrNoTrans, OrTrans, KVD, D, S, 1.0f, dv, S, xnl, S, 0.0f, dW, D);
     grad_project(gl + L.Av, gl + L.Bv, dW, th + L.Av, th + L.Bv, KVD, r, D);
+    if (dw) memcpy(dWv, dW, sizeof(float) * (size_t)KVD * D);
     float* Wq_e = merged(m->Wq[l], th + L.Bq, th + L.Aq, QD, r, D);
     float* Wk_e = merged(m->Wk[l], th + L.Bk, th + L.Ak, KVD, r, D);
     float* Wv_e = merged(m->Wv[l], th + L.Bv, th + L.Av, KVD, r, D);
@@ -673,11 +705,40 @@ float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens,
     or_rmsnorm_bwd(dy, gl + L.rms_att, dxr, x_pre + DS * l, th + L.rms_att, D, S);
     for (size_t i = 0; i < DS; i++) dy[i] = dy[i] + dx2[i];
   }
+  if (dw) {
+    /* embed_backward (cpu_ops.h:199-207) then vocab_scatter_grads (cpu_ops.h:176-182) of
+     * gcembed = dlogitsᵀ · x_finalᵀ (train.m:938-941) */
+    memset(gembed, 0, sizeof(float) * (size_t)m->vocab * D);
+    for (int t = 0; t < S; t++) {
+      float* row = gembed + (size_t)tokens[t] * D;
+      for (int d = 0; d < D; d++) row[d] = dy[(size_t)d * S + t] + row[d];
+    }
+    float* gce = (float*)xmalloc(sizeof(float) * (size_t)CV * D);
+    cblas_sgemm(OrRowMajor, OrTrans, OrTrans, CV, D, S, 1.0f, logits, CV, xn_final, S, 0.0f, gce, D);
+    for (int v = 0; v < CV; v++) {
+      float* row = gembed + (size_t)(c2f ? c2f[v] : v) * D;
+      for (int d = 0; d < D; d++) row[d] = gce[(size_t)v * D + d] + row[d];
+    }
+    free(gce);
+    free(x2n);
+    free(gate);
+    free(xn_final);
+  }
   free(x_pre); free(xnorm); free(Qs); free(Ks); free(Vs); free(att); free(x2); free(h1); free(h3);
   free(x); free(xn); free(Q); free(K); free(Kt); free(Vt); free(o); free(g); free(tmp); free(logits);
   free(dy); free(dxr); free(dx2); free(dx2s); free(dsl); free(dh1); free(dh3); free(da); free(dqf); free(dkf);
   free(dvf); free(dk); free(dv); free(dW);
   return loss;
+}
+
+float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
+                  float* grad) {
+  return backprop(m, theta, tokens, ctargets, grad, NULL, NULL, NULL);
+}
+
+float or_full_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
+                   float* grad, float* dw, float* gembed, const int32_t* c2f) {
+  return backprop(m, theta, tokens, ctargets, grad, dw, gembed, c2f);
 }
 
 /* adam_update (cpu_ops.h:62-104), one rounding per vectorised operation */

@@ -106,6 +106,11 @@ void or_sdpa_backward(const float* Q, const float* Kt, const float* Vt, const fl
  * base weights + split LoRA (conv-fused P16), backward through W + B·A. */
 float or_p16_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
                   float* grad);
+/* Full backprop (train.m:686-1192): the P16 gradient plus dW of every projection
+ * (dw: per layer Wq, Wk, Wv, Wo, W1, W2, W3, each [out, in]) and the embedding
+ * gradient gembed [vocab, dim] (c2f: compact -> full id, NULL = identity). */
+float or_full_grad(const or_model* m, const float* theta, const uint16_t* tokens, const uint16_t* ctargets,
+                   float* grad, float* dw, float* gembed, const int32_t* c2f);
 /* adam_update (cpu_ops.h:62-104) over n elements, step t >= 1 */
 void or_adam(float* w, const float* g, float* m, float* v, size_t n, int t, float lr, float b1, float b2, float eps,
              float wd);

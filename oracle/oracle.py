@@ -74,6 +74,10 @@ def lib() -> C.CDLL:
         L.or_p16_grad.restype = C.c_float
         L.or_p16_grad.argtypes = [C.POINTER(_Model), C.POINTER(C.c_float), C.POINTER(C.c_uint16),
                                   C.POINTER(C.c_uint16), C.POINTER(C.c_float)]
+        L.or_full_grad.restype = C.c_float
+        L.or_full_grad.argtypes = [C.POINTER(_Model), C.POINTER(C.c_float), C.POINTER(C.c_uint16),
+                                   C.POINTER(C.c_uint16), C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                   C.POINTER(C.c_float), C.POINTER(C.c_int32)]
         L.or_adam.argtypes = [C.POINTER(C.c_float)] * 4 + [C.c_size_t, C.c_int] + [C.c_float] * 5
         L.or_sgemm_nn.argtypes = [C.c_int] * 3 + [C.POINTER(C.c_float)] * 3 + [C.c_float]
         for n in ("or_rmsnorm",):
@@ -233,6 +237,31 @@ class OracleModel:
                                  _u16(np.ascontiguousarray(tokens, np.uint16)),
                                  _u16(np.ascontiguousarray(ctargets, np.uint16)), _f(grad))
         return float(loss), grad
+
+    def full_grad(self, theta: np.ndarray, tokens, ctargets, c2f=None):
+        """(loss, theta-layout grad, dW per layer (dict name -> list), embedding grad) of one sequence."""
+        cfg = self.cfg
+        D, H, QD, KVD = cfg.dim, cfg.hidden, cfg.q_dim, cfg.kv_dim
+        shapes = [("Wq", (QD, D)), ("Wk", (KVD, D)), ("Wv", (KVD, D)), ("Wo", (D, QD)), ("W1", (H, D)),
+                  ("W2", (D, H)), ("W3", (H, D))]
+        per_l = sum(a * b for _, (a, b) in shapes)
+        dw = np.zeros(per_l * cfg.nlayers, np.float32)
+        gembed = np.zeros((cfg.vocab, D), np.float32)
+        grad = np.zeros_like(theta)
+        cp = None
+        if c2f is not None:
+            c2f = np.ascontiguousarray(c2f, np.int32)
+            cp = c2f.ctypes.data_as(C.POINTER(C.c_int32))
+        loss = lib().or_full_grad(C.byref(self.m), _f(np.ascontiguousarray(theta, np.float32)),
+                                  _u16(np.ascontiguousarray(tokens, np.uint16)),
+                                  _u16(np.ascontiguousarray(ctargets, np.uint16)), _f(grad), _f(dw), _f(gembed), cp)
+        out = {n: [] for n, _ in shapes}
+        o = 0
+        for l in range(cfg.nlayers):
+            for n, (a, b) in shapes:
+                out[n].append(dw[o:o + a * b].reshape(a, b))
+                o += a * b
+        return float(loss), grad, out, gembed
 
     def mezo_step(self, theta: np.ndarray, tokens, ctargets, seed: int, eps: float, lr: float):
         lp, lm, g = C.c_float(), C.c_float(), C.c_float()

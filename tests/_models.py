@@ -84,3 +84,14 @@ def small_cfg(nlayers=2, seq=128, rank=8):
     """A SmolLM2-shaped (GQA 15/5, hd 64) slice with fewer layers, for fast parity runs."""
     return O.ModelCfg(dim=960, hidden=2560, heads=15, kv_heads=5, hd=64, seq=seq, nlayers=nlayers, vocab=49152,
                       rank=rank, rope_theta=100000.0)
+
+
+def rms_slices(syn):
+    """Slices of the RMS weights (rms_att, rms_ffn per layer, rms_final) in the trainable layout."""
+    lay, D = syn.layout, syn.cfg.dim
+    out = []
+    for l in range(syn.cfg.nlayers):
+        b = l * lay.layer_size
+        out += [slice(b + lay.rms_att, b + lay.rms_att + D), slice(b + lay.rms_ffn, b + lay.rms_ffn + D)]
+    out.append(slice(lay.rms_final, lay.rms_final + D))
+    return out
