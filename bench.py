@@ -290,7 +290,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true", help="skip the in-region per-GEMM CUDA events")
     ap.add_argument("--p16-seqs", type=int, default=P16_SEQS_PER_GPU, help="sequences per GPU per P16 step")
-    ap.add_argument("--workload", choices=["mezo", "p16", "gemm"], default="mezo",
+    ap.add_argument("--full-seqs", type=int, default=32, help="sequences per GPU per full-backprop step")
+    ap.add_argument("--workload", choices=["mezo", "p16", "full", "gemm"], default="mezo",
                     help="mezo: the headline DP MeZO-LoRA-split step; p16: DP backprop-LoRA step; "
                          "gemm: projection-GEMM sweep (one line per shape)")
     args = ap.parse_args()
@@ -300,6 +301,8 @@ def main():
         return run_reference(args) if args.workload == "mezo" else run_reference_p16(args)
     if args.workload == "p16":
         return run_p16(args)
+    if args.workload == "full":
+        return run_full(args)
 
     import torch
     import torch.distributed as dist
@@ -719,6 +722,142 @@ def run_reference_p16(args):
                       "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0,
                               "d2h_bytes_per_step": 0}}), flush=True)
     return 0
+
+
+# --------------------------------------------------------------------------- full backprop (config 0)
+AR_DIMS = dict(dim=512, hidden=1408, heads=8, kv_heads=2, head_dim=64, seq=128, nlayers=4, vocab=49152, rank=8,
+               rope_theta=10000.0)  # training/models/autoresearch.h
+REF_FULL_MS = 24.0  # reference train.m CPU step on the autoresearch model (FINDINGS.md:94)
+
+
+def full_flops_per_seq() -> float:
+    """Projection FLOPs of one train.m step per sequence: forward + dX + dW of the 7 projections and the
+    compact classifier (3 x forward)."""
+    d = AR_DIMS
+    s, D, H = d["seq"], d["dim"], d["hidden"]
+    qd, kvd = d["heads"] * d["head_dim"], d["kv_heads"] * d["head_dim"]
+    per_layer = D * (qd + 2 * kvd) + qd * D + 3 * D * H
+    return 3.0 * (d["nlayers"] * 2 * s * per_layer + 2 * s * N_ACTIVE * D)
+
+
+def ar_synth(layer: int):
+    rng = np.random.default_rng([4242, layer])
+    D, H = AR_DIMS["dim"], AR_DIMS["hidden"]
+    qd, kvd = AR_DIMS["heads"] * AR_DIMS["head_dim"], AR_DIMS["kv_heads"] * AR_DIMS["head_dim"]
+    shapes = [(qd, D), (kvd, D), (kvd, D), (D, qd), (H, D), (D, H), (H, D)]
+    return [rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02) for sh in shapes]
+
+
+def run_full(args):
+    import torch
+    from autoane_b200 import _lib
+    from autoane_b200.model import BF16, F16, Config, Model
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    _lib.call("b2p_init", local)
+    NSEQ = args.full_seqs
+    cfg = Config(dtype=BF16 if args.dtype == "bf16" else F16, max_groups=NSEQ, **AR_DIMS)
+    model = Model(cfg)
+    ws = [ar_synth(l) for l in range(AR_DIMS["nlayers"])]
+    for l in range(AR_DIMS["nlayers"]):
+        model.set_layer(l, *ws[l])
+    rng = np.random.default_rng([4242, 99])
+    embed = (rng.standard_normal((AR_DIMS["vocab"], AR_DIMS["dim"]), dtype=np.float32) * 0.02).astype(np.float32)
+    model.set_embedding(embed, np.arange(N_ACTIVE, dtype=np.int32))
+    D, r, L = AR_DIMS["dim"], AR_DIMS["rank"], AR_DIMS["nlayers"]
+    qd, kvd = AR_DIMS["heads"] * 64, AR_DIMS["kv_heads"] * 64
+    theta = np.zeros(model.P, np.float32)
+    per = [r * D, qd * r, r * D, kvd * r, r * D, kvd * r, r * qd, D * r, D, D]
+    o = 0
+    for l in range(L):
+        for k, n in enumerate(per):
+            if k >= 8:
+                theta[o:o + n] = 1.0  # RMS weights; LoRA B = 0 so the adapters do not act
+            elif k % 2 == 0:
+                theta[o:o + n] = rng.standard_normal(n).astype(np.float32) / np.sqrt(r)
+            o += n
+    theta[o:o + D] = 1.0
+    model.set_trainable(theta)
+    tokens = token_stream()
+    W, K = args.warmup, args.steps
+    seq = AR_DIMS["seq"]
+
+    def batch(step):
+        g = np.random.default_rng([7919, step, rank])
+        pos = g.integers(0, int(len(tokens) * 0.9) - seq - 1, NSEQ)
+        return (np.stack([tokens[p:p + seq] for p in pos]), np.stack([tokens[p + 1:p + 1 + seq] for p in pos]))
+    batches = [batch(s) for s in range(W + K)]
+    stream = torch.cuda.ExternalStream(model.stream)
+    for s in range(W):
+        model.full_step(*batches[s], 3e-4, 0.1, 1.0)
+    torch.cuda.synchronize()
+    try:
+        phys = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    except (KeyError, ValueError, IndexError):
+        phys = local
+    clocks = ClockSampler(phys)
+    clocks.start()
+    n0 = int(_lib.load().b2p_launch_count())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    t0 = time.perf_counter()
+    last = (0.0, 0.0)
+    for s in range(W, W + K):
+        last = model.full_step(*batches[s], 3e-4, 0.1, 1.0)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    host_s = time.perf_counter() - t0
+    dev_ms = ev0.elapsed_time(ev1)
+    n_launch = int(_lib.load().b2p_launch_count()) - n0
+    clk = clocks.stop()
+    units = NSEQ * K
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_full_rate(ws, embed, theta, tokens)
+        line = {"metric": "full-backprop (train.m) seq-steps/s, autoresearch 36.4M (4L d512 8/2 heads FFN 1408) T128",
+                "value": round(units / (dev_ms / 1000.0), 3), "unit": "seq-steps/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": round(units / (dev_ms / 1000.0) / (1000.0 / REF_FULL_MS), 2), "dtype": args.dtype,
+                "data": "synthetic",
+                "config": {"workload": f"full backprop, per GPU {NSEQ} x 128-token sequences per step; forward, dX and "
+                                       "dW of every projection, tied-embedding gradient, global-norm clip 1.0, AdamW "
+                                       "(lr 3e-4, wd 0.1); replicas on N > 1 GPUs", "model": "autoresearch-4L-512d",
+                           "global_batch": NSEQ * world, "seq_len": seq, "parallelism": f"replicas x{world}",
+                           "tflops_per_gpu": round(NSEQ * full_flops_per_seq() * K / (dev_ms / 1000.0) / 1e12, 2),
+                           "last_loss": round(float(last[0]), 5), "last_grad_norm": round(float(last[1]), 5),
+                           "inputs": "host tokens staged every step (16 KB H2D incl. the per-token segment table)"},
+                "e2e": {"value": round(units / host_s, 3), "unit": "seq-steps/s",
+                        "h2d_bytes_per_step": NSEQ * seq * 2 * 4 + (2 * NSEQ * seq + 2) * 4,
+                        "d2h_bytes_per_step": 8},
+                "gpu_launches": n_launch, "roofline": None, "clocks": clk, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    model.close()
+    return 0
+
+
+def cpu_full_rate(ws, embed, theta, tokens, max_seconds: float = 20.0):
+    """The oracle's train.m step (or_full_grad + adam_update), batch 1, on this host's cores."""
+    from oracle import oracle as O
+    threads = O.set_threads(os.cpu_count() or 1)
+    cfg = O.ModelCfg(dim=AR_DIMS["dim"], hidden=AR_DIMS["hidden"], heads=AR_DIMS["heads"],
+                     kv_heads=AR_DIMS["kv_heads"], hd=64, seq=AR_DIMS["seq"], nlayers=AR_DIMS["nlayers"],
+                     vocab=AR_DIMS["vocab"], rank=AR_DIMS["rank"], rope_theta=AR_DIMS["rope_theta"])
+    weights = {k: [w[i] for w in ws] for i, k in enumerate(("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3"))}
+    om = O.OracleModel(cfg, weights, embed, np.ascontiguousarray(embed[:N_ACTIVE]))
+    seq = AR_DIMS["seq"]
+    n, t0 = 0, time.perf_counter()
+    while n < 3 or (time.perf_counter() - t0 < max_seconds and n < 200):
+        p = (n * 7919) % (len(tokens) - seq - 2)
+        loss, g, dw, ge = om.full_grad(theta, tokens[p:p + seq], tokens[p + 1:p + 1 + seq])
+        flat = np.concatenate([a.ravel() for k in dw for a in dw[k]])
+        zeros = np.zeros_like(flat)
+        O.adam(flat, flat.copy(), zeros, zeros.copy(), 1, 3e-4, wd=0.1)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "seq-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{n} train.m steps (batch 1, T 128) of the oracle restatement (or_full_grad + adam_update over "
+                      "the projection weights), OpenBLAS; the reference's train.m is Objective-C and does not build here"}
 
 
 # --------------------------------------------------------------------------- projection-GEMM sweep
