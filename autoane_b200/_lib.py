@@ -67,6 +67,9 @@ ABI: dict[str, tuple] = {
     "b2p_full_step": (i32, [vp, u16p, u16p, i32, f32, f32, f32, fp, fp]),
     "b2p_full_weight_count": (i64, [vp]),
     "b2p_full_read": (i32, [vp, i32, vp, i64]),
+    "b2p_ckpt_read_header": (i32, [cstr, vp]),
+    "b2p_ckpt_save": (i32, [vp, cstr, cstr, vp]),
+    "b2p_ckpt_load": (i32, [vp, cstr, cstr, ip, i32, i32, vp]),
     "b2p_compile": (vp, [vp, C.POINTER(fp)]),
     "b2p_input_bytes": (szt, [vp, i32]),
     "b2p_output_bytes": (szt, [vp, i32]),
@@ -102,6 +105,17 @@ class OpDesc(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("kind", "ic", "oc", "seq", "q_dim", "kv_dim", "hidden")] + [
         ("res_alpha", C.c_float), ("dtype", C.c_int), ("n_parts", C.c_int), ("part_oc", C.c_int * 3)]
 
+
+class CkptHeader(C.Structure):
+    """b2p_ckpt_header: the reference's 96-byte BLZT v4 CkptHdr (training/config.h:99-108)."""
+    _fields_ = [(n, C.c_int) for n in ("magic", "version", "step", "total_steps", "n_layers", "vocab_size", "dim",
+                                        "hidden_dim", "n_heads", "seq_len")] + [
+        ("lr", C.c_float), ("loss", C.c_float), ("cum_compile", C.c_double), ("cum_train", C.c_double),
+        ("cum_wall", C.c_double)] + [(n, C.c_int) for n in ("cum_steps", "cum_batches", "adam_t", "kv_heads",
+                                                              "head_dim", "q_dim")]
+
+
+CKPT_MAGIC, CKPT_VERSION, LORA_MAGIC = 0x424C5A54, 4, 0x4C4F5241
 
 OP_CONV1X1, OP_QKV_FUSED, OP_FFN_FUSED, OP_DYN_MATMUL, OP_LM_HEAD_CE, OP_DX = range(6)
 

@@ -707,6 +707,7 @@ int b2p_model_set_embedding(b2p_model* m, const float* embed, const int32_t* com
   m->d_c2f = nullptr;
   B2P_CHECK_CUDA(cudaMalloc(&m->d_c2f, (size_t)cv * sizeof(int32_t)));
   B2P_CHECK_CUDA(cudaMemcpy(m->d_c2f, compact_to_full, (size_t)cv * sizeof(int32_t), cudaMemcpyHostToDevice));
+  m->h_c2f.assign(compact_to_full, compact_to_full + cv);
   int rc = upload16(m, m->cembed, ce.data(), ce.size());
   if (rc) return rc;
   m->embed_set = true;

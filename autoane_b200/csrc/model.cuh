@@ -79,6 +79,7 @@ struct b2p_model {
   float* prep_wf = nullptr;       // [max_groups][dim] perturbed rms_final per variant
   int prep_ld = 0;
   int32_t* d_c2f = nullptr;       // [cv] compact -> full vocabulary id (device copy)
+  std::vector<int32_t> h_c2f;     // host copy of the same map (checkpoint loads rebuild the compact rows)
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
   Stager stg;
@@ -125,5 +126,19 @@ struct ForwardSaves {
   float* row_lse = nullptr;  // [R] lm-head log-sum-exp per row
 };
 int model_run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv);
+
+// Device buffers of the backprop state that checkpoints read and write (p16.cu).
+// The full-mode fields are null unless the model is (or, with make_full, is made)
+// a full-backprop model.
+struct TrainView {
+  float *adam_m = nullptr, *adam_v = nullptr;  // trainable-set Adam moments
+  int* adam_t = nullptr;
+  bool full = false;
+  float *mw = nullptr, *am_w = nullptr, *av_w = nullptr;  // projection masters + AdamW moments
+  float *am_e = nullptr, *av_e = nullptr;                 // embedding AdamW moments
+  long long o_qkv = 0, o_o = 0, o_13 = 0, o_2 = 0;
+  int* full_t = nullptr;
+};
+int p16_view(b2p_model* m, bool make_full, TrainView* v);
 
 }  // namespace b2p

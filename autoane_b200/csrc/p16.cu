@@ -1741,6 +1741,39 @@ int b2p_p16_grad_device(b2p_model* m, const int32_t* d_tokens, const int32_t* d_
   return B2P_OK;
 }
 
+}  // extern "C"
+
+namespace b2p {
+
+int p16_view(b2p_model* m, bool make_full, TrainView* v) {
+  int rc = ensure_model_state(m);
+  if (rc) return rc;
+  if (make_full && (rc = ensure_full(m))) return rc;
+  P16State* s = m->p16;
+  *v = TrainView();
+  v->adam_m = s->adam_m;
+  v->adam_v = s->adam_v;
+  v->adam_t = &s->adam_t;
+  if (s->full && s->mw) {
+    v->full = true;
+    v->mw = s->mw;
+    v->am_w = s->am_w;
+    v->av_w = s->av_w;
+    v->am_e = s->am_e;
+    v->av_e = s->av_e;
+    v->o_qkv = s->o_qkv;
+    v->o_o = s->o_o;
+    v->o_13 = s->o_13;
+    v->o_2 = s->o_2;
+    v->full_t = &s->full_t;
+  }
+  return B2P_OK;
+}
+
+}  // namespace b2p
+
+extern "C" {
+
 void* b2p_model_grad(b2p_model* m) { return (m && m->p16) ? (void*)m->p16->grad : nullptr; }
 
 int b2p_adam_step(b2p_model* m, float lr, float b1, float b2, float eps, float wd) {

@@ -254,12 +254,39 @@ class Model:
     def set_option(self, option: int, value: int):
         _lib.call("b2p_model_set_option", self.h, option, value)
 
+    # ---- checkpoints (BLZT v4 + LORA sidecar) ----
+    def save_checkpoint(self, path, lora_path=None, **header):
+        """b2p_ckpt_save; header keywords (step, total_steps, lr, loss, cum_*) fill the CkptHdr."""
+        h = _lib.CkptHeader(**header)
+        _lib.call("b2p_ckpt_save", self.h, str(path).encode(), None if lora_path is None else str(lora_path).encode(),
+                  C.byref(h))
+
+    def load_checkpoint(self, path, lora_path=None, compact_to_full=None, full: bool = False) -> dict:
+        """b2p_ckpt_load; returns the file's header as a dict."""
+        h = _lib.CkptHeader()
+        c2f = None if compact_to_full is None else np.ascontiguousarray(compact_to_full, np.int32)
+        _lib.call("b2p_ckpt_load", self.h, str(path).encode(), None if lora_path is None else str(lora_path).encode(),
+                  None if c2f is None else c2f.ctypes.data_as(C.POINTER(C.c_int)), 0 if c2f is None else len(c2f),
+                  int(full), C.byref(h))
+        return header_dict(h)
+
     def sign_masks(self, seeds) -> np.ndarray:
         sd = np.ascontiguousarray(seeds, np.uint64)
         words = (self.P + 31) // 32
         out = np.empty((len(sd), words), np.uint32)
         _lib.call("b2p_sign_masks", self.h, _u64(sd), len(sd), out.ctypes.data_as(C.POINTER(C.c_uint32)))
         return out
+
+
+def header_dict(h: _lib.CkptHeader) -> dict:
+    return {name: getattr(h, name) for name, _ in h._fields_}
+
+
+def read_checkpoint_header(path) -> dict:
+    """b2p_ckpt_read_header (host only: no device work)."""
+    h = _lib.CkptHeader()
+    _lib.call("b2p_ckpt_read_header", str(path).encode(), C.byref(h))
+    return header_dict(h)
 
 
 def load_synthetic(model: Model, weights: dict, embed, compact_to_full, theta):

@@ -38,6 +38,7 @@ extern "C" {
 #define B2P_ERR_DEVICE (-3)
 #define B2P_ERR_STATE (-4)
 #define B2P_ERR_UNSUPPORTED (-5)
+#define B2P_ERR_IO (-6)
 
 /* ---- compute dtypes ---- */
 #define B2P_F16 0
@@ -288,6 +289,59 @@ long long b2p_full_weight_count(b2p_model* m);
 #define B2P_FULL_EMBED_GRAD 3
 #define B2P_FULL_TRAINABLE_GRAD 4
 int b2p_full_read(b2p_model* m, int what, float* out, long long n);
+
+/* ======================================================================
+ * Checkpoints: the reference's BLZT v4 file (CkptHdr, training/config.h:99-108;
+ * writers mezo_save_checkpoint, train_mezo.m:706-744, and save_checkpoint,
+ * train.m:176-208) and the LORA adapter sidecar (lora_save_checkpoint,
+ * train_mezo.m:791-815). Little-endian fp32 in the reference's order, so the
+ * reference's readers (generate.py, tools/export_to_gguf.py) take these files.
+ * ====================================================================== */
+typedef struct {
+  int magic, version, step, total_steps;
+  int n_layers, vocab_size, dim, hidden_dim, n_heads, seq_len;
+  float lr, loss;
+  double cum_compile, cum_train, cum_wall;
+  int cum_steps, cum_batches, adam_t;
+  int kv_heads, head_dim, q_dim;
+} b2p_ckpt_header; /* 96 bytes */
+#define B2P_CKPT_MAGIC 0x424C5A54 /* "BLZT" */
+#define B2P_CKPT_VERSION 4
+#define B2P_LORA_MAGIC 0x4C4F5241 /* "LORA" */
+
+/* Read a BLZT file's header and check magic, version and that step and adam_t
+ * lie in [0, 1e7] (train.m:217-229). Host only. */
+int b2p_ckpt_read_header(const char* path, b2p_ckpt_header* hdr);
+
+/* Write the model as BLZT v4. The structural fields come from the model; step,
+ * total_steps, lr, loss, cum_* come from `hdr` (may be NULL: zeros).
+ *   - full-backprop models write the fp32 masters, the AdamW moments and t
+ *     (save_checkpoint, train.m:176-208);
+ *   - other models write their frozen projections (the 16-bit values the forward
+ *     uses, widened to fp32) with zero Adam slots and adam_t 0
+ *     (mezo_save_checkpoint, train_mezo.m:706-744).
+ * RMS vectors come from the trainable set, the embedding from the model.
+ * With `lora_path` non-NULL the adapters also go to that sidecar (its adam_t is
+ * the backprop-LoRA Adam step count) and the BLZT Wq/Wk/Wv/Wo are the merged
+ * W + B·A (lora_merge_weight, config.h:278-283), as the backprop-LoRA run leaves
+ * them in its checkpoint (train_mezo.m:2107-2110, 3180-3191). */
+int b2p_ckpt_save(b2p_model* m, const char* path, const char* lora_path, const b2p_ckpt_header* hdr);
+
+/* Load a BLZT v4 file written for this model's shapes (every structural header
+ * field must match; load_checkpoint, train.m:211-258, mezo_load_checkpoint,
+ * train_mezo.m:746-789): frozen projections, RMS vectors (into the trainable
+ * set), rms_final and the embedding (compact rows rebuilt from
+ * `compact_to_full`/`cv`, or from the model's current map when NULL).
+ * Full-backprop models, or any model when `full` is 1, also take the fp32
+ * masters, the AdamW moments and t. With `lora_path` non-NULL the sidecar's
+ * adapters go into the trainable set, the backprop-LoRA Adam state restarts at
+ * the sidecar's step count with zero moments, and the projections are
+ * un-merged (W - B·A in fp32, train_mezo.m:1134-1151) before the upload. A
+ * missing sidecar is an error (the reference falls back to fresh adapters;
+ * here the caller chooses by passing NULL). hdr (may be NULL) receives the
+ * file's header. Reads are length-checked; a short file is B2P_ERR_IO. */
+int b2p_ckpt_load(b2p_model* m, const char* path, const char* lora_path, const int32_t* compact_to_full, int cv,
+                  int full, b2p_ckpt_header* hdr);
 
 /* ======================================================================
  * Kern-level boundary: one compiled operator with baked weights and

@@ -95,3 +95,36 @@ def rms_slices(syn):
         out += [slice(b + lay.rms_att, b + lay.rms_att + D), slice(b + lay.rms_ffn, b + lay.rms_ffn + D)]
     out.append(slice(lay.rms_final, lay.rms_final + D))
     return out
+
+
+CKPT_TINY = O.ModelCfg(dim=128, hidden=256, heads=2, kv_heads=1, hd=64, seq=64, nlayers=2, vocab=300, rank=8)
+
+
+def ckpt_case(cfg, seed: int = 5):
+    """Seeded checkpoint contents for `cfg`: per-layer frozen weights (fp16-representable, so a
+    16-bit device copy widens back to the same fp32), RMS vectors, rms_final, embedding, adapters
+    and the flat trainable vector holding the adapters and RMS vectors."""
+    rng = np.random.default_rng(seed)
+    D, H, QD, KVD, r = cfg.dim, cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.rank
+    shapes = {"Wq": (QD, D), "Wk": (KVD, D), "Wv": (KVD, D), "Wo": (D, QD), "W1": (H, D), "W2": (D, H),
+              "W3": (H, D)}
+    lay = O.lora_layout(cfg.nlayers, D, QD, KVD, r)
+    theta = np.zeros(lay.total, np.float32)
+    layers = []
+    for l in range(cfg.nlayers):
+        lw = {k: (rng.standard_normal(s) * 0.02).astype(np.float16).astype(np.float32) for k, s in shapes.items()}
+        b = l * lay.layer_size
+        for k, s in (("Aq", (r, D)), ("Bq", (QD, r)), ("Ak", (r, D)), ("Bk", (KVD, r)), ("Av", (r, D)),
+                     ("Bv", (KVD, r)), ("Ao", (r, QD)), ("Bo", (D, r))):
+            n = s[0] * s[1]
+            scale = 1.0 / np.sqrt(r) if k[0] == "A" else 0.01
+            theta[b + getattr(lay, k): b + getattr(lay, k) + n] = rng.standard_normal(n) * scale
+        for k in ("rms_att", "rms_ffn"):
+            v = (1.0 + 0.05 * rng.standard_normal(D)).astype(np.float32)
+            theta[b + getattr(lay, k): b + getattr(lay, k) + D] = v
+            lw[k] = v
+        layers.append(lw)
+    rms_final = (1.0 + 0.05 * rng.standard_normal(D)).astype(np.float32)
+    theta[lay.rms_final: lay.rms_final + D] = rms_final
+    embed = (rng.standard_normal((cfg.vocab, D)) * 0.02).astype(np.float32)
+    return layers, rms_final, embed, theta, lay
