@@ -1,0 +1,462 @@
+// attn_tc.cu — causal GQA attention forward on the tcgen05 tensor cores, for
+// sequences of 128 or 256 tokens (causal SDPA with the GQA tile of
+// training/io.h:439-446 and training/cpu_ops.h:321-360; softmax with the
+// 1/sqrt(64) scale, exact row maximum, fp32 sums).
+//
+// Work unit: (sequence g, KV head, 128-row query block qb). Its K and V rows
+// [0, 128·(qb+1)) are loaded once by TMA and serve the unit's heads/kv_heads
+// query heads. Persistent CTAs (one per SM) take units from a device counter,
+// heaviest query blocks first; the counter resets itself when the last CTA
+// finishes.
+//
+// Per query head (one 128 x 64 Q tile):
+//   MMA warp:   S = Q·Kᵀ  (tcgen05.mma, M 128, N = keys, K 64) into TMEM
+//   softmax WG: reads S rows (one TMEM lane per thread), exact row max over the
+//               causal keys, P = exp2((s - max)·scale·log2e) written back to TMEM
+//               as 16-bit pairs over the consumed S columns, row sum l in fp32
+//   MMA warp:   O = P·V   (A = P from TMEM, B = V in shared memory, MN-major)
+//   softmax WG: O / l to 16 bit, 128-byte row stores; row log2-sum-exp saved
+//               for the backward.
+// Two TMEM buffers of 256 columns (S, then P in its first half and O at
+// column 128) and two softmax warpgroups alternate over the heads, so the
+// softmax of one head overlaps the MMAs of the next.
+//
+// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM owner, 3 idle, 4-7 and 8-11
+// softmax warpgroups (warp % 4 selects its 32-lane TMEM quarter).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "engine.cuh"
+#include "kernels.cuh"
+#include "mma.cuh"
+#include "ptx.cuh"
+
+namespace b2p {
+namespace {
+
+constexpr int kAtRows = 128;   // query rows per tile (UMMA M)
+constexpr int kAtHD = 64;      // head dim
+constexpr int kAtMaxKeys = 256;
+constexpr int kAtThreads = 384;
+constexpr int kAtRing = 4;     // unit-id ring between the producer and the consumers
+constexpr uint32_t kAtTmemCols = 512;
+
+struct AtSmem {
+  static constexpr int kQ = kAtRows * kAtHD * 2;         // 16 KB Q tile
+  static constexpr int kKV = kAtMaxKeys * kAtHD * 2;     // 32 KB K or V tile
+  static constexpr int kQOff = 0;                        // 2 Q tiles (head double buffer)
+  static constexpr int kKOff = kQOff + 2 * kQ;           // 2 K tiles (unit double buffer)
+  static constexpr int kVOff = kKOff + 2 * kKV;          // 2 V tiles
+  static constexpr int kBarOff = kVOff + 2 * kKV;
+  static constexpr int kNumBars = 16 + 2 * kAtRing + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kTotal = kMiscOff + 64 + 1024;    // + 1024-byte alignment slack
+};
+
+// MN-major operand tile written by TMA with 128-byte swizzle: each 128-byte row
+// holds 64 consecutive N elements at one K index; groups of 8 K rows sit 1024 B
+// apart (SBO). The tile is one 64-element atom wide in N, so LBO is not used.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;             // LBO (single atom in N)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;     // SBO: 8 K rows x 128 B
+  d |= static_cast<uint64_t>(1u) << 46;             // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 (A read from tensor memory).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 TMEM lanes x 32 bit, 16 consecutive columns <- 16 registers per thread.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+struct Unit {
+  int g, kvh, qb, nkeys;
+};
+
+__device__ __forceinline__ Unit decode_unit(int u, const AttnArgs& a) {
+  const int per_qb = a.ngroups * a.kv_heads;
+  const int nqb = a.seq / kAtRows;
+  Unit r;
+  r.qb = nqb - 1 - u / per_qb;  // longest query blocks first
+  const int rem = u % per_qb;
+  r.g = rem / a.kv_heads;
+  r.kvh = rem % a.kv_heads;
+  r.nkeys = (r.qb + 1) * kAtRows;
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kAtThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a, float scale_log2, int total_units,
+                   uint32_t* status) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + AtSmem::kQOff;
+  uint8_t* sK = smem + AtSmem::kKOff;
+  uint8_t* sV = smem + AtSmem::kVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AtSmem::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* kv_full = bars + 4;
+  uint64_t* kv_empty = bars + 6;
+  uint64_t* s_full = bars + 8;
+  uint64_t* p_full = bars + 10;
+  uint64_t* o_full = bars + 12;
+  uint64_t* t_empty = bars + 14;
+  uint64_t* u_full = bars + 16;
+  uint64_t* u_empty = u_full + kAtRing;
+  uint64_t* drain_bar = u_empty + kAtRing;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + AtSmem::kMiscOff);
+  uint32_t* tmem_holder = misc;
+  volatile uint32_t* abort_flag = misc + 1;
+  volatile uint32_t* wg_abort = misc + 2;  // [2]
+  volatile int* ring = reinterpret_cast<volatile int*>(misc + 4);  // [kAtRing]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gq = a.heads / a.kv_heads;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);   // one arrive per softmax warp
+      mbar_init(&o_full[i], 1);
+      mbar_init(&t_empty[i], 4);
+    }
+    for (int i = 0; i < kAtRing; ++i) {
+      mbar_init(&u_full[i], 1);
+      mbar_init(&u_empty[i], 1 + 8);  // MMA thread + one arrive per softmax warp
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    wg_abort[0] = wg_abort[1] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, kAtTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: unit ids, K/V per unit, Q per head ----------------
+    if (lane == 0) {
+      int t = 0, k = 0;
+      bool ok = true;
+      for (;; ++k) {
+        const int slot = k % kAtRing;
+        const uint32_t ph = (uint32_t)(k / kAtRing) & 1u;
+        if (!mbar_wait(&u_empty[slot], ph ^ 1u, abort_flag, status, DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        const int u = atomicAdd(a.sched, 1);
+        ring[slot] = u;
+        mbar_arrive(&u_full[slot]);
+        if (u >= total_units) break;
+        const Unit un = decode_unit(u, a);
+        const int kvs = k & 1;
+        if (!mbar_wait(&kv_empty[kvs], ((uint32_t)(k >> 1) & 1u) ^ 1u, abort_flag, status, DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[kvs], (uint32_t)(2 * un.nkeys * kAtHD * 2));
+        const int row0 = un.g * a.seq;
+        for (int kb = 0; kb <= un.qb; ++kb) {
+          tma_load_2d(sK + kvs * AtSmem::kKV + kb * AtSmem::kQ, &tm, &kv_full[kvs], a.k_off + un.kvh * kAtHD,
+                      row0 + kb * kAtRows);
+          tma_load_2d(sV + kvs * AtSmem::kKV + kb * AtSmem::kQ, &tm, &kv_full[kvs], a.v_off + un.kvh * kAtHD,
+                      row0 + kb * kAtRows);
+        }
+        for (int j = 0; j < gq && ok; ++j, ++t) {
+          const int qs = t & 1;
+          if (!mbar_wait(&q_empty[qs], ((uint32_t)(t >> 1) & 1u) ^ 1u, abort_flag, status, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_full[qs], (uint32_t)AtSmem::kQ);
+          tma_load_2d(sQ + qs * AtSmem::kQ, &tm, &q_full[qs], a.q_off + (un.kvh * gq + j) * kAtHD,
+                      row0 + un.qb * kAtRows);
+        }
+        if (!ok) break;
+      }
+      if (!ok) {
+        // Let the copies in flight land before the CTA can exit (bounded waits).
+        for (int i = 1; i <= 2 && t - i >= 0; ++i) mbar_wait_drain(&q_full[(t - i) & 1], ((uint32_t)((t - i) >> 1)) & 1u);
+        for (int i = 1; i <= 2 && k - i >= 0; ++i)
+          mbar_wait_drain(&kv_full[(k - i) & 1], ((uint32_t)((k - i) >> 1)) & 1u);
+        // (the abort flag is set: every consumer's bounded wait returns)
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_s128 = umma_idesc_f16(BF16, kAtRows, 128);
+      const uint32_t idesc_s256 = umma_idesc_f16(BF16, kAtRows, 256);
+      const uint32_t idesc_o = umma_idesc_f16(BF16, kAtRows, kAtHD) | (1u << 16);  // B = V, MN-major
+      bool ok = true, issued_any = false;
+      // the head whose P·V is still to be issued (software pipeline: S of the next head first)
+      int pend_t = -1, pend_kvs = 0, pend_nkeys = 0;
+      bool pend_last = false;
+      auto issue_pv = [&]() -> bool {
+        const int b = pend_t & 1;
+        if (!mbar_wait(&p_full[b], (uint32_t)(pend_t >> 1) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t o_tmem = tmem_base + b * 256 + 128;
+        const uint32_t p_tmem = tmem_base + b * 256;
+        const uint32_t v_base = smem_u32(sV + pend_kvs * AtSmem::kKV);
+        for (int ks = 0; ks < pend_nkeys / 16; ++ks)
+          umma_f16_ts(o_tmem, p_tmem + ks * 8, sw128_mnmajor_desc(v_base + ks * 2048), idesc_o, ks > 0 ? 1u : 0u);
+        umma_commit(&o_full[b]);
+        if (pend_last) umma_commit(&kv_empty[pend_kvs]);
+        return true;
+      };
+      int t = 0;
+      for (int k = 0; ok; ++k) {
+        const int slot = k % kAtRing;
+        if (!mbar_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        const int u = ring[slot];
+        mbar_arrive(&u_empty[slot]);
+        if (u >= total_units) break;
+        const Unit un = decode_unit(u, a);
+        const int kvs = k & 1;
+        if (!mbar_wait(&kv_full[kvs], (uint32_t)(k >> 1) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        const uint32_t k_base = smem_u32(sK + kvs * AtSmem::kKV);
+        const uint32_t idesc_s = un.nkeys == 256 ? idesc_s256 : idesc_s128;
+        for (int j = 0; j < gq; ++j, ++t) {
+          const int b = t & 1;
+          const uint32_t n = (uint32_t)(t >> 1) & 1u;
+          if (!mbar_wait(&q_full[b], n, abort_flag, status, DEV_TIMEOUT_MMA) ||
+              !mbar_wait(&t_empty[b], n ^ 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(sQ + b * AtSmem::kQ);
+          for (int kk = 0; kk < kAtHD / 16; ++kk)
+            umma_f16_ss(tmem_base + b * 256, sw128_kmajor_desc(q_base + kk * 32), sw128_kmajor_desc(k_base + kk * 32),
+                        idesc_s, kk > 0 ? 1u : 0u);
+          umma_commit(&s_full[b]);
+          umma_commit(&q_empty[b]);
+          issued_any = true;
+          if (pend_t >= 0 && !issue_pv()) {
+            ok = false;
+            break;
+          }
+          pend_t = t;
+          pend_kvs = kvs;
+          pend_nkeys = un.nkeys;
+          pend_last = (j == gq - 1);
+        }
+      }
+      if (ok && pend_t >= 0) ok = issue_pv();
+      if (!ok && issued_any) {
+        umma_commit(drain_bar);
+        mbar_wait_drain(drain_bar, 0);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax / output warpgroups ----------------
+    const int wg = (warp - 4) >> 2;      // buffer this group owns
+    const int quarter = warp & 3;        // TMEM lane quarter
+    const int r = quarter * 32 + lane;   // row inside the query tile
+    const int wt = threadIdx.x - 128 - wg * 128;  // 0..127 within the group
+    const uint32_t bar_id = 3 + wg;
+    auto agree = [&](bool ok_wait) -> bool {
+      // every thread of the group takes the same continue/abort decision
+      named_bar_sync(bar_id, 128);
+      if (wt == 0) wg_abort[wg] = (*abort_flag || !ok_wait) ? 1u : 0u;
+      named_bar_sync(bar_id, 128);
+      return wg_abort[wg] == 0;
+    };
+    int t = 0;
+    for (int k = 0;; ++k) {
+      const int slot = k % kAtRing;
+      const bool okw = mbar_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u, abort_flag, status, DEV_TIMEOUT_EPILOGUE);
+      if (!agree(okw)) break;
+      const int u = ring[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&u_empty[slot]);
+      if (u >= total_units) break;
+      const Unit un = decode_unit(u, a);
+      const int qpos = un.qb * kAtRows + r;
+      const int diag = un.qb * 4 + quarter;  // 32-key chunk holding this warp's diagonal
+      const int nch = un.nkeys / 32;
+      bool stop = false;
+      for (int j = 0; j < gq; ++j, ++t) {
+        if ((t & 1) != wg) continue;
+        const uint32_t n = (uint32_t)(t >> 1) & 1u;
+        const int h = un.kvh * gq + j;
+        if (!agree(mbar_wait(&s_full[wg], n, abort_flag, status, DEV_TIMEOUT_EPILOGUE))) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + wg * 256 + ((uint32_t)(quarter * 32) << 16);
+        // pass 1: exact row maximum over the causal keys
+        float mx = -INFINITY;
+        for (int c = 0; c <= diag; c += 2) {
+          uint32_t v0[32], v1[32];
+          tmem_ld32(t_row + c * 32, v0);
+          const bool two = c + 1 <= diag;
+          if (two) tmem_ld32(t_row + (c + 1) * 32, v1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i <= qpos) mx = fmaxf(mx, __uint_as_float(v0[i]));
+          if (two) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if ((c + 1) * 32 + i <= qpos) mx = fmaxf(mx, __uint_as_float(v1[i]));
+          }
+        }
+        // pass 2: P = exp2((s - max)·scale), written as 16-bit pairs over consumed S columns
+        const float ms = mx * scale_log2;
+        float l = 0.f;
+        for (int c = 0; c < nch; ++c) {
+          uint32_t pk[16];
+          if (c <= diag) {
+            uint32_t v[32];
+            tmem_ld32(t_row + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const int key = c * 32 + i;
+              const float p0 = key <= qpos ? exp2f(fmaf(__uint_as_float(v[i]), scale_log2, -ms)) : 0.f;
+              const float p1 = key + 1 <= qpos ? exp2f(fmaf(__uint_as_float(v[i + 1]), scale_log2, -ms)) : 0.f;
+              l += p0 + p1;
+              pk[i >> 1] = pack_h2<T>(p0, p1);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          }
+          tmem_st16(t_row + c * 16, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[wg]);
+        const long long row = (long long)un.g * a.seq + qpos;
+        if (a.lse) a.lse[row * a.heads + h] = ms + log2f(l);
+        // output: O / l
+        if (!agree(mbar_wait(&o_full[wg], n, abort_flag, status, DEV_TIMEOUT_EPILOGUE))) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        uint32_t o0[32], o1[32];
+        tmem_ld32(t_row + 128, o0);
+        tmem_ld32(t_row + 160, o1);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&t_empty[wg]);
+        const float inv = 1.0f / l;
+        T* out = static_cast<T*>(a.out) + row * a.ld_out + h * kAtHD;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int col = c * 8 + 2 * e;
+            const float x0 = __uint_as_float(col < 32 ? o0[col] : o1[col - 32]);
+            const float x1 = __uint_as_float(col + 1 < 32 ? o0[col + 1] : o1[col + 1 - 32]);
+            w[e] = pack_h2<T>(x0 * inv, x1 * inv);
+          }
+          *reinterpret_cast<uint4*>(out + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      if (stop) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kAtTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    // the last CTA to finish resets the unit counter for the next launch
+    __threadfence();
+    if (atomicAdd(a.sched + 1, 1) == (int)gridDim.x - 1) {
+      a.sched[0] = 0;
+      a.sched[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace
+
+bool attention_tc_supported(const AttnArgs& a) {
+  return a.sched != nullptr && (a.seq == 128 || a.seq == 256) && a.ld_out % 8 == 0 && a.ld_qkv % 8 == 0 &&
+         a.q_off % 8 == 0 && a.k_off % 8 == 0 && a.v_off % 8 == 0 && a.kv_heads > 0 && a.heads % a.kv_heads == 0;
+}
+
+template <typename T>
+int launch_tc_t(const AttnArgs& a, cudaStream_t st) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  DeviceCtx* c = nullptr;
+  int rc = ctx_get(&c);
+  if (rc) return rc;
+  const long long rows = (long long)a.ngroups * a.seq;
+  CUtensorMap tm;
+  if ((rc = make_tmap_2d(&tm, a.qkv, BF16 ? TM_BF16 : TM_F16, (uint64_t)a.ld_qkv, (uint64_t)rows,
+                         (uint64_t)a.ld_qkv, kAtHD, kAtRows, 128)))
+    return rc;
+  const int total = a.ngroups * a.kv_heads * (a.seq / kAtRows);
+  const int grid = total < c->num_sms ? total : c->num_sms;
+  const float scale_log2 = (1.0f / sqrtf((float)kAtHD)) * 1.4426950408889634f;
+  static thread_local uint64_t attr_mask = 0;  // one per instantiation (per dtype)
+  if (!(attr_mask & (1ull << (c->device & 63)))) {
+    B2P_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtSmem::kTotal));
+    attr_mask |= 1ull << (c->device & 63);
+  }
+  attn_tc_kernel<T><<<grid, kAtThreads, AtSmem::kTotal, st>>>(tm, a, scale_log2, total, c->status);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
+int launch_attention_tc(const AttnArgs& a, bool bf16, cudaStream_t st) {
+  B2P_REQUIRE(attention_tc_supported(a), "tcgen05 attention needs seq 128 or 256, 16-byte aligned operands and a "
+                                         "unit counter");
+  return bf16 ? launch_tc_t<__nv_bfloat16>(a, st) : launch_tc_t<__half>(a, st);
+}
+
+}  // namespace b2p

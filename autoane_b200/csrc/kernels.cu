@@ -599,6 +599,7 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnArgs a, float scale_l
 }
 
 int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st) {
+  if (attention_tc_supported(a)) return launch_attention_tc(a, bf16, st);
   B2P_REQUIRE(a.seq % kAttnTile == 0, "attention needs seq %% 64 == 0 (got %d)", a.seq);
   B2P_REQUIRE(a.kv_heads > 0 && a.heads % a.kv_heads == 0, "heads must be a multiple of kv_heads");
   B2P_REQUIRE(a.ld_qkv % 8 == 0 && a.q_off % 8 == 0 && a.k_off % 8 == 0 && a.v_off % 8 == 0 && a.ld_out % 2 == 0,

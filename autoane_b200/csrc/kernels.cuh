@@ -78,8 +78,13 @@ struct AttnArgs {
   int ld_out;
   int seq, heads, kv_heads, ngroups;
   float* lse;  // optional [rows, heads]: each row's log2-domain softmax normaliser (for the backward)
+  int* sched = nullptr;  // 2 zeroed ints owned by the caller: enables the tcgen05 kernel (seq 128 / 256)
 };
+// Causal GQA attention: the tcgen05 kernel (attn_tc.cu) where it applies, else
+// the mma.sync kernel (64 x 64 tiles).
 int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st);
+bool attention_tc_supported(const AttnArgs& a);
+int launch_attention_tc(const AttnArgs& a, bool bf16, cudaStream_t st);
 
 // Row losses from the lm-head partials: loss_row = -(logit_tgt - M) + log(Σ s_i e^{m_i - M})
 // (training/cpu_ops.h:108-133); group_loss[g] = mean over the group's rows.

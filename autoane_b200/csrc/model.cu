@@ -52,6 +52,8 @@ int model_alloc(b2p_model* m) {
   B2P_CHECK_CUDA(cudaMalloc(&m->d_row_tgt, R * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->d_meta, 2 * m->max_groups * sizeof(int)));
   B2P_CHECK_CUDA(cudaMalloc(&m->d_var, m->max_groups * sizeof(VariantInfo)));
+  B2P_CHECK_CUDA(cudaMalloc(&m->attn_sched, 2 * sizeof(int)));
+  B2P_CHECK_CUDA(cudaMemset(m->attn_sched, 0, 2 * sizeof(int)));
   m->prep_ld = (std::max(c.dim, m->q_dim) + 7) / 8 * 8;
   B2P_CHECK_CUDA(cudaMalloc(&m->prep_a, (size_t)c.nlayers * m->max_groups * 4 * c.rank * m->prep_ld * e));
   B2P_CHECK_CUDA(cudaMalloc(&m->prep_w, (size_t)c.nlayers * m->max_groups * 2 * c.dim * 4));
@@ -90,7 +92,7 @@ void model_release(b2p_model* m) {
   void* dev[] = {m->wqkv, m->wo, m->w13, m->w2, m->cembed, m->embed, m->theta, m->masks, m->d_bufs,
                  m->d_polys, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
                  m->ce_tgt, m->row_loss, m->group_loss, m->var_loss, m->pairs, m->d_tok, m->d_row_tgt, m->d_meta,
-                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf, m->d_c2f};
+                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf, m->d_c2f, m->attn_sched};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (m->stg.base) cudaFreeHost(m->stg.base);
@@ -285,6 +287,7 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     aa.kv_heads = c.kv_heads;
     aa.ngroups = G;
     aa.lse = sv ? sv->lse + (size_t)l * R * c.heads : nullptr;
+    aa.sched = m->tc_attn ? m->attn_sched : nullptr;
     if ((rc = launch_attention(aa, m->bf16, m->st))) return rc;
     // LoRA-down of the attention output for Wo
     NormLoraArgs nb;
@@ -885,6 +888,9 @@ int b2p_model_set_option(b2p_model* m, int option, int value) {
       return B2P_OK;
     case B2P_OPT_GRAPHS:
       m->graphs = value != 0;
+      return B2P_OK;
+    case B2P_OPT_TC_ATTENTION:
+      m->tc_attn = value != 0;
       return B2P_OK;
     case B2P_OPT_GRAD_SCALE_LOG2:
       B2P_REQUIRE(value >= -30 && value <= 30, "gradient scale exponent %d out of range [-30, 30]", value);

@@ -85,7 +85,7 @@ struct P16State {
   struct Graph {
     const void* tok = nullptr;
     int n_seq = 0, gen = -1, scale_log2 = 0, prof_epoch = -1;
-    bool pair = true;
+    bool pair = true, tc_attn = true;
     cudaGraphExec_t exec = nullptr;
     long long launches = 0;
   } graph;
@@ -1251,7 +1251,8 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
   // re-records them, so b2p_model_profile_read reports the latest step.
   P16State::Graph& gr = s->graph;
   const bool hit = gr.exec && gr.tok == d_tok && gr.n_seq == n_seq && gr.gen == s->gen &&
-                   gr.scale_log2 == m->grad_scale_log2 && gr.pair == m->use_pair && gr.prof_epoch == m->prof_epoch;
+                   gr.scale_log2 == m->grad_scale_log2 && gr.pair == m->use_pair && gr.tc_attn == m->tc_attn &&
+                   gr.prof_epoch == m->prof_epoch;
   if (!hit) {
     if (gr.exec) cudaGraphExecDestroy(gr.exec);
     gr.exec = nullptr;
@@ -1280,6 +1281,7 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
     gr.gen = s->gen;
     gr.scale_log2 = m->grad_scale_log2;
     gr.pair = m->use_pair;
+    gr.tc_attn = m->tc_attn;
     gr.prof_epoch = m->prof_epoch;
     gr.launches = captured;
   }

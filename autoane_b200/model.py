@@ -16,7 +16,7 @@ import numpy as np
 from . import _lib
 
 F16, BF16 = 0, 1
-OPT_PAIR_GEMM, OPT_GRAD_SCALE_LOG2, OPT_GRAPHS = 1, 2, 3
+OPT_PAIR_GEMM, OPT_GRAD_SCALE_LOG2, OPT_GRAPHS, OPT_TC_ATTENTION = 1, 2, 3, 4
 
 
 @dataclass

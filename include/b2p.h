@@ -207,6 +207,10 @@ long long b2p_launch_count(void);
  * into a CUDA graph per (token buffer, batch size, buffers) and replayed; 0 issues
  * every kernel from the host instead. */
 #define B2P_OPT_GRAPHS 3
+/* B2P_OPT_TC_ATTENTION (default 1): causal attention on the tcgen05 kernel
+ * (sequences of 128 or 256 tokens); 0 uses the mma.sync kernel (64 x 64 tiles).
+ * Same results up to fp32 summation order. */
+#define B2P_OPT_TC_ATTENTION 4
 int b2p_model_set_option(b2p_model* m, int option, int value);
 
 /* ======================================================================
