@@ -21,8 +21,10 @@
 // column 128) and two softmax warpgroups alternate over the heads, so the
 // softmax of one head overlaps the MMAs of the next.
 //
-// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM owner, 3 idle, 4-7 and 8-11
-// softmax warpgroups (warp % 4 selects its 32-lane TMEM quarter).
+// Warps: 0 TMEM owner and TMA producer, 1 MMA issuer, 2-5 and 6-9 softmax
+// warpgroups (warp % 4 selects the warp's 32-lane TMEM quarter). The MMA
+// issuer polls its barriers and issues whichever of S(next) and P·V(oldest) is
+// ready first.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -37,8 +39,9 @@ namespace {
 constexpr int kAtRows = 128;   // query rows per tile (UMMA M)
 constexpr int kAtHD = 64;      // head dim
 constexpr int kAtMaxKeys = 256;
-constexpr int kAtThreads = 384;
+constexpr int kAtThreads = 320;
 constexpr int kAtRing = 4;     // unit-id ring between the producer and the consumers
+constexpr int kAtBatch = 1;    // 32-key chunks per TMEM round trip in the softmax passes
 constexpr uint32_t kAtTmemCols = 512;
 
 struct AtSmem {
@@ -87,6 +90,71 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Wait for this thread's outstanding tcgen05.ld; the destination registers pass
+// through the wait so no use of them is scheduled above it.
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// The SFU base-2 exponential (ex2.approx.ftz.f32; the inputs here are <= 0 and
+// results below 2^-126 flush to zero, far below what a 16-bit P can hold).
+__device__ __forceinline__ float sfu_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Max over a 32-key chunk; keys above `lim` (the query position) are masked when MASK.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+template <bool MASK>
+__device__ __forceinline__ float chunk_max(const uint32_t (&v)[32], float mx, int key0, int lim) {
+  if (MASK) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (key0 + i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+    return mx;
+  }
+  float m0 = mx, m1 = __uint_as_float(v[0]);
+#pragma unroll
+  for (int i = 1; i < 31; i += 4) {
+    m0 = max3(m0, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+    m1 = max3(m1, __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+  }
+  return max3(m0, m1, __uint_as_float(v[31]));
+}
+
+// P = exp2(s·scale - ms) of a 32-key chunk as 16 packed 16-bit pairs; adds the
+// fp32 values to l. Keys above `lim` (the query position) get P = 0 when MASK.
+template <typename T, bool MASK>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&v)[32], uint32_t (&pk)[16], float& l, float scale,
+                                          float ms, int key0, int lim) {
+  float la = 0.f, lb = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float p0 = sfu_exp2(fmaf(__uint_as_float(v[i]), scale, -ms));
+    float p1 = sfu_exp2(fmaf(__uint_as_float(v[i + 1]), scale, -ms));
+    if (MASK) {
+      p0 = key0 + i <= lim ? p0 : 0.f;
+      p1 = key0 + i + 1 <= lim ? p1 : 0.f;
+    }
+    la += p0;
+    lb += p1;
+    pk[i >> 1] = pack_h2<T>(p0, p1);
+  }
+  l += la + lb;
+}
 
 struct Unit {
   int g, kvh, qb, nkeys;
@@ -157,7 +225,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tm);
   }
-  if (warp == 2) {
+  if (warp == 0) {
     tmem_alloc(tmem_holder, kAtTmemCols);
     tmem_relinquish();
   }
@@ -222,80 +290,111 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const uint32_t idesc_s128 = umma_idesc_f16(BF16, kAtRows, 128);
       const uint32_t idesc_s256 = umma_idesc_f16(BF16, kAtRows, 256);
       const uint32_t idesc_o = umma_idesc_f16(BF16, kAtRows, kAtHD) | (1u << 16);  // B = V, MN-major
-      bool ok = true, issued_any = false;
-      // the head whose P·V is still to be issued (software pipeline: S of the next head first)
-      int pend_t = -1, pend_kvs = 0, pend_nkeys = 0;
-      bool pend_last = false;
-      auto issue_pv = [&]() -> bool {
-        const int b = pend_t & 1;
-        if (!mbar_wait(&p_full[b], (uint32_t)(pend_t >> 1) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) return false;
-        tc_fence_after();
-        const uint32_t o_tmem = tmem_base + b * 256 + 128;
-        const uint32_t p_tmem = tmem_base + b * 256;
-        const uint32_t v_base = smem_u32(sV + pend_kvs * AtSmem::kKV);
-        for (int ks = 0; ks < pend_nkeys / 16; ++ks)
-          umma_f16_ts(o_tmem, p_tmem + ks * 8, sw128_mnmajor_desc(v_base + ks * 2048), idesc_o, ks > 0 ? 1u : 0u);
-        umma_commit(&o_full[b]);
-        if (pend_last) umma_commit(&kv_empty[pend_kvs]);
-        return true;
-      };
-      int t = 0;
-      for (int k = 0; ok; ++k) {
-        const int slot = k % kAtRing;
-        if (!mbar_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        const int u = ring[slot];
-        mbar_arrive(&u_empty[slot]);
-        if (u >= total_units) break;
-        const Unit un = decode_unit(u, a);
-        const int kvs = k & 1;
-        if (!mbar_wait(&kv_full[kvs], (uint32_t)(k >> 1) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        const uint32_t k_base = smem_u32(sK + kvs * AtSmem::kKV);
-        const uint32_t idesc_s = un.nkeys == 256 ? idesc_s256 : idesc_s128;
-        for (int j = 0; j < gq; ++j, ++t) {
-          const int b = t & 1;
-          const uint32_t n = (uint32_t)(t >> 1) & 1u;
-          if (!mbar_wait(&q_full[b], n, abort_flag, status, DEV_TIMEOUT_MMA) ||
-              !mbar_wait(&t_empty[b], n ^ 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
-            ok = false;
-            break;
-          }
+      // S side: next head t_s of unit k (head j of gq); P·V side: oldest head t_p < t_s.
+      int t_s = 0, t_p = 0, k = 0, j = 0;
+      bool need_unit = true, need_kv = false, done_s = false, issued_any = false, ok = true;
+      Unit un{};
+      // per TMEM buffer: K/V stage, key count, last head of its unit (packed: bit 0 stage,
+      // bit 1 last, bits 8+ keys), so the state stays in registers
+      uint32_t pv_info0 = 0, pv_info1 = 0;
+      uint64_t t_idle = 0;
+      for (uint32_t it = 0;; ++it) {
+        bool did = false;
+        if (t_p < t_s && mbar_try_wait(&p_full[t_p & 1], (uint32_t)(t_p >> 1) & 1u)) {
+          const int b = t_p & 1;
+          const uint32_t info = b ? pv_info1 : pv_info0;
+          const int kvs = (int)(info & 1u), nkeys = (int)(info >> 8);
           tc_fence_after();
-          const uint32_t q_base = smem_u32(sQ + b * AtSmem::kQ);
-          for (int kk = 0; kk < kAtHD / 16; ++kk)
-            umma_f16_ss(tmem_base + b * 256, sw128_kmajor_desc(q_base + kk * 32), sw128_kmajor_desc(k_base + kk * 32),
-                        idesc_s, kk > 0 ? 1u : 0u);
-          umma_commit(&s_full[b]);
-          umma_commit(&q_empty[b]);
-          issued_any = true;
-          if (pend_t >= 0 && !issue_pv()) {
+          const uint32_t o_tmem = tmem_base + b * 256 + 128;
+          const uint32_t p_tmem = tmem_base + b * 256;
+          const uint32_t v_base = smem_u32(sV + kvs * AtSmem::kKV);
+          for (int ks = 0; ks < nkeys / 16; ++ks)
+            umma_f16_ts(o_tmem, p_tmem + ks * 8, sw128_mnmajor_desc(v_base + ks * 2048), idesc_o,
+                        ks > 0 ? 1u : 0u);
+          umma_commit(&o_full[b]);
+          if (info & 2u) umma_commit(&kv_empty[kvs]);
+          ++t_p;
+          did = true;
+        }
+        if (!done_s && t_s < t_p + 2) {
+          if (need_unit) {
+            const int slot = k % kAtRing;
+            if (mbar_try_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u)) {
+              const int u = ring[slot];
+              mbar_arrive(&u_empty[slot]);
+              if (u >= total_units) {
+                done_s = true;
+              } else {
+                un = decode_unit(u, a);
+                need_unit = false;
+                need_kv = true;
+                j = 0;
+              }
+              did = true;
+            }
+          } else if (need_kv) {
+            if (mbar_try_wait(&kv_full[k & 1], (uint32_t)(k >> 1) & 1u)) {
+              need_kv = false;
+              did = true;
+            }
+          } else {
+            const int b = t_s & 1;
+            const uint32_t n = (uint32_t)(t_s >> 1) & 1u;
+            if (mbar_try_wait(&q_full[b], n) && mbar_try_wait(&t_empty[b], n ^ 1u)) {
+              tc_fence_after();
+              const int kvs = k & 1;
+              const uint32_t q_base = smem_u32(sQ + b * AtSmem::kQ);
+              const uint32_t k_base = smem_u32(sK + kvs * AtSmem::kKV);
+              const uint32_t idesc_s = un.nkeys == 256 ? idesc_s256 : idesc_s128;
+              for (int kk = 0; kk < kAtHD / 16; ++kk)
+                umma_f16_ss(tmem_base + b * 256, sw128_kmajor_desc(q_base + kk * 32),
+                            sw128_kmajor_desc(k_base + kk * 32), idesc_s, kk > 0 ? 1u : 0u);
+              umma_commit(&s_full[b]);
+              umma_commit(&q_empty[b]);
+              issued_any = true;
+              const uint32_t info = (uint32_t)kvs | (j == gq - 1 ? 2u : 0u) | ((uint32_t)un.nkeys << 8);
+              if (b) pv_info1 = info; else pv_info0 = info;
+              ++t_s;
+              if (++j == gq) {
+                ++k;
+                need_unit = true;
+              }
+              did = true;
+            }
+          }
+        }
+        if (done_s && t_p == t_s) break;
+        // bounded: give up after the wait budget without progress, or when another role aborted
+        if (did) {
+          t_idle = 0;
+        } else if ((it & 255u) == 0u) {
+          if (*abort_flag) {
             ok = false;
             break;
           }
-          pend_t = t;
-          pend_kvs = kvs;
-          pend_nkeys = un.nkeys;
-          pend_last = (j == gq - 1);
+          const uint64_t now = global_timer_ns();
+          if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitBudgetNs) {
+            *abort_flag = 1;
+            atomicCAS(status, 0u, (uint32_t)DEV_TIMEOUT_MMA);
+            ok = false;
+            break;
+          }
         }
       }
-      if (ok && pend_t >= 0) ok = issue_pv();
       if (!ok && issued_any) {
         umma_commit(drain_bar);
         mbar_wait_drain(drain_bar, 0);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- softmax / output warpgroups ----------------
-    const int wg = (warp - 4) >> 2;      // buffer this group owns
+  } else {
+    // ---------------- softmax / output warpgroups (warps 2-5, 6-9) ----------------
+    const int wg = (warp - 2) >> 2;      // buffer this group owns
     const int quarter = warp & 3;        // TMEM lane quarter
     const int r = quarter * 32 + lane;   // row inside the query tile
-    const int wt = threadIdx.x - 128 - wg * 128;  // 0..127 within the group
-    const uint32_t bar_id = 3 + wg;
+    const int wt = threadIdx.x - 64 - wg * 128;  // 0..127 within the group
+    const uint32_t bar_id = 1 + wg;
     auto agree = [&](bool ok_wait) -> bool {
       // every thread of the group takes the same continue/abort decision
       named_bar_sync(bar_id, 128);
@@ -315,7 +414,6 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const Unit un = decode_unit(u, a);
       const int qpos = un.qb * kAtRows + r;
       const int diag = un.qb * 4 + quarter;  // 32-key chunk holding this warp's diagonal
-      const int nch = un.nkeys / 32;
       bool stop = false;
       for (int j = 0; j < gq; ++j, ++t) {
         if ((t & 1) != wg) continue;
@@ -327,78 +425,90 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         tc_fence_after();
         const uint32_t t_row = tmem_base + wg * 256 + ((uint32_t)(quarter * 32) << 16);
-        // pass 1: exact row maximum over the causal keys
+        // pass 1: exact row maximum over the causal keys (chunks 0..diag). Chunks are
+        // loaded kAtBatch at a time back to back and waited for together (one TMEM
+        // round trip per batch); only the diagonal chunk is masked.
         float mx = -INFINITY;
-        for (int c = 0; c <= diag; c += 2) {
-          uint32_t v0[32], v1[32];
-          tmem_ld32(t_row + c * 32, v0);
-          const bool two = c + 1 <= diag;
-          if (two) tmem_ld32(t_row + (c + 1) * 32, v1);
-          tmem_ld_wait();
+        for (int c0 = 0; c0 <= diag; c0 += kAtBatch) {
+          uint32_t v[kAtBatch][32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i <= qpos) mx = fmaxf(mx, __uint_as_float(v0[i]));
-          if (two) {
+          for (int q = 0; q < kAtBatch; ++q)
+            if (c0 + q <= diag) tmem_ld32(t_row + (c0 + q) * 32, v[q]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if ((c + 1) * 32 + i <= qpos) mx = fmaxf(mx, __uint_as_float(v1[i]));
+          for (int q = 0; q < kAtBatch; ++q)
+            if (c0 + q <= diag) tmem_ld_wait_regs(v[q]);
+#pragma unroll
+          for (int q = 0; q < kAtBatch; ++q) {
+            if (c0 + q < diag)
+              mx = chunk_max<false>(v[q], mx, 0, 0);
+            else if (c0 + q == diag)
+              mx = chunk_max<true>(v[q], mx, (c0 + q) * 32, qpos);
           }
         }
-        // pass 2: P = exp2((s - max)·scale), written as 16-bit pairs over consumed S columns
+        // pass 2: P = exp2((s - max)·scale) as 16-bit pairs over the consumed S columns
+        // (chunk c goes to columns [16c, 16c + 16), all read by the time it is stored),
+        // then zeros past the diagonal.
         const float ms = mx * scale_log2;
         float l = 0.f;
-        for (int c = 0; c < nch; ++c) {
-          uint32_t pk[16];
-          if (c <= diag) {
-            uint32_t v[32];
-            tmem_ld32(t_row + c * 32, v);
-            tmem_ld_wait();
+        for (int c0 = 0; c0 <= diag; c0 += kAtBatch) {
+          uint32_t v[kAtBatch][32];
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const int key = c * 32 + i;
-              const float p0 = key <= qpos ? exp2f(fmaf(__uint_as_float(v[i]), scale_log2, -ms)) : 0.f;
-              const float p1 = key + 1 <= qpos ? exp2f(fmaf(__uint_as_float(v[i + 1]), scale_log2, -ms)) : 0.f;
-              l += p0 + p1;
-              pk[i >> 1] = pack_h2<T>(p0, p1);
+          for (int q = 0; q < kAtBatch; ++q)
+            if (c0 + q <= diag) tmem_ld32(t_row + (c0 + q) * 32, v[q]);
+#pragma unroll
+          for (int q = 0; q < kAtBatch; ++q)
+            if (c0 + q <= diag) tmem_ld_wait_regs(v[q]);
+#pragma unroll
+          for (int q = 0; q < kAtBatch; ++q) {
+            uint32_t pk[16];
+            if (c0 + q < diag) {
+              chunk_exp<T, false>(v[q], pk, l, scale_log2, ms, 0, 0);
+              tmem_st16(t_row + (c0 + q) * 16, pk);
+            } else if (c0 + q == diag) {
+              chunk_exp<T, true>(v[q], pk, l, scale_log2, ms, (c0 + q) * 32, qpos);
+              tmem_st16(t_row + (c0 + q) * 16, pk);
             }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = 0u;
           }
-          tmem_st16(t_row + c * 16, pk);
+        }
+        {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          for (int c = diag + 1; c < un.nkeys / 32; ++c) tmem_st16(t_row + c * 16, pk);
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[wg]);
         const long long row = (long long)un.g * a.seq + qpos;
-        if (a.lse) a.lse[row * a.heads + h] = ms + log2f(l);
         // output: O / l
         if (!agree(mbar_wait(&o_full[wg], n, abort_flag, status, DEV_TIMEOUT_EPILOGUE))) {
           stop = true;
           break;
         }
         tc_fence_after();
-        uint32_t o0[32], o1[32];
-        tmem_ld32(t_row + 128, o0);
-        tmem_ld32(t_row + 160, o1);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&t_empty[wg]);
+        // O / l in two 32-column halves; the buffer is released after the second load
+        if (a.lse) a.lse[row * a.heads + h] = ms + log2f(l);
         const float inv = 1.0f / l;
         T* out = static_cast<T*>(a.out) + row * a.ld_out + h * kAtHD;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int col = c * 8 + 2 * e;
-            const float x0 = __uint_as_float(col < 32 ? o0[col] : o1[col - 32]);
-            const float x1 = __uint_as_float(col + 1 < 32 ? o0[col + 1] : o1[col + 1 - 32]);
-            w[e] = pack_h2<T>(x0 * inv, x1 * inv);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t o[32];
+          tmem_ld32(t_row + 128 + half * 32, o);
+          tmem_ld_wait_regs(o);
+          if (half == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&t_empty[wg]);
           }
-          *reinterpret_cast<uint4*>(out + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack_h2<T>(__uint_as_float(o[c * 8 + 2 * e]) * inv, __uint_as_float(o[c * 8 + 2 * e + 1]) * inv);
+            *reinterpret_cast<uint4*>(out + half * 32 + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
         }
       }
       if (stop) break;
@@ -407,7 +517,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kAtTmemCols);
   }
