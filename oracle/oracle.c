@@ -104,8 +104,12 @@ void or_sign_mask(uint64_t seed, const int64_t* sizes, int nbuf, uint32_t* mask)
 
 /* ---------------- LoRA-split parameter layout (train_mezo.m:560-588) ---------------- */
 or_layout or_lora_layout(int nlayers, int dim, int q_dim, int kv_dim, int rank) {
+  return or_lora_layout_ffn(nlayers, dim, q_dim, kv_dim, 0, rank, 0);
+}
+
+or_layout or_lora_layout_ffn(int nlayers, int dim, int q_dim, int kv_dim, int hidden, int rank, int ffn) {
   or_layout L;
-  const int64_t r = rank, D = dim, Q = q_dim, KV = kv_dim;
+  const int64_t r = rank, D = dim, Q = q_dim, KV = kv_dim, H = hidden;
   int64_t o = 0;
   L.Aq = o; o += r * D;
   L.Bq = o; o += Q * r;
@@ -115,6 +119,15 @@ or_layout or_lora_layout(int nlayers, int dim, int q_dim, int kv_dim, int rank) 
   L.Bv = o; o += KV * r;
   L.Ao = o; o += r * Q;
   L.Bo = o; o += D * r;
+  L.A1 = L.B1 = L.A2 = L.B2 = L.A3 = L.B3 = -1;
+  if (ffn) { /* train_mezo.m:575-582 */
+    L.A1 = o; o += r * D;
+    L.B1 = o; o += H * r;
+    L.A2 = o; o += r * H;
+    L.B2 = o; o += D * r;
+    L.A3 = o; o += r * D;
+    L.B3 = o; o += H * r;
+  }
   L.rms_att = o; o += D;
   L.rms_ffn = o; o += D;
   L.layer_size = o;
@@ -124,7 +137,12 @@ or_layout or_lora_layout(int nlayers, int dim, int q_dim, int kv_dim, int rank) 
 }
 
 int or_lora_buffer_sizes(int nlayers, int dim, int q_dim, int kv_dim, int rank, int64_t* sz) {
-  const int64_t r = rank, D = dim, Q = q_dim, KV = kv_dim;
+  return or_lora_buffer_sizes_ffn(nlayers, dim, q_dim, kv_dim, 0, rank, 0, sz);
+}
+
+int or_lora_buffer_sizes_ffn(int nlayers, int dim, int q_dim, int kv_dim, int hidden, int rank, int ffn,
+                             int64_t* sz) {
+  const int64_t r = rank, D = dim, Q = q_dim, KV = kv_dim, H = hidden;
   int n = 0;
   for (int l = 0; l < nlayers; l++) {
     sz[n++] = r * D;   /* Aq */
@@ -135,6 +153,14 @@ int or_lora_buffer_sizes(int nlayers, int dim, int q_dim, int kv_dim, int rank, 
     sz[n++] = KV * r;  /* Bv */
     sz[n++] = r * Q;   /* Ao */
     sz[n++] = D * r;   /* Bo */
+    if (ffn) {
+      sz[n++] = r * D; /* A1 */
+      sz[n++] = H * r; /* B1 */
+      sz[n++] = r * H; /* A2 */
+      sz[n++] = D * r; /* B2 */
+      sz[n++] = r * D; /* A3 */
+      sz[n++] = H * r; /* B3 */
+    }
     sz[n++] = D;       /* rms_att */
     sz[n++] = D;       /* rms_ffn */
   }
@@ -144,8 +170,14 @@ int or_lora_buffer_sizes(int nlayers, int dim, int q_dim, int kv_dim, int rank, 
 
 void or_perturb_lora(float* theta, int nlayers, int dim, int q_dim, int kv_dim, int rank, uint64_t seed,
                      float scale) {
-  int64_t* sz = (int64_t*)xmalloc(sizeof(int64_t) * (size_t)(10 * nlayers + 1));
-  const int nb = or_lora_buffer_sizes(nlayers, dim, q_dim, kv_dim, rank, sz);
+  or_perturb_lora_ffn(theta, nlayers, dim, q_dim, kv_dim, 0, rank, 0, seed, scale);
+}
+
+/* perturb_lora_weights (train_mezo.m:560-588): one xoshiro stream over every buffer in order */
+void or_perturb_lora_ffn(float* theta, int nlayers, int dim, int q_dim, int kv_dim, int hidden, int rank, int ffn,
+                         uint64_t seed, float scale) {
+  int64_t* sz = (int64_t*)xmalloc(sizeof(int64_t) * (size_t)(16 * nlayers + 1));
+  const int nb = or_lora_buffer_sizes_ffn(nlayers, dim, q_dim, kv_dim, hidden, rank, ffn, sz);
   or_xo st;
   or_xo_seed(&st, seed);
   int64_t off = 0;
@@ -293,7 +325,7 @@ float or_forward_loss(const or_model* m, const float* theta, const uint16_t* tok
                       or_taps* taps) {
   const int D = m->dim, H = m->hidden, S = m->seq, QD = m->heads * m->hd, KVD = m->kv_heads * m->hd;
   const int r = m->rank;
-  const or_layout L = or_lora_layout(m->nlayers, D, QD, KVD, r);
+  const or_layout L = or_lora_layout_ffn(m->nlayers, D, QD, KVD, H, r, m->lora_ffn);
   float* x = (float*)xmalloc(sizeof(float) * (size_t)D * S);
   float* xn = (float*)xmalloc(sizeof(float) * (size_t)D * S);
   float* Q = (float*)xmalloc(sizeof(float) * (size_t)QD * S);
@@ -338,11 +370,16 @@ float or_forward_loss(const or_model* m, const float* theta, const uint16_t* tok
     or_rmsnorm(xn, x, th + L.rms_ffn, D, S);
     or_sgemm_nn(H, S, D, m->W1[l], xn, h1, 0.0f);
     or_sgemm_nn(H, S, D, m->W3[l], xn, h3, 0.0f);
+    if (m->lora_ffn) { /* train_mezo.m:1634-1638 */
+      or_lora_addmm(h1, th + L.A1, th + L.B1, xn, tmp, H, r, D, S);
+      or_lora_addmm(h3, th + L.A3, th + L.B3, xn, tmp, H, r, D, S);
+    }
     for (size_t i = 0; i < (size_t)H * S; i++) {
       const float s = h1[i] / (1.0f + expf(-h1[i]));
       h1[i] = s * h3[i];
     }
     or_sgemm_nn(D, S, H, m->W2[l], h1, o, 0.0f);
+    if (m->lora_ffn) or_lora_addmm(o, th + L.A2, th + L.B2, h1, tmp, D, r, H, S); /* train_mezo.m:1658-1661 */
     resid_add(x, o, m->res_alpha, (size_t)D * S);
   }
   if (taps && taps->layer_x)
@@ -363,14 +400,14 @@ float or_forward_loss(const or_model* m, const float* theta, const uint16_t* tok
 void or_mezo_step(const or_model* m, float* theta, const uint16_t* tokens, const uint16_t* ctargets, uint64_t seed,
                   float eps, float lr, float* loss_plus, float* loss_minus, float* proj_grad) {
   const int QD = m->heads * m->hd, KVD = m->kv_heads * m->hd;
-  or_perturb_lora(theta, m->nlayers, m->dim, QD, KVD, m->rank, seed, +eps);
+  or_perturb_lora_ffn(theta, m->nlayers, m->dim, QD, KVD, m->hidden, m->rank, m->lora_ffn, seed, +eps);
   const float lp = or_forward_loss(m, theta, tokens, ctargets, NULL);
-  or_perturb_lora(theta, m->nlayers, m->dim, QD, KVD, m->rank, seed, -2.0f * eps);
+  or_perturb_lora_ffn(theta, m->nlayers, m->dim, QD, KVD, m->hidden, m->rank, m->lora_ffn, seed, -2.0f * eps);
   const float lm = or_forward_loss(m, theta, tokens, ctargets, NULL);
-  or_perturb_lora(theta, m->nlayers, m->dim, QD, KVD, m->rank, seed, +eps);
+  or_perturb_lora_ffn(theta, m->nlayers, m->dim, QD, KVD, m->hidden, m->rank, m->lora_ffn, seed, +eps);
   const float g = (lp - lm) / (2.0f * eps);
   const float update_scale = -lr * g;
-  or_perturb_lora(theta, m->nlayers, m->dim, QD, KVD, m->rank, seed, update_scale);
+  or_perturb_lora_ffn(theta, m->nlayers, m->dim, QD, KVD, m->hidden, m->rank, m->lora_ffn, seed, update_scale);
   if (loss_plus) *loss_plus = lp;
   if (loss_minus) *loss_minus = lm;
   if (proj_grad) *proj_grad = g;

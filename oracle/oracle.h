@@ -35,19 +35,27 @@ void or_sign_mask(uint64_t seed, const int64_t* sizes, int nbuf, uint32_t* mask)
 
 /* ---- LoRA-split trainable-parameter layout (training/train_mezo.m:560-588) ----
  * theta = per layer [Aq r*D | Bq Q*r | Ak r*D | Bk KV*r | Av r*D | Bv KV*r |
- *                    Ao r*Q | Bo D*r | rms_att D | rms_ffn D], then rms_final D. */
+ *                    Ao r*Q | Bo D*r | (--lora-ffn: A1 r*D | B1 H*r | A2 r*H | B2 D*r |
+ *                    A3 r*D | B3 H*r) | rms_att D | rms_ffn D], then rms_final D. */
 typedef struct {
   int64_t Aq, Bq, Ak, Bk, Av, Bv, Ao, Bo, rms_att, rms_ffn; /* offsets inside a layer */
   int64_t layer_size;
   int64_t rms_final; /* offset of rms_final */
   int64_t total;
+  int64_t A1, B1, A2, B2, A3, B3; /* FFN adapters (-1 without --lora-ffn) */
 } or_layout;
 or_layout or_lora_layout(int nlayers, int dim, int q_dim, int kv_dim, int rank);
+or_layout or_lora_layout_ffn(int nlayers, int dim, int q_dim, int kv_dim, int hidden, int rank, int ffn);
 /* Buffer sizes in perturbation order (11 per layer... 10 per layer + 1). Returns count. */
 int or_lora_buffer_sizes(int nlayers, int dim, int q_dim, int kv_dim, int rank, int64_t* sizes_out);
+/* The same with the FFN adapters of --lora-ffn after Bo (train_mezo.m:575-582); 16 per layer + 1. */
+int or_lora_buffer_sizes_ffn(int nlayers, int dim, int q_dim, int kv_dim, int hidden, int rank, int ffn,
+                             int64_t* sizes_out);
 /* perturb_lora_weights (train_mezo.m:560-588) over the flat theta. */
 void or_perturb_lora(float* theta, int nlayers, int dim, int q_dim, int kv_dim, int rank, uint64_t seed,
                      float scale);
+void or_perturb_lora_ffn(float* theta, int nlayers, int dim, int q_dim, int kv_dim, int hidden, int rank, int ffn,
+                         uint64_t seed, float scale);
 
 /* ---- model ---- */
 typedef struct {
@@ -63,6 +71,7 @@ typedef struct {
   const float* const* W3;
   const float* embed;  /* [vocab, dim] */
   const float* cembed; /* [cv, dim] compact tied embedding (vocab_compact_embed, cpu_ops.h:171) */
+  int lora_ffn;        /* --lora-ffn: adapters on W1, W2, W3 as well */
 } or_model;
 
 /* ---- ops (training/cpu_ops.h) ---- */

@@ -27,7 +27,7 @@ def _u16(a):
 class Layout(C.Structure):
     _fields_ = [(n, C.c_int64) for n in
                 ("Aq", "Bq", "Ak", "Bk", "Av", "Bv", "Ao", "Bo", "rms_att", "rms_ffn", "layer_size", "rms_final",
-                 "total")]
+                 "total", "A1", "B1", "A2", "B2", "A3", "B3")]
 
 
 class _Model(C.Structure):
@@ -35,7 +35,8 @@ class _Model(C.Structure):
                                          "cv", "rank")]
                 + [("rope_theta", C.c_float), ("res_alpha", C.c_float)]
                 + [(n, C.POINTER(C.POINTER(C.c_float))) for n in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")]
-                + [("embed", C.POINTER(C.c_float)), ("cembed", C.POINTER(C.c_float))])
+                + [("embed", C.POINTER(C.c_float)), ("cembed", C.POINTER(C.c_float))]
+                + [("lora_ffn", C.c_int)])
 
 
 class _Taps(C.Structure):
@@ -59,6 +60,10 @@ def lib() -> C.CDLL:
         L.or_lora_layout.argtypes = [C.c_int] * 5
         L.or_perturb_lora.argtypes = [C.POINTER(C.c_float)] + [C.c_int] * 5 + [C.c_uint64, C.c_float]
         L.or_lora_buffer_sizes.argtypes = [C.c_int] * 5 + [C.POINTER(C.c_int64)]
+        L.or_lora_layout_ffn.restype = Layout
+        L.or_lora_layout_ffn.argtypes = [C.c_int] * 7
+        L.or_lora_buffer_sizes_ffn.argtypes = [C.c_int] * 7 + [C.POINTER(C.c_int64)]
+        L.or_perturb_lora_ffn.argtypes = [C.POINTER(C.c_float)] + [C.c_int] * 7 + [C.c_uint64, C.c_float]
         L.or_forward_loss.restype = C.c_float
         L.or_forward_loss.argtypes = [C.POINTER(_Model), C.POINTER(C.c_float), C.POINTER(C.c_uint16),
                                       C.POINTER(C.c_uint16), C.POINTER(_Taps)]
@@ -118,6 +123,25 @@ def sign_mask(seed: int, sizes) -> np.ndarray:
 
 def lora_layout(nlayers, dim, q_dim, kv_dim, rank) -> Layout:
     return lib().or_lora_layout(nlayers, dim, q_dim, kv_dim, rank)
+
+
+def lora_layout_ffn(nlayers, dim, q_dim, kv_dim, hidden, rank, ffn) -> Layout:
+    """or_lora_layout_ffn: the layout with the --lora-ffn adapters after Bo (train_mezo.m:575-582)."""
+    return lib().or_lora_layout_ffn(nlayers, dim, q_dim, kv_dim, hidden, rank, int(ffn))
+
+
+def lora_buffer_sizes_ffn(nlayers, dim, q_dim, kv_dim, hidden, rank, ffn) -> np.ndarray:
+    out = np.zeros(16 * nlayers + 1, np.int64)
+    n = lib().or_lora_buffer_sizes_ffn(nlayers, dim, q_dim, kv_dim, hidden, rank, int(ffn),
+                                       out.ctypes.data_as(C.POINTER(C.c_int64)))
+    return out[:n]
+
+
+def perturb_lora_ffn(theta: np.ndarray, nlayers, dim, q_dim, kv_dim, hidden, rank, ffn, seed: int,
+                     scale: float) -> None:
+    assert theta.dtype == np.float32 and theta.flags.c_contiguous
+    lib().or_perturb_lora_ffn(_f(theta), nlayers, dim, q_dim, kv_dim, hidden, rank, int(ffn), seed,
+                              np.float32(scale))
 
 
 def lora_buffer_sizes(nlayers, dim, q_dim, kv_dim, rank) -> np.ndarray:
@@ -184,6 +208,7 @@ class ModelCfg:
     rank: int = 8
     rope_theta: float = 100000.0
     res_alpha: float = 1.0
+    lora_ffn: bool = False  # --lora-ffn: adapters on W1, W2, W3 too
 
     @property
     def q_dim(self):
@@ -207,6 +232,7 @@ class OracleModel:
         for f in ("dim", "hidden", "heads", "kv_heads", "hd", "seq", "nlayers", "vocab", "rank"):
             setattr(m, f, getattr(cfg, f))
         m.cv = self.cembed.shape[0]
+        m.lora_ffn = int(getattr(cfg, "lora_ffn", False))
         m.rope_theta = cfg.rope_theta
         m.res_alpha = cfg.res_alpha
         for n in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3"):
@@ -289,5 +315,6 @@ def ref_lib(model: str):
     L = C.CDLL(str(p))
     L.ref_cross_entropy.restype = C.c_float
     L.ref_forward_loss.restype = C.c_float
+    L.ref_forward_loss_ffn.restype = C.c_float
     L.ref_p16_grad.restype = C.c_float
     return L

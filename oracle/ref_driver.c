@@ -54,11 +54,30 @@ static void ref_lora_addmm(float* out, const float* A, const float* B, const flo
  * transcribed over the reference's compiled cpu_ops.h functions.
  * lora[l*8 + {0..7}] = Aq,Bq,Ak,Bk,Av,Bv,Ao,Bo of layer l; rms[l*2 + {0,1}] =
  * rms_att, rms_ffn. */
+float ref_forward_loss_ffn(const float* const* Wq, const float* const* Wk, const float* const* Wv,
+                           const float* const* Wo, const float* const* W1, const float* const* W2,
+                           const float* const* W3, const float* const* lora, const float* const* rms,
+                           const float* rms_final, const float* embed, const float* cembed, int CV, int rank,
+                           float res_alpha, const uint16_t* input_toks, const uint16_t* ctargets,
+                           const float* const* ffn);
+
 float ref_forward_loss(const float* const* Wq, const float* const* Wk, const float* const* Wv,
                        const float* const* Wo, const float* const* W1, const float* const* W2,
                        const float* const* W3, const float* const* lora, const float* const* rms,
                        const float* rms_final, const float* embed, const float* cembed, int CV, int rank,
                        float res_alpha, const uint16_t* input_toks, const uint16_t* ctargets) {
+  return ref_forward_loss_ffn(Wq, Wk, Wv, Wo, W1, W2, W3, lora, rms, rms_final, embed, cembed, CV, rank, res_alpha,
+                              input_toks, ctargets, NULL);
+}
+
+/* The same forward with --lora-ffn (train_mezo.m:1634-1661) when ffn != NULL:
+ * ffn[l*6 + {0..5}] = A1, B1, A2, B2, A3, B3 of layer l. */
+float ref_forward_loss_ffn(const float* const* Wq, const float* const* Wk, const float* const* Wv,
+                           const float* const* Wo, const float* const* W1, const float* const* W2,
+                           const float* const* W3, const float* const* lora, const float* const* rms,
+                           const float* rms_final, const float* embed, const float* cembed, int CV, int rank,
+                           float res_alpha, const uint16_t* input_toks, const uint16_t* ctargets,
+                           const float* const* ffn) {
   float* x_cur = (float*)safe_malloc((size_t)SEQ * DIM * 4);
   float* xnorm_buf = (float*)safe_malloc((size_t)SEQ * DIM * 4);
   float* Q = (float*)safe_malloc((size_t)SEQ * Q_DIM * 4);
@@ -102,12 +121,18 @@ float ref_forward_loss(const float* const* Wq, const float* const* Wk, const flo
                 0.0f, h1, SEQ);
     cblas_sgemm(CblasRowMajor, CblasNoTrans, CblasNoTrans, HIDDEN, SEQ, DIM, 1.0f, W3[L], DIM, xnorm_buf, SEQ,
                 0.0f, h3, SEQ);
+    const float* const* lf = ffn ? ffn + (size_t)L * 6 : NULL;
+    if (lf) {
+      ref_lora_addmm(h1, lf[0], lf[1], xnorm_buf, lora_tmp, HIDDEN, rank, DIM);
+      ref_lora_addmm(h3, lf[4], lf[5], xnorm_buf, lora_tmp, HIDDEN, rank, DIM);
+    }
     for (int i = 0; i < HIDDEN * SEQ; i++) {
       float s = h1[i] / (1.0f + expf(-h1[i]));
       silu_out[i] = s * h3[i];
     }
     cblas_sgemm(CblasRowMajor, CblasNoTrans, CblasNoTrans, DIM, SEQ, HIDDEN, 1.0f, W2[L], HIDDEN, silu_out, SEQ,
                 0.0f, o_out, SEQ);
+    if (lf) ref_lora_addmm(o_out, lf[2], lf[3], silu_out, lora_tmp, DIM, rank, HIDDEN);
     vDSP_vsma(o_out, 1, &res_alpha, x_cur, 1, x_cur, 1, (vDSP_Length)(SEQ * DIM));
   }
   rmsnorm(xnorm_buf, x_cur, rms_final, DIM, SEQ);

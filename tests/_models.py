@@ -42,7 +42,8 @@ def make_model(cfg: O.ModelCfg, n_active: int, seed: int = 42, b_scale: float = 
     full_to_compact[:n_active] = np.arange(n_active)
     compact_to_full = np.arange(n_active, dtype=np.int32)
     cembed = np.ascontiguousarray(embed[compact_to_full])
-    lay = O.lora_layout(L, D, QD, KVD, r)
+    ffn = bool(getattr(cfg, "lora_ffn", False))
+    lay = O.lora_layout_ffn(L, D, QD, KVD, H, r, ffn)
     theta = np.zeros(lay.total, np.float32)
     a_std = 1.0 / np.sqrt(r)
     for l in range(L):
@@ -52,6 +53,12 @@ def make_model(cfg: O.ModelCfg, n_active: int, seed: int = 42, b_scale: float = 
         if b_scale:
             for off, n in ((lay.Bq, QD * r), (lay.Bk, KVD * r), (lay.Bv, KVD * r), (lay.Bo, D * r)):
                 theta[base + off: base + off + n] = rng.standard_normal(n, dtype=np.float32) * b_scale
+        if ffn:  # --lora-ffn adapters (train_mezo.m:1079-1091): A random, B small random when b_scale
+            for off, n in ((lay.A1, r * D), (lay.A2, r * H), (lay.A3, r * D)):
+                theta[base + off: base + off + n] = rng.standard_normal(n, dtype=np.float32) * a_std
+            if b_scale:
+                for off, n in ((lay.B1, H * r), (lay.B2, D * r), (lay.B3, H * r)):
+                    theta[base + off: base + off + n] = rng.standard_normal(n, dtype=np.float32) * b_scale
         theta[base + lay.rms_att: base + lay.rms_att + D] = 1.0
         theta[base + lay.rms_ffn: base + lay.rms_ffn + D] = 1.0
         if rms_jitter:

@@ -49,10 +49,15 @@ def signs_to_words(signs: np.ndarray) -> list[int]:
     return [int(w) for w in words]
 
 
-def lora_sizes(nlayers, dim, q_dim, kv_dim, r):
+def lora_sizes(nlayers, dim, q_dim, kv_dim, r, hidden=0, ffn=False):
+    """Buffer sizes in perturb_lora_weights order (train_mezo.m:566-587); the --lora-ffn
+    adapters A1, B1, A2, B2, A3, B3 come after Bo."""
     sz = []
     for _ in range(nlayers):
-        sz += [r * dim, q_dim * r, r * dim, kv_dim * r, r * dim, kv_dim * r, r * q_dim, dim * r, dim, dim]
+        sz += [r * dim, q_dim * r, r * dim, kv_dim * r, r * dim, kv_dim * r, r * q_dim, dim * r]
+        if ffn:
+            sz += [r * dim, hidden * r, r * hidden, dim * r, r * dim, hidden * r]
+        sz += [dim, dim]
     sz.append(dim)
     return sz
 
@@ -86,16 +91,17 @@ def main() -> None:
     out["ragged"] = {"sizes": ragged, "seed": 12345, "words": mask_for(Xo, 12345, ragged)}
     # 3. full LoRA layouts
     layouts = {}
-    for name, (L, D, Q, KV, r) in {"smollm2_360m": (32, 960, 960, 320, 8),
-                                   "autoresearch": (4, 512, 512, 128, 8),
-                                   "autoresearch_r4": (4, 512, 512, 128, 4)}.items():
-        sizes = lora_sizes(L, D, Q, KV, r)
+    for name, dims in {"smollm2_360m": (32, 960, 960, 320, 8),
+                       "autoresearch": (4, 512, 512, 128, 8),
+                       "autoresearch_r4": (4, 512, 512, 128, 4),
+                       "smollm2_360m_lora_ffn": (32, 960, 960, 320, 8, 2560, 1)}.items():
+        sizes = lora_sizes(*dims)
         seeds = [42, 1 * 1000003 + 42] if name == "smollm2_360m" else [42]
-        layouts[name] = {"dims": [L, D, Q, KV, r], "total": int(sum(sizes)), "masks": {}}
+        layouts[name] = {"dims": list(dims), "total": int(sum(sizes)), "masks": {}}
         for s in seeds:
             w = mask_for(Xo, s, sizes)
             entry = {"sha256": digest(w), "head": w[:64], "tail": w[-16:]}
-            if name != "smollm2_360m":
+            if not name.startswith("smollm2_360m"):
                 entry["words"] = w
             layouts[name]["masks"][str(s)] = entry
     out["layouts"] = layouts

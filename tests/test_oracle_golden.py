@@ -31,8 +31,9 @@ def test_ragged_buffers_tail_uses_one_draw_per_element():
 @pytest.mark.parametrize("name", list(PRNG["layouts"].keys()))
 def test_lora_layout_masks(name):
     lay = PRNG["layouts"][name]
-    L, D, Q, KV, r = lay["dims"]
-    sizes = O.lora_buffer_sizes(L, D, Q, KV, r)
+    L, D, Q, KV, r = lay["dims"][:5]
+    H, ffn = lay["dims"][5:] if len(lay["dims"]) > 5 else (0, 0)
+    sizes = O.lora_buffer_sizes_ffn(L, D, Q, KV, H, r, ffn)
     assert int(sizes.sum()) == lay["total"]
     for seed, ent in lay["masks"].items():
         m = O.sign_mask(int(seed), sizes)

@@ -88,6 +88,54 @@ def test_forward_loss_matches_reference_code(model, cfg):
     assert 7.0 < loss_o < 9.0  # ≈ ln(3000) for a random-init model
 
 
+def test_forward_loss_lora_ffn_matches_reference_code():
+    """--lora-ffn forward (adapters on W1, W2, W3) against the reference code path."""
+    import dataclasses
+    ref = need("autoresearch")
+    cfg = dataclasses.replace(M.AUTORESEARCH, lora_ffn=True)
+    syn = M.make_model(cfg, n_active=3000, seed=6, b_scale=0.01, rms_jitter=0.05)
+    toks = M.make_tokens(4096, 3000, seed=6)
+    inp, tgt = M.sample_sequence(toks, cfg.seq, syn.full_to_compact, 23)
+    om = O.OracleModel(cfg, syn.weights, syn.embed, syn.cembed)
+    loss_o = om.forward_loss(syn.theta, inp, tgt)
+    plain = dataclasses.replace(cfg, lora_ffn=False)
+    keep = []
+
+    def plist(arrs):
+        p = (F * len(arrs))(*[f(a) for a in arrs])
+        keep.append((arrs, p))
+        return p
+
+    lay = syn.layout
+    lora, rms, ffn = [], [], []
+    for l in range(cfg.nlayers):
+        base = l * lay.layer_size
+        lora += [np.ascontiguousarray(syn.theta[base + o:]) for o in (lay.Aq, lay.Bq, lay.Ak, lay.Bk, lay.Av, lay.Bv,
+                                                                       lay.Ao, lay.Bo)]
+        ffn += [np.ascontiguousarray(syn.theta[base + o:]) for o in (lay.A1, lay.B1, lay.A2, lay.B2, lay.A3, lay.B3)]
+        rms += [np.ascontiguousarray(syn.theta[base + o:]) for o in (lay.rms_att, lay.rms_ffn)]
+    ref.ref_forward_loss_ffn.argtypes = [C.POINTER(F)] * 9 + [F, F, F, C.c_int, C.c_int, C.c_float,
+                                                              C.POINTER(C.c_uint16), C.POINTER(C.c_uint16),
+                                                              C.POINTER(F)]
+    rf = np.ascontiguousarray(syn.theta[lay.rms_final:])
+    loss_r = ref.ref_forward_loss_ffn(*[plist(syn.weights[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")],
+                                      plist(lora), plist(rms), f(rf), f(syn.embed), f(syn.cembed),
+                                      syn.cembed.shape[0], cfg.rank, C.c_float(cfg.res_alpha),
+                                      inp.ctypes.data_as(C.POINTER(C.c_uint16)),
+                                      tgt.ctypes.data_as(C.POINTER(C.c_uint16)), plist(ffn))
+    assert abs(loss_o - loss_r) < 1e-5, (loss_o, loss_r)
+    # the FFN adapters change the loss (they are not inert)
+    th0 = np.zeros(O.lora_layout(plain.nlayers, plain.dim, plain.q_dim, plain.kv_dim, plain.rank).total, np.float32)
+    lay0 = O.lora_layout(plain.nlayers, plain.dim, plain.q_dim, plain.kv_dim, plain.rank)
+    for l in range(cfg.nlayers):
+        b0, b = l * lay0.layer_size, l * lay.layer_size
+        th0[b0: b0 + lay0.rms_att] = syn.theta[b: b + lay.Bo + cfg.dim * cfg.rank]
+        th0[b0 + lay0.rms_att: b0 + lay0.layer_size] = syn.theta[b + lay.rms_att: b + lay.layer_size]
+    th0[lay0.rms_final:] = syn.theta[lay.rms_final:]
+    loss_plain = O.OracleModel(plain, syn.weights, syn.embed, syn.cembed).forward_loss(th0, inp, tgt)
+    assert abs(loss_plain - loss_o) > 1e-5
+
+
 def _theta_lists(syn, L):
     lay = syn.layout
     lora, rms = [], []
