@@ -92,7 +92,8 @@ class ModelConfig(C.Structure):
     """b2p_model_config (include/b2p.h)."""
     _fields_ = [(n, C.c_int) for n in ("dim", "hidden", "heads", "kv_heads", "head_dim", "seq", "nlayers", "vocab",
                                         "rank")] + [("rope_theta", C.c_float), ("res_alpha", C.c_float),
-                                                     ("dtype", C.c_int), ("max_groups", C.c_int)]
+                                                     ("dtype", C.c_int), ("max_groups", C.c_int),
+                                                     ("lora_ffn", C.c_int)]
 
 
 class Variant(C.Structure):

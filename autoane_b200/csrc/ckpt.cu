@@ -237,8 +237,9 @@ int write_sidecar(const b2p_model* m, const char* path, const float* theta, int 
   if (!f.f) return io_fail("cannot write", path);
   const int head[4] = {B2P_LORA_MAGIC, m->cfg.rank, m->cfg.nlayers, adam_t};
   int rc = put(f.f, head, sizeof(head), path);
-  // Aq..Bo are the first eight blocks of each layer's trainable block, in file order
-  const size_t n = (size_t)m->oRa;
+  // Aq..Bo are the first eight blocks of each layer's trainable block, in file order (the
+  // sidecar holds the attention adapters only, as lora_save_checkpoint writes it)
+  const size_t n = (size_t)(m->oBo + (long long)m->cfg.dim * m->cfg.rank);
   for (int l = 0; l < m->cfg.nlayers && !rc; ++l) rc = put(f.f, theta + (size_t)l * m->layer_size, n * 4, path);
   if (!rc && std::fflush(f.f) != 0) rc = io_fail("cannot flush", path);
   return rc;
@@ -264,7 +265,7 @@ int read_sidecar(const b2p_model* m, const char* path, float* theta, int* adam_t
     set_error("LoRA sidecar %s has an invalid adam_t %d", path, head[3]);
     return B2P_ERR_ARG;
   }
-  const size_t n = (size_t)m->oRa;
+  const size_t n = (size_t)(m->oBo + (long long)m->cfg.dim * m->cfg.rank);
   if (file_size(f.f) != (long long)(16 + (size_t)m->cfg.nlayers * n * 4))
     return io_fail("wrong size for a LoRA sidecar of this model:", path);
   for (int l = 0; l < m->cfg.nlayers && !rc; ++l) rc = get(f.f, theta + (size_t)l * m->layer_size, n * 4, path);
@@ -299,7 +300,7 @@ int save(b2p_model* m, const char* path, const char* lora_path, const b2p_ckpt_h
   h.head_dim = c.head_dim;
   h.q_dim = m->q_dim;
   h.adam_t = tv.full ? *tv.full_t : 0;  // the MeZO writer stores zero Adam slots and t 0
-  if (lora_path && (rc = write_sidecar(m, lora_path, theta.data(), *tv.adam_t))) return rc;
+  if (lora_path && (rc = write_sidecar(m, lora_path, theta.data(), tv.adam_t ? *tv.adam_t : 0))) return rc;
 
   File f;
   f.f = std::fopen(path, "wb");
@@ -460,7 +461,7 @@ int load(b2p_model* m, const char* path, const char* lora_path, const int32_t* c
     if ((rc = get(f.f, buf.data(), V * D * 4, path)) || (rc = h2d(m, tv.av_e, buf.data(), V * D * 4))) return rc;
     *tv.full_t = h.adam_t;
   }
-  if (lora_path) {
+  if (lora_path && tv.adam_m) {
     // train_mezo.m:1134-1137: the adapters resume at the sidecar's step count with fresh moments
     B2P_CHECK_CUDA(cudaMemsetAsync(tv.adam_m, 0, (size_t)m->P * 4, m->st));
     B2P_CHECK_CUDA(cudaMemsetAsync(tv.adam_v, 0, (size_t)m->P * 4, m->st));

@@ -236,6 +236,8 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
     B2P_REQUIRE(ep.head_dim == 64 && ep.seq_len % kBM == 0 && ep.rope_cols % 64 == 0,
                 "RoPE epilogue needs head_dim 64, seq %% 128 == 0 and whole heads");
   if (kind == EPI_SWIGLU) B2P_REQUIRE(N % 256 == 0, "SwiGLU needs N %% 256 == 0");
+  B2P_REQUIRE(!(kind == EPI_SWIGLU && ep.has_lora),
+              "SwiGLU with LoRA runs on the CTA-pair engine only (M >= 256, variant groups of whole 256-row tiles)");
   if (kind == EPI_CE_GRAD) B2P_REQUIRE(ep.targets && ep.row_lse, "CE gradient needs targets and row LSE");
   if (bf16) return dispatch_kind<__nv_bfloat16, true>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
   return dispatch_kind<__half, false>(bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);

@@ -81,6 +81,8 @@ int dispatch_pair(int kind, const void* X, int ldx, const void* W, int ldw, int 
       break;
     case EPI_SWIGLU:
       if (nseg == 0) return launch_pair_t<256, EPI_SWIGLU, H, BF16, 0>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
+      if (nseg == 2 && ep.lora.inter128)
+        return launch_pair_t<256, EPI_SWIGLU, H, BF16, 2>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       break;
     case EPI_CE:
       if (nseg == 0) return launch_pair_t<256, EPI_CE, H, BF16, 0>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
@@ -98,7 +100,9 @@ bool pair_supported(int kind, int M, int N, const EpiParams& ep) {
   if (kind == EPI_CE_GRAD) return false;  // single-CTA engine only
   if (ep.has_lora) {
     if (ep.lora.group_rows % (2 * kBM) != 0) return false;
-    if (!(kind == EPI_QKV_ROPE && ep.lora.nseg == 3) && !(kind == EPI_RESID && ep.lora.nseg == 1)) return false;
+    if (!(kind == EPI_QKV_ROPE && ep.lora.nseg == 3) && !(kind == EPI_RESID && ep.lora.nseg == 1) &&
+        !(kind == EPI_SWIGLU && ep.lora.nseg == 2 && ep.lora.inter128))
+      return false;
   }
   if (kind == EPI_QKV_ROPE && ep.seq_len % (2 * kBM) != 0 && ep.seq_len % kBM != 0) return false;
   return true;

@@ -91,6 +91,8 @@ struct LoraEpi {
   int seg_start[4];            // seg_start[nseg] == N; every boundary a multiple of BN
   long long seg_boff[3];       // offset of segment's B [rows, rank] inside theta (multiple of rank)
   int seg_ucol[3];             // first U16 column of the segment (multiple of 16)
+  int inter128;                // 1: two segments interleaved in 128-column blocks (the W1|W3 tiles of the
+                               // SwiGLU GEMM): column c is row ((c/256)*128 + c%128) of segment (c/128)%2
 };
 
 struct EpiParams {

@@ -263,13 +263,19 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int i = 0; i < RPL; ++i) {
           const int col = c0 + lane + 32 * i;
-          int seg = 0;
+          int seg = 0, rel;
+          if (NSEG == 2 && ep.lora.inter128) {
+            seg = (col >> 7) & 1;
+            rel = ((col >> 8) << 7) + (col & 127);
+          } else {
 #pragma unroll
-          for (int s = 1; s < NSEG; ++s)
-            if (col >= ep.lora.seg_start[s]) seg = s;
+            for (int s = 1; s < NSEG; ++s)
+              if (col >= ep.lora.seg_start[s]) seg = s;
+            rel = col - ep.lora.seg_start[seg];
+          }
           const bool ok = lane + 32 * i < HB && col < N;
           sg[i] = ok ? seg : -1;
-          const long long p0 = ep.lora.seg_boff[seg] + (long long)(col - ep.lora.seg_start[seg]) * rank_r;
+          const long long p0 = ep.lora.seg_boff[seg] + (long long)rel * rank_r;
           th[i][0] = ok ? __ldg(reinterpret_cast<const float4*>(ep.lora.theta + p0)) : make_float4(0.f, 0.f, 0.f, 0.f);
           th[i][1] = (ok && rank_r > 4) ? __ldg(reinterpret_cast<const float4*>(ep.lora.theta + p0 + 4))
                                         : make_float4(0.f, 0.f, 0.f, 0.f);

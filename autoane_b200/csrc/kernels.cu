@@ -398,6 +398,7 @@ static int launch_nl_na(const NormLoraArgs& a, size_t smem, int blocks, cudaStre
     case 4: return launch_nl_mma<NP, T, NORM, 4>(a, st);
     case 8: return launch_nl_mma<NP, T, NORM, 8>(a, st);
     case 12: return launch_nl_mma<NP, T, NORM, 12>(a, st);
+    case 16: return launch_nl_mma<NP, T, NORM, 16>(a, st);
     case 24: return launch_nl_mma<NP, T, NORM, 24>(a, st);
     default:
       set_error("norm/LoRA-down: unsupported LoRA-down row count %d", a.n_a * a.rank);
@@ -415,6 +416,20 @@ static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
     case 15: return launch_nl_na<15, T, NORM>(a, smem, blocks, st);
     case 16: return launch_nl_na<16, T, NORM>(a, smem, blocks, st);
     case 32: return launch_nl_na<32, T, NORM>(a, smem, blocks, st);
+    default:
+      break;
+  }
+  // LoRA-down of a gated FFN activation (--lora-ffn A2, no norm): the hidden widths
+  if (!NORM && a.a_prep && (a.n_a * a.rank == 4 || a.n_a * a.rank == 8)) {
+    const bool r8 = a.n_a * a.rank == 8;
+    switch (np) {
+      case 18: return r8 ? launch_nl_mma<18, T, false, 8>(a, st) : launch_nl_mma<18, T, false, 4>(a, st);
+      case 22: return r8 ? launch_nl_mma<22, T, false, 8>(a, st) : launch_nl_mma<22, T, false, 4>(a, st);
+      case 40: return r8 ? launch_nl_mma<40, T, false, 8>(a, st) : launch_nl_mma<40, T, false, 4>(a, st);
+      default: break;
+    }
+  }
+  switch (np) {
     default:
       set_error("norm/LoRA-down: unsupported width %d (need dim in {512, 960, 1024, 2048})", a.dim);
       return B2P_ERR_UNSUPPORTED;
@@ -783,23 +798,37 @@ int launch_tm_to_cf32(const void* src, int ld_src, bool src_f32, bool bf16, int 
 template <typename T>
 __global__ void lora_prep_kernel(LoraPrepArgs a) {
   const int r = a.rank;
-  const long long per_a = 4LL * r * a.ld;             // A elements per (layer, variant)
+  const long long per_a = (long long)a.segs * r * a.ld;  // A elements per (layer, variant)
+  const long long per_a2 = a.a2_out ? (long long)r * a.hidden : 0;
   const long long per_w = 2LL * a.dim;                // rms elements per (layer, variant)
   const long long n_a = (long long)a.nlayers * a.n_var * per_a;
+  const long long n_a2 = (long long)a.nlayers * a.n_var * per_a2;
   const long long n_w = (long long)a.nlayers * a.n_var * per_w + (long long)a.n_var * a.dim;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_a + n_w;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_a + n_a2 + n_w;
        i += (long long)gridDim.x * blockDim.x) {
     long long p;
     int v;
     bool valid = true;
-    if (i < n_a) {
-      const long long lv = i / per_a, e = i - lv * per_a;
+    if (i < n_a + n_a2) {
+      const bool a2 = i >= n_a;
+      const long long ii = a2 ? i - n_a : i;
+      const long long per = a2 ? per_a2 : per_a;
+      const int ld = a2 ? a.hidden : a.ld;
+      const long long lv = ii / per, e = ii - lv * per;
       const int l = (int)(lv / a.n_var);
       v = (int)(lv - (long long)l * a.n_var);
-      const int row = (int)(e / a.ld), c = (int)(e - (long long)row * a.ld);
+      const int row = (int)(e / ld), c = (int)(e - (long long)row * ld);
       const int m = row / r, j = row - m * r;
-      const int width = m < 3 ? a.dim : a.q_dim;
-      const long long off = m == 0 ? a.oAq : (m == 1 ? a.oAk : (m == 2 ? a.oAv : a.oAo));
+      int width;
+      long long off;
+      if (a2) {
+        width = a.hidden;
+        off = a.oA2;
+      } else {
+        width = (m < 3 || m > 3) ? a.dim : a.q_dim;
+        const long long offs[6] = {a.oAq, a.oAk, a.oAv, a.oAo, a.oA1, a.oA3};
+        off = offs[m];
+      }
       valid = c < width;
       p = (long long)l * a.layer_size + off + (long long)j * width + c;
       float val = 0.f;
@@ -809,10 +838,13 @@ __global__ void lora_prep_kernel(LoraPrepArgs a) {
         const uint32_t bit = vi.mode ? (__ldg(mask + (p >> 5)) >> (p & 31)) & 1u : 0u;
         val = perturb_value(__ldg(a.theta + p), bit, vi);
       }
-      static_cast<T*>(a.a_out)[i] = static_cast<T>(val);
+      if (a2)
+        static_cast<T*>(a.a2_out)[ii] = static_cast<T>(val);
+      else
+        static_cast<T*>(a.a_out)[ii] = static_cast<T>(val);
       continue;
     }
-    const long long k = i - n_a;
+    const long long k = i - n_a - n_a2;
     float* dst;
     const long long nl = (long long)a.nlayers * a.n_var * per_w;
     if (k < nl) {
@@ -836,7 +868,8 @@ __global__ void lora_prep_kernel(LoraPrepArgs a) {
 }
 
 int launch_lora_prep(const LoraPrepArgs& a, bool bf16, cudaStream_t st) {
-  B2P_REQUIRE(a.n_var >= 1 && a.rank >= 1 && a.rank <= 8 && a.ld >= a.dim && a.ld >= a.q_dim && a.ld % 8 == 0,
+  B2P_REQUIRE(a.n_var >= 1 && a.rank >= 1 && a.rank <= 8 && a.ld >= a.dim && a.ld >= a.q_dim && a.ld % 8 == 0 &&
+                  (a.segs == 4 || a.segs == 6) && (!a.a2_out || a.hidden % 8 == 0),
               "bad LoRA prep shape");
   if (bf16)
     lora_prep_kernel<__nv_bfloat16><<<148 * 8, 256, 0, st>>>(a);

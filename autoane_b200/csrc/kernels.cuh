@@ -52,7 +52,9 @@ struct NormLoraArgs {
 int launch_norm_lora(const NormLoraArgs& a, bool bf16, cudaStream_t st);
 
 // Per-variant perturbed LoRA-down operands of every layer, made once per forward:
-//   a_out[l][v][4r][ld]: rows 0..3r-1 = A_q, A_k, A_v (dim columns), rows 3r..4r-1 = A_o (q_dim columns), 16-bit
+//   a_out[l][v][segs*r][ld]: rows 0..3r-1 = A_q, A_k, A_v (dim columns), rows 3r..4r-1 = A_o
+//     (q_dim columns), with --lora-ffn rows 4r..6r-1 = A_1, A_3 (dim columns); 16-bit
+//   a2_out[l][v][r][hidden]: A_2 (--lora-ffn), 16-bit
 //   w_out[l][v][2][dim]: rms_att, rms_ffn (fp32); w_final[v][dim]: rms_final
 // each parameter as perturb_value(theta, sign bit of the variant's seed).
 struct LoraPrepArgs {
@@ -60,9 +62,10 @@ struct LoraPrepArgs {
   const uint32_t* masks;
   long long mask_words;
   const VariantInfo* variants;
-  int n_var, nlayers, dim, q_dim, rank, ld;
-  long long layer_size, oAq, oAk, oAv, oAo, oRa, oRf, oRfinal;
+  int n_var, nlayers, dim, q_dim, rank, ld, segs, hidden;
+  long long layer_size, oAq, oAk, oAv, oAo, oA1, oA3, oA2, oRa, oRf, oRfinal;
   void* a_out;
+  void* a2_out;
   float* w_out;
   float* w_final;
 };

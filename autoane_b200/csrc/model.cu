@@ -55,7 +55,10 @@ int model_alloc(b2p_model* m) {
   B2P_CHECK_CUDA(cudaMalloc(&m->attn_sched, 2 * sizeof(int)));
   B2P_CHECK_CUDA(cudaMemset(m->attn_sched, 0, 2 * sizeof(int)));
   m->prep_ld = (std::max(c.dim, m->q_dim) + 7) / 8 * 8;
-  B2P_CHECK_CUDA(cudaMalloc(&m->prep_a, (size_t)c.nlayers * m->max_groups * 4 * c.rank * m->prep_ld * e));
+  B2P_CHECK_CUDA(
+      cudaMalloc(&m->prep_a, (size_t)c.nlayers * m->max_groups * m->prep_segs * c.rank * m->prep_ld * e));
+  if (m->ffn)
+    B2P_CHECK_CUDA(cudaMalloc(&m->prep_a2, (size_t)c.nlayers * m->max_groups * c.rank * c.hidden * e));
   B2P_CHECK_CUDA(cudaMalloc(&m->prep_w, (size_t)c.nlayers * m->max_groups * 2 * c.dim * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->prep_wf, (size_t)m->max_groups * c.dim * 4));
   B2P_CHECK_CUDA(cudaMalloc(&m->rope_cos, (size_t)c.seq * (c.head_dim / 2) * 4));
@@ -92,7 +95,8 @@ void model_release(b2p_model* m) {
   void* dev[] = {m->wqkv, m->wo, m->w13, m->w2, m->cembed, m->embed, m->theta, m->masks, m->d_bufs,
                  m->d_polys, m->d_seeds, m->x, m->xn, m->U, m->qkv, m->attn, m->hbuf, m->ce_part,
                  m->ce_tgt, m->row_loss, m->group_loss, m->var_loss, m->pairs, m->d_tok, m->d_row_tgt, m->d_meta,
-                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf, m->d_c2f, m->attn_sched};
+                 m->d_var, m->rope_cos, m->rope_sin, m->prep_a, m->prep_w, m->prep_wf, m->d_c2f, m->attn_sched,
+                 m->prep_a2};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (m->stg.base) cudaFreeHost(m->stg.base);
@@ -202,14 +206,19 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
   lp.q_dim = QD;
   lp.rank = c.rank;
   lp.ld = m->prep_ld;
+  lp.segs = m->prep_segs;
+  lp.hidden = H;
   lp.layer_size = m->layer_size;
   lp.oAq = m->oAq; lp.oAk = m->oAk; lp.oAv = m->oAv; lp.oAo = m->oAo;
+  lp.oA1 = m->oA1; lp.oA3 = m->oA3; lp.oA2 = m->oA2;
   lp.oRa = m->oRa; lp.oRf = m->oRf; lp.oRfinal = m->oRfinal;
   lp.a_out = m->prep_a;
+  lp.a2_out = m->ffn ? m->prep_a2 : nullptr;
   lp.w_out = m->prep_w;
   lp.w_final = m->prep_wf;
   if ((rc = launch_lora_prep(lp, m->bf16, m->st))) return rc;
-  const long long a_vstride = 4LL * c.rank * m->prep_ld;
+  const long long a_vstride = (long long)m->prep_segs * c.rank * m->prep_ld;
+  const long long a2_vstride = (long long)c.rank * H;
   auto prep_a = [&](int l, int row) -> const void* {
     return static_cast<const char*>(m->prep_a) + ((size_t)l * nv * a_vstride + (size_t)row * m->prep_ld) * e;
   };
@@ -335,6 +344,17 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     nf.w_off = lb + m->oRf;
     nf.n_a = 0;
     nf.pc = pc;
+    if (m->ffn) {  // LoRA-down for W1 and W3 (U16 columns 0 and 16; q/k/v/o are consumed by now)
+      nf.n_a = 2;
+      nf.a_off[0] = lb + m->oA1;
+      nf.a_off[1] = lb + m->oA3;
+      nf.rank = c.rank;
+      nf.U = U;
+      nf.u_col = 0;
+      nf.a_prep = prep_a(l, 4 * c.rank);
+      nf.a_prep_vstride = a_vstride;
+      nf.a_prep_ld = m->prep_ld;
+    }
     nf.w_prep = m->prep_w + (size_t)l * nv * 2 * D + D;
     nf.w_prep_vstride = 2LL * D;
     if ((rc = launch_norm_lora(nf, m->bf16, m->st))) return rc;
@@ -343,13 +363,45 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     std::memset(&es, 0, sizeof(es));
     es.M = R;
     es.N = 2 * H;
+    if (m->ffn) {  // h1 += B1·u1, h3 += B3·u3 (train_mezo.m:1634-1638)
+      es.has_lora = 1;
+      es.lora = lora_epi(m);
+      es.lora.nseg = 2;
+      es.lora.inter128 = 1;
+      es.lora.seg_start[0] = 0;
+      es.lora.seg_start[1] = H;
+      es.lora.seg_start[2] = 2 * H;
+      es.lora.seg_boff[0] = lb + m->oB1;
+      es.lora.seg_boff[1] = lb + m->oB3;
+      es.lora.seg_ucol[0] = 0;
+      es.lora.seg_ucol[1] = 16;
+    }
     const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
     if (sv) {
       void* h13 = slab(sv->h13, l, (size_t)2 * H * e);
       if ((rc = gemm(m, 256, EPI_H16, xn2, D, w13, D, R, 2 * H, D, h13, 2 * H, es))) return rc;
       if ((rc = launch_swiglu_gate(h13, R, H, m->hbuf, m->bf16, m->st))) return rc;
     } else {
-      if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, m->hbuf, H, es))) return rc;
+      if ((rc = gemm(m, 256, EPI_SWIGLU, m->xn, D, w13, D, R, 2 * H, D, m->hbuf, H, es, m->ffn ? U : nullptr)))
+        return rc;
+    }
+    if (m->ffn) {  // LoRA-down of the gated activation for W2 (U16 column 32)
+      NormLoraArgs ng;
+      std::memset(&ng, 0, sizeof(ng));
+      ng.in = m->hbuf;
+      ng.rows = R;
+      ng.dim = H;
+      ng.norm = 0;
+      ng.n_a = 1;
+      ng.a_off[0] = lb + m->oA2;
+      ng.rank = c.rank;
+      ng.U = U;
+      ng.u_col = 32;
+      ng.pc = pc;
+      ng.a_prep = static_cast<const char*>(m->prep_a2) + (size_t)l * nv * a2_vstride * e;
+      ng.a_prep_vstride = a2_vstride;
+      ng.a_prep_ld = H;
+      if ((rc = launch_norm_lora(ng, m->bf16, m->st))) return rc;
     }
     // x += alpha * (h · W2^T)
     EpiParams e2;
@@ -357,8 +409,18 @@ int run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv 
     e2.M = R;
     e2.N = D;
     e2.alpha = c.res_alpha;
+    if (m->ffn) {  // o += B2·u2 (train_mezo.m:1658-1661)
+      e2.has_lora = 1;
+      e2.lora = lora_epi(m);
+      e2.lora.nseg = 1;
+      e2.lora.seg_start[0] = 0;
+      e2.lora.seg_start[1] = D;
+      e2.lora.seg_boff[0] = lb + m->oB2;
+      e2.lora.seg_ucol[0] = 32;
+    }
     const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
-    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->hbuf, H, w2, H, R, D, H, m->x, D, e2)))
+    if ((rc = gemm(m, pick_bn(D, EPI_RESID), EPI_RESID, m->hbuf, H, w2, H, R, D, H, m->x, D, e2,
+                   m->ffn ? U : nullptr)))
       return rc;
   }
   // final RMSNorm + lm-head with fused cross-entropy partials
@@ -579,6 +641,10 @@ b2p_model* b2p_model_create(const b2p_model_config* cfg) {
   if (c.rank != 4 && c.rank != 8) return bad("LoRA rank must be 4 or 8");
   if (c.dtype != B2P_F16 && c.dtype != B2P_BF16) return bad("dtype must be B2P_F16 or B2P_BF16");
   if (c.max_groups < 1 || c.max_groups > 256) return bad("max_groups must be in [1, 256]");
+  if (c.lora_ffn != 0 && c.lora_ffn != 1) return bad("lora_ffn must be 0 or 1");
+  if (c.lora_ffn && c.seq % 256) return bad("--lora-ffn needs seq %% 256 == 0 (two-segment SwiGLU LoRA tiles)");
+  if (c.lora_ffn && c.hidden != 1152 && c.hidden != 1408 && c.hidden != 2560)
+    return bad("--lora-ffn needs hidden in {1152, 1408, 2560} (LoRA-down width of the gated activation)");
   const int qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
   if (qd % 128 && qd % 160) return bad("q_dim must be a multiple of 128 or 160");
   const int qkv_bn = (qd % 160 == 0 && kvd % 160 == 0) ? 160 : ((qd % 128 == 0 && kvd % 128 == 0) ? 128 : 0);
@@ -600,6 +666,17 @@ b2p_model* b2p_model_create(const b2p_model_config* cfg) {
   m->oBv = o; o += KV * r;
   m->oAo = o; o += r * Q;
   m->oBo = o; o += D * r;
+  if (c.lora_ffn) {  // train_mezo.m:575-582
+    const long long H = c.hidden;
+    m->ffn = true;
+    m->prep_segs = 6;
+    m->oA1 = o; o += r * D;
+    m->oB1 = o; o += H * r;
+    m->oA2 = o; o += r * H;
+    m->oB2 = o; o += D * r;
+    m->oA3 = o; o += r * D;
+    m->oB3 = o; o += H * r;
+  }
   m->oRa = o; o += D;
   m->oRf = o; o += D;
   m->layer_size = o;
@@ -620,9 +697,16 @@ b2p_model* b2p_model_create(const b2p_model_config* cfg) {
   if (!rc) rc = model_alloc(m);
   if (!rc) {
     std::vector<long long> sizes;
+    const long long H = c.hidden;
     for (int l = 0; l < c.nlayers; ++l) {
-      const long long s[10] = {r * D, Q * r, r * D, KV * r, r * D, KV * r, r * Q, D * r, D, D};
-      sizes.insert(sizes.end(), s, s + 10);
+      const long long s[8] = {r * D, Q * r, r * D, KV * r, r * D, KV * r, r * Q, D * r};
+      sizes.insert(sizes.end(), s, s + 8);
+      if (m->ffn) {
+        const long long f[6] = {r * D, H * r, r * H, D * r, r * D, H * r};
+        sizes.insert(sizes.end(), f, f + 6);
+      }
+      sizes.push_back(D);
+      sizes.push_back(D);
     }
     sizes.push_back(D);
     SignPlan plan = make_sign_plan(sizes);

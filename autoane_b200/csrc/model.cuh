@@ -35,6 +35,8 @@ struct b2p_model {
   int q_dim = 0, kv_dim = 0, qkv_dim = 0, ffn2 = 0;
   // trainable layout (offsets inside a layer block, then rms_final)
   long long oAq, oBq, oAk, oBk, oAv, oBv, oAo, oBo, oRa, oRf, layer_size, oRfinal, P;
+  bool ffn = false;  // --lora-ffn: FFN adapters after Bo in every layer (-1 offsets otherwise)
+  long long oA1 = -1, oB1 = -1, oA2 = -1, oB2 = -1, oA3 = -1, oB3 = -1;
   // frozen weights (16-bit), per-layer contiguous
   void *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr, *cembed = nullptr;
   float* embed = nullptr;
@@ -74,7 +76,10 @@ struct b2p_model {
   int32_t* d_row_tgt = nullptr;  // [max_rows]
   int* d_meta = nullptr;         // group_seq[max_groups] | group_var[max_groups]
   b2p::VariantInfo* d_var = nullptr;
-  void* prep_a = nullptr;         // [L][max_groups][4r][prep_ld] perturbed A rows per variant (16-bit)
+  void* prep_a = nullptr;         // [L][max_groups][prep_segs*r][prep_ld] perturbed A rows per variant (16-bit):
+                                  // Aq, Ak, Av, Ao (+ A1, A3 with --lora-ffn)
+  int prep_segs = 4;
+  void* prep_a2 = nullptr;        // [L][max_groups][r][hidden] perturbed A2 rows per variant (--lora-ffn)
   float* prep_w = nullptr;        // [L][max_groups][2][dim] perturbed rms_att / rms_ffn per variant
   float* prep_wf = nullptr;       // [max_groups][dim] perturbed rms_final per variant
   int prep_ld = 0;

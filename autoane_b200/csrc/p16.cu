@@ -957,6 +957,8 @@ int attention_backward(const AttnBwdArgs& a0, bool bf16, cudaStream_t st) {
 
 int ensure_model_state(b2p_model* m) {
   if (m->p16) return B2P_OK;
+  // bp_lora_backward (backprop_lora.h:147-288) has no FFN-adapter gradients
+  B2P_REQUIRE(!m->ffn, "backprop-LoRA and full backprop are not defined for --lora-ffn models");
   const auto& c = m->cfg;
   const size_t L = c.nlayers, D = c.dim, H = c.hidden, QD = m->q_dim, QKV = m->qkv_dim, r = c.rank;
   const size_t e = model_esz(m);
@@ -1748,6 +1750,8 @@ int b2p_p16_grad_device(b2p_model* m, const int32_t* d_tokens, const int32_t* d_
 namespace b2p {
 
 int p16_view(b2p_model* m, bool make_full, TrainView* v) {
+  *v = TrainView();
+  if (m->ffn && !make_full) return B2P_OK;  // --lora-ffn models keep no backprop state
   int rc = ensure_model_state(m);
   if (rc) return rc;
   if (make_full && (rc = ensure_full(m))) return rc;

@@ -34,11 +34,12 @@ class Config:
     res_alpha: float = 1.0
     dtype: int = F16
     max_groups: int = 64
+    lora_ffn: bool = False
 
     def c(self) -> _lib.ModelConfig:
         return _lib.ModelConfig(self.dim, self.hidden, self.heads, self.kv_heads, self.head_dim, self.seq,
                                 self.nlayers, self.vocab, self.rank, self.rope_theta, self.res_alpha, self.dtype,
-                                self.max_groups)
+                                self.max_groups, int(self.lora_ffn))
 
 
 def _fp(a):

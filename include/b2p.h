@@ -96,6 +96,10 @@ typedef struct {
   float res_alpha;   /* residual scale (train_mezo.m:1262): 1 for fine-tuning */
   int dtype;         /* B2P_F16 or B2P_BF16 compute type, fp32 accumulation */
   int max_groups;    /* max (variant x sequence) forwards evaluated in one call */
+  int lora_ffn;      /* --lora-ffn (train_mezo.m:866, 898): adapters on W1, W2, W3 too; the
+                        trainable set then holds A1, B1, A2, B2, A3, B3 after Bo in every layer
+                        (perturb_lora_weights order, train_mezo.m:575-582). MeZO only; needs
+                        seq % 256 == 0 and hidden in {1152, 1408, 2560}. */
 } b2p_model_config;
 
 /* One evaluation point of the trainable parameters θ:

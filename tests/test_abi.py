@@ -36,8 +36,8 @@ def test_version_and_error_strings():
 
 
 def test_struct_layouts_match_header():
-    # b2p_model_config: 9 ints, 2 floats, 2 ints; b2p_variant: u64, int, 2 floats
-    assert C.sizeof(_lib.ModelConfig) == 13 * 4
+    # b2p_model_config: 9 ints, 2 floats, 3 ints; b2p_variant: u64, int, 2 floats
+    assert C.sizeof(_lib.ModelConfig) == 14 * 4
     assert C.sizeof(_lib.Variant) == 24
 
 
