@@ -44,13 +44,15 @@ LR = np.float32(1e-4)
 REF_STEPS_PER_S = 3.82    # reference best: ANE conv-fused MeZO-LoRA-split r8, M2 Pro (README.md:16)
 
 
-def fwd_flops_per_seq() -> float:
+def fwd_flops_per_seq(ffn: bool = False) -> float:
     """Algorithmic FLOPs of one 256-token forward (projections + lm-head + LoRA + dense attention)."""
     d = DIMS
     s, D, H, r = d["seq"], d["dim"], d["hidden"], d["rank"]
     qd, kvd = d["heads"] * d["head_dim"], d["kv_heads"] * d["head_dim"]
     proj = 2 * s * (D * (qd + 2 * kvd) + qd * D + 3 * D * H)
     lora = 2 * s * r * ((3 * D + qd) + (qd + 2 * kvd + D))  # LoRA-down (A·x) + LoRA-up (B·U)
+    if ffn:  # --lora-ffn: A1, A3 over xn2, A2 over the gated activation; B1, B3, B2
+        lora += 2 * s * r * ((2 * D + H) + (2 * H + D))
     attn = 2 * 2 * d["heads"] * s * s * d["head_dim"]
     head = 2 * s * N_ACTIVE * D
     return float(d["nlayers"] * (proj + lora + attn) + head)
@@ -76,24 +78,32 @@ def synth_embed():
 def synth_theta(layout):
     """LoRA A ~ N(0, 1/r), B = 0, RMS weights 1 (workload definition)."""
     rng = np.random.default_rng([42, 20_000])
-    L, D, r = DIMS["nlayers"], DIMS["dim"], DIMS["rank"]
+    L, D, r, H = DIMS["nlayers"], DIMS["dim"], DIMS["rank"], DIMS["hidden"]
     qd = DIMS["heads"] * DIMS["head_dim"]
     theta = np.zeros(layout["total"], np.float32)
+    a_blocks = [("Aq", r * D), ("Ak", r * D), ("Av", r * D), ("Ao", r * qd)]
+    if "A1" in layout:
+        a_blocks += [("A1", r * D), ("A2", r * H), ("A3", r * D)]
     for l in range(L):
         b = l * layout["layer"]
-        for off, n in ((layout["Aq"], r * D), (layout["Ak"], r * D), (layout["Av"], r * D), (layout["Ao"], r * qd)):
+        for name, n in a_blocks:
+            off = layout[name]
             theta[b + off:b + off + n] = rng.standard_normal(n, dtype=np.float32) / np.float32(np.sqrt(r))
         theta[b + layout["rms_att"]:b + layout["rms_att"] + 2 * D] = 1.0
     theta[layout["rms_final"]:] = 1.0
     return theta
 
 
-def lora_layout():
-    D, r = DIMS["dim"], DIMS["rank"]
+def lora_layout(ffn: bool = False):
+    """Trainable layout in perturb_lora_weights order (train_mezo.m:566-587)."""
+    D, r, H = DIMS["dim"], DIMS["rank"], DIMS["hidden"]
     qd, kvd = DIMS["heads"] * DIMS["head_dim"], DIMS["kv_heads"] * DIMS["head_dim"]
     o, lay = 0, {}
-    for name, n in (("Aq", r * D), ("Bq", qd * r), ("Ak", r * D), ("Bk", kvd * r), ("Av", r * D), ("Bv", kvd * r),
-                    ("Ao", r * qd), ("Bo", D * r), ("rms_att", D), ("rms_ffn", D)):
+    blocks = [("Aq", r * D), ("Bq", qd * r), ("Ak", r * D), ("Bk", kvd * r), ("Av", r * D), ("Bv", kvd * r),
+              ("Ao", r * qd), ("Bo", D * r)]
+    if ffn:
+        blocks += [("A1", r * D), ("B1", H * r), ("A2", r * H), ("B2", D * r), ("A3", r * D), ("B3", H * r)]
+    for name, n in blocks + [("rms_att", D), ("rms_ffn", D)]:
         lay[name] = o
         o += n
     lay["layer"] = o
@@ -269,9 +279,10 @@ def run_reference(args):
     return 0
 
 
-def workload_config(world: int):
+def workload_config(world: int, ffn: bool = False):
+    adapters = "adapters on Wq/Wk/Wv/Wo/W1/W2/W3 (--lora-ffn)" if ffn else "adapters on Wq/Wk/Wv/Wo"
     return {"workload": "DP MeZO-LoRA-split r8, SmolLM2-360M shapes (32L, d960, 15/5 heads, FFN 2560, "
-                        "compact vocab 16893), SEQ 256; per GPU 8 sequences x 4 seeds x (+eps, -eps)",
+                        f"compact vocab 16893), SEQ 256; {adapters}; per GPU 8 sequences x 4 seeds x (+eps, -eps)",
             "model": "SmolLM2-360M-shaped (random init)", "global_batch": SEQS_PER_GPU * world, "seq_len": DIMS["seq"],
             "parallelism": f"dp{world}", "seeds_per_gpu": SEEDS_PER_GPU, "lora_rank": DIMS["rank"],
             "eps": float(EPS), "lr": float(LR), "seq_steps_per_step": SEQS_PER_GPU * SEEDS_PER_GPU * world,
@@ -289,6 +300,7 @@ def main():
     ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true", help="skip the in-region per-GEMM CUDA events")
+    ap.add_argument("--lora-ffn", action="store_true", help="MeZO workload with LoRA on W1/W2/W3 too")
     ap.add_argument("--p16-seqs", type=int, default=P16_SEQS_PER_GPU, help="sequences per GPU per P16 step")
     ap.add_argument("--full-seqs", type=int, default=32, help="sequences per GPU per full-backprop step")
     ap.add_argument("--workload", choices=["mezo", "p16", "full", "gemm"], default="mezo",
@@ -316,10 +328,12 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     _lib.call("b2p_init", local)
     cfg = Config(dtype=BF16 if args.dtype == "bf16" else F16, max_groups=2 * SEEDS_PER_GPU * SEQS_PER_GPU,
+                 lora_ffn=args.lora_ffn,
                  **{k: DIMS[k] for k in ("dim", "hidden", "heads", "kv_heads", "head_dim", "seq", "nlayers", "vocab",
                                          "rank", "rope_theta")})
     model = Model(cfg)
-    keep_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    # the timed CPU reference is the plain (attention-adapter) MeZO step
+    keep_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline and not args.lora_ffn
     cpu_w = {k: [] for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")} if keep_cpu else None
     for l in range(DIMS["nlayers"]):
         ws = synth_weights(l)
@@ -329,7 +343,7 @@ def main():
                 cpu_w[k].append(w)
     embed = synth_embed()
     model.set_embedding(embed, np.arange(N_ACTIVE, dtype=np.int32))
-    lay = lora_layout()
+    lay = lora_layout(args.lora_ffn)
     model.set_trainable(synth_theta(lay))
     tokens = token_stream()
 
@@ -445,9 +459,9 @@ def main():
                 "value": round(value, 3), "unit": "seq-steps/s", "n_gpus": world, "steps": K, "warmup": W,
                 "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": round(value / REF_STEPS_PER_S, 2), "dtype": args.dtype, "data": "synthetic",
-                "config": workload_config(world) | {
+                "config": workload_config(world, args.lora_ffn) | {
                     "optimizer_steps_per_s": round(K / (dev_ms / 1000.0), 3),
-                    "tflops_per_gpu": round(2 * SEQS_PER_GPU * SEEDS_PER_GPU * fwd_flops_per_seq() * K /
+                    "tflops_per_gpu": round(2 * SEQS_PER_GPU * SEEDS_PER_GPU * fwd_flops_per_seq(args.lora_ffn) * K /
                                             (dev_ms / 1000.0) / 1e12, 2)},
                 "e2e": {"value": round(e2e_value, 3), "unit": "seq-steps/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
