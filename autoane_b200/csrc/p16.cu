@@ -31,6 +31,9 @@ namespace b2p {
 
 // One factored LoRA weight-gradient: out = scale * sum_t X[t, c] * U[t, ucol + j]
 // for c < ncols, j < rank, written [ncols][rank] (B layout) or [rank][ncols] (A layout).
+// One factored weight gradient out_s[c][j] = sum_t X[t, c] · U[t, ucol + 16 s + j] for the
+// nu segments s of U (16-column groups), stored in the A ([rank][ncols]) or B ([ncols][rank])
+// layout of the trainable set.
 struct WgradJob {
   const void* X;
   long long ldx;
@@ -38,11 +41,11 @@ struct WgradJob {
   int ucol;
   const void* U;  // [R][ldu]
   long long ldu;
-  float* out;
+  float* out[3];
+  int nu;
   int a_layout;
-  int pad;
 };
-constexpr int kMaxWgradJobs = 8;
+constexpr int kMaxWgradJobs = 6;
 constexpr int kWgradSplit = 8;  // row chunks per weight gradient (partials summed in chunk order)
 constexpr int kRmsTeam = 128;   // threads per row of the RMSNorm backward
 constexpr int kRmsTeams = 4;    // rows in flight per block
@@ -362,104 +365,135 @@ __global__ void rms_part_reduce_kernel(const float* __restrict__ part, int nvec,
 
 // ---------------------------------------------------------------------------
 // factored LoRA weight gradients (lora_grad_project, training/config.h:286-292,
-// without forming dW): one block per (64-column tile, job, row chunk) writes
-// part[job][chunk][c][j] = sum_{t in chunk} X[t, c] * U[t, j]; a second kernel
-// sums the chunks in order, scales and stores in the A or B layout.
+// without forming dW) on the tensor cores: Xᵀ·U as an [ncols x R]·[R x 8 nu] product.
+// One block per (128-column tile, job, row chunk); 8 warps own 16 columns each and
+// run mma.sync m16n8k16 (fp32 accumulation) over the chunk's rows, 64 rows per
+// cp.async stage, two stages in flight. Xᵀ and U fragments come from ldmatrix.trans
+// of the row-major tiles. Partials part[job][chunk][c][24] are summed over the chunks
+// in order by a second kernel (deterministic), which scales and stores them.
 // ---------------------------------------------------------------------------
-// 256 threads: column group cg = tid % 16 (4 columns) x row group rg = tid / 16;
-// each thread accumulates 4 columns x 8 rank outputs over its rows of the tile.
+constexpr int kWgRows = 64;    // rows per stage
+constexpr int kWgCols = 128;   // columns per block
+constexpr int kWgXs = kWgCols + 8;  // padded smem row (elements): conflict-free ldmatrix
+constexpr int kWgUs = 40;           // up to three 8-column U segments; 80-byte rows: conflict-free ldmatrix
+constexpr int kWgPartJ = 24;        // partial entries per column
+
 template <typename T>
-__global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restrict__ jobs, int rows, int rank,
+__global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restrict__ jobs, int rows,
                                                         float* __restrict__ part, int max_cols) {
-  __shared__ __align__(16) T s_x[64][64];
-  __shared__ __align__(16) float s_u[64][8];
-  __shared__ float s_sum[16][64 * 8 + 4];
+  __shared__ __align__(128) T s_x[2][kWgRows][kWgXs];
+  __shared__ __align__(128) T s_u[2][kWgRows][kWgUs];
   const WgradJob jb = jobs[blockIdx.y];
-  const int c0 = blockIdx.x * 64;
+  const int c0 = blockIdx.x * kWgCols;
   if (c0 >= jb.ncols) return;
   const int chunk_rows = (rows + kWgradSplit - 1) / kWgradSplit;
   const int r_begin = blockIdx.z * chunk_rows, r_end = min(rows, r_begin + chunk_rows);
-  const int tid = threadIdx.x;
-  const int cg = tid & 15, rg = tid >> 4;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const T* X = static_cast<const T*>(jb.X);
   const T* U = static_cast<const T*>(jb.U);
-  float acc[4][8];
-#pragma unroll
-  for (int a = 0; a < 4; ++a)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[a][j] = 0.f;
-  for (int t0 = r_begin; t0 < r_end; t0 += 64) {
-    for (int i = tid; i < 64 * 8; i += 256) {
-      const int r = i >> 3, ch = i & 7;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  const int nu = jb.nu;
+  const uint32_t sx0 = smem_u32(&s_x[0][0][0]), su0 = smem_u32(&s_u[0][0][0]);
+  constexpr uint32_t kXStage = kWgRows * kWgXs * 2, kUStage = kWgRows * kWgUs * 2;
+
+  auto load_stage = [&](int st, int t0) {
+    // X: 64 rows x 128 columns = 1024 chunks of 16 B; columns past ncols and rows past
+    // the chunk are zero-filled
+    for (int i = tid; i < kWgRows * (kWgCols / 8); i += 256) {
+      const int r = i >> 4, ch = i & 15;
+      const uint32_t dst = sx0 + st * kXStage + (uint32_t)((r * kWgXs + ch * 8) * 2);
       if (t0 + r < r_end && c0 + ch * 8 < jb.ncols)
-        v = *reinterpret_cast<const uint4*>(X + (long long)(t0 + r) * jb.ldx + c0 + ch * 8);
-      *reinterpret_cast<uint4*>(&s_x[r][ch * 8]) = v;
+        cp_async16(dst, X + (long long)(t0 + r) * jb.ldx + c0 + ch * 8);
+      else
+        *reinterpret_cast<uint4*>(&s_x[st][r][ch * 8]) = make_uint4(0u, 0u, 0u, 0u);
     }
-    for (int i = tid; i < 64 * 8; i += 256) {
-      const int r = i >> 3, j = i & 7;
-      s_u[r][j] =
-          (t0 + r < r_end && j < rank) ? static_cast<float>(U[(long long)(t0 + r) * jb.ldu + jb.ucol + j]) : 0.f;
+    // U: 64 rows x nu segments of 8 columns (16 B each)
+    for (int i = tid; i < kWgRows * 3; i += 256) {
+      const int r = i / 3, sg = i - r * 3;
+      if (sg >= nu) continue;
+      const uint32_t dst = su0 + st * kUStage + (uint32_t)((r * kWgUs + sg * 8) * 2);
+      if (t0 + r < r_end)
+        cp_async16(dst, U + (long long)(t0 + r) * jb.ldu + jb.ucol + 16 * sg);
+      else
+        *reinterpret_cast<uint4*>(&s_u[st][r][sg * 8]) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    cp_async_commit();
+  };
+
+  float acc[3][4];
+#pragma unroll
+  for (int s3 = 0; s3 < 3; ++s3) acc[s3][0] = acc[s3][1] = acc[s3][2] = acc[s3][3] = 0.f;
+  const int nst = (r_end - r_begin + kWgRows - 1) / kWgRows;
+  if (nst > 0) load_stage(0, r_begin);
+  const int q = lane >> 3, lr = lane & 7;
+  for (int it = 0; it < nst; ++it) {
+    const int st = it & 1;
+    if (it + 1 < nst) {
+      load_stage(st ^ 1, r_begin + (it + 1) * kWgRows);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int t = rg + 16 * q;
-      const uint2 xr = *reinterpret_cast<const uint2*>(&s_x[t][cg * 4]);
-      const float2 x01 = H2<T>::to_f2(*reinterpret_cast<const typename H2<T>::V*>(&xr.x));
-      const float2 x23 = H2<T>::to_f2(*reinterpret_cast<const typename H2<T>::V*>(&xr.y));
-      const float4 ua = *reinterpret_cast<const float4*>(&s_u[t][0]);
-      const float4 ub = *reinterpret_cast<const float4*>(&s_u[t][4]);
-      const float xs[4] = {x01.x, x01.y, x23.x, x23.y};
-      const float us[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+    for (int kk = 0; kk < kWgRows / 16; ++kk) {
+      // A = Xᵀ (16 columns x 16 rows): matrices (m 0-7 | 8-15) x (k 0-7 | 8-15), transposed
+      uint32_t a[4];
+      const int k_row = kk * 16 + (q >> 1) * 8 + lr, m_col = warp * 16 + (q & 1) * 8;
+      ldsm_x4_t(sx0 + st * kXStage + (uint32_t)((k_row * kWgXs + m_col) * 2), a[0], a[1], a[2], a[3]);
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[a][j] += xs[a] * us[j];
+      for (int sg = 0; sg < 3; ++sg) {
+        if (sg >= nu) break;
+        // B = U (16 rows x 8 columns), transposed: (k 0-7) and (k 8-15)
+        uint32_t b0, b1, b2, b3;
+        const int u_row = kk * 16 + (q & 1) * 8 + lr;
+        ldsm_x4_t(su0 + st * kUStage + (uint32_t)((u_row * kWgUs + sg * 8) * 2), b0, b1, b2, b3);
+        mma16816<T>(acc[sg], a, b0, b1);
+      }
     }
-    __syncthreads();
+    __syncthreads();  // stage `st` is refilled by the next iteration's prefetch
   }
-  // sum the 16 row groups in order
+  // D fragment: rows = columns c (lane/4, +8), cols = j (2 (lane%4) + {0,1})
+  float* p = part + (long long)(blockIdx.y * kWgradSplit + blockIdx.z) * max_cols * kWgPartJ;
+  const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int sg = 0; sg < 3; ++sg) {
+    if (sg >= nu) break;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s_sum[rg][(cg * 4 + a) * 8 + j] = acc[a][j];
-  __syncthreads();
-  float* p = part + (long long)(blockIdx.y * kWgradSplit + blockIdx.z) * max_cols * 8;
-  for (int o = tid; o < 64 * 8; o += 256) {
-    const int col = c0 + o / 8;
-    if (col >= jb.ncols) continue;
-    float sum = 0.f;
-#pragma unroll
-    for (int g = 0; g < 16; ++g) sum += s_sum[g][o];
-    p[(long long)col * 8 + (o & 7)] = sum;
+    for (int e = 0; e < 4; ++e) {
+      const int col = c0 + warp * 16 + g + ((e >> 1) << 3);
+      const int jj = 2 * t4 + (e & 1);
+      if (col < jb.ncols) p[(long long)col * kWgPartJ + sg * 8 + jj] = acc[sg][e];
+    }
   }
 }
 
 __global__ void lora_wgrad_reduce_kernel(const WgradJob* __restrict__ jobs, int rank, const float* __restrict__ part,
                                          int max_cols, float scale) {
   const WgradJob jb = jobs[blockIdx.y];
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (col, j)
-  if (i >= jb.ncols * rank) return;
-  const int col = i / rank, j = i - col * rank;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (segment, col, j)
+  const int per = jb.ncols * rank;
+  if (i >= jb.nu * per) return;
+  const int sg = i / per, rem = i - sg * per;
+  const int col = rem / rank, j = rem - col * rank;
   float s = 0.f;
-  for (int z = 0; z < kWgradSplit; ++z) s += part[((long long)(blockIdx.y * kWgradSplit + z) * max_cols + col) * 8 + j];
+  for (int z = 0; z < kWgradSplit; ++z)
+    s += part[((long long)(blockIdx.y * kWgradSplit + z) * max_cols + col) * kWgPartJ + sg * 8 + j];
   if (jb.a_layout)
-    jb.out[(long long)j * jb.ncols + col] = s * scale;
+    jb.out[sg][(long long)j * jb.ncols + col] = s * scale;
   else
-    jb.out[(long long)col * rank + j] = s * scale;
+    jb.out[sg][(long long)col * rank + j] = s * scale;
 }
 
 int lora_wgrad(const WgradJob* d_jobs, int njobs, int max_cols, int rows, int rank, float scale, float* part,
                bool bf16, cudaStream_t st) {
   B2P_REQUIRE(rank == 4 || rank == 8, "LoRA rank must be 4 or 8");
-  dim3 grid((max_cols + 63) / 64, njobs, kWgradSplit);
+  dim3 grid((max_cols + kWgCols - 1) / kWgCols, njobs, kWgradSplit);
   if (bf16)
-    lora_wgrad_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(d_jobs, rows, rank, part, max_cols);
+    lora_wgrad_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(d_jobs, rows, part, max_cols);
   else
-    lora_wgrad_kernel<__half><<<grid, 256, 0, st>>>(d_jobs, rows, rank, part, max_cols);
+    lora_wgrad_kernel<__half><<<grid, 256, 0, st>>>(d_jobs, rows, part, max_cols);
   B2P_POST_LAUNCH();
-  dim3 g2((max_cols * rank + 255) / 256, njobs);
+  dim3 g2((3 * max_cols * rank + 255) / 256, njobs);
   lora_wgrad_reduce_kernel<<<g2, 256, 0, st>>>(d_jobs, rank, part, max_cols, scale);
   B2P_POST_LAUNCH();
   return B2P_OK;
@@ -1070,7 +1104,7 @@ int ensure_rows(b2p_model* m, int R) {
   P16_ALLOC(s->dvec, Rz * heads * 4);
   const size_t nblk = rms_blocks(R);
   P16_ALLOC(s->rms_part, (2 * L + 1) * nblk * D * 4);
-  P16_ALLOC(s->wgrad_part, (size_t)kMaxWgradJobs * kWgradSplit * std::max(D, QD) * 8 * 4);
+  P16_ALLOC(s->wgrad_part, (size_t)kMaxWgradJobs * kWgradSplit * std::max(D, QD) * kWgPartJ * 4);
   if (s->full) {
     const size_t rows_t = std::max<size_t>(std::max<size_t>(QKV, 2 * H), (size_t)s->cv_pad);
     P16_ALLOC(s->tA, rows_t * Rz * e);
@@ -1094,14 +1128,14 @@ int ensure_rows(b2p_model* m, int R) {
     const long long ldq = QKV + kUCols;
     const void* up = dq + QKV * e;  // U'_{q,k,v} = dQKV · B, columns QKV.. of dqkv
     WgradJob* j = &jobs[l * kMaxWgradJobs];
-    j[0] = {s->d16, (long long)D, (int)D, 48, Ul, kUCols, g + m->oBo, 0, 0};                 // dB_o
-    j[1] = {at(v.attn, l, QD), (long long)QD, (int)QD, 0, s->ub_o, kUCols, g + m->oAo, 1, 0};  // dA_o
-    j[2] = {dq, ldq, (int)QD, 0, Ul, kUCols, g + m->oBq, 0, 0};                               // dB_q
-    j[3] = {dq + QD * e, ldq, (int)KVD, 16, Ul, kUCols, g + m->oBk, 0, 0};                    // dB_k
-    j[4] = {dq + (QD + KVD) * e, ldq, (int)KVD, 32, Ul, kUCols, g + m->oBv, 0, 0};            // dB_v
-    j[5] = {xnl, (long long)D, (int)D, 0, up, ldq, g + m->oAq, 1, 0};                          // dA_q
-    j[6] = {xnl, (long long)D, (int)D, 16, up, ldq, g + m->oAk, 1, 0};                         // dA_k
-    j[7] = {xnl, (long long)D, (int)D, 32, up, ldq, g + m->oAv, 1, 0};                         // dA_v
+    j[0] = {s->d16, (long long)D, (int)D, 48, Ul, kUCols, {g + m->oBo, nullptr, nullptr}, 1, 0};  // dB_o
+    j[1] = {at(v.attn, l, QD), (long long)QD, (int)QD, 0, s->ub_o, kUCols, {g + m->oAo, nullptr, nullptr}, 1,
+            1};                                                                                       // dA_o
+    j[2] = {dq, ldq, (int)QD, 0, Ul, kUCols, {g + m->oBq, nullptr, nullptr}, 1, 0};                  // dB_q
+    j[3] = {dq + QD * e, ldq, (int)KVD, 16, Ul, kUCols, {g + m->oBk, nullptr, nullptr}, 1, 0};       // dB_k
+    j[4] = {dq + (QD + KVD) * e, ldq, (int)KVD, 32, Ul, kUCols, {g + m->oBv, nullptr, nullptr}, 1, 0};  // dB_v
+    // dA_q, dA_k, dA_v share X = xn: one pass over it with the three U' segments
+    j[5] = {xnl, (long long)D, (int)D, 0, up, ldq, {g + m->oAq, g + m->oAk, g + m->oAv}, 3, 1};
   }
   B2P_CHECK_CUDA(cudaMemcpy(s->d_jobs, jobs.data(), jobs.size() * sizeof(WgradJob), cudaMemcpyHostToDevice));
   return B2P_OK;
