@@ -371,6 +371,144 @@ __global__ void __launch_bounds__(256, 2) norm_lora_mma_kernel(NormLoraArgs a) {
   }
 }
 
+// LoRA-down of a 16-bit input (no norm) with prepared per-variant A rows, as a
+// persistent kernel: every CTA takes a contiguous range of RT-row tiles, keeps the
+// next tile's cp.async copy in flight while the current one is multiplied, and
+// splits each tile's K (= dim) over its 8 warps (mma.sync m16n8k16, fp32), summing
+// the warps' partials in a fixed order. A rows are restaged only when the tile's
+// variant changes (a contiguous range crosses few variant groups).
+template <int NP, int RT, int NA>
+struct LdSmem {
+  static constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, MT = RT / 16;
+  static constexpr int kX = RT * XS * 2;            // one x tile (16-bit)
+  static constexpr int kA = NT * 8 * XS * 2;        // A rows (16-bit, zero padded to whole n-tiles)
+  static constexpr int kRed = 8 * RT * NT * 8 * 4;  // per-warp partial U
+  static constexpr int kTotal = 2 * kX + kA + kRed;
+};
+
+template <int NP, typename T, int NA, int RT>
+__global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
+  using S = LdSmem<NP, RT, NA>;
+  constexpr int dim = S::dim, XS = S::XS, NT = S::NT, MT = S::MT, KS = dim / 16;
+  extern __shared__ __align__(16) uint8_t smx[];
+  T* s_x = reinterpret_cast<T*>(smx);                         // [2][RT][XS]
+  T* s_a = reinterpret_cast<T*>(smx + 2 * S::kX);             // [NT*8][XS]
+  float* s_red = reinterpret_cast<float*>(smx + 2 * S::kX + S::kA);  // [8][RT][NT*8]
+  const int ntiles = (a.rows + RT - 1) / RT;
+  const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+  if (t_begin >= t_end) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sx0 = smem_u32(s_x), sab = smem_u32(s_a);
+
+  auto load_x = [&](int tile, int buf) {
+    const int row0 = tile * RT;
+    for (int i = threadIdx.x; i < RT * (dim / 8); i += 256) {
+      const int r = i / (dim / 8), c8 = i - r * (dim / 8);
+      const int row = row0 + r;
+      if (row < a.rows)
+        cp_async16(sx0 + (uint32_t)(((buf * RT + r) * XS + c8 * 8) * 2),
+                   static_cast<const T*>(a.in) + (long long)row * dim + c8 * 8);
+      else
+        *reinterpret_cast<uint4*>(s_x + (buf * RT + r) * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  load_x(t_begin, 0);
+  cp_async_commit();
+  int cur_var = -1;
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    const int buf = (tile - t_begin) & 1;
+    const int var = a.pc.group_variant[(tile * RT) / a.pc.group_rows];
+    if (var != cur_var) {
+      __syncthreads();  // every warp is done with the previous A rows
+      const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
+      for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 256) {
+        const int r = i / (dim / 8), c8 = i - r * (dim / 8);
+        if (r < NA)
+          cp_async16(sab + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
+        else
+          *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      cp_async_commit();
+      cur_var = var;
+    }
+    if (tile + 1 < t_end) load_x(tile + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();  // this tile's rows and the A rows have landed
+    __syncthreads();
+
+    // ---- split-K mma: warp w takes k-steps [w KS/8, (w+1) KS/8) of every (m16, n8) task ----
+    float c[MT][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) c[mt][nt][0] = c[mt][nt][1] = c[mt][nt][2] = c[mt][nt][3] = 0.f;
+    const int lm = lane >> 3, lr = lane & 7;
+    const uint32_t sxb = sx0 + (uint32_t)(buf * RT * XS * 2);
+    for (int kk = warp * KS / 8; kk < (warp + 1) * KS / 8; ++kk) {
+      uint32_t bf[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        uint32_t b2, b3;
+        ldsm_x4(sab + (uint32_t)(((nt * 8 + lr) * XS + kk * 16 + (lm & 1) * 8) * 2), bf[nt][0], bf[nt][1], b2, b3);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t af[4];
+        ldsm_x4(sxb + (uint32_t)(((mt * 16 + (lm & 1) * 8 + lr) * XS + kk * 16 + (lm >> 1) * 8) * 2), af[0], af[1],
+                af[2], af[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<T>(c[mt][nt], af, bf[nt][0], bf[nt][1]);
+      }
+    }
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int rr = mt * 16 + g + ((e >> 1) << 3), n = nt * 8 + 2 * t4 + (e & 1);
+          s_red[(warp * RT + rr) * (NT * 8) + n] = c[mt][nt][e];
+        }
+    __syncthreads();
+    // ---- partials summed in warp order, rounded to 16 bit like the LoRA-up operand ----
+    for (int i = threadIdx.x; i < RT * NA; i += 256) {
+      const int rr = i / NA, n = i - rr * NA;
+      const int row = tile * RT + rr;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) v += s_red[(w * RT + rr) * (NT * 8) + n];
+      if (row < a.rows) {
+        const int m = n / a.rank, j = n - m * a.rank;
+        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(v);
+      }
+    }
+  }
+}
+
+template <int NP, typename T, int NA>
+static int launch_lora_down(const NormLoraArgs& a, cudaStream_t st) {
+  constexpr int RT = NP * 64 <= 1024 ? 32 : 16;
+  using S = LdSmem<NP, RT, NA>;
+  static_assert(S::kTotal <= 227 * 1024, "LoRA-down tiles exceed shared memory");
+  B2P_REQUIRE(a.pc.group_rows % RT == 0, "variant groups must be multiples of %d rows", RT);
+  DeviceCtx* c = nullptr;
+  int rc = ctx_get(&c);
+  if (rc) return rc;
+  auto k = lora_down_kernel<NP, T, NA, RT>;
+  static thread_local uint64_t attr_mask = 0;  // one per instantiation
+  if (!(attr_mask & (1ull << (c->device & 63)))) {
+    B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+    attr_mask |= 1ull << (c->device & 63);
+  }
+  const int ntiles = (a.rows + RT - 1) / RT;
+  const int grid = ntiles < c->num_sms ? ntiles : c->num_sms;
+  k<<<grid, 256, S::kTotal, st>>>(a);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
 template <int NP, typename T, bool NORM, int NA>
 static int launch_nl_mma(const NormLoraArgs& a, cudaStream_t st) {
   constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8;
@@ -393,6 +531,13 @@ static int launch_nl(const NormLoraArgs& a, size_t smem, int blocks, cudaStream_
 
 template <int NP, typename T, bool NORM>
 static int launch_nl_na(const NormLoraArgs& a, size_t smem, int blocks, cudaStream_t st) {
+  if (!NORM && a.a_prep) {
+    switch (a.n_a * a.rank) {
+      case 4: return launch_lora_down<NP, T, 4>(a, st);
+      case 8: return launch_lora_down<NP, T, 8>(a, st);
+      default: break;
+    }
+  }
   switch (a.n_a * a.rank) {
     case 0: return launch_nl<NP, T, NORM, 0>(a, smem, blocks, st);
     case 4: return launch_nl_mma<NP, T, NORM, 4>(a, st);
@@ -423,9 +568,9 @@ static int launch_norm_lora_t(const NormLoraArgs& a, cudaStream_t st) {
   if (!NORM && a.a_prep && (a.n_a * a.rank == 4 || a.n_a * a.rank == 8)) {
     const bool r8 = a.n_a * a.rank == 8;
     switch (np) {
-      case 18: return r8 ? launch_nl_mma<18, T, false, 8>(a, st) : launch_nl_mma<18, T, false, 4>(a, st);
-      case 22: return r8 ? launch_nl_mma<22, T, false, 8>(a, st) : launch_nl_mma<22, T, false, 4>(a, st);
-      case 40: return r8 ? launch_nl_mma<40, T, false, 8>(a, st) : launch_nl_mma<40, T, false, 4>(a, st);
+      case 18: return r8 ? launch_lora_down<18, T, 8>(a, st) : launch_lora_down<18, T, 4>(a, st);
+      case 22: return r8 ? launch_lora_down<22, T, 8>(a, st) : launch_lora_down<22, T, 4>(a, st);
+      case 40: return r8 ? launch_lora_down<40, T, 8>(a, st) : launch_lora_down<40, T, 4>(a, st);
       default: break;
     }
   }
