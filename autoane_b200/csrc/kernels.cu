@@ -487,6 +487,161 @@ __global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
   }
 }
 
+// RMSNorm (perturbed weight) + LoRA-down with prepared operands, persistent like
+// lora_down_kernel: the fp32 rows of the next 16-row tile are copied by cp.async
+// while the current tile is normalised (xn to HBM and to a 16-bit smem tile, the
+// same arithmetic as norm_lora_mma_kernel) and multiplied (split-K mma.sync).
+template <int NP, int NA>
+struct NdSmem {
+  static constexpr int RT = 16, dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, MT = 1;
+  static constexpr int kXf = RT * dim * 4;          // one fp32 input tile
+  static constexpr int kX = RT * XS * 2;            // normalised 16-bit tile
+  static constexpr int kA = NT * 8 * XS * 2;
+  static constexpr int kW = dim * 4;
+  static constexpr int kRed = 8 * RT * NT * 8 * 4;
+  static constexpr int kTotal = 2 * kXf + kX + kA + kW + kRed;
+};
+
+template <int NP, typename T, int NA>
+__global__ void __launch_bounds__(256, 1) norm_down_kernel(NormLoraArgs a) {
+  using S = NdSmem<NP, NA>;
+  constexpr int RT = S::RT, dim = S::dim, XS = S::XS, NT = S::NT, KS = dim / 16;
+  using HV = typename H2<T>::V;
+  extern __shared__ __align__(16) uint8_t smx[];
+  float* s_xf = reinterpret_cast<float*>(smx);                                  // [2][RT][dim]
+  T* s_x = reinterpret_cast<T*>(smx + 2 * S::kXf);                              // [RT][XS]
+  T* s_a = reinterpret_cast<T*>(smx + 2 * S::kXf + S::kX);                      // [NT*8][XS]
+  float* s_w = reinterpret_cast<float*>(smx + 2 * S::kXf + S::kX + S::kA);      // [dim]
+  float* s_red = reinterpret_cast<float*>(smx + 2 * S::kXf + S::kX + S::kA + S::kW);  // [8][RT][NT*8]
+  const int ntiles = (a.rows + RT - 1) / RT;
+  const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+  if (t_begin >= t_end) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sxf0 = smem_u32(s_xf), sx0 = smem_u32(s_x), sab = smem_u32(s_a), swb = smem_u32(s_w);
+
+  auto load_x = [&](int tile, int buf) {
+    const int row0 = tile * RT;
+    for (int i = threadIdx.x; i < RT * (dim / 4); i += 256) {
+      const int r = i / (dim / 4), c4 = i - r * (dim / 4);
+      const int row = row0 + r;
+      float* d = s_xf + (buf * RT + r) * dim + c4 * 4;
+      if (row < a.rows)
+        cp_async16(sxf0 + (uint32_t)(((buf * RT + r) * dim + c4 * 4) * 4),
+                   static_cast<const float*>(a.in) + (long long)row * dim + c4 * 4);
+      else
+        *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  load_x(t_begin, 0);
+  cp_async_commit();
+  int cur_var = -1;
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    const int buf = (tile - t_begin) & 1;
+    const int var = a.pc.group_variant[(tile * RT) / a.pc.group_rows];
+    if (var != cur_var) {
+      __syncthreads();  // every warp is done with the previous operands
+      const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
+      for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 256) {
+        const int r = i / (dim / 8), c8 = i - r * (dim / 8);
+        if (r < NA)
+          cp_async16(sab + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
+        else
+          *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      const float* wp = a.w_prep + (long long)var * a.w_prep_vstride;
+      for (int i = threadIdx.x; i < dim / 4; i += 256) cp_async16(swb + 16u * i, wp + 4 * i);
+      cp_async_commit();
+      cur_var = var;
+    }
+    if (tile + 1 < t_end) load_x(tile + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    // ---- RMSNorm of the tile's rows (two per warp): xn to HBM and to the 16-bit tile ----
+    for (int r = warp; r < RT; r += 8) {
+      const int row = tile * RT + r;
+      const float2* src = reinterpret_cast<const float2*>(s_xf + (buf * RT + r) * dim);
+      float2 v[NP];
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = src[lane + 32 * k];
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
+      ss = warp_sum(ss);
+      const float m = __fmul_rn(ss, 1.0f / (float)dim);
+      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
+      HV* sx = reinterpret_cast<HV*>(s_x + r * XS);
+      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        const int c = 2 * (lane + 32 * k);
+        const HV h = H2<T>::from_f2(__fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]),
+                                    __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]));
+        if (row < a.rows) dst[lane + 32 * k] = h;
+        sx[lane + 32 * k] = h;
+      }
+    }
+    __syncthreads();
+    // ---- split-K mma over the normalised tile ----
+    float c[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
+    const int lm = lane >> 3, lr = lane & 7;
+    for (int kk = warp * KS / 8; kk < (warp + 1) * KS / 8; ++kk) {
+      uint32_t af[4];
+      ldsm_x4(sx0 + (uint32_t)((((lm & 1) * 8 + lr) * XS + kk * 16 + (lm >> 1) * 8) * 2), af[0], af[1], af[2], af[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(sab + (uint32_t)(((nt * 8 + lr) * XS + kk * 16 + (lm & 1) * 8) * 2), b0, b1, b2, b3);
+        mma16816<T>(c[nt], af, b0, b1);
+      }
+    }
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rr = g + ((e >> 1) << 3), n = nt * 8 + 2 * t4 + (e & 1);
+        s_red[(warp * RT + rr) * (NT * 8) + n] = c[nt][e];
+      }
+    __syncthreads();
+    for (int i = threadIdx.x; i < RT * NA; i += 256) {
+      const int rr = i / NA, n = i - rr * NA;
+      const int row = tile * RT + rr;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) v += s_red[(w * RT + rr) * (NT * 8) + n];
+      if (row < a.rows) {
+        const int m = n / a.rank, j = n - m * a.rank;
+        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(v);
+      }
+    }
+  }
+}
+
+template <int NP, typename T, int NA>
+static int launch_norm_down(const NormLoraArgs& a, cudaStream_t st) {
+  using S = NdSmem<NP, NA>;
+  static_assert(S::kTotal <= 227 * 1024, "norm/LoRA-down tiles exceed shared memory");
+  B2P_REQUIRE(a.pc.group_rows % S::RT == 0, "variant groups must be multiples of %d rows", S::RT);
+  DeviceCtx* c = nullptr;
+  int rc = ctx_get(&c);
+  if (rc) return rc;
+  auto k = norm_down_kernel<NP, T, NA>;
+  static thread_local uint64_t attr_mask = 0;  // one per instantiation
+  if (!(attr_mask & (1ull << (c->device & 63)))) {
+    B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+    attr_mask |= 1ull << (c->device & 63);
+  }
+  const int ntiles = (a.rows + S::RT - 1) / S::RT;
+  const int grid = ntiles < c->num_sms ? ntiles : c->num_sms;
+  k<<<grid, 256, S::kTotal, st>>>(a);
+  B2P_POST_LAUNCH();
+  return B2P_OK;
+}
+
 template <int NP, typename T, int NA>
 static int launch_lora_down(const NormLoraArgs& a, cudaStream_t st) {
   constexpr int RT = NP * 64 <= 1024 ? 32 : 16;
@@ -536,6 +691,17 @@ static int launch_nl_na(const NormLoraArgs& a, size_t smem, int blocks, cudaStre
       case 4: return launch_lora_down<NP, T, 4>(a, st);
       case 8: return launch_lora_down<NP, T, 8>(a, st);
       default: break;
+    }
+  }
+  if constexpr (NORM && NP <= 15) {  // two fp32 row tiles in flight fit up to dim 960
+    if (a.a_prep && a.w_prep) {
+      switch (a.n_a * a.rank) {
+        case 8: return launch_norm_down<NP, T, 8>(a, st);
+        case 12: return launch_norm_down<NP, T, 12>(a, st);
+        case 16: return launch_norm_down<NP, T, 16>(a, st);
+        case 24: return launch_norm_down<NP, T, 24>(a, st);
+        default: break;
+      }
     }
   }
   switch (a.n_a * a.rank) {
