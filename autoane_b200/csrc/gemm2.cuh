@@ -9,7 +9,7 @@
 // the peer) and each CTA runs the same epilogues as the single-CTA engine on its
 // own 128 rows.
 //
-// Synchronisation (no multicast anywhere):
+// Synchronisation (every TMA load lands in its own CTA; commits name each CTA):
 //   full[s]   leader only. The leader's producer arrives with the bytes of both
 //             CTAs; both producers' TMA loads complete on it.
 //   empty[s]  both CTAs; the leader's MMA thread commits to each in turn.
