@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       uint64_t t_idle = 0;
       for (uint32_t it = 0;; ++it) {
         bool did = false;
-        if (t_p < t_s && mbar_try_wait(&p_full[t_p & 1], (uint32_t)(t_p >> 1) & 1u)) {
+        if (t_p < t_s && mbar_test_wait(&p_full[t_p & 1], (uint32_t)(t_p >> 1) & 1u)) {
           const int b = t_p & 1;
           const uint32_t info = b ? pv_info1 : pv_info0;
           const int kvs = (int)(info & 1u), nkeys = (int)(info >> 8);
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         if (!done_s && t_s < t_p + 2) {
           if (need_unit) {
             const int slot = k % kAtRing;
-            if (mbar_try_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u)) {
+            if (mbar_test_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u)) {
               const int u = ring[slot];
               mbar_arrive(&u_empty[slot]);
               if (u >= total_units) {
@@ -333,14 +333,14 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               did = true;
             }
           } else if (need_kv) {
-            if (mbar_try_wait(&kv_full[k & 1], (uint32_t)(k >> 1) & 1u)) {
+            if (mbar_test_wait(&kv_full[k & 1], (uint32_t)(k >> 1) & 1u)) {
               need_kv = false;
               did = true;
             }
           } else {
             const int b = t_s & 1;
             const uint32_t n = (uint32_t)(t_s >> 1) & 1u;
-            if (mbar_try_wait(&q_full[b], n) && mbar_try_wait(&t_empty[b], n ^ 1u)) {
+            if (mbar_test_wait(&q_full[b], n) && mbar_test_wait(&t_empty[b], n ^ 1u)) {
               tc_fence_after();
               const int kvs = k & 1;
               const uint32_t q_base = smem_u32(sQ + b * AtSmem::kQ);

@@ -58,6 +58,52 @@ struct PairSmem {
   static_assert(kBStage % 1024 == 0 && kLoraOff % 1024 == 0 && kOutOff % 1024 == 0, "swizzle alignment");
 };
 
+// Output tiles of a pair launch: num_m row tiles of 256 rows times nfull column tiles of BN columns, then
+// (when N is not a multiple of BN and the epilogue allows it) one column tile per row tile of nw_last
+// columns, issued as narrower MMAs instead of BN-wide ones over zero-filled W rows. Tile i < num_m * nfull
+// is (row i / nfull, column i % nfull); the narrow tiles follow in row order. In round r cluster c takes
+// tile r * ncl + (r odd ? ncl - 1 - c : c), so the cheap narrow tiles at the end of the order go first to
+// the clusters that received one full tile fewer.
+struct PairTiles {
+  int num_m, nfull, nw_last, total;
+};
+
+template <int BN>
+__device__ __forceinline__ PairTiles pair_tiles(int M, int N, bool narrow) {
+  PairTiles t;
+  t.num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  if (narrow) {
+    t.nfull = N / BN;
+    const int rem = N - t.nfull * BN;
+    t.nw_last = (rem + 31) & ~31;  // a multiple of 32 columns: 16 W rows per CTA at least
+  } else {
+    t.nfull = (N + BN - 1) / BN;
+    t.nw_last = 0;
+  }
+  t.total = t.num_m * (t.nfull + (t.nw_last > 0 ? 1 : 0));
+  return t;
+}
+
+__device__ __forceinline__ int pair_tile_at(int r, int cid, int ncl) {
+  return r * ncl + ((r & 1) ? ncl - 1 - cid : cid);
+}
+
+// tile i -> row tile mt, column tile nt, first column n0, width nw
+template <int BN>
+__device__ __forceinline__ void pair_tile(const PairTiles& t, int i, int& mt, int& nt, int& n0, int& nw) {
+  const int nf = t.num_m * t.nfull;
+  if (i < nf) {
+    mt = i / t.nfull;
+    nt = i - mt * t.nfull;
+    nw = BN;
+  } else {
+    mt = i - nf;
+    nt = t.nfull;
+    nw = t.nw_last;
+  }
+  n0 = nt * BN;
+}
+
 template <int BN, int KIND, typename OutT, bool BF16, int NSEG>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
@@ -123,9 +169,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
-  const int num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  // SwiGLU tiles interleave gate and up halves and the cross-entropy partials are indexed per BN tile:
+  // those two keep BN-wide tiles throughout
+  const PairTiles tl = pair_tiles<BN>(M, N, KIND != EPI_SWIGLU && KIND != EPI_CE);
   const int kblocks = (K + kBK - 1) / kBK;
   const int cid = (int)cluster_id_x(), ncl = (int)nclusters_x();
 
@@ -136,8 +182,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
-        const int mt = tile / num_n, nt = tile % num_n;
+      for (int r = 0; ok; ++r) {
+        const int tile = pair_tile_at(r, cid, ncl);
+        if (tile >= tl.total) break;
+        int mt, nt, n0, nw;
+        pair_tile<BN>(tl, tile, mt, nt, n0, nw);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, ep.status, DEV_TIMEOUT_PRODUCER)) {
             ok = false;
@@ -146,7 +195,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * S::kStageBytes);
           tma_load_2d_pair(sA + stage * S::kAStage, &tmX, fb, kb * kBK, mt * 2 * kBM + (int)rank * kBM);
-          tma_load_2d_pair(sB + stage * S::kBStage, &tmW, fb, kb * kBK, nt * BN + (int)rank * HB);
+          tma_load_2d_pair(sB + stage * S::kBStage, &tmW, fb, kb * kBK, n0 + (int)rank * (nw / 2));
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -170,7 +219,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   } else if (warp == 1) {
     // ---------------- UMMA issuer (leader only) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(BF16, 2 * kBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -179,7 +227,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t lphase = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
+      for (int r = 0; ok; ++r) {
+        const int tile = pair_tile_at(r, cid, ncl);
+        if (tile >= tl.total) break;
+        int mt, nt, n0, nw;
+        pair_tile<BN>(tl, tile, mt, nt, n0, nw);
+        const uint32_t idesc = umma_idesc_f16(BF16, 2 * kBM, nw);
         if (!mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, ep.status, DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
@@ -251,10 +304,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int lb = 0;
       uint32_t lphase = 0;
       const int rank_r = ep.lora.rank;
-      for (int tile = cid; tile < num_tiles; tile += ncl) {
-        const int mt = tile / num_n, nt = tile % num_n;
+      for (int r = 0;; ++r) {
+        const int tile = pair_tile_at(r, cid, ncl);
+        if (tile >= tl.total) break;
+        int mt, nt, n0, nw;
+        pair_tile<BN>(tl, tile, mt, nt, n0, nw);
+        const int hw = nw / 2;                               // W rows of this CTA in this tile
         const int m0 = mt * 2 * kBM + (int)rank * kBM;      // this CTA's first row
-        const int c0 = nt * BN + (int)rank * HB;             // this CTA's first W row / output column
+        const int c0 = n0 + (int)rank * hw;                  // this CTA's first W row / output column
         const VariantInfo vi = s_var[s_gvar[(mt * 2 * kBM) / ep.lora.group_rows]];
         const uint32_t* mask = ep.lora.masks + (long long)(vi.mode ? vi.mask_slot : 0) * ep.lora.mask_words;
         float4 th[RPL][2];
@@ -273,7 +330,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               if (col >= ep.lora.seg_start[s]) seg = s;
             rel = col - ep.lora.seg_start[seg];
           }
-          const bool ok = lane + 32 * i < HB && col < N;
+          const bool ok = lane + 32 * i < hw && col < N;
           sg[i] = ok ? seg : -1;
           const long long p0 = ep.lora.seg_boff[seg] + (long long)rel * rank_r;
           th[i][0] = ok ? __ldg(reinterpret_cast<const float4*>(ep.lora.theta + p0)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -339,9 +396,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = cid; tile < num_tiles; tile += ncl) {
-      const int mt = tile / num_n, nt = tile % num_n;
-      const int m0 = mt * 2 * kBM + (int)rank * kBM, n0 = nt * BN;
+    for (int r = 0;; ++r) {
+      const int tile = pair_tile_at(r, cid, ncl);
+      if (tile >= tl.total) break;
+      int mt, nt, n0, nw;
+      pair_tile<BN>(tl, tile, mt, nt, n0, nw);
+      const int m0 = mt * 2 * kBM + (int)rank * kBM;
+      const int nch = (KIND == EPI_SWIGLU) ? NCHUNK : nw / 32;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < M;
 
@@ -365,7 +426,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
 
 #pragma unroll 1
-      for (int ch = half; ch < NCHUNK; ch += 2) {
+      for (int ch = half; ch < nch; ch += 2) {
         float v[32];
         int col;
         __syncwarp();

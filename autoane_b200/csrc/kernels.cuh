@@ -89,6 +89,27 @@ int launch_attention(const AttnArgs& a, bool bf16, cudaStream_t st);
 bool attention_tc_supported(const AttnArgs& a);
 int launch_attention_tc(const AttnArgs& a, bool bf16, cudaStream_t st);
 
+// Causal GQA attention backward operands (cpu_sdpa_backward, training/cpu_ops.h:213-290).
+struct AttnBwdArgs {
+  const void* qkv;  // [rows][ld] post-RoPE Q|K|V
+  int ld, q_off, k_off, v_off;
+  const void* o;    // [rows][ld_o] attention output
+  const void* dout; // [rows][ld_o] dO
+  int ld_o;
+  const float* lse; // [rows][heads] forward row normaliser, log2 domain
+  float* dvec;      // [rows][heads] D = sum_d dO O
+  void* dqkv;       // [rows][ld_d] dQ | dK | dV, same column offsets as qkv
+  int ld_d;
+  const float* rope_cos;
+  const float* rope_sin;  // [seq][32]
+  int seq, heads, kv_heads, ngroups;
+  float scale_log2, scale;
+  int* sched = nullptr;   // 2 zeroed ints: enables the tcgen05 kernels (seq 128 / 256)
+};
+// dK|dV and dQ on the tcgen05 tensor cores (attn_bwd_tc.cu), D already in dvec.
+bool attention_backward_tc_supported(const AttnBwdArgs& a);
+int launch_attention_backward_tc(const AttnBwdArgs& a, bool bf16, cudaStream_t st);
+
 // Row losses from the lm-head partials: loss_row = -(logit_tgt - M) + log(Σ s_i e^{m_i - M})
 // (training/cpu_ops.h:108-133); group_loss[g] = mean over the group's rows.
 int launch_ce_reduce(const float2* part, int ntiles, const float* tgt_logit, int rows, int seq, float* row_loss,

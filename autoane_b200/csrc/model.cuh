@@ -100,6 +100,7 @@ struct b2p_model {
   int prof_epoch = 0;       // bumped by every b2p_model_profile call
   bool graphs = true;       // B2P_OPT_GRAPHS
   bool tc_attn = true;      // B2P_OPT_TC_ATTENTION
+  bool tc_attn_bwd = true;  // B2P_OPT_TC_ATTENTION_BWD
   int* attn_sched = nullptr;  // [2] unit counter of the tcgen05 attention kernel (self-resetting)
 };
 

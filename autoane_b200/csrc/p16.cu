@@ -88,7 +88,7 @@ struct P16State {
   struct Graph {
     const void* tok = nullptr;
     int n_seq = 0, gen = -1, scale_log2 = 0, prof_epoch = -1;
-    bool pair = true, tc_attn = true;
+    bool pair = true, tc_attn = true, tc_attn_bwd = true;
     cudaGraphExec_t exec = nullptr;
     long long launches = 0;
   } graph;
@@ -621,21 +621,6 @@ constexpr int kAT = 64;   // tile rows (queries or keys)
 constexpr int kAHD = 64;  // head_dim
 constexpr int kDkdvSmem = 6 * kAT * kAHD * 2 + 4 * kAT * 4;
 
-struct AttnBwdArgs {
-  const void* qkv;  // [rows][ld] post-RoPE Q|K|V
-  int ld, q_off, k_off, v_off;
-  const void* o;    // [rows][ld_o] attention output
-  const void* dout; // [rows][ld_o] dO
-  int ld_o;
-  const float* lse; // [rows][heads]
-  float* dvec;      // [rows][heads]
-  void* dqkv;       // [rows][ld_d] dQ | dK | dV, same column offsets as qkv
-  int ld_d;
-  const float* rope_cos;
-  const float* rope_sin;  // [seq][32]
-  int seq, heads, kv_heads, ngroups;
-  float scale_log2, scale;
-};
 
 template <typename T>
 __device__ __forceinline__ void ab_load_tile(uint32_t s_base, const T* g, long long ld) {
@@ -947,7 +932,7 @@ __global__ void __launch_bounds__(128) attn_bwd_dkdv_kernel(AttnBwdArgs a) {
   }
 }
 
-int attention_backward(const AttnBwdArgs& a0, bool bf16, cudaStream_t st) {
+int attention_backward(const AttnBwdArgs& a0, bool bf16, bool use_tc, cudaStream_t st) {
   AttnBwdArgs a = a0;
   B2P_REQUIRE(a.seq % kAT == 0, "attention backward needs seq %% 64 == 0 (got %d)", a.seq);
   B2P_REQUIRE(a.kv_heads > 0 && a.heads % a.kv_heads == 0, "heads must be a multiple of kv_heads");
@@ -959,6 +944,14 @@ int attention_backward(const AttnBwdArgs& a0, bool bf16, cudaStream_t st) {
   const long long n = (long long)a.ngroups * a.seq * a.heads;
   const int pb = (int)((n + 255) / 256);
   dim3 gq(a.seq / kAT, a.heads, a.ngroups), gk(a.seq / kAT, a.kv_heads, a.ngroups);
+  if (use_tc && attention_backward_tc_supported(a)) {  // D first, then dK|dV and dQ on tcgen05
+    if (bf16)
+      attn_bwd_prep_kernel<__nv_bfloat16><<<pb, 256, 0, st>>>(a);
+    else
+      attn_bwd_prep_kernel<__half><<<pb, 256, 0, st>>>(a);
+    B2P_POST_LAUNCH();
+    return launch_attention_backward_tc(a, bf16, st);
+  }
   if (bf16) {
     B2P_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_kernel<__nv_bfloat16>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kDkdvSmem));
@@ -1288,6 +1281,7 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
   P16State::Graph& gr = s->graph;
   const bool hit = gr.exec && gr.tok == d_tok && gr.n_seq == n_seq && gr.gen == s->gen &&
                    gr.scale_log2 == m->grad_scale_log2 && gr.pair == m->use_pair && gr.tc_attn == m->tc_attn &&
+                   gr.tc_attn_bwd == m->tc_attn_bwd &&
                    gr.prof_epoch == m->prof_epoch;
   if (!hit) {
     if (gr.exec) cudaGraphExecDestroy(gr.exec);
@@ -1318,6 +1312,7 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
     gr.scale_log2 = m->grad_scale_log2;
     gr.pair = m->use_pair;
     gr.tc_attn = m->tc_attn;
+    gr.tc_attn_bwd = m->tc_attn_bwd;
     gr.prof_epoch = m->prof_epoch;
     gr.launches = captured;
   }
@@ -1500,7 +1495,8 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
     ab.heads = c.heads;
     ab.kv_heads = c.kv_heads;
     ab.ngroups = n_seq;
-    if ((rc = attention_backward(ab, bf, m->st))) return rc;
+    ab.sched = m->tc_attn_bwd ? m->attn_sched : nullptr;
+    if ((rc = attention_backward(ab, bf, m->tc_attn_bwd, m->st))) return rc;
     // dWq|dWk|dWv = dQKV^T · xnorm  (train.m:1143-1151)
     if (s->full && (rc = wgrad_gemm(s->dqkv, QKV + kUCols, QKV, slab(v.xn, l, D), D, D,
                                     s->gw + s->o_qkv + (size_t)l * QKV * D)))

@@ -215,6 +215,10 @@ long long b2p_launch_count(void);
  * (sequences of 128 or 256 tokens); 0 uses the mma.sync kernel (64 x 64 tiles).
  * Same results up to fp32 summation order. */
 #define B2P_OPT_TC_ATTENTION 4
+/* B2P_OPT_TC_ATTENTION_BWD (default 1): the backprop-LoRA attention backward on
+ * the tcgen05 kernels (dK|dV then dQ, sequences of 128 or 256 tokens, 64-wide
+ * heads); 0 uses the mma.sync kernels. Same results up to fp32 summation order. */
+#define B2P_OPT_TC_ATTENTION_BWD 5
 int b2p_model_set_option(b2p_model* m, int option, int value);
 
 /* ======================================================================
