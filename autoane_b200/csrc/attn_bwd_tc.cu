@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_enter();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     // ---------------- TMA producer (lane 0) + (lse, D) copies (all lanes) ----------------
@@ -481,10 +482,10 @@ __global__ void __launch_bounds__(kBwThreads, 1)
             ok = false;
             break;
           }
-          const uint64_t now = global_timer_ns();
+          const uint64_t now = sm_cycles();
           if (t_idle == 0) {
             t_idle = now;
-          } else if (now - t_idle > kWaitBudgetNs) {
+          } else if (now - t_idle > kWaitBudgetCycles) {
             *abort_flag = 1;
             atomicCAS(status, 0u, (uint32_t)DEV_TIMEOUT_MMA);
             ok = false;
@@ -673,7 +674,8 @@ int launch_bw(const AttnBwdArgs& a, cudaStream_t st) {
         cudaFuncSetAttribute(attn_bwd_tc_kernel<T, DKDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwSmem::kTotal));
     attr_mask |= 1ull << (c->device & 63);
   }
-  attn_bwd_tc_kernel<T, DKDV><<<grid, kBwThreads, BwSmem::kTotal, st>>>(tq, td, tdq, a, total, c->status);
+  B2P_CHECK_CUDA(launch_pdl(attn_bwd_tc_kernel<T, DKDV>, dim3(grid), dim3(kBwThreads), BwSmem::kTotal, st, tq, td,
+                            tdq, a, total, c->status));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }

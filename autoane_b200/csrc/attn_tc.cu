@@ -233,6 +233,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_enter();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     // ---------------- TMA producer: unit ids, K/V per unit, Q per head ----------------
@@ -372,10 +373,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             ok = false;
             break;
           }
-          const uint64_t now = global_timer_ns();
+          const uint64_t now = sm_cycles();
           if (t_idle == 0) {
             t_idle = now;
-          } else if (now - t_idle > kWaitBudgetNs) {
+          } else if (now - t_idle > kWaitBudgetCycles) {
             *abort_flag = 1;
             atomicCAS(status, 0u, (uint32_t)DEV_TIMEOUT_MMA);
             ok = false;
@@ -558,7 +559,8 @@ int launch_tc_t(const AttnArgs& a, cudaStream_t st) {
     B2P_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtSmem::kTotal));
     attr_mask |= 1ull << (c->device & 63);
   }
-  attn_tc_kernel<T><<<grid, kAtThreads, AtSmem::kTotal, st>>>(tm, a, scale_log2, total, c->status);
+  B2P_CHECK_CUDA(launch_pdl(attn_tc_kernel<T>, dim3(grid), dim3(kAtThreads), AtSmem::kTotal, st, tm, a, scale_log2,
+                            total, c->status));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }

@@ -47,6 +47,26 @@ long long launch_count();
     B2P_CHECK_CUDA(cudaGetLastError());           \
   } while (0)
 
+// Launch with programmatic stream serialization: the kernel may start (prologue: barrier
+// init, TMEM allocation, descriptor prefetch) while the previous kernel in the stream is
+// still finishing. Every kernel launched this way calls pdl_enter() before touching global
+// memory: that waits until the preceding grid has completed and its writes are visible.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 struct DeviceCtx {
   int device = -1;
   int num_sms = 0;

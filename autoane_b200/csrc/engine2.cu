@@ -48,13 +48,15 @@ int launch_pair_t(const void* X, int ldx, const void* W, int ldw, int M, int N, 
   cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = S::kTotal;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel calls pdl_enter()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   B2P_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tw, to, tu, M, N, K, e));
   B2P_POST_LAUNCH();
   return B2P_OK;

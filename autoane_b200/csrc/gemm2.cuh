@@ -41,7 +41,10 @@ struct PairSmem {
   static constexpr int kLoraU = kBM * kMaxRank * 2;           // 4 KB per segment
   static constexpr int kLoraB = (BN / 2) * kMaxRank * 2;      // BN/2 x 32 B per segment
   static constexpr int kLoraBuf = NSEG * (kLoraU + kLoraB);
-  static constexpr int kLoraBytes = 2 * kLoraBuf;
+  // Two or more segments: one operand buffer, so the shared memory goes to a deeper K pipeline
+  // (the LoRA warp fills it for the next tile during that tile's whole main loop).
+  static constexpr int kLoraBufs = NSEG >= 2 ? 1 : 2;
+  static constexpr int kLoraBytes = kLoraBufs * kLoraBuf;
   static constexpr int kVarBytes = NSEG ? kMaxGroups * 20 : 0;
   static constexpr int kBudget = 224 * 1024;
   static constexpr int kFree = kBudget - kOutBytes - kLoraBytes - kVarBytes - 1024 - 256;
@@ -168,6 +171,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_enter();  // the previous kernel's outputs are complete from here on
 
   // SwiGLU tiles interleave gate and up halves and the cross-entropy partials are indexed per BN tile:
   // those two keep BN-wide tiles throughout
@@ -274,7 +278,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint32_t le = smem_u32(&lempty_bar[lb]);
           umma_commit_pair(le);
           umma_commit_pair(mapa_shared(le, peer));
-          if (++lb == 2) {
+          if (++lb == S::kLoraBufs) {
             lb = 0;
             lphase ^= 1u;
           }
@@ -378,7 +382,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           for (int s = 0; s < NSEG; ++s) tma_load_2d_pair(buf + s * S::kLoraU, &tmU, lf, ep.lora.seg_ucol[s], m0);
           if (!leader) mbar_arrive_cluster(lf);
         }
-        if (++lb == 2) {
+        if (++lb == S::kLoraBufs) {
           lb = 0;
           lphase ^= 1u;
         }

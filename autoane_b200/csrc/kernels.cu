@@ -78,6 +78,7 @@ struct PadPow2 {
 template <int NP, typename T, bool NORM, int NA>
 __global__ void __launch_bounds__(kNormThreads) norm_lora_kernel(NormLoraArgs a) {
   extern __shared__ float sm[];
+  pdl_enter();
   float* s_w = sm;                  // [dim]   perturbed rms weight
   float* s_a = sm + a.dim;          // [NA][dim] perturbed LoRA A rows
   using HV = typename H2<T>::V;
@@ -373,27 +374,28 @@ __global__ void __launch_bounds__(256, 2) norm_lora_mma_kernel(NormLoraArgs a) {
 
 // LoRA-down of a 16-bit input (no norm) with prepared per-variant A rows, as a
 // persistent kernel: every CTA takes a contiguous range of RT-row tiles, keeps the
-// next tile's cp.async copy in flight while the current one is multiplied, and
-// splits each tile's K (= dim) over its 8 warps (mma.sync m16n8k16, fp32), summing
-// the warps' partials in a fixed order. A rows are restaged only when the tile's
-// variant changes (a contiguous range crosses few variant groups).
-template <int NP, int RT, int NA>
+// copies of the next STAGES - 1 tiles in flight (cp.async ring) while the current one
+// is multiplied, and splits each tile's K (= dim) over its 8 warps (mma.sync
+// m16n8k16, fp32), summing the warps' partials in a fixed order. A rows are restaged
+// only when the tile's variant changes (a contiguous range crosses few variant groups).
+template <int NP, int RT, int NA, int STAGES>
 struct LdSmem {
   static constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, MT = RT / 16;
   static constexpr int kX = RT * XS * 2;            // one x tile (16-bit)
   static constexpr int kA = NT * 8 * XS * 2;        // A rows (16-bit, zero padded to whole n-tiles)
   static constexpr int kRed = 8 * RT * NT * 8 * 4;  // per-warp partial U
-  static constexpr int kTotal = 2 * kX + kA + kRed;
+  static constexpr int kTotal = STAGES * kX + kA + kRed;
 };
 
-template <int NP, typename T, int NA, int RT>
+template <int NP, typename T, int NA, int RT, int STAGES>
 __global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
-  using S = LdSmem<NP, RT, NA>;
+  using S = LdSmem<NP, RT, NA, STAGES>;
   constexpr int dim = S::dim, XS = S::XS, NT = S::NT, MT = S::MT, KS = dim / 16;
   extern __shared__ __align__(16) uint8_t smx[];
-  T* s_x = reinterpret_cast<T*>(smx);                         // [2][RT][XS]
-  T* s_a = reinterpret_cast<T*>(smx + 2 * S::kX);             // [NT*8][XS]
-  float* s_red = reinterpret_cast<float*>(smx + 2 * S::kX + S::kA);  // [8][RT][NT*8]
+  T* s_x = reinterpret_cast<T*>(smx);                              // [STAGES][RT][XS]
+  T* s_a = reinterpret_cast<T*>(smx + STAGES * S::kX);             // [NT*8][XS]
+  float* s_red = reinterpret_cast<float*>(smx + STAGES * S::kX + S::kA);  // [8][RT][NT*8]
+  pdl_enter();
   const int ntiles = (a.rows + RT - 1) / RT;
   const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
   const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
@@ -413,12 +415,18 @@ __global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
         *reinterpret_cast<uint4*>(s_x + (buf * RT + r) * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
     }
   };
-  load_x(t_begin, 0);
-  cp_async_commit();
+  // prologue: tiles t_begin .. t_begin + STAGES - 2 in flight (one commit group each)
+#pragma unroll
+  for (int i = 0; i < STAGES - 1; ++i) {
+    if (t_begin + i < t_end) load_x(t_begin + i, i);
+    cp_async_commit();
+  }
   int cur_var = -1;
+  int next_var = a.pc.group_variant[(t_begin * RT) / a.pc.group_rows];  // loaded one tile ahead
   for (int tile = t_begin; tile < t_end; ++tile) {
-    const int buf = (tile - t_begin) & 1;
-    const int var = a.pc.group_variant[(tile * RT) / a.pc.group_rows];
+    const int buf = (tile - t_begin) % STAGES;
+    const int var = next_var;
+    if (tile + 1 < t_end) next_var = a.pc.group_variant[((tile + 1) * RT) / a.pc.group_rows];
     if (var != cur_var) {
       __syncthreads();  // every warp is done with the previous A rows
       const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
@@ -430,11 +438,14 @@ __global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
           *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
       }
       cp_async_commit();
+      cp_async_wait<0>();  // (rare) A rows and every tile in flight have landed
       cur_var = var;
     }
-    if (tile + 1 < t_end) load_x(tile + 1, buf ^ 1);
+    // the buffer of tile + STAGES - 1 was last read by the previous iteration's mma (all
+    // warps passed the barrier before that iteration's reduction since)
+    if (tile + STAGES - 1 < t_end) load_x(tile + STAGES - 1, (tile - t_begin + STAGES - 1) % STAGES);
     cp_async_commit();
-    cp_async_wait<1>();  // this tile's rows and the A rows have landed
+    cp_async_wait<STAGES - 1>();  // this tile's rows have landed
     __syncthreads();
 
     // ---- split-K mma: warp w takes k-steps [w KS/8, (w+1) KS/8) of every (m16, n8) task ----
@@ -487,62 +498,64 @@ __global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
   }
 }
 
-// RMSNorm (perturbed weight) + LoRA-down with prepared operands, persistent like
-// lora_down_kernel: the fp32 rows of the next 16-row tile are copied by cp.async
-// while the current tile is normalised (xn to HBM and to a 16-bit smem tile, the
-// same arithmetic as norm_lora_mma_kernel) and multiplied (split-K mma.sync).
+// RMSNorm (perturbed weight) + LoRA-down with prepared operands, as a persistent
+// kernel of 16 warps over a contiguous range of 16-row tiles: warp w owns row w of
+// every tile and keeps the fp32 rows of the next two tiles in flight in registers
+// (a three-deep ring) while it normalises the current one (xn to HBM and to a 16-bit
+// smem tile, the same arithmetic and per-lane order as norm_lora_mma_kernel). The
+// tile's LoRA-down then runs as split-K mma.sync over the 16 warps, partials summed
+// in warp order. A rows and the rms weight are restaged when the variant changes.
 template <int NP, int NA>
 struct NdSmem {
-  static constexpr int RT = 16, dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, MT = 1;
-  static constexpr int kXf = RT * dim * 4;          // one fp32 input tile
+  static constexpr int RT = 16, WARPS = 16, dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8;
   static constexpr int kX = RT * XS * 2;            // normalised 16-bit tile
-  static constexpr int kA = NT * 8 * XS * 2;
+  static constexpr int kA = NT * 8 * XS * 2;        // A rows (16-bit, zero padded to whole n-tiles)
   static constexpr int kW = dim * 4;
-  static constexpr int kRed = 8 * RT * NT * 8 * 4;
-  static constexpr int kTotal = 2 * kXf + kX + kA + kW + kRed;
+  static constexpr int kRed = WARPS * RT * NT * 8 * 4;
+  static constexpr int kTotal = kX + kA + kW + kRed;
 };
 
 template <int NP, typename T, int NA>
-__global__ void __launch_bounds__(256, 1) norm_down_kernel(NormLoraArgs a) {
+__global__ void __launch_bounds__(512, 1) norm_down_kernel(NormLoraArgs a) {
   using S = NdSmem<NP, NA>;
-  constexpr int RT = S::RT, dim = S::dim, XS = S::XS, NT = S::NT, KS = dim / 16;
+  constexpr int RT = S::RT, W = S::WARPS, dim = S::dim, XS = S::XS, NT = S::NT, KS = dim / 16;
   using HV = typename H2<T>::V;
   extern __shared__ __align__(16) uint8_t smx[];
-  float* s_xf = reinterpret_cast<float*>(smx);                                  // [2][RT][dim]
-  T* s_x = reinterpret_cast<T*>(smx + 2 * S::kXf);                              // [RT][XS]
-  T* s_a = reinterpret_cast<T*>(smx + 2 * S::kXf + S::kX);                      // [NT*8][XS]
-  float* s_w = reinterpret_cast<float*>(smx + 2 * S::kXf + S::kX + S::kA);      // [dim]
-  float* s_red = reinterpret_cast<float*>(smx + 2 * S::kXf + S::kX + S::kA + S::kW);  // [8][RT][NT*8]
+  T* s_x = reinterpret_cast<T*>(smx);                                      // [RT][XS]
+  T* s_a = reinterpret_cast<T*>(smx + S::kX);                              // [NT*8][XS]
+  float* s_w = reinterpret_cast<float*>(smx + S::kX + S::kA);              // [dim]
+  float* s_red = reinterpret_cast<float*>(smx + S::kX + S::kA + S::kW);    // [W][RT][NT*8]
+  pdl_enter();
   const int ntiles = (a.rows + RT - 1) / RT;
   const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
   const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
   if (t_begin >= t_end) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t sxf0 = smem_u32(s_xf), sx0 = smem_u32(s_x), sab = smem_u32(s_a), swb = smem_u32(s_w);
+  const uint32_t sx0 = smem_u32(s_x), sab = smem_u32(s_a), swb = smem_u32(s_w);
+  const float2* in = static_cast<const float2*>(a.in);
 
-  auto load_x = [&](int tile, int buf) {
-    const int row0 = tile * RT;
-    for (int i = threadIdx.x; i < RT * (dim / 4); i += 256) {
-      const int r = i / (dim / 4), c4 = i - r * (dim / 4);
-      const int row = row0 + r;
-      float* d = s_xf + (buf * RT + r) * dim + c4 * 4;
-      if (row < a.rows)
-        cp_async16(sxf0 + (uint32_t)(((buf * RT + r) * dim + c4 * 4) * 4),
-                   static_cast<const float*>(a.in) + (long long)row * dim + c4 * 4);
-      else
-        *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto load_row = [&](int tile, float2 (&v)[NP]) {
+    const int row = tile * RT + warp;
+    if (tile < t_end && row < a.rows) {
+      const float2* src = in + (long long)row * (dim / 2);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = __ldg(src + lane + 32 * k);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NP; ++k) v[k] = make_float2(0.f, 0.f);
     }
   };
-  load_x(t_begin, 0);
-  cp_async_commit();
+
   int cur_var = -1;
-  for (int tile = t_begin; tile < t_end; ++tile) {
-    const int buf = (tile - t_begin) & 1;
-    const int var = a.pc.group_variant[(tile * RT) / a.pc.group_rows];
-    if (var != cur_var) {
-      __syncthreads();  // every warp is done with the previous operands
+  // variant of the next tile, loaded one tile ahead (its latency off the tile's path)
+  int next_var = a.pc.group_variant[(t_begin * RT) / a.pc.group_rows];
+  auto process = [&](int tile, const float2 (&v)[NP]) {
+    const int var = next_var;
+    if (tile + 1 < t_end) next_var = a.pc.group_variant[((tile + 1) * RT) / a.pc.group_rows];
+    if (var != cur_var) {  // uniform over the CTA: every warp walks the same tiles
+      __syncthreads();     // every warp is done with the previous operands
       const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
-      for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 256) {
+      for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 32 * W) {
         const int r = i / (dim / 8), c8 = i - r * (dim / 8);
         if (r < NA)
           cp_async16(sab + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
@@ -550,45 +563,38 @@ __global__ void __launch_bounds__(256, 1) norm_down_kernel(NormLoraArgs a) {
           *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
       }
       const float* wp = a.w_prep + (long long)var * a.w_prep_vstride;
-      for (int i = threadIdx.x; i < dim / 4; i += 256) cp_async16(swb + 16u * i, wp + 4 * i);
+      for (int i = threadIdx.x; i < dim / 4; i += 32 * W) cp_async16(swb + 16u * i, wp + 4 * i);
       cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
       cur_var = var;
     }
-    if (tile + 1 < t_end) load_x(tile + 1, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    // ---- RMSNorm of the tile's rows (two per warp): xn to HBM and to the 16-bit tile ----
-    for (int r = warp; r < RT; r += 8) {
-      const int row = tile * RT + r;
-      const float2* src = reinterpret_cast<const float2*>(s_xf + (buf * RT + r) * dim);
-      float2 v[NP];
+    // ---- RMSNorm of this warp's row: xn to HBM and to the 16-bit tile ----
+    const int row = tile * RT + warp;
+    float ss = 0.f;
 #pragma unroll
-      for (int k = 0; k < NP; ++k) v[k] = src[lane + 32 * k];
-      float ss = 0.f;
+    for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
+    ss = warp_sum(ss);
+    const float m = __fmul_rn(ss, 1.0f / (float)dim);
+    const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
+    HV* sx = reinterpret_cast<HV*>(s_x + warp * XS);
+    HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
 #pragma unroll
-      for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
-      ss = warp_sum(ss);
-      const float m = __fmul_rn(ss, 1.0f / (float)dim);
-      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
-      HV* sx = reinterpret_cast<HV*>(s_x + r * XS);
-      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
-#pragma unroll
-      for (int k = 0; k < NP; ++k) {
-        const int c = 2 * (lane + 32 * k);
-        const HV h = H2<T>::from_f2(__fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]),
-                                    __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]));
-        if (row < a.rows) dst[lane + 32 * k] = h;
-        sx[lane + 32 * k] = h;
-      }
+    for (int k = 0; k < NP; ++k) {
+      const int c = 2 * (lane + 32 * k);
+      const HV h = H2<T>::from_f2(__fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]),
+                                  __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]));
+      if (row < a.rows) dst[lane + 32 * k] = h;
+      sx[lane + 32 * k] = h;
     }
     __syncthreads();
-    // ---- split-K mma over the normalised tile ----
+    // ---- split-K mma over the normalised tile: warp w takes k-steps [w KS/W, (w+1) KS/W) ----
     float c[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
     const int lm = lane >> 3, lr = lane & 7;
-    for (int kk = warp * KS / 8; kk < (warp + 1) * KS / 8; ++kk) {
+#pragma unroll 1  // 3-4 steps per warp; the next tiles' rows hold 2 NP registers meanwhile
+    for (int kk = warp * KS / W; kk < (warp + 1) * KS / W; ++kk) {
       uint32_t af[4];
       ldsm_x4(sx0 + (uint32_t)((((lm & 1) * 8 + lr) * XS + kk * 16 + (lm >> 1) * 8) * 2), af[0], af[1], af[2], af[3]);
 #pragma unroll
@@ -606,18 +612,33 @@ __global__ void __launch_bounds__(256, 1) norm_down_kernel(NormLoraArgs a) {
         const int rr = g + ((e >> 1) << 3), n = nt * 8 + 2 * t4 + (e & 1);
         s_red[(warp * RT + rr) * (NT * 8) + n] = c[nt][e];
       }
-    __syncthreads();
-    for (int i = threadIdx.x; i < RT * NA; i += 256) {
+    __syncthreads();  // (also: every warp's reads of s_x are done before the next tile's rows land there)
+    for (int i = threadIdx.x; i < RT * NA; i += 32 * W) {
       const int rr = i / NA, n = i - rr * NA;
-      const int row = tile * RT + rr;
-      float v = 0.f;
+      const int orow = tile * RT + rr;
+      float sum = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) v += s_red[(w * RT + rr) * (NT * 8) + n];
-      if (row < a.rows) {
-        const int m = n / a.rank, j = n - m * a.rank;
-        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(v);
+      for (int w = 0; w < W; ++w) sum += s_red[(w * RT + rr) * (NT * 8) + n];
+      if (orow < a.rows) {
+        const int mi = n / a.rank, j = n - mi * a.rank;
+        static_cast<T*>(a.U)[(long long)orow * kUCols + a.u_col + 16 * mi + j] = static_cast<T>(sum);
       }
     }
+  };
+
+  // three-deep register ring: tiles t+1 and t+2 in flight while tile t is processed
+  float2 xa[NP], xb[NP], xc[NP];
+  load_row(t_begin, xa);
+  load_row(t_begin + 1, xb);
+  for (int tile = t_begin; tile < t_end; tile += 3) {
+    load_row(tile + 2, xc);
+    process(tile, xa);
+    if (tile + 1 >= t_end) break;
+    load_row(tile + 3, xa);
+    process(tile + 1, xb);
+    if (tile + 2 >= t_end) break;
+    load_row(tile + 4, xb);
+    process(tile + 2, xc);
   }
 }
 
@@ -637,21 +658,21 @@ static int launch_norm_down(const NormLoraArgs& a, cudaStream_t st) {
   }
   const int ntiles = (a.rows + S::RT - 1) / S::RT;
   const int grid = ntiles < c->num_sms ? ntiles : c->num_sms;
-  k<<<grid, 256, S::kTotal, st>>>(a);
+  B2P_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(32 * S::WARPS), S::kTotal, st, a));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
 template <int NP, typename T, int NA>
 static int launch_lora_down(const NormLoraArgs& a, cudaStream_t st) {
-  constexpr int RT = NP * 64 <= 1024 ? 32 : 16;
-  using S = LdSmem<NP, RT, NA>;
+  constexpr int RT = 16, STAGES = NP * 64 <= 1024 ? 4 : 2;
+  using S = LdSmem<NP, RT, NA, STAGES>;
   static_assert(S::kTotal <= 227 * 1024, "LoRA-down tiles exceed shared memory");
   B2P_REQUIRE(a.pc.group_rows % RT == 0, "variant groups must be multiples of %d rows", RT);
   DeviceCtx* c = nullptr;
   int rc = ctx_get(&c);
   if (rc) return rc;
-  auto k = lora_down_kernel<NP, T, NA, RT>;
+  auto k = lora_down_kernel<NP, T, NA, RT, STAGES>;
   static thread_local uint64_t attr_mask = 0;  // one per instantiation
   if (!(attr_mask & (1ull << (c->device & 63)))) {
     B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
@@ -659,7 +680,7 @@ static int launch_lora_down(const NormLoraArgs& a, cudaStream_t st) {
   }
   const int ntiles = (a.rows + RT - 1) / RT;
   const int grid = ntiles < c->num_sms ? ntiles : c->num_sms;
-  k<<<grid, 256, S::kTotal, st>>>(a);
+  B2P_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(256), S::kTotal, st, a));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -679,7 +700,7 @@ template <int NP, typename T, bool NORM, int NA>
 static int launch_nl(const NormLoraArgs& a, size_t smem, int blocks, cudaStream_t st) {
   auto k = norm_lora_kernel<NP, T, NORM, NA>;
   B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<blocks, kNormThreads, smem, st>>>(a);
+  B2P_CHECK_CUDA(launch_pdl(k, dim3(blocks), dim3(kNormThreads), smem, st, a));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -693,7 +714,7 @@ static int launch_nl_na(const NormLoraArgs& a, size_t smem, int blocks, cudaStre
       default: break;
     }
   }
-  if constexpr (NORM && NP <= 15) {  // two fp32 row tiles in flight fit up to dim 960
+  if constexpr (NORM && NP <= 15) {  // the three-row register ring fits up to dim 960
     if (a.a_prep && a.w_prep) {
       switch (a.n_a * a.rank) {
         case 8: return launch_norm_down<NP, T, 8>(a, st);

@@ -24,14 +24,28 @@ enum DevErr : uint32_t {
   DEV_NONFINITE_GRAD = 6,
 };
 
-// Time budget for one mbarrier wait, in nanoseconds of %globaltimer. Every
-// legitimate wait in these kernels is micro- to milliseconds long.
-constexpr uint64_t kWaitBudgetNs = 4000000000ull;
+// Budget for one bounded wait, in SM clock cycles (about 4 s at the B200's
+// 1.9-2 GHz, longer at lower clocks). Every legitimate wait in these kernels is
+// micro- to milliseconds long. The SM cycle counter is read instead of
+// %globaltimer because it costs a few cycles: a polling loop that reads the
+// global timer reacts that much later to the barrier it waits for.
+constexpr uint64_t kWaitBudgetCycles = 8000000000ull;
+
+__device__ __forceinline__ uint64_t sm_cycles() { return static_cast<uint64_t>(clock64()); }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Programmatic dependent launch, entry of a kernel launched by launch_pdl: allow the next
+// kernel in the stream to begin launching (its blocks take SMs as this grid's blocks exit),
+// then wait until the preceding grid has completed and its memory is visible. Called by
+// every thread before its first global-memory access.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -85,12 +99,12 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
                                           uint32_t* status, uint32_t code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = sm_cycles();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitBudgetNs) break;
+      if (sm_cycles() - t0 > kWaitBudgetCycles) break;
     }
   }
   *abort_flag = 1;
@@ -100,9 +114,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // Bounded drain wait used on the abort path (no status update).
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = sm_cycles();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > kWaitBudgetNs) return;
+    if (sm_cycles() - t0 > kWaitBudgetCycles) return;
   }
 }
 
@@ -219,12 +233,12 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
                                                   uint32_t* status, uint32_t code) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = sm_cycles();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitBudgetNs) break;
+      if (sm_cycles() - t0 > kWaitBudgetCycles) break;
     }
   }
   *abort_flag = 1;

@@ -898,36 +898,48 @@ def run_gemm_sweep(args):
     for name, (M, K) in GEMM_SHAPES.items():
         for T in (128, 256, 1024, 8192):
             # enough operand copies that one pass over them exceeds L2 (126 MB): every launch reads from HBM
-            per = 2 * (T * K + M * K) + 4 * T * ((M + 3) // 4 * 4)
+            per = 2 * (T * K + M * K) + 4 * T * ((M + 3) // 4 * 4) + 4 * T * ((M + 7) // 8 * 8)
             ncopy = max(2, min(64, -(-(256 << 20) // per)))
             xs = [torch.randn(T, K, device=dev).to(dt) for _ in range(ncopy)]
             ws = [(0.02 * torch.randn(M, K, device=dev)).to(dt) for _ in range(ncopy)]
             ys = [torch.empty(T, (M + 3) // 4 * 4, device=dev, dtype=torch.float32) for _ in range(ncopy)]
+            hs = [torch.empty(T, (M + 7) // 8 * 8, device=dev, dtype=dt) for _ in range(ncopy)]
+            cs = [torch.empty(T, M, device=dev, dtype=dt) for _ in range(ncopy)]
             fn = "b2p_gemm_pair" if T >= 256 else "b2p_gemm"
 
-            def run(i):
+            def ours(i, f32=True):
                 st = torch.cuda.current_stream().cuda_stream
-                _lib.call(fn, xs[i].data_ptr(), ws[i].data_ptr(), ys[i].data_ptr(), T, M, K, ys[i].shape[1], code, 1,
-                          st)
-            for i in range(ncopy):
-                run(i)
-            torch.cuda.synchronize()
-            # back-to-back launches over the rotating copies, recorded once into a CUDA graph so the
-            # host's per-call cost stays out of the timed region
-            reps = max(ncopy, 8 * max(5, args.steps))
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for i in range(reps):
-                    run(i % ncopy)
-            graph.replay()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / reps
-            del graph
+                y = ys[i] if f32 else hs[i]
+                _lib.call(fn, xs[i].data_ptr(), ws[i].data_ptr(), y.data_ptr(), T, M, K, y.shape[1], code,
+                          1 if f32 else 0, st)
+
+            def cublas(i):  # the library baseline: cuBLAS through torch, 16-bit output
+                torch.mm(xs[i], ws[i].t(), out=cs[i])
+
+            def graph_ms(run):
+                for i in range(ncopy):
+                    run(i)
+                torch.cuda.synchronize()
+                # back-to-back launches over the rotating copies, recorded once into a CUDA graph so
+                # the host's per-call cost stays out of the timed region
+                reps = max(ncopy, 8 * max(5, args.steps))
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for i in range(reps):
+                        run(i % ncopy)
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                del graph
+                return e0.elapsed_time(e1) / reps, reps
+
+            ms, reps = graph_ms(ours)
+            ms16, _ = graph_ms(lambda i: ours(i, False))
+            msc, _ = graph_ms(cublas)
             flops = 2.0 * M * K * T
             byts = 2.0 * M * K + 2.0 * K * T + 4.0 * M * T
             roof = min(tc, bw * 1e9 * flops / byts / 1e12)
@@ -936,10 +948,11 @@ def run_gemm_sweep(args):
                               "dtype": args.dtype, "value": round(ach, 2), "unit": "TFLOP/s", "us": round(ms * 1e3, 2),
                               "roofline_tflops": round(roof, 1), "frac_of_roofline": round(ach / roof, 3),
                               "bound": "tensor" if roof >= tc else "hbm", "engine": fn,
+                              "us_16bit_out": round(ms16 * 1e3, 2), "cublas_us_16bit_out": round(msc * 1e3, 2),
                               "l2": f"operands rotate over {ncopy} copies (> 256 MB) so every launch reads HBM",
                               "timing": f"{reps} back-to-back launches in one CUDA graph, CUDA events"}),
                   flush=True)
-            del xs, ws, ys
+            del xs, ws, ys, hs, cs
     return 0
 
 
