@@ -14,7 +14,11 @@ std::mutex g_ctx_mu;
 DeviceCtx g_ctx[64];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::atomic<long long> g_launches{0};
+std::atomic<int> g_pdl{1};
 }  // namespace
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+void set_pdl(bool on) { g_pdl.store(on ? 1 : 0, std::memory_order_relaxed); }
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 void count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
@@ -167,7 +171,7 @@ static int launch_t(const void* X, int ldx, const void* W, int ldw, int M, int N
   const int grid = (int)(tiles < c->num_sms ? tiles : c->num_sms);
   EpiParams e = ep;
   e.status = c->status;
-  kern<<<grid, kGemmThreads, S::kTotal, st>>>(tx, tw, to, tu, M, N, K, e);
+  B2P_CHECK_CUDA(launch_pdl(kern, dim3(grid), dim3(kGemmThreads), S::kTotal, st, tx, tw, to, tu, M, N, K, e));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }

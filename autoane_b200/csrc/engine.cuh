@@ -47,10 +47,15 @@ long long launch_count();
     B2P_CHECK_CUDA(cudaGetLastError());           \
   } while (0)
 
+// Programmatic dependent launch on or off for the whole process (B2P_OPT_PDL).
+bool pdl_enabled();
+void set_pdl(bool on);
+
 // Launch with programmatic stream serialization: the kernel may start (prologue: barrier
 // init, TMEM allocation, descriptor prefetch) while the previous kernel in the stream is
 // still finishing. Every kernel launched this way calls pdl_enter() before touching global
 // memory: that waits until the preceding grid has completed and its writes are visible.
+// With PDL off the attribute is left out and pdl_enter() returns at once.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                        Args&&... args) {
@@ -63,7 +68,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 

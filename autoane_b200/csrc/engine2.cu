@@ -56,7 +56,7 @@ int launch_pair_t(const void* X, int ldx, const void* W, int ldw, int M, int N, 
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel calls pdl_enter()
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   B2P_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tw, to, tu, M, N, K, e));
   B2P_POST_LAUNCH();
   return B2P_OK;

@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_enter();  // the previous kernel's outputs are complete from here on
 
   const int num_m = (M + kBM - 1) / kBM;
   const int num_n = (N + BN - 1) / BN;

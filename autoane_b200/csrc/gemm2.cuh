@@ -46,7 +46,7 @@ struct PairSmem {
   static constexpr int kLoraBufs = NSEG >= 2 ? 1 : 2;
   static constexpr int kLoraBytes = kLoraBufs * kLoraBuf;
   static constexpr int kVarBytes = NSEG ? kMaxGroups * 20 : 0;
-  static constexpr int kBudget = 224 * 1024;
+  static constexpr int kBudget = 227 * 1024;  // the opt-in per-CTA limit (232448 B)
   static constexpr int kFree = kBudget - kOutBytes - kLoraBytes - kVarBytes - 1024 - 256;
   static constexpr int kStages = (kFree / kStageBytes) > 8 ? 8 : (kFree / kStageBytes);
   static constexpr int kOutOff = kStages * kStageBytes;

@@ -1213,6 +1213,7 @@ int launch_lora_prep(const LoraPrepArgs& a, bool bf16, cudaStream_t st) {
 
 template <typename T>
 __global__ void swiglu_gate_kernel(const T* __restrict__ h13, int rows, int H, T* __restrict__ gate) {
+  pdl_enter();
   const long long n8 = (long long)rows * H / 8;  // 8 gate columns per thread (never straddle a 128-block)
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const long long e = i * 8;
@@ -1238,11 +1239,11 @@ int launch_swiglu_gate(const void* h13, int rows, int H, void* gate, bool bf16, 
   const long long n8 = (long long)rows * H / 8;
   const int blocks = (int)std::min<long long>((n8 + 255) / 256, 148 * 16);
   if (bf16)
-    swiglu_gate_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(h13), rows, H,
-                                                              static_cast<__nv_bfloat16*>(gate));
+    B2P_CHECK_CUDA(launch_pdl(swiglu_gate_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st,
+                              static_cast<const __nv_bfloat16*>(h13), rows, H, static_cast<__nv_bfloat16*>(gate)));
   else
-    swiglu_gate_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(h13), rows, H,
-                                                       static_cast<__half*>(gate));
+    B2P_CHECK_CUDA(launch_pdl(swiglu_gate_kernel<__half>, dim3(blocks), dim3(256), 0, st,
+                              static_cast<const __half*>(h13), rows, H, static_cast<__half*>(gate)));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }

@@ -979,6 +979,9 @@ int b2p_model_set_option(b2p_model* m, int option, int value) {
     case B2P_OPT_TC_ATTENTION_BWD:
       m->tc_attn_bwd = value != 0;
       return B2P_OK;
+    case B2P_OPT_PDL:
+      set_pdl(value != 0);
+      return B2P_OK;
     case B2P_OPT_GRAD_SCALE_LOG2:
       B2P_REQUIRE(value >= -30 && value <= 30, "gradient scale exponent %d out of range [-30, 30]", value);
       m->grad_scale_log2 = value;

@@ -88,7 +88,7 @@ struct P16State {
   struct Graph {
     const void* tok = nullptr;
     int n_seq = 0, gen = -1, scale_log2 = 0, prof_epoch = -1;
-    bool pair = true, tc_attn = true, tc_attn_bwd = true;
+    bool pair = true, tc_attn = true, tc_attn_bwd = true, pdl = true;
     cudaGraphExec_t exec = nullptr;
     long long launches = 0;
   } graph;
@@ -150,6 +150,7 @@ int transpose16(const void* src, int rows, int cols, long long ld_src, void* dst
 
 template <typename T>
 __global__ void scale16_kernel(const float* __restrict__ src, long long n, float alpha, T* __restrict__ dst) {
+  pdl_enter();
   for (long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n;
        i += (long long)gridDim.x * blockDim.x * 4) {
     const float4 v = *reinterpret_cast<const float4*>(src + i);
@@ -163,9 +164,11 @@ __global__ void scale16_kernel(const float* __restrict__ src, long long n, float
 int scale16(const float* src, long long n, float alpha, void* dst, bool bf16, cudaStream_t st) {
   const int blocks = (int)std::min<long long>((n / 4 + 255) / 256, 148 * 8);
   if (bf16)
-    scale16_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, n, alpha, static_cast<__nv_bfloat16*>(dst));
+    B2P_CHECK_CUDA(launch_pdl(scale16_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, src, n, alpha,
+                              static_cast<__nv_bfloat16*>(dst)));
   else
-    scale16_kernel<__half><<<blocks, 256, 0, st>>>(src, n, alpha, static_cast<__half*>(dst));
+    B2P_CHECK_CUDA(launch_pdl(scale16_kernel<__half>, dim3(blocks), dim3(256), 0, st, src, n, alpha,
+                              static_cast<__half*>(dst)));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -178,6 +181,7 @@ int scale16(const float* src, long long n, float alpha, void* dst, bool bf16, cu
 template <typename T>
 __global__ void swiglu_bwd_kernel(const float* __restrict__ dsilu, const T* __restrict__ h13, int rows, int H,
                                   T* __restrict__ dh13) {
+  pdl_enter();
   const long long n4 = (long long)rows * H / 4;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     const long long e = i * 4;
@@ -209,11 +213,11 @@ int swiglu_bwd(const float* dsilu, const void* h13, int rows, int H, void* dh13,
   const long long n4 = (long long)rows * H / 4;
   const int blocks = (int)std::min<long long>((n4 + 255) / 256, 148 * 16);
   if (bf16)
-    swiglu_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(dsilu, static_cast<const __nv_bfloat16*>(h13), rows, H,
-                                                             static_cast<__nv_bfloat16*>(dh13));
+    B2P_CHECK_CUDA(launch_pdl(swiglu_bwd_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, dsilu,
+                              static_cast<const __nv_bfloat16*>(h13), rows, H, static_cast<__nv_bfloat16*>(dh13)));
   else
-    swiglu_bwd_kernel<__half><<<blocks, 256, 0, st>>>(dsilu, static_cast<const __half*>(h13), rows, H,
-                                                      static_cast<__half*>(dh13));
+    B2P_CHECK_CUDA(launch_pdl(swiglu_bwd_kernel<__half>, dim3(blocks), dim3(256), 0, st, dsilu,
+                              static_cast<const __half*>(h13), rows, H, static_cast<__half*>(dh13)));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -242,6 +246,7 @@ struct RmsBwdArgs {
 // covers a fixed, deterministic row set.
 template <typename T, int NCH>
 __global__ void __launch_bounds__(kRmsTeam * kRmsTeams) rms_bwd_kernel(RmsBwdArgs a, int D) {
+  pdl_enter();
   __shared__ float s_red[kRmsTeams][2][4][2];  // [team][row parity][warp][ss, dot]
   __shared__ float4 s_acc[kRmsTeams][kRmsTeam * NCH];
   const int team = threadIdx.x / kRmsTeam, tt = threadIdx.x % kRmsTeam;
@@ -336,10 +341,10 @@ int rms_bwd_t(const RmsBwdArgs& a, int D, cudaStream_t st) {
   const int blocks = rms_blocks(a.rows);
   const int nch = (D / 4 + kRmsTeam - 1) / kRmsTeam;
   switch (nch) {
-    case 1: rms_bwd_kernel<T, 1><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
-    case 2: rms_bwd_kernel<T, 2><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
-    case 3: rms_bwd_kernel<T, 3><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
-    case 4: rms_bwd_kernel<T, 4><<<blocks, kRmsTeam * kRmsTeams, 0, st>>>(a, D); break;
+    case 1: B2P_CHECK_CUDA(launch_pdl(rms_bwd_kernel<T, 1>, dim3(blocks), dim3(kRmsTeam * kRmsTeams), 0, st, a, D)); break;
+    case 2: B2P_CHECK_CUDA(launch_pdl(rms_bwd_kernel<T, 2>, dim3(blocks), dim3(kRmsTeam * kRmsTeams), 0, st, a, D)); break;
+    case 3: B2P_CHECK_CUDA(launch_pdl(rms_bwd_kernel<T, 3>, dim3(blocks), dim3(kRmsTeam * kRmsTeams), 0, st, a, D)); break;
+    case 4: B2P_CHECK_CUDA(launch_pdl(rms_bwd_kernel<T, 4>, dim3(blocks), dim3(kRmsTeam * kRmsTeams), 0, st, a, D)); break;
     default: set_error("RMSNorm backward: unsupported width %d", D); return B2P_ERR_UNSUPPORTED;
   }
   B2P_POST_LAUNCH();
@@ -381,6 +386,7 @@ constexpr int kWgPartJ = 24;        // partial entries per column
 template <typename T>
 __global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restrict__ jobs, int rows,
                                                         float* __restrict__ part, int max_cols) {
+  pdl_enter();
   __shared__ __align__(128) T s_x[2][kWgRows][kWgXs];
   __shared__ __align__(128) T s_u[2][kWgRows][kWgUs];
   const WgradJob jb = jobs[blockIdx.y];
@@ -469,6 +475,7 @@ __global__ void __launch_bounds__(256) lora_wgrad_kernel(const WgradJob* __restr
 
 __global__ void lora_wgrad_reduce_kernel(const WgradJob* __restrict__ jobs, int rank, const float* __restrict__ part,
                                          int max_cols, float scale) {
+  pdl_enter();
   const WgradJob jb = jobs[blockIdx.y];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (segment, col, j)
   const int per = jb.ncols * rank;
@@ -489,12 +496,12 @@ int lora_wgrad(const WgradJob* d_jobs, int njobs, int max_cols, int rows, int ra
   B2P_REQUIRE(rank == 4 || rank == 8, "LoRA rank must be 4 or 8");
   dim3 grid((max_cols + kWgCols - 1) / kWgCols, njobs, kWgradSplit);
   if (bf16)
-    lora_wgrad_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(d_jobs, rows, part, max_cols);
+    B2P_CHECK_CUDA(launch_pdl(lora_wgrad_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, d_jobs, rows, part, max_cols));
   else
-    lora_wgrad_kernel<__half><<<grid, 256, 0, st>>>(d_jobs, rows, part, max_cols);
+    B2P_CHECK_CUDA(launch_pdl(lora_wgrad_kernel<__half>, grid, dim3(256), 0, st, d_jobs, rows, part, max_cols));
   B2P_POST_LAUNCH();
   dim3 g2((3 * max_cols * rank + 255) / 256, njobs);
-  lora_wgrad_reduce_kernel<<<g2, 256, 0, st>>>(d_jobs, rank, part, max_cols, scale);
+  B2P_CHECK_CUDA(launch_pdl(lora_wgrad_reduce_kernel, g2, dim3(256), 0, st, d_jobs, rank, part, max_cols, scale));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
@@ -634,6 +641,7 @@ __device__ __forceinline__ void ab_load_tile(uint32_t s_base, const T* g, long l
 
 template <typename T>
 __global__ void attn_bwd_prep_kernel(AttnBwdArgs a) {
+  pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long n = (long long)a.ngroups * a.seq * a.heads;
   if (i >= n) return;
@@ -946,9 +954,9 @@ int attention_backward(const AttnBwdArgs& a0, bool bf16, bool use_tc, cudaStream
   dim3 gq(a.seq / kAT, a.heads, a.ngroups), gk(a.seq / kAT, a.kv_heads, a.ngroups);
   if (use_tc && attention_backward_tc_supported(a)) {  // D first, then dK|dV and dQ on tcgen05
     if (bf16)
-      attn_bwd_prep_kernel<__nv_bfloat16><<<pb, 256, 0, st>>>(a);
+      B2P_CHECK_CUDA(launch_pdl(attn_bwd_prep_kernel<__nv_bfloat16>, dim3(pb), dim3(256), 0, st, a));
     else
-      attn_bwd_prep_kernel<__half><<<pb, 256, 0, st>>>(a);
+      B2P_CHECK_CUDA(launch_pdl(attn_bwd_prep_kernel<__half>, dim3(pb), dim3(256), 0, st, a));
     B2P_POST_LAUNCH();
     return launch_attention_backward_tc(a, bf16, st);
   }
@@ -1281,7 +1289,7 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
   P16State::Graph& gr = s->graph;
   const bool hit = gr.exec && gr.tok == d_tok && gr.n_seq == n_seq && gr.gen == s->gen &&
                    gr.scale_log2 == m->grad_scale_log2 && gr.pair == m->use_pair && gr.tc_attn == m->tc_attn &&
-                   gr.tc_attn_bwd == m->tc_attn_bwd &&
+                   gr.tc_attn_bwd == m->tc_attn_bwd && gr.pdl == pdl_enabled() &&
                    gr.prof_epoch == m->prof_epoch;
   if (!hit) {
     if (gr.exec) cudaGraphExecDestroy(gr.exec);
@@ -1313,6 +1321,7 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
     gr.pair = m->use_pair;
     gr.tc_attn = m->tc_attn;
     gr.tc_attn_bwd = m->tc_attn_bwd;
+    gr.pdl = pdl_enabled();
     gr.prof_epoch = m->prof_epoch;
     gr.launches = captured;
   }

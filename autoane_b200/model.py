@@ -16,7 +16,7 @@ import numpy as np
 from . import _lib
 
 F16, BF16 = 0, 1
-OPT_PAIR_GEMM, OPT_GRAD_SCALE_LOG2, OPT_GRAPHS, OPT_TC_ATTENTION, OPT_TC_ATTENTION_BWD = 1, 2, 3, 4, 5
+OPT_PAIR_GEMM, OPT_GRAD_SCALE_LOG2, OPT_GRAPHS, OPT_TC_ATTENTION, OPT_TC_ATTENTION_BWD, OPT_PDL = 1, 2, 3, 4, 5, 6
 
 
 @dataclass

@@ -219,6 +219,12 @@ long long b2p_launch_count(void);
  * the tcgen05 kernels (dK|dV then dQ, sequences of 128 or 256 tokens, 64-wide
  * heads); 0 uses the mma.sync kernels. Same results up to fp32 summation order. */
 #define B2P_OPT_TC_ATTENTION_BWD 5
+/* B2P_OPT_PDL (default 1): the hot kernels (projection GEMMs, attention, RMSNorm /
+ * LoRA-down, backward elementwise kernels) launch with programmatic dependent
+ * launch, so each one's launch and prologue overlap the previous kernel's tail;
+ * 0 launches them with plain stream order. Process-wide (all models and devices);
+ * results are identical either way. */
+#define B2P_OPT_PDL 6
 int b2p_model_set_option(b2p_model* m, int option, int value);
 
 /* ======================================================================
