@@ -911,7 +911,11 @@ def run_gemm_sweep(args):
             ws = [(0.02 * torch.randn(M, K, device=dev)).to(dt) for _ in range(ncopy)]
             ys = [torch.empty(T, (M + 3) // 4 * 4, device=dev, dtype=torch.float32) for _ in range(ncopy)]
             hs = [torch.empty(T, (M + 7) // 8 * 8, device=dev, dtype=dt) for _ in range(ncopy)]
-            cs = [torch.empty(T, M, device=dev, dtype=dt) for _ in range(ncopy)]
+            # cuBLAS gets the same 8-element-aligned output rows as the engine (W zero-padded to M8 rows):
+            # an odd leading dimension would put it on a slow unaligned path
+            M8 = (M + 7) // 8 * 8
+            wc = [torch.cat([w, torch.zeros(M8 - M, K, device=dev, dtype=dt)]) if M8 > M else w for w in ws]
+            cs = [torch.empty(T, M8, device=dev, dtype=dt) for _ in range(ncopy)]
             fn = "b2p_gemm_pair" if T >= 256 else "b2p_gemm"
 
             def ours(i, f32=True):
@@ -921,7 +925,7 @@ def run_gemm_sweep(args):
                           1 if f32 else 0, st)
 
             def cublas(i):  # the library baseline: cuBLAS through torch, 16-bit output
-                torch.mm(xs[i], ws[i].t(), out=cs[i])
+                torch.mm(xs[i], wc[i].t(), out=cs[i])
 
             def graph_ms(run):
                 for i in range(ncopy):
@@ -959,7 +963,7 @@ def run_gemm_sweep(args):
                               "l2": f"operands rotate over {ncopy} copies (> 256 MB) so every launch reads HBM",
                               "timing": f"{reps} back-to-back launches in one CUDA graph, CUDA events"}),
                   flush=True)
-            del xs, ws, ys, hs, cs
+            del xs, ws, ys, hs, cs, wc
     return 0
 
 
