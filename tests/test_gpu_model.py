@@ -165,3 +165,25 @@ def test_pair_engine_seq256_matches_oracle_and_single_engine(b2p):
         assert abs(g - r) < 1e-3, (got_pair, ref)
         assert abs(g - s) < 2e-4, (got_pair, got_single)
     model.close()
+
+
+def test_programmatic_dependent_launch_changes_no_result(b2p):
+    """B2P_OPT_PDL only changes how kernels are launched: MeZO losses and the P16 gradient
+    (forward, tcgen05 attention backward, elementwise backward kernels) are bit-identical
+    with it on and off. The option is process-wide, so it is restored afterwards."""
+    from autoane_b200.model import OPT_PDL
+    cfg = M.small_cfg(nlayers=2, seq=256)
+    syn, om, model, toks = make_pair(cfg, max_groups=8)
+    inp, tgt = seqs(syn, toks, 2, cfg.seq, base=321)
+    variants = [(0, 0, 0.0, 0.0), (5, 1, 1e-3, 0.0), (5, 2, 1e-3, -2e-3)]
+    try:
+        out = {}
+        for pdl in (1, 0):
+            model.set_option(OPT_PDL, pdl)
+            out[pdl] = (model.eval(inp, tgt, variants), model.p16_grad(inp, tgt))
+    finally:
+        model.set_option(OPT_PDL, 1)
+    assert np.array_equal(out[1][0].view(np.uint32), out[0][0].view(np.uint32))
+    assert out[1][1][0] == out[0][1][0]
+    assert np.array_equal(out[1][1][1].view(np.uint32), out[0][1][1].view(np.uint32))
+    model.close()
