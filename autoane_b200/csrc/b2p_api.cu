@@ -34,8 +34,11 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
   ep.M = M;
   ep.N = N;
   const int kind = out_f32 ? EPI_F32 : EPI_H16;
-  return launch_gemm(pick_bn(N, kind), kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, nullptr, ep,
-                     static_cast<cudaStream_t>(stream));
+  DeviceCtx* c = nullptr;
+  int rc = ctx_get(&c);
+  if (rc) return rc;
+  return launch_gemm(pick_bn_rows(M, N, kind, c->num_sms), kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy,
+                     nullptr, ep, static_cast<cudaStream_t>(stream));
 }
 
 int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,

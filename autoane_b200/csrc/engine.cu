@@ -118,6 +118,14 @@ int make_tmap_2d(CUtensorMap* map, const void* base, TmapType type, uint64_t inn
   return B2P_OK;
 }
 
+int pick_bn_rows(int M, int N, int kind, int ctas) {
+  const int bn = pick_bn(N, kind);
+  if (kind != EPI_F32 && kind != EPI_H16) return bn;
+  const long long mt = (M + kBM - 1) / kBM;
+  if (mt * ((N + bn - 1) / bn) >= ctas) return bn;
+  return mt * ((N + 127) / 128) >= ctas ? 128 : 64;
+}
+
 int pick_bn(int N, int kind) {
   if (kind == EPI_SWIGLU) return 256;
   if (kind == EPI_CE) return 256;
@@ -180,6 +188,7 @@ template <int KIND, typename OutH, bool BF16, bool LORA>
 static int dispatch_bn(int bn, const void* X, int ldx, const void* W, int ldw, int M, int N, int K, void* out,
                        int ldo, const void* u16, const EpiParams& ep, cudaStream_t st) {
   switch (bn) {
+    case 64: return launch_t<64, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case 128: return launch_t<128, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case 160: return launch_t<160, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
     case 192: return launch_t<192, KIND, OutH, BF16, LORA>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);

@@ -111,5 +111,9 @@ int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W,
 // Pick the tile width for an N-column output (largest width whose padding
 // waste is minimal; SwiGLU and CE need multiples of 64 / any).
 int pick_bn(int N, int kind);
+// Tile width for a plain fp32 / 16-bit output GEMM of M rows on `ctas` CTAs: pick_bn's width
+// when its tiles fill every CTA once, else 128 or 64 columns so that more CTAs share the weight
+// stream (small M: the T <= 1024 token counts of single calls).
+int pick_bn_rows(int M, int N, int kind, int ctas);
 
 }  // namespace b2p

@@ -66,11 +66,26 @@ template <typename H, bool BF16>
 int dispatch_pair(int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K, void* out, int ldo,
                   const void* u16, const EpiParams& ep, cudaStream_t st) {
   const int nseg = ep.has_lora ? ep.lora.nseg : 0;
+  // plain outputs whose 256 x 256 tiles would keep fewer than a quarter of the clusters busy (small
+  // M): 64-column tiles put four times as many clusters on the weight stream. (Measured: at a
+  // quarter or more, and with 128-column tiles, the extra per-tile cost outweighs the parallelism.)
+  int bn = 256;
+  if ((kind == EPI_F32 || kind == EPI_H16) && nseg == 0) {
+    DeviceCtx* c = nullptr;
+    int rc = ctx_get(&c);
+    if (rc) return rc;
+    const long long mt = (M + 2 * kBM - 1) / (2 * kBM), clusters = c->num_sms / 2;
+    if (4 * mt * ((N + 255) / 256) < clusters) bn = 64;
+  }
   switch (kind) {
     case EPI_F32:
+      if (nseg == 0 && bn == 64)
+        return launch_pair_t<64, EPI_F32, H, BF16, 0>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       if (nseg == 0) return launch_pair_t<256, EPI_F32, H, BF16, 0>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       break;
     case EPI_H16:
+      if (nseg == 0 && bn == 64)
+        return launch_pair_t<64, EPI_H16, H, BF16, 0>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       if (nseg == 0) return launch_pair_t<256, EPI_H16, H, BF16, 0>(X, ldx, W, ldw, M, N, K, out, ldo, u16, ep, st);
       break;
     case EPI_QKV_ROPE:
