@@ -68,3 +68,12 @@ def test_kern_compile_without_gpu_fails_loudly():
     import numpy as np
     with pytest.raises(_lib.B2PError):
         KN.compile_conv1x1_kern(np.zeros((64, 64), np.float32), 64, 64, 128)
+
+
+def test_model_option_constants_match_header():
+    """Every B2P_OPT_* macro of b2p.h has the same value as the binding's OPT_* constant."""
+    from autoane_b200 import model
+    opts = dict(re.findall(r"#define\s+B2P_OPT_(\w+)\s+(\d+)", HEADER.read_text()))
+    assert {"PAIR_GEMM", "GRAD_SCALE_LOG2", "GRAPHS", "TC_ATTENTION", "TC_ATTENTION_BWD", "PDL"} <= set(opts)
+    for name, value in opts.items():
+        assert getattr(model, "OPT_" + name) == int(value), name
