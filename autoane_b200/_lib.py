@@ -34,6 +34,8 @@ ABI: dict[str, tuple] = {
     "b2p_version": (cstr, []),
     "b2p_device_status": (i32, [vp]),
     "b2p_gemm": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+    "b2p_attention": (i32, [vp, i32, vp, i32, vp, i32, i32, i32, i32, i32, vp]),
+    "b2p_attention_backward": (i32, [vp, i32, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp]),
     "b2p_model_create": (vp, [vp]),
     "b2p_model_free": (None, [vp]),
     "b2p_model_trainable_count": (i64, [vp]),
@@ -43,6 +45,7 @@ ABI: dict[str, tuple] = {
     "b2p_model_set_trainable": (i32, [vp, vp, i64]),
     "b2p_model_get_trainable": (i32, [vp, vp, i64]),
     "b2p_model_eval": (i32, [vp, u16p, u16p, i32, vp, i32, fp]),
+    "b2p_model_group_losses": (i32, [vp, vp, i32]),
     "b2p_mezo_step": (i32, [vp, u16p, u16p, u64, f32, f32, fp, fp, fp]),
     "b2p_mezo_eval": (i32, [vp, u16p, u16p, i32, u64p, i32, f32, vp]),
     "b2p_mezo_update": (i32, [vp, u64p, vp, i32, f32, f32]),

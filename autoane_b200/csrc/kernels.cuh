@@ -106,6 +106,11 @@ struct AttnBwdArgs {
   float scale_log2, scale;
   int* sched = nullptr;   // 2 zeroed ints: enables the tcgen05 kernels (seq 128 / 256)
 };
+// D = rowsum(dO·O) into dvec, then dK|dV and dQ: the tcgen05 kernels where they apply
+// and use_tc is set, else the mma.sync kernels (64 x 64 tiles). dQ and dK leave with the
+// inverse RoPE applied (rope_backward_inplace, training/cpu_ops.h:364), dK and dV summed
+// over each KV head's query heads (gqa_reduce_kv, training/io.h:448-459).
+int launch_attention_backward(const AttnBwdArgs& a, bool bf16, bool use_tc, cudaStream_t st);
 // dK|dV and dQ on the tcgen05 tensor cores (attn_bwd_tc.cu), D already in dvec.
 bool attention_backward_tc_supported(const AttnBwdArgs& a);
 int launch_attention_backward_tc(const AttnBwdArgs& a, bool bf16, cudaStream_t st);

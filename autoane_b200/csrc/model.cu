@@ -846,6 +846,16 @@ int b2p_model_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctarget
   return copy_losses(m, losses, n_var);
 }
 
+int b2p_model_group_losses(b2p_model* m, float* out, int n) {
+  B2P_REQUIRE(m && out, "null argument");
+  B2P_REQUIRE(m->cur_groups >= 1, "no forward has run on this model");
+  B2P_REQUIRE(n >= 1 && n <= m->cur_groups, "%d group losses requested, the last forward had %d groups", n,
+              m->cur_groups);
+  B2P_CHECK_CUDA(cudaMemcpyAsync(out, m->group_loss, (size_t)n * 4, cudaMemcpyDefault, m->st));
+  B2P_CHECK_CUDA(cudaStreamSynchronize(m->st));
+  return check_device_status(m->st);
+}
+
 int b2p_mezo_step(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, uint64_t seed, float eps,
                   float lr, float* loss_plus, float* loss_minus, float* proj_grad) {
   int rc = ready(m);

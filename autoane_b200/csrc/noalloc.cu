@@ -52,7 +52,11 @@ int na_setup(unsigned char** out) {
       set_error("xoshiro jump polynomial could not be established");
       return B2P_ERR_STATE;
     }
-    B2P_CHECK_CUDA(cudaMemcpy(p, polys.data(), kNaPolyBytes, cudaMemcpyHostToDevice));
+    // A copy from pageable memory may return before it reaches the device, and a
+    // kernel on a non-blocking stream is not ordered after the legacy stream: wait
+    // for the copy itself before any call can launch on this device.
+    B2P_CHECK_CUDA(cudaMemcpyAsync(p, polys.data(), kNaPolyBytes, cudaMemcpyHostToDevice, cudaStreamLegacy));
+    B2P_CHECK_CUDA(cudaStreamSynchronize(cudaStreamLegacy));
     g_na_dev[dev] = static_cast<unsigned char*>(p);
   }
   *out = g_na_dev[dev];
@@ -83,6 +87,12 @@ extern "C" int b2p_sign_masks_noalloc(const int64_t* buffer_sizes, int nbufs, co
   B2P_CHECK_CUDA(cudaPointerGetAttributes(&attr, out_words));
   B2P_REQUIRE(attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged,
               "out_words must be device memory");
+  int cur = 0;
+  B2P_CHECK_CUDA(cudaGetDevice(&cur));
+  // the scratch and the launch belong to the current device; another GPU's buffer
+  // would be written over peer access or fault, so it is refused before any work
+  B2P_REQUIRE(attr.type == cudaMemoryTypeManaged || attr.device == cur,
+              "out_words lives on device %d but device %d is current", attr.device, cur);
   unsigned char* scratch = nullptr;
   int rc = na_setup(&scratch);
   if (rc) return rc;

@@ -1746,6 +1746,10 @@ int full_update(b2p_model* m, float lr, float wd, float clip) {
 
 }  // namespace
 
+int launch_attention_backward(const AttnBwdArgs& a, bool bf16, bool use_tc, cudaStream_t st) {
+  return attention_backward(a, bf16, use_tc, st);
+}
+
 void p16_release(P16State* s) {
   if (!s) return;
   if (s->graph.exec) cudaGraphExecDestroy(s->graph.exec);

@@ -113,6 +113,12 @@ class Model:
                   _fp(out))
         return out
 
+    def group_losses(self, n: int) -> np.ndarray:
+        """Per-group losses of the last forward: group g = v * n_seq + q (sequence q, variant v)."""
+        out = np.empty(n, np.float32)
+        _lib.call("b2p_model_group_losses", self.h, out.ctypes.data, n)
+        return out
+
     def mezo_step(self, tokens, ctargets, seed: int, eps: float, lr: float):
         tok = np.ascontiguousarray(tokens, np.uint16)
         tgt = np.ascontiguousarray(ctargets, np.uint16)

@@ -76,6 +76,35 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
 int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
                   void* stream);
 
+/* Causal GQA attention on device buffers (cpu_sdpa_forward,
+ * training/cpu_ops.h:321-360, with K/V tiled over the query heads by
+ * gqa_tile_kv, training/io.h:439-446), for n_seq independent sequences of
+ * `seq` tokens stored as token-major 16-bit rows:
+ *   qkv [n_seq*seq][ld_qkv]: post-RoPE Q in columns [0, 64*heads), K in the
+ *       next 64*kv_heads columns, V after it (head_dim 64; query head h reads
+ *       KV head h / (heads / kv_heads));
+ *   out [n_seq*seq][ld_out]: softmax(Q·Kᵀ/8 + causal mask)·V per head, 64*heads columns;
+ *   lse (may be NULL) fp32 [n_seq*seq][heads]: each row's softmax normaliser
+ *       in the log2 domain, max·log2(e)/8 + log2(sum), the input b2p_attention_backward needs.
+ * seq a multiple of 64 (the tcgen05 kernel takes 128 and 256, the mma.sync
+ * kernel other lengths); row pitches multiples of 8 elements, 16-byte aligned
+ * pointers. Asynchronous on `stream`; allocates its 8-byte work counter with
+ * cudaMallocAsync on that stream. */
+int b2p_attention(const void* qkv, int ld_qkv, void* out, int ld_out, float* lse, int n_seq, int seq, int heads,
+                  int kv_heads, int dtype, void* stream);
+
+/* Attention backward as bp_lora_backward runs it (training/backprop_lora.h:241-252):
+ * cpu_sdpa_backward (cpu_ops.h:213-290) on post-RoPE Q, K, V and the output
+ * gradient dout [n_seq*seq][ld_o], then dK and dV summed over each KV head's
+ * query heads (gqa_reduce_kv, io.h:448-459) and the inverse RoPE of theta
+ * rope_theta applied to dQ and dK (rope_backward_inplace, cpu_ops.h:364).
+ * `out` and `lse` are b2p_attention's outputs for the same qkv. Writes dQ | dK | dV
+ * into dqkv [n_seq*seq][ld_d] at qkv's column offsets. Same shape rules as
+ * b2p_attention. Asynchronous on `stream` (its scratch comes from cudaMallocAsync). */
+int b2p_attention_backward(const void* qkv, int ld_qkv, const void* out, const void* dout, int ld_o,
+                           const float* lse, void* dqkv, int ld_d, int n_seq, int seq, int heads, int kv_heads,
+                           float rope_theta, int dtype, void* stream);
+
 /* ======================================================================
  * Device-resident model: the MeZO-LoRA-split hot path on the GPU.
  *
@@ -141,6 +170,13 @@ int b2p_model_get_trainable(b2p_model* m, float* theta, long long n);
 int b2p_model_eval(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, int n_seq,
                    const b2p_variant* vars, int n_var, float* losses);
 
+/* Per-group losses of the model's last forward (any eval, MeZO or backprop-LoRA
+ * call): out[g] = per-token mean CE of group g = v*n_seq + q, i.e. sequence q
+ * under variant v (the single-sequence loss the reference's DO_FORWARD_PASS
+ * returns, train_mezo.m:1695-1698). n <= the last forward's group count; host
+ * or device `out`; synchronises the model stream. */
+int b2p_model_group_losses(b2p_model* m, float* out, int n);
+
 /* One MeZO-LoRA-split step exactly as train_mezo.m:2938-3012: evaluate θ+εz and
  * θ-εz (batched), then θ ← ((θ+εz)-2εz)+εz and θ ← θ - lr·g·z with
  * g = (L+ - L-)/(2ε) computed on the device. Outputs may be NULL. */
@@ -176,11 +212,15 @@ int b2p_sign_masks(b2p_model* m, const uint64_t* seeds, int n, uint32_t* out_wor
  * (1 = +), drawn as perturb_buffer draws it (training/train_mezo.m:122-136).
  * Host inputs: buffer_sizes[nbufs], seeds[nseeds]. Limits: nbufs <= 1024,
  * nseeds <= 64, at most 524,288 draws per seed; larger inputs are rejected with
- * B2P_ERR_ARG. Scratch is a fixed 281 KiB __device__ array that every GPU
- * loading the library keeps until exit. The first call on a device fills it
- * (synchronous copy); make that call before any stream capture. All calls on a
- * device share the array, so calls that overlap on the GPU race. Asynchronous
- * on `stream` otherwise. Calls no cudaMalloc/cudaFree. */
+ * B2P_ERR_ARG. out_words must be on the current device (another device's
+ * buffer is refused with B2P_ERR_ARG). Scratch is a fixed 281 KiB __device__
+ * array that every GPU loading the library keeps until exit. The first call on
+ * a device loads the library's device code there if CUDA has not yet done so
+ * (lazy module loading brings the array in at that moment) and fills the array
+ * with a copy it waits for; make that first call during set-up, before any
+ * stream capture. All calls on a device share the array, so calls that overlap
+ * on the GPU race. Asynchronous on `stream` otherwise. Calls no
+ * cudaMalloc/cudaFree. */
 int b2p_sign_masks_noalloc(const int64_t* buffer_sizes, int nbufs, const uint64_t* seeds, int nseeds,
                            uint32_t* out_words, void* stream);
 

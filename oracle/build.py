@@ -7,8 +7,9 @@
   oracle/_ref/validation_*    the reference's standalone C validators
                               (results/validation_*.c), compiled unchanged
 
-The _ref part needs the reference tree (REF_ROOT, default /root/reference) and
-is skipped when it is absent; the prebuilt files travel with the repository.
+The _ref part needs the reference tree, named by the AUTOANE_REF_ROOT
+environment variable; without it (or where that tree is absent) the _ref part is
+skipped, and prebuilt files already in oracle/_ref are used as they are.
 Nothing here is used by libb2p.so.
 """
 from __future__ import annotations
@@ -21,15 +22,15 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("AUTOANE_REF_ROOT", "/root/reference"))
+REF_ROOT = Path(os.environ["AUTOANE_REF_ROOT"]) if os.environ.get("AUTOANE_REF_ROOT") else None
 REF_OUT = HERE / "_ref"
 LIBORACLE = HERE / "liboracle.so"
 # reference model headers compiled into _ref (training/models/*.h) plus our own
 # header for the 8/8-head, 1152-hidden variant of the 36.4M configuration
 REF_MODELS = {
-    "smollm2_360m": REF_ROOT / "training" / "models" / "smollm2_360m.h",
-    "autoresearch": REF_ROOT / "training" / "models" / "autoresearch.h",
-    "autoresearch_mha": HERE / "models" / "autoresearch_mha.h",
+    "smollm2_360m": ("ref", "training/models/smollm2_360m.h"),
+    "autoresearch": ("ref", "training/models/autoresearch.h"),
+    "autoresearch_mha": ("here", "models/autoresearch_mha.h"),
 }
 CFLAGS = ["-O2", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-w"]
 
@@ -82,15 +83,17 @@ def build_oracle(force: bool = False) -> Path:
 
 def build_ref(force: bool = False) -> list[Path]:
     """Compile the reference's own C from REF_ROOT into oracle/_ref (skipped when absent)."""
-    if not (REF_ROOT / "training" / "cpu_ops.h").exists():
+    if REF_ROOT is None or not (REF_ROOT / "training" / "cpu_ops.h").exists():
         return []
     REF_OUT.mkdir(exist_ok=True)
     blas = find_openblas()
     out = []
     driver = HERE / "ref_driver.c"
-    for name, header in REF_MODELS.items():
+    newest = max(p.stat().st_mtime for p in [driver, *(HERE / "shim").glob("*.h")])
+    for name, (where, rel) in REF_MODELS.items():
+        header = (REF_ROOT if where == "ref" else HERE) / rel
         lib = REF_OUT / f"libref_{name}.so"
-        if lib.exists() and not force and lib.stat().st_mtime >= driver.stat().st_mtime:
+        if lib.exists() and not force and lib.stat().st_mtime >= newest:
             out.append(lib)
             continue
         # -I<shim> -I- : quoted includes resolve in the shim first and never in the

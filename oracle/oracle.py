@@ -317,4 +317,5 @@ def ref_lib(model: str):
     L.ref_forward_loss.restype = C.c_float
     L.ref_forward_loss_ffn.restype = C.c_float
     L.ref_p16_grad.restype = C.c_float
+    L.ref_p16_grad_dw.restype = C.c_float
     return L

@@ -268,3 +268,21 @@ float ref_p16_grad(const float* const* Wq, const float* const* Wk, const float* 
   free(v_tiled); free(logits); free(dlogits); free(lora_tmp); free(x_pre_final);
   return loss;
 }
+
+/* ref_p16_grad that also returns the projection weight gradients the reference
+ * materialises before projecting them onto the adapters (work->dW_Wo, dW_q and
+ * dW_kv, training/backprop_lora.h:223-270): dw receives, for L = NLAYERS-1 down
+ * to 0, dW_o [DIM, Q_DIM], dW_q [Q_DIM, DIM], dW_k [KV_DIM, DIM], dW_v [KV_DIM, DIM]. */
+float ref_p16_grad_dw(const float* const* Wq, const float* const* Wk, const float* const* Wv, const float* const* Wo,
+                      const float* const* W1, const float* const* W2, const float* const* W3,
+                      const float* const* lora, const float* const* rms, const float* rms_final, const float* embed,
+                      const float* cembed, int CV, int rank, float res_alpha, const uint16_t* input_toks,
+                      const uint16_t* ctargets, float* const* glora, float* const* grms, float* grms_final,
+                      float* dw) {
+  ref_dw_sink = dw;
+  ref_dw_pos = 0;
+  const float loss = ref_p16_grad(Wq, Wk, Wv, Wo, W1, W2, W3, lora, rms, rms_final, embed, cembed, CV, rank,
+                                  res_alpha, input_toks, ctargets, glora, grms, grms_final);
+  ref_dw_sink = 0;
+  return loss;
+}

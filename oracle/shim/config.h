@@ -121,9 +121,19 @@ typedef struct {
 } LoRALayer;
 typedef struct { float *Aq, *Bq, *Ak, *Bk, *Av, *Bv, *Ao, *Bo; } LoRAGrads;
 
+/* Test hook: while ref_dw_sink is set, every dW that bp_lora_backward hands to
+ * lora_grad_project is also copied there, back to back in call order (per layer
+ * from the last: Wo, Wq, Wk, Wv; training/backprop_lora.h:223-270). */
+static float* ref_dw_sink = 0;
+static size_t ref_dw_pos = 0;
+
 /* dB += dW·Aᵀ ; dA += Bᵀ·dW  (same contract as the reference's lora_grad_project) */
 static void lora_grad_project(float* dA, float* dB, const float* dW, const float* A, const float* B, int out_dim,
                               int rank, int in_dim) {
+  if (ref_dw_sink) {
+    memcpy(ref_dw_sink + ref_dw_pos, dW, (size_t)out_dim * in_dim * sizeof(float));
+    ref_dw_pos += (size_t)out_dim * in_dim;
+  }
   cblas_sgemm(CblasRowMajor, CblasNoTrans, CblasTrans, out_dim, rank, in_dim, 1.0f, dW, in_dim, A, in_dim, 1.0f,
               dB, rank);
   cblas_sgemm(CblasRowMajor, CblasTrans, CblasNoTrans, rank, in_dim, out_dim, 1.0f, B, rank, dW, in_dim, 1.0f, dA,

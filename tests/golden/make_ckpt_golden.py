@@ -1,9 +1,9 @@
 """Pin oracle/ckpt.py (the BLZT v4 / LORA restatement) on the reference's own reader.
 
-Run once in a checkout that has the AutoANE reference tree (default
-/root/reference, override with AUTOANE_REF_ROOT):
+Run once where the AutoANE reference tree is present, with AUTOANE_REF_ROOT
+naming its root directory (required; the script refuses to guess a path):
 
-    python tests/golden/make_ckpt_golden.py
+    AUTOANE_REF_ROOT=<reference tree> python tests/golden/make_ckpt_golden.py
 
 It writes a BLZT v4 file for the tiny case of tests/_models.py (CKPT_TINY,
 ckpt_case seed 5) with oracle.ckpt.write_blzt, once with zero Adam slots (the
@@ -28,7 +28,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("AUTOANE_REF_ROOT", "/root/reference"))
+if not os.environ.get("AUTOANE_REF_ROOT"):
+    sys.exit("set AUTOANE_REF_ROOT to the AutoANE reference tree")
+REF = Path(os.environ["AUTOANE_REF_ROOT"])
 sys.path.insert(0, str(ROOT))
 
 from oracle import ckpt as K  # noqa: E402

@@ -1,9 +1,9 @@
 """Generate the golden fixtures that pin the oracle (and through it the CUDA path).
 
-Run once in a checkout that has the AutoANE reference tree (default
-/root/reference, override with AUTOANE_REF_ROOT):
+Run once where the AutoANE reference tree is present, with AUTOANE_REF_ROOT
+naming its root directory (required; the script refuses to guess a path):
 
-    python tests/golden/make_golden.py
+    AUTOANE_REF_ROOT=<reference tree> python tests/golden/make_golden.py
 
 It imports the reference's own Python replicas and writes small JSON files
 next to this script; tests read only those JSON files:
@@ -29,7 +29,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("AUTOANE_REF_ROOT", "/root/reference"))
+if not os.environ.get("AUTOANE_REF_ROOT"):
+    sys.exit("set AUTOANE_REF_ROOT to the AutoANE reference tree")
+REF = Path(os.environ["AUTOANE_REF_ROOT"])
 
 
 def _import(path: Path, name: str):

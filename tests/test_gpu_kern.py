@@ -39,6 +39,7 @@ def rnd(rng, shape, std=1.0):
 def close(got, ref, rel):
     err = np.max(np.abs(got - ref))
     scale = max(np.max(np.abs(ref)), 1e-6)
+    print(f"max rel err {err / scale:.2e} (gate {rel})")
     assert err <= rel * scale, f"max err {err:.3e} vs scale {scale:.3e} (rel {err / scale:.2e} > {rel})"
 
 

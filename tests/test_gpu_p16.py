@@ -3,7 +3,7 @@ itself pinned to the reference's bp_lora_backward in tests/test_oracle_vs_ref.py
 
 Tolerances (fp16 compute, 16-bit activations and gradient operands, fp32
 accumulation and fp32 residual-stream gradients):
-  * loss: |L_gpu - L_oracle| < 1e-3 nats (2e-3 for bf16 / 32 layers)
+  * loss: |L_gpu - L_oracle| < 1e-3 nats (2e-3 for bf16)
   * gradient, per parameter block (each A, B, RMS vector of each layer):
     relative L2 error < 5e-2 and cosine similarity > 0.998 (fp16);
     < 1e-1 and > 0.99 for bf16 (8-bit mantissa)
@@ -44,7 +44,9 @@ def compare_grads(cfg, lay, got, ref, rel_tol, cos_tol):
         cos = float(g @ r / (np.linalg.norm(g) * nr))
         worst.append((rel, cos, name))
         assert rel < rel_tol and cos > cos_tol, f"{name}: rel {rel:.3e} cos {cos:.6f}"
-    return max(worst)
+    w = max(worst)
+    print(f"worst gradient block {w[2]}: rel L2 {w[0]:.3e}, cos {min(c for _, c, _ in worst):.6f}")
+    return w
 
 
 def seqs(syn, toks, n, seq, base):
@@ -164,7 +166,8 @@ def test_p16_full_smollm2_360m_gradient(b2p):
     inp, tgt = M.sample_sequence(toks, cfg.seq, syn.full_to_compact, 12345)
     loss, grad = model.p16_grad(inp[None], tgt[None])
     rloss, rgrad = om.p16_grad(syn.theta, inp, tgt)
-    assert abs(loss - rloss) < 2e-3, (loss, rloss)
+    print(f"P16 SmolLM2-360M loss gap {abs(loss - rloss):.3e}")
+    assert abs(loss - rloss) < 1e-3, (loss, rloss)
     assert 9.0 < loss < 10.5
     compare_grads(cfg, syn.layout, grad, rgrad, 5e-2, 0.998)
     model.close()

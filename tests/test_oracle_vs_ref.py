@@ -210,3 +210,55 @@ def test_adam_matches_reference_bit_exact():
         assert np.array_equal(w1.view(np.uint32), w2.view(np.uint32))
         assert np.array_equal(m1.view(np.uint32), m2.view(np.uint32))
         assert np.array_equal(v1.view(np.uint32), v2.view(np.uint32))
+
+
+@pytest.mark.parametrize("model,cfg", [("autoresearch", M.AUTORESEARCH), ("autoresearch_mha", M.AUTORESEARCH_MHA)])
+def test_full_grad_dw_matches_reference_materialised_dw(model, cfg):
+    """Config 0 (full backprop, train.m) weight gradients of Wq/Wk/Wv/Wo against the dW
+    matrices the reference's compiled bp_lora_backward materialises before projecting them
+    onto the adapters (training/backprop_lora.h:223-270). With B = 0 the merged weights are
+    the base weights, so both are dL/dW of the same network. res_alpha 1/sqrt(2L) as the
+    from-scratch configuration scales its residual branches (train.m DeepNet init)."""
+    import dataclasses
+    ref = need(model)
+    cfg = dataclasses.replace(cfg, res_alpha=float(np.float32(1.0 / np.sqrt(2 * cfg.nlayers))))
+    syn = M.make_model(cfg, n_active=3000, seed=13, b_scale=0.0, rms_jitter=0.05, w_std=0.05)
+    toks = M.make_tokens(4096, 3000, seed=13)
+    inp, tgt = M.sample_sequence(toks, cfg.seq, syn.full_to_compact, 41)
+    om = O.OracleModel(cfg, syn.weights, syn.embed, syn.cembed)
+    loss_o, _, dw_o, _ = om.full_grad(syn.theta, inp, tgt)
+    L, lay, r, D, QD, KVD = cfg.nlayers, syn.layout, cfg.rank, cfg.dim, cfg.q_dim, cfg.kv_dim
+    keep = []
+
+    def plist(arrs):
+        p = (F * len(arrs))(*[f(a) for a in arrs])
+        keep.append((arrs, p))
+        return p
+
+    lora, rms = _theta_lists(syn, L)
+    sizes = [r * D, QD * r, r * D, KVD * r, r * D, KVD * r, r * QD, D * r]
+    glora = [np.zeros(sizes[k % 8], np.float32) for k in range(8 * L)]
+    grms = [np.zeros(D, np.float32) for _ in range(2 * L)]
+    grf = np.zeros(D, np.float32)
+    rf = np.ascontiguousarray(syn.theta[lay.rms_final:])
+    per_layer = [("Wo", (D, QD)), ("Wq", (QD, D)), ("Wk", (KVD, D)), ("Wv", (KVD, D))]
+    dw = np.zeros(L * sum(a * b for _, (a, b) in per_layer), np.float32)
+    ref.ref_p16_grad_dw.argtypes = [C.POINTER(F)] * 9 + [F, F, F, C.c_int, C.c_int, C.c_float,
+                                                         C.POINTER(C.c_uint16), C.POINTER(C.c_uint16),
+                                                         C.POINTER(F), C.POINTER(F), F, F]
+    loss_r = ref.ref_p16_grad_dw(*[plist(syn.weights[k]) for k in ("Wq", "Wk", "Wv", "Wo", "W1", "W2", "W3")],
+                                 plist(lora), plist(rms), f(rf), f(syn.embed), f(syn.cembed), syn.cembed.shape[0], r,
+                                 C.c_float(cfg.res_alpha), inp.ctypes.data_as(C.POINTER(C.c_uint16)),
+                                 tgt.ctypes.data_as(C.POINTER(C.c_uint16)), plist(glora), plist(grms), f(grf), f(dw))
+    assert abs(loss_o - loss_r) < 1e-5, (loss_o, loss_r)
+    o, worst = 0, 0.0
+    for l in reversed(range(L)):
+        for name, (a, b) in per_layer:
+            got, want = dw_o[name][l].astype(np.float64), dw[o:o + a * b].reshape(a, b)
+            o += a * b
+            assert np.linalg.norm(want) > 0, (name, l)
+            e = np.linalg.norm(got - want) / np.linalg.norm(want)
+            worst = max(worst, e)
+            # same fp32 arithmetic through the same BLAS; only summation order differs
+            assert e < 1e-4, (name, l, e)
+    assert o == dw.size
