@@ -47,6 +47,7 @@ def _deps_mtime() -> float:
 def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile every CUDA source for sm_100a and link libb2p.so. Returns its path."""
     if LIB.exists() and not force and LIB.stat().st_mtime >= _deps_mtime():
+        build_host()
         return LIB
     nvcc = _nvcc()
     OBJ_DIR.mkdir(parents=True, exist_ok=True)
@@ -71,7 +72,28 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr[-8000:]}")
     os.replace(tmp, LIB)
+    build_host()
     return LIB
+
+
+HOST_SRC = PKG / "host" / "train_mezo.c"
+HOST_EXE = PKG / "host" / "train_mezo"
+
+
+def build_host(force: bool = False) -> Path:
+    """The plain-C training loop (host/train_mezo.c) linked against libb2p.so."""
+    if HOST_EXE.exists() and not force and HOST_EXE.stat().st_mtime >= max(
+            HOST_SRC.stat().st_mtime, LIB.stat().st_mtime, (ROOT / "include" / "b2p.h").stat().st_mtime):
+        return HOST_EXE
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if not cc:
+        raise RuntimeError("no C compiler for the host loop")
+    cmd = [cc, "-std=c11", "-O2", "-Wall", "-Wextra", "-I", str(ROOT / "include"), str(HOST_SRC), "-L", str(PKG),
+           "-lb2p", "-Wl,-rpath,$ORIGIN/..", "-lm", "-o", str(HOST_EXE)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host loop build failed:\n{r.stderr[-4000:]}")
+    return HOST_EXE
 
 
 if __name__ == "__main__":

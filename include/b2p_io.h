@@ -10,13 +10,20 @@
  *   make_surface, IOSurfaceLock/Unlock/GetBaseAddress    io.h:6 (IOSurface)
  *   cvt_f16_f32, cvt_f32_f16                             io.h:33-51
  *   io_write_fp16, io_read_fp16, io_write_fp16_at, io_copy   io.h:53-77
+ *   io_write_dyn, io_write_dyn_acts                      io.h:79-101
  *   io_write_conv_acts, io_read_dyn                      io.h:102-114
+ *   compile_kern_mil_w (dynamic-matmul programs)         io.h:116-150
  *   compile_conv1x1_kern, compile_qkv_fused_conv1x1_kern,
  *   compile_ffn_fused_conv1x1_kern                       io.h:165-229
  *   io_write_ffn_fused_conv_input                        io.h:232-240
- *   ane_eval, free_kern                                  io.h:152, 242
+ *   ane_eval, ane_eval_req, make_request, free_kern      io.h:152, 242-257
  *   gen_conv1x1_mil, gen_qkv_fused_conv1x1_mil,
- *   gen_ffn_fused_conv1x1_mil                            mil_dynamic.h:17-131
+ *   gen_ffn_fused_conv1x1_mil, gen_dyn_matmul_mil        mil_dynamic.h:17-173
+ *
+ * Objective-C literals at the call sites become C: the weights dictionary of
+ * compile_kern_mil_w is NULL (its dynamic-matmul programs take no baked
+ * weights, train.m:82-106 passes @{}), and requests are released with
+ * CFRelease as surfaces are.
  *
  * A surface is a host fp16 buffer, as an IOSurface is: writes land in it, and
  * ane_eval uploads the input surface of a kernel (fp16 -> fp32 -> device)
@@ -43,18 +50,31 @@
 extern "C" {
 #endif
 
-typedef char NSString; /* MIL text stand-in: the operator tag returned by gen_*_mil */
+typedef char NSString;   /* MIL text stand-in: the operator tag returned by gen_*_mil */
+typedef void NSDictionary; /* compile_kern_mil_w weights: NULL (no baked weights) */
+
+#define B2P_IO_SURFACE_TAG 0x53524643 /* first word of a surface */
+#define B2P_IO_REQUEST_TAG 0x51455243 /* first word of a request */
 
 typedef struct b2p_surface {
+  int tag;
   size_t bytes;
   int channels, width; /* [channels, width] fp16 when bound to a kernel */
-  _Float16* mem;      /* the surface contents (fp16, channel-first) */
-  b2p_kernel* owner;  /* kernel this surface is bound to (NULL: free-standing) */
+  int split;           /* two-input kernels: columns of input 0 in each row (0: one input) */
+  _Float16* mem;       /* the surface contents (fp16, channel-first) */
+  b2p_kernel* owner;   /* kernel this surface is bound to (NULL: free-standing) */
   int is_output;
-  int dirty;          /* input written since the last upload */
-  int stale;          /* output not yet fetched since the last eval */
+  int dirty;           /* input written since the last upload */
+  int stale;           /* output not yet fetched since the last eval */
+  struct b2p_surface* uploaded; /* kernel input surfaces: which surface the device input holds */
 } b2p_surface;
 typedef b2p_surface* IOSurfaceRef;
+
+typedef struct {
+  int tag;
+  void* kern;       /* Kern* the request evaluates */
+  IOSurfaceRef in;  /* its input surface (make_request, io.h:250-257) */
+} b2p_request;
 
 typedef struct {
   void* model; /* b2p_kernel* */
@@ -76,6 +96,7 @@ static inline IOSurfaceRef make_surface(size_t bytes) {
     fprintf(stderr, "b2p_io: out of host memory\n");
     abort();
   }
+  s->tag = B2P_IO_SURFACE_TAG;
   s->bytes = bytes;
   return s;
 }
@@ -118,7 +139,19 @@ static inline int IOSurfaceUnlock(IOSurfaceRef s, unsigned flags, void* seed) {
   return 0;
 }
 static inline void* IOSurfaceGetBaseAddress(IOSurfaceRef s) { return s->mem; }
-static inline void CFRelease(IOSurfaceRef s) { b2p_io_free_surface(s); }
+/* Releases a surface (make_surface) or a request (make_request). */
+static inline void CFRelease(const void* obj) {
+  if (!obj) return;
+  if (*(const int*)obj == B2P_IO_REQUEST_TAG) {
+    free((void*)obj);
+    return;
+  }
+  if (*(const int*)obj != B2P_IO_SURFACE_TAG) {
+    fprintf(stderr, "b2p_io: CFRelease of an object this shim did not make\n");
+    abort();
+  }
+  b2p_io_free_surface((IOSurfaceRef)obj);
+}
 
 /* ---- surface I/O, channel-first [C, S] (io.h:53-114) ---- */
 static inline void io_write_fp16(IOSurfaceRef s, const float* data, int channels, int sp) {
@@ -136,6 +169,20 @@ static inline void io_copy(IOSurfaceRef dst, int dst_ch, IOSurfaceRef src, int s
 }
 static inline void io_write_fp16_at(IOSurfaceRef s, int ch_off, const float* data, int channels, int sp) {
   cvt_f32_f16(s->mem + (size_t)ch_off * sp, data, channels * sp);
+  s->dirty = 1;
+}
+/* Dynamic-matmul input surface [ic, seq + oc]: row d holds act[d, :] then W[d, :] (io.h:79-89). */
+static inline void io_write_dyn(IOSurfaceRef s, const float* act, int ic, int seq, const float* W, int oc) {
+  const int sp = seq + oc;
+  for (int d = 0; d < ic; d++) {
+    cvt_f32_f16(s->mem + (size_t)d * sp, act + (size_t)d * seq, seq);
+    cvt_f32_f16(s->mem + (size_t)d * sp + seq, W + (size_t)d * oc, oc);
+  }
+  s->dirty = 1;
+}
+/* Activations only, the weights already staged in the surface (io.h:92-99). */
+static inline void io_write_dyn_acts(IOSurfaceRef s, const float* act, int ic, int seq, int sp) {
+  for (int d = 0; d < ic; d++) cvt_f32_f16(s->mem + (size_t)d * sp, act + (size_t)d * seq, seq);
   s->dirty = 1;
 }
 static inline void io_write_conv_acts(IOSurfaceRef s, const float* act, int ic, int seq) {
@@ -164,9 +211,20 @@ static inline NSString* gen_ffn_fused_conv1x1_mil(int dim, int hidden, int seq) 
   (void)dim; (void)hidden; (void)seq;
   return (NSString*)"ffn_fused_conv1x1";
 }
+/* y[oc, seq] = W^T · act with W staged in the input surface (mil_dynamic.h:157-173).
+ * The tag carries the sizes; it lives in a per-thread ring of 8 buffers. */
+static inline NSString* gen_dyn_matmul_mil(int ic, int oc, int seq) {
+  static _Thread_local char ring[8][64];
+  static _Thread_local int next = 0;
+  char* t = ring[next];
+  next = (next + 1) % 8;
+  snprintf(t, sizeof(ring[0]), "dyn_matmul:%d:%d:%d", ic, oc, seq);
+  return (NSString*)t;
+}
 
 /* ---- compile / eval / free ---- */
-static inline Kern* b2p_io_kern(const b2p_op_desc* d, const float* const* w, int in_ch, int in_w, int out_ch) {
+static inline Kern* b2p_io_kern(const b2p_op_desc* d, const float* const* w, int in_ch, int in_w, int out_ch,
+                                int split) {
   b2p_kernel* bk = b2p_compile(d, w);
   if (!bk) {
     printf("  [compile] FAIL: %s\n", b2p_last_error()); /* compile_kern_mil_w reports and returns NULL */
@@ -179,6 +237,7 @@ static inline Kern* b2p_io_kern(const b2p_op_desc* d, const float* const* w, int
   k->ioOut = make_surface((size_t)out_ch * d->seq * 2);
   k->ioIn->channels = in_ch;
   k->ioIn->width = in_w;
+  k->ioIn->split = split;
   k->ioOut->channels = out_ch;
   k->ioOut->width = d->seq;
   k->ioIn->owner = bk;
@@ -203,7 +262,7 @@ static inline Kern* compile_conv1x1_kern(NSString* mil, const float* W, int ic, 
   b2p_op_desc d = b2p_io_desc(B2P_OP_CONV1X1, ic, seq);
   d.oc = oc;
   const float* w[1] = {W};
-  return b2p_io_kern(&d, w, ic, seq, oc);
+  return b2p_io_kern(&d, w, ic, seq, oc, 0);
 }
 
 static inline Kern* compile_qkv_fused_conv1x1_kern(NSString* mil, const float* Wq, const float* Wk, const float* Wv,
@@ -213,7 +272,7 @@ static inline Kern* compile_qkv_fused_conv1x1_kern(NSString* mil, const float* W
   d.q_dim = q_dim;
   d.kv_dim = kv_dim;
   const float* w[3] = {Wq, Wk, Wv};
-  return b2p_io_kern(&d, w, dim, seq, q_dim + 2 * kv_dim);
+  return b2p_io_kern(&d, w, dim, seq, q_dim + 2 * kv_dim, 0);
 }
 
 static inline Kern* compile_ffn_fused_conv1x1_kern(NSString* mil, const float* W1, const float* W3, const float* W2,
@@ -222,40 +281,83 @@ static inline Kern* compile_ffn_fused_conv1x1_kern(NSString* mil, const float* W
   b2p_op_desc d = b2p_io_desc(B2P_OP_FFN_FUSED, dim, seq);
   d.hidden = hidden;
   const float* w[3] = {W1, W3, W2};
-  return b2p_io_kern(&d, w, dim, 2 * seq, dim);
+  return b2p_io_kern(&d, w, dim, 2 * seq, dim, seq);
 }
 
-/* Upload a kernel's input surface: [C, S] for conv / qkv, [dim, 2S] = xnorm | x_cur per row for ffn. */
-static inline void b2p_io_upload(Kern* k) {
+/* Upload input surface `s` (the kernel's own or a request's) with the kernel's input
+ * layout: [C, S] for conv / qkv; two inputs side by side in each row for ffn
+ * ([xnorm_d (S) | x_d (S)]) and dynamic matmul ([act_d (seq) | W_d (oc)]). */
+static inline void b2p_io_upload(Kern* k, IOSurfaceRef s) {
   b2p_kernel* bk = (b2p_kernel*)k->model;
-  IOSurfaceRef s = k->ioIn;
-  const size_t n = (size_t)s->channels * s->width;
+  const IOSurfaceRef g = k->ioIn; /* geometry */
+  const size_t n = (size_t)g->channels * g->width;
+  if (s->bytes < n * 2) b2p_io_fail("input upload (surface smaller than the kernel's input)");
   float* tmp = (float*)malloc(n * 4);
   if (!tmp) b2p_io_fail("input upload (host memory)");
   int rc;
-  if (b2p_input_bytes(bk, 1) == 0) {
+  if (g->split == 0) {
     cvt_f16_f32(tmp, s->mem, (int)n);
     rc = b2p_write_input(bk, 0, tmp, n * 4);
   } else {
-    /* ffn: row d of the surface is [xnorm_d (S) | x_d (S)]; the two halves are inputs 0 and 1 */
-    const int S = s->width / 2;
-    float* b = tmp + n / 2;
-    for (int d = 0; d < s->channels; d++) {
-      cvt_f16_f32(tmp + (size_t)d * S, s->mem + (size_t)d * 2 * S, S);
-      cvt_f16_f32(b + (size_t)d * S, s->mem + (size_t)d * 2 * S + S, S);
+    const int a = g->split, b = g->width - g->split;
+    float* t1 = tmp + (size_t)g->channels * a;
+    for (int d = 0; d < g->channels; d++) {
+      cvt_f16_f32(tmp + (size_t)d * a, s->mem + (size_t)d * g->width, a);
+      cvt_f16_f32(t1 + (size_t)d * b, s->mem + (size_t)d * g->width + a, b);
     }
-    rc = b2p_write_input(bk, 0, tmp, n * 2);
-    if (rc == 0) rc = b2p_write_input(bk, 1, b, n * 2);
+    rc = b2p_write_input(bk, 0, tmp, (size_t)g->channels * a * 4);
+    if (rc == 0) rc = b2p_write_input(bk, 1, t1, (size_t)g->channels * b * 4);
   }
   free(tmp);
   if (rc != 0) b2p_io_fail("b2p_write_input");
   s->dirty = 0;
+  g->uploaded = s;
 }
 
-static inline void ane_eval(Kern* k) {
-  if (k->ioIn->dirty) b2p_io_upload(k);
+static inline void b2p_io_eval_with(Kern* k, IOSurfaceRef in) {
+  if (in->dirty || k->ioIn->uploaded != in) b2p_io_upload(k, in);
   if (b2p_eval((b2p_kernel*)k->model) != 0) b2p_io_fail("b2p_eval");
   k->ioOut->stale = 1;
+}
+
+static inline void ane_eval(Kern* k) { b2p_io_eval_with(k, k->ioIn); }
+
+/* A request binds another input surface to a compiled kernel, whose output goes
+ * to the kernel's ioOut (make_request, io.h:250-257). */
+static inline void* make_request(Kern* k, IOSurfaceRef ioIn) {
+  b2p_request* r = (b2p_request*)calloc(1, sizeof(b2p_request));
+  if (!r) b2p_io_fail("make_request (host memory)");
+  r->tag = B2P_IO_REQUEST_TAG;
+  r->kern = k;
+  r->in = ioIn;
+  return r;
+}
+
+static inline void ane_eval_req(Kern* k, void* request) {
+  b2p_request* r = (b2p_request*)request;
+  if (!r || r->tag != B2P_IO_REQUEST_TAG || r->kern != (void*)k) b2p_io_fail("ane_eval_req (request of another kernel)");
+  b2p_io_eval_with(k, r->in);
+}
+
+/* Compile a program from its MIL text (io.h:116-150). The tags of gen_dyn_matmul_mil
+ * compile to B2P_OP_DYN_MATMUL; ic_bytes / oc_bytes size the surfaces as in the
+ * reference and must match the program. Other programs, or a weights dictionary,
+ * are reported and give NULL, as a failed compile does there. */
+static inline Kern* compile_kern_mil_w(NSString* mil, NSDictionary* weights, int ic_bytes, int oc_bytes) {
+  int ic = 0, oc = 0, seq = 0;
+  if (!mil || weights || sscanf(mil, "dyn_matmul:%d:%d:%d", &ic, &oc, &seq) != 3) {
+    printf("  [compile] FAIL: this shim compiles only gen_dyn_matmul_mil programs without weights (got %s)\n",
+           mil ? mil : "NULL");
+    return NULL;
+  }
+  if ((long long)ic_bytes != (long long)ic * (seq + oc) * 2 || (long long)oc_bytes != (long long)oc * seq * 2) {
+    printf("  [compile] FAIL: surface sizes %d / %d do not match dyn_matmul %d x %d x %d\n", ic_bytes, oc_bytes, ic,
+           oc, seq);
+    return NULL;
+  }
+  b2p_op_desc d = b2p_io_desc(B2P_OP_DYN_MATMUL, ic, seq);
+  d.oc = oc;
+  return b2p_io_kern(&d, NULL, ic, seq + oc, oc, seq);
 }
 
 static inline void free_kern(Kern* k) {

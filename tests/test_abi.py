@@ -54,9 +54,10 @@ def test_missing_library_fails_loudly(tmp_path):
 def test_io_shim_header_compiles_as_c(tmp_path):
     """include/b2p_io.h builds as C11 with warnings as errors (no GPU work)."""
     import subprocess
-    src = Path(__file__).resolve().parent / "shim" / "conv_fused_site.c"
-    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", str(HEADER.parent),
-                    str(src)], check=True)
+    for name in ("conv_fused_site.c", "dyn_site.c"):
+        src = Path(__file__).resolve().parent / "shim" / name
+        subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", str(HEADER.parent),
+                        str(src)], check=True)
 
 
 def test_kern_compile_without_gpu_fails_loudly():

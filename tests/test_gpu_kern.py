@@ -292,3 +292,22 @@ def test_io_shim_call_site_compiles_and_matches(b2p, tmp_path):
     h1, h3 = O.sgemm(h16(w["W1"]), h16(x2n)), O.sgemm(h16(w["W3"]), h16(x2n))
     ffn = O.sgemm(h16(w["W2"]), h16(h1 / (1.0 + np.exp(-h1)) * h3))
     close(x_io - h16(xc), ffn, 1e-2)
+
+
+def test_io_shim_dyn_matmul_requests_compile_and_match(b2p, tmp_path):
+    """compile_kern_mil_w / io_write_dyn / make_request / ane_eval_req / io_write_dyn_acts from C."""
+    so = tmp_path / "dyn.so"
+    subprocess.run(["gcc", "-std=c11", "-O2", "-Wall", "-Wextra", "-Werror", "-shared", "-fPIC", "-I",
+                    str(ROOT / "include"), str(ROOT / "tests" / "shim" / "dyn_site.c"), "-o", str(so),
+                    "-L", str(ROOT / "autoane_b200"), "-lb2p", f"-Wl,-rpath,{ROOT / 'autoane_b200'}"], check=True)
+    lib = C.CDLL(str(so))
+    rng = np.random.default_rng(23)
+    ic, oc, S = 960, 320, 256
+    a1, a2, a3 = rnd(rng, (ic, S)), rnd(rng, (ic, S)), rnd(rng, (ic, S))
+    w1, w2 = rnd(rng, (ic, oc), 0.02), rnd(rng, (ic, oc), 0.02)
+    out = np.zeros((4, oc, S), np.float32)
+    fp = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))  # noqa: E731
+    assert lib.site_dyn(fp(a1), fp(w1), fp(a2), fp(w2), fp(a3), ic, oc, S, fp(out)) == 0
+    # results pass through the fp16 output surface (io.h:109-114)
+    for got, (w, a) in zip(out, ((w1, a1), (w2, a2), (w2, a3), (w1, a1))):
+        close(got, h16(O.sgemm(h16(w).T, h16(a))), 1e-3)
