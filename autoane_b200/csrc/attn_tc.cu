@@ -11,20 +11,26 @@
 //
 // Per query head (one 128 x 64 Q tile):
 //   MMA warp:   S = Q·Kᵀ  (tcgen05.mma, M 128, N = keys, K 64) into TMEM
-//   softmax WG: reads S rows (one TMEM lane per thread), exact row max over the
-//               causal keys, P = exp2((s - max)·scale·log2e) written back to TMEM
-//               as 16-bit pairs over the consumed S columns, row sum l in fp32
-//   MMA warp:   O = P·V   (A = P from TMEM, B = V in shared memory, MN-major)
-//   softmax WG: O / l to 16 bit, 128-byte row stores; row log2-sum-exp saved
-//               for the backward.
-// Two TMEM buffers of 256 columns (S, then P in its first half and O at
-// column 128) and two softmax warpgroups alternate over the heads, so the
-// softmax of one head overlaps the MMAs of the next.
+//   softmax:    two warpgroups share the head, one per half of its keys (A: the
+//               first nkeys/2, B: the rest). Each reads its half of the S rows
+//               (one TMEM lane per thread), takes the row maximum over its causal
+//               keys; the two partial maxima meet in shared memory; each writes
+//               P = exp2((s - max)·scale·log2e) as 16-bit pairs into its own part
+//               of the consumed S columns (A at columns [0, nkeys/4), B at
+//               [nkeys/2, 3·nkeys/4)), and the partial row sums meet the same way
+//   MMA warp:   O = P·V   (A = P from TMEM, B = V in shared memory, MN-major),
+//               O at columns [192, 256) of the buffer
+//   softmax:    A writes output columns 0-31 of O / l, B columns 32-63, both in
+//               16 bit with 64-byte row stores; A saves the row log2-sum-exp for
+//               the backward.
+// Two TMEM buffers of 256 columns and two warpgroup pairs alternate over the
+// heads, so the softmax of one head overlaps the MMAs of the next; splitting a
+// head's keys halves the serial softmax path of its rows.
 //
-// Warps: 0 TMEM owner and TMA producer, 1 MMA issuer, 2-5 and 6-9 softmax
-// warpgroups (warp % 4 selects the warp's 32-lane TMEM quarter). The MMA
-// issuer polls its barriers and issues whichever of S(next) and P·V(oldest) is
-// ready first.
+// Warps: 0 TMEM owner and TMA producer, 1 MMA issuer, 2-9 the pair of buffer 0
+// (2-5 side A, 6-9 side B), 10-17 the pair of buffer 1 (warp % 4 selects the
+// warp's 32-lane TMEM quarter). The MMA issuer polls its barriers and issues
+// whichever of S(next) and P·V(oldest) is ready first.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -39,7 +45,9 @@ namespace {
 constexpr int kAtRows = 128;   // query rows per tile (UMMA M)
 constexpr int kAtHD = 64;      // head dim
 constexpr int kAtMaxKeys = 256;
-constexpr int kAtThreads = 320;
+constexpr int kAtThreads = 576;   // 2 + 16 warps
+constexpr int kAtSoftWarps = 8;    // per buffer: 4 on each half of the keys
+constexpr int kAtOCol = 192;       // O = P·V columns inside a 256-column buffer
 constexpr int kAtRing = 4;     // unit-id ring between the producer and the consumers
 constexpr int kAtBatch = 1;    // 32-key chunks per TMEM round trip in the softmax passes
 constexpr uint32_t kAtTmemCols = 512;
@@ -53,7 +61,8 @@ struct AtSmem {
   static constexpr int kBarOff = kVOff + 2 * kKV;
   static constexpr int kNumBars = 16 + 2 * kAtRing + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kTotal = kMiscOff + 64 + 1024;    // + 1024-byte alignment slack
+  static constexpr int kRedOff = kMiscOff + 64;           // [buffer][side][128] partial max, then sum
+  static constexpr int kTotal = kRedOff + 2 * 2 * 128 * 4 + 1024;  // + 1024-byte alignment slack
 };
 
 // MN-major operand tile written by TMA with 128-byte swizzle: each 128-byte row
@@ -211,13 +220,13 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);   // one arrive per softmax warp
+      mbar_init(&p_full[i], kAtSoftWarps);   // one arrive per softmax warp of the buffer
       mbar_init(&o_full[i], 1);
-      mbar_init(&t_empty[i], 4);
+      mbar_init(&t_empty[i], kAtSoftWarps);
     }
     for (int i = 0; i < kAtRing; ++i) {
       mbar_init(&u_full[i], 1);
-      mbar_init(&u_empty[i], 1 + 8);  // MMA thread + one arrive per softmax warp
+      mbar_init(&u_empty[i], 1 + 2 * kAtSoftWarps);  // MMA thread + one arrive per softmax warp
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -306,12 +315,13 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           const uint32_t info = b ? pv_info1 : pv_info0;
           const int kvs = (int)(info & 1u), nkeys = (int)(info >> 8);
           tc_fence_after();
-          const uint32_t o_tmem = tmem_base + b * 256 + 128;
+          const uint32_t o_tmem = tmem_base + b * 256 + kAtOCol;
           const uint32_t p_tmem = tmem_base + b * 256;
           const uint32_t v_base = smem_u32(sV + kvs * AtSmem::kKV);
+          const int nch = nkeys / 32;  // 16-key steps ks < nch hold side A's P, the rest side B's
           for (int ks = 0; ks < nkeys / 16; ++ks)
-            umma_f16_ts(o_tmem, p_tmem + ks * 8, sw128_mnmajor_desc(v_base + ks * 2048), idesc_o,
-                        ks > 0 ? 1u : 0u);
+            umma_f16_ts(o_tmem, p_tmem + ks * 8 + (ks >= nch ? nch * 8 : 0), sw128_mnmajor_desc(v_base + ks * 2048),
+                        idesc_o, ks > 0 ? 1u : 0u);
           umma_commit(&o_full[b]);
           if (info & 2u) umma_commit(&kv_empty[kvs]);
           ++t_p;
@@ -390,17 +400,19 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax / output warpgroups (warps 2-5, 6-9) ----------------
-    const int wg = (warp - 2) >> 2;      // buffer this group owns
-    const int quarter = warp & 3;        // TMEM lane quarter
-    const int r = quarter * 32 + lane;   // row inside the query tile
-    const int wt = threadIdx.x - 64 - wg * 128;  // 0..127 within the group
+    // ---------------- softmax / output warpgroup pairs (warps 2-9, 10-17) ----------------
+    const int wg = (warp - 2) >> 3;          // buffer this pair owns
+    const int side = ((warp - 2) >> 2) & 1;  // 0: first half of the keys, 1: second half
+    const int quarter = warp & 3;            // TMEM lane quarter
+    const int r = quarter * 32 + lane;       // row inside the query tile
+    const int wt = threadIdx.x - 64 - wg * 256;  // 0..255 within the pair
     const uint32_t bar_id = 1 + wg;
+    float* red = reinterpret_cast<float*>(smem + AtSmem::kRedOff) + wg * 256;  // [side][128]
     auto agree = [&](bool ok_wait) -> bool {
-      // every thread of the group takes the same continue/abort decision
-      named_bar_sync(bar_id, 128);
+      // every thread of the pair takes the same continue/abort decision
+      named_bar_sync(bar_id, 256);
       if (wt == 0) wg_abort[wg] = (*abort_flag || !ok_wait) ? 1u : 0u;
-      named_bar_sync(bar_id, 128);
+      named_bar_sync(bar_id, 256);
       return wg_abort[wg] == 0;
     };
     int t = 0;
@@ -415,6 +427,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const Unit un = decode_unit(u, a);
       const int qpos = un.qb * kAtRows + r;
       const int diag = un.qb * 4 + quarter;  // 32-key chunk holding this warp's diagonal
+      const int nch = un.nkeys / 32;
+      const int c_lo = side ? nch / 2 : 0, c_hi = side ? nch : nch / 2;  // this side's chunks
+      const int c_last = min(c_hi - 1, diag);                           // last causal chunk of the side
+      const int p_off = side ? nch * 8 : 0;  // P of chunk c at column 16c + p_off
       bool stop = false;
       for (int j = 0; j < gq; ++j, ++t) {
         if ((t & 1) != wg) continue;
@@ -426,90 +442,72 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         tc_fence_after();
         const uint32_t t_row = tmem_base + wg * 256 + ((uint32_t)(quarter * 32) << 16);
-        // pass 1: exact row maximum over the causal keys (chunks 0..diag). Chunks are
-        // loaded kAtBatch at a time back to back and waited for together (one TMEM
-        // round trip per batch); only the diagonal chunk is masked.
+        // pass 1: row maximum over this side's causal keys (only the diagonal chunk is
+        // masked); the two sides' maxima meet in shared memory
         float mx = -INFINITY;
-        for (int c0 = 0; c0 <= diag; c0 += kAtBatch) {
-          uint32_t v[kAtBatch][32];
-#pragma unroll
-          for (int q = 0; q < kAtBatch; ++q)
-            if (c0 + q <= diag) tmem_ld32(t_row + (c0 + q) * 32, v[q]);
-#pragma unroll
-          for (int q = 0; q < kAtBatch; ++q)
-            if (c0 + q <= diag) tmem_ld_wait_regs(v[q]);
-#pragma unroll
-          for (int q = 0; q < kAtBatch; ++q) {
-            if (c0 + q < diag)
-              mx = chunk_max<false>(v[q], mx, 0, 0);
-            else if (c0 + q == diag)
-              mx = chunk_max<true>(v[q], mx, (c0 + q) * 32, qpos);
-          }
+        for (int c = c_lo; c <= c_last; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_row + c * 32, v);
+          tmem_ld_wait_regs(v);
+          mx = c < diag ? chunk_max<false>(v, mx, 0, 0) : chunk_max<true>(v, mx, c * 32, qpos);
         }
-        // pass 2: P = exp2((s - max)·scale) as 16-bit pairs over the consumed S columns
-        // (chunk c goes to columns [16c, 16c + 16), all read by the time it is stored),
-        // then zeros past the diagonal.
+        red[side * 128 + r] = mx;
+        named_bar_sync(bar_id, 256);
+        mx = fmaxf(mx, red[(side ^ 1) * 128 + r]);
+        // pass 2: P = exp2((s - max)·scale) as 16-bit pairs, chunk c at columns
+        // [16c + p_off, +16) (this side's own S columns, read before they are written),
+        // zeros past the diagonal
         const float ms = mx * scale_log2;
         float l = 0.f;
-        for (int c0 = 0; c0 <= diag; c0 += kAtBatch) {
-          uint32_t v[kAtBatch][32];
-#pragma unroll
-          for (int q = 0; q < kAtBatch; ++q)
-            if (c0 + q <= diag) tmem_ld32(t_row + (c0 + q) * 32, v[q]);
-#pragma unroll
-          for (int q = 0; q < kAtBatch; ++q)
-            if (c0 + q <= diag) tmem_ld_wait_regs(v[q]);
-#pragma unroll
-          for (int q = 0; q < kAtBatch; ++q) {
-            uint32_t pk[16];
-            if (c0 + q < diag) {
-              chunk_exp<T, false>(v[q], pk, l, scale_log2, ms, 0, 0);
-              tmem_st16(t_row + (c0 + q) * 16, pk);
-            } else if (c0 + q == diag) {
-              chunk_exp<T, true>(v[q], pk, l, scale_log2, ms, (c0 + q) * 32, qpos);
-              tmem_st16(t_row + (c0 + q) * 16, pk);
-            }
-          }
+        for (int c = c_lo; c <= c_last; ++c) {
+          uint32_t v[32];
+          uint32_t pk[16];
+          tmem_ld32(t_row + c * 32, v);
+          tmem_ld_wait_regs(v);
+          if (c < diag)
+            chunk_exp<T, false>(v, pk, l, scale_log2, ms, 0, 0);
+          else
+            chunk_exp<T, true>(v, pk, l, scale_log2, ms, c * 32, qpos);
+          tmem_st16(t_row + c * 16 + p_off, pk);
         }
         {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = 0u;
-          for (int c = diag + 1; c < un.nkeys / 32; ++c) tmem_st16(t_row + c * 16, pk);
+          for (int c = max(c_lo, diag + 1); c < c_hi; ++c) tmem_st16(t_row + c * 16 + p_off, pk);
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[wg]);
+        // the partial sums meet (both sides read the maxima before this barrier)
+        named_bar_sync(bar_id, 256);
+        red[side * 128 + r] = l;
+        named_bar_sync(bar_id, 256);
+        l += red[(side ^ 1) * 128 + r];
         const long long row = (long long)un.g * a.seq + qpos;
-        // output: O / l
+        // output: this side's 32 columns of O / l
         if (!agree(mbar_wait(&o_full[wg], n, abort_flag, status, DEV_TIMEOUT_EPILOGUE))) {
           stop = true;
           break;
         }
         tc_fence_after();
-        // O / l in two 32-column halves; the buffer is released after the second load
-        if (a.lse) a.lse[row * a.heads + h] = ms + log2f(l);
+        if (a.lse && side == 0) a.lse[row * a.heads + h] = ms + log2f(l);
         const float inv = 1.0f / l;
-        T* out = static_cast<T*>(a.out) + row * a.ld_out + h * kAtHD;
+        T* out = static_cast<T*>(a.out) + row * a.ld_out + h * kAtHD + side * 32;
+        uint32_t o[32];
+        tmem_ld32(t_row + kAtOCol + side * 32, o);
+        tmem_ld_wait_regs(o);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&t_empty[wg]);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t o[32];
-          tmem_ld32(t_row + 128 + half * 32, o);
-          tmem_ld_wait_regs(o);
-          if (half == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&t_empty[wg]);
-          }
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w[e] = pack_h2<T>(__uint_as_float(o[c * 8 + 2 * e]) * inv, __uint_as_float(o[c * 8 + 2 * e + 1]) * inv);
-            *reinterpret_cast<uint4*>(out + half * 32 + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
+          for (int e = 0; e < 4; ++e)
+            w[e] = pack_h2<T>(__uint_as_float(o[c * 8 + 2 * e]) * inv, __uint_as_float(o[c * 8 + 2 * e + 1]) * inv);
+          *reinterpret_cast<uint4*>(out + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       if (stop) break;

@@ -279,6 +279,28 @@ def run_reference(args):
     return 0
 
 
+def rank_checks(model, dev_ms_local: float, steps: int, world: int, dev):
+    """N > 1 only, called by every rank at the same point: each rank's device ms per step
+    (the spread between ranks separates skew from the collective's own cost) and a
+    bit-identity check of the trainable parameters across ranks (SHA-256 of θ)."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return None
+    t = torch.tensor([dev_ms_local / steps], device=dev, dtype=torch.float64)
+    allt = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(allt, t)
+    digest = hashlib.sha256(model.get_trainable().tobytes()).digest()[:8]
+    hv = torch.tensor([int.from_bytes(digest, "little", signed=True)], device=dev, dtype=torch.int64)
+    allh = [torch.zeros_like(hv) for _ in range(world)]
+    dist.all_gather(allh, hv)
+    ms = [float(x.item()) for x in allt]
+    return {"rank_ms_per_step": {"min": round(min(ms), 4), "max": round(max(ms), 4)},
+            "theta_identical_across_ranks": len({int(x.item()) for x in allh}) == 1}
+
+
 def workload_config(world: int, ffn: bool = False):
     adapters = "adapters on Wq/Wk/Wv/Wo/W1/W2/W3 (--lora-ffn)" if ffn else "adapters on Wq/Wk/Wv/Wo"
     return {"workload": "DP MeZO-LoRA-split r8, SmolLM2-360M shapes (32L, d960, 15/5 heads, FFN 2560, "
@@ -415,6 +437,8 @@ def main():
         model.sync()
         torch.cuda.synchronize()
         barrier()
+        clocks_e2e = ClockSampler(phys)
+        clocks_e2e.start()
         t0 = time.perf_counter()
         for s in range(K):
             seeds = step_seeds(10_000 + s, world)
@@ -430,7 +454,9 @@ def main():
         model.sync()
         torch.cuda.synchronize()
         e2e_s = time.perf_counter() - t0
+        clk_e2e = clocks_e2e.stop()
         barrier()
+        ranks = rank_checks(model, dev_ms, K, world, dev)
 
     # max over ranks
     t = torch.tensor([dev_ms, e2e_s, gemm_ms], device=dev, dtype=torch.float64)
@@ -471,12 +497,18 @@ def main():
                     "tflops_per_gpu": round(2 * SEQS_PER_GPU * SEEDS_PER_GPU * fwd_flops_per_seq(args.lora_ffn) * K /
                                             (dev_ms / 1000.0) / 1e12, 2)},
                 "e2e": {"value": round(e2e_value, 3), "unit": "seq-steps/s", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h},
+                        "d2h_bytes_per_step": d2h,
+                        "sm_mhz": clk_e2e["sm_mhz"] if clk_e2e else None},
                 "gpu_launches": n_launch, "roofline": roofline, "clocks": clk, "cpu_baseline": cpu}
+        if ranks:
+            line["ranks"] = ranks
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:
         dist.destroy_process_group()
+    if ranks and not ranks["theta_identical_across_ranks"]:
+        print("ERROR: the trainable parameters differ between ranks", file=sys.stderr)
+        return 1
     return 0
 
 
@@ -619,6 +651,7 @@ def run_p16(args):
         torch.cuda.synchronize()
         e2e_s = time.perf_counter() - t0
         barrier()
+        ranks = rank_checks(model, dev_ms, K, world, dev)
     t = torch.tensor([dev_ms, e2e_s, gemm_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -651,10 +684,15 @@ def run_p16(args):
                         "h2d_bytes_per_step": 2 * NSEQ * DIMS["seq"] * 4 + 2 * cfg.max_groups * 4 + 16,
                         "d2h_bytes_per_step": 4},
                 "gpu_launches": n_launch, "roofline": roofline, "clocks": clk, "cpu_baseline": cpu}
+        if ranks:
+            line["ranks"] = ranks
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:
         dist.destroy_process_group()
+    if ranks and not ranks["theta_identical_across_ranks"]:
+        print("ERROR: the trainable parameters differ between ranks", file=sys.stderr)
+        return 1
     return 0
 
 

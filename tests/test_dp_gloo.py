@@ -109,3 +109,49 @@ def test_two_gloo_ranks_stay_identical_and_match_serial_update():
         assert np.array_equal(pairs, p0[step])
         ref.mezo_update(seeds, pairs, 1e-3, 1e-3)
     assert np.array_equal(ref.theta.view(np.uint32), th0.view(np.uint32))
+
+
+class _ThetaModel:
+    def __init__(self, theta):
+        self.theta = theta
+
+    def get_trainable(self):
+        return self.theta
+
+
+def checks_worker(rank, world, port, q, diverge):
+    """bench.rank_checks on gloo ranks: rank 1 perturbs one parameter by one ulp when `diverge`."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    try:
+        import bench
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        theta = np.linspace(-1, 1, 1001, dtype=np.float32)
+        if diverge and rank == 1:
+            theta[500] = np.nextafter(theta[500], np.float32(2))
+        out = bench.rank_checks(_ThetaModel(theta), 100.0 + 10.0 * rank, 10, world, torch.device("cpu"))
+        q.put((rank, out))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("diverge", [False, True])
+def test_bench_rank_checks_detect_diverged_replicas(diverge):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=checks_worker, args=(r, 2, port, q, diverge)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in range(2)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+    for r, out in res:
+        assert isinstance(out, dict), f"rank {r}: {out}"
+        assert out["rank_ms_per_step"] == {"min": 10.0, "max": 11.0}
+        assert out["theta_identical_across_ranks"] is (not diverge)

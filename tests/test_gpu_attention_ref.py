@@ -7,13 +7,14 @@ around them (training/backprop_lora.h:241-252), from oracle/_ref.
 Inputs are fp16-representable, so both sides see the same Q, K, V and dO. The
 device keeps P, dS and its outputs in 16 bit with fp32 accumulation; the tolerance
 is normwise relative L2 per tensor (||dev - ref|| / ||ref||):
-  * forward output O: < 2e-3 (16-bit P and O: unit roundoff 4.9e-4, summed over
-    <= 256 keys with random signs);
-  * dV, dK, dQ: < 1e-2 (16-bit P and dS operands of four chained products, and
+  * forward output O: < 1e-3 (16-bit P and O: unit roundoff 4.9e-4, averaged over
+    up to 256 keys; measured 2.3e-4);
+  * dV, dK, dQ: < 2e-3 (16-bit P and dS operands of four chained products, and
     the dS = P·(dP - D) cancellation, which grows the relative error of small dS
-    entries; a 2-4% error in any one product would fail).
+    entries; measured 2.9-3.9e-4; a wrong term in any one product fails by far).
 Cases: SmolLM2-360M heads (15 query / 5 KV, theta 100000) at 256 and 128 tokens, fp16,
-over 3 sequences (tcgen05 kernels), plus one bf16 case at < 2e-2 (8-bit mantissa).
+over 3 sequences (tcgen05 kernels), plus one bf16 case at < 5e-3 / 1e-2 (8-bit mantissa;
+measured 1.8e-3 / 3.0e-3).
 """
 import ctypes as C
 
@@ -54,8 +55,8 @@ def rel(a, b):
     return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b.astype(np.float64)))
 
 
-@pytest.mark.parametrize("seq,dtype,tol_o,tol_g", [(256, 0, 2e-3, 1e-2), (128, 0, 2e-3, 1e-2),
-                                                   (256, 1, 1e-2, 2e-2)],
+@pytest.mark.parametrize("seq,dtype,tol_o,tol_g", [(256, 0, 1e-3, 2e-3), (128, 0, 1e-3, 2e-3),
+                                                   (256, 1, 5e-3, 1e-2)],
                          ids=["seq256_f16", "seq128_f16", "seq256_bf16"])
 def test_attention_matches_reference_sdpa(b2p, seq, dtype, tol_o, tol_g):
     ref = O.ref_lib("smollm2_360m")  # ROPE_THETA 100000 compiled in (training/models/smollm2_360m.h)

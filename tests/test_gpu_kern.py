@@ -9,7 +9,7 @@ intermediates named in each test. Tolerances are relative to the output's
 largest magnitude:
   * plain projections (fp32 accumulate, fp32 out): 1e-5
   * LoRA (16-bit A·x and perturbed B operands):    2e-3
-  * FFN (16-bit gate between the two GEMMs):       4e-3
+  * FFN (16-bit gate between the two GEMMs):       1e-3 (measured 8e-5 - 1.2e-4)
   * cross-entropy: |ΔL| < 1e-3 nats
 """
 import ctypes as C
@@ -169,7 +169,7 @@ def test_ffn_fused_matches_oracle(b2p, S, alpha):
     h1, h3 = O.sgemm(h16(W1), h16(xn)), O.sgemm(h16(W3), h16(xn))
     gate = h16(h1 / (1.0 + np.exp(-h1)) * h3)
     ref = (xc + np.float32(alpha) * O.sgemm(h16(W2), gate)).astype(np.float32)
-    close(y - xc, ref - xc, 4e-3)
+    close(y - xc, ref - xc, 1e-3)
     # eval is repeatable: the residual input is not consumed
     KN.ane_eval(k)
     close(KN.io_read_dyn(k), y, 0.0)
@@ -291,7 +291,12 @@ def test_io_shim_call_site_compiles_and_matches(b2p, tmp_path):
     close(oo, O.sgemm(h16(w["Wo"]), h16(attn)), 1e-3)
     h1, h3 = O.sgemm(h16(w["W1"]), h16(x2n)), O.sgemm(h16(w["W3"]), h16(x2n))
     ffn = O.sgemm(h16(w["W2"]), h16(h1 / (1.0 + np.exp(-h1)) * h3))
-    close(x_io - h16(xc), ffn, 1e-2)
+    # x_cur comes back through the fp16 surface (io_read_dyn, io.h:109-114): every element
+    # is the fp16 rounding of x + FFN(x), so it may differ from the rounded oracle value by
+    # at most one fp16 ulp (the FFN itself is checked unrounded above at 1e-3)
+    ref16 = h16(h16(xc) + ffn)
+    ulp = np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float32)
+    assert np.all(np.abs(x_io - ref16) <= ulp), np.max(np.abs(x_io - ref16) / ulp)
 
 
 def test_io_shim_dyn_matmul_requests_compile_and_match(b2p, tmp_path):

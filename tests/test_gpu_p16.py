@@ -5,8 +5,15 @@ Tolerances (fp16 compute, 16-bit activations and gradient operands, fp32
 accumulation and fp32 residual-stream gradients):
   * loss: |L_gpu - L_oracle| < 1e-3 nats (2e-3 for bf16)
   * gradient, per parameter block (each A, B, RMS vector of each layer):
-    relative L2 error < 5e-2 and cosine similarity > 0.998 (fp16);
-    < 1e-1 and > 0.99 for bf16 (8-bit mantissa)
+    relative L2 error < 1e-2 and cosine similarity > 0.9999 (fp16);
+    < 5e-2 and > 0.999 for bf16 (8-bit mantissa).
+    Budget: every backward GEMM and the attention backward take 16-bit operands
+    (unit roundoff u = 2^-11 for fp16), so each block's gradient carries the
+    relative error of a chain of about ten rounded products, which adds like a
+    random walk: a few u (~2e-3) per layer pair, growing with depth. Measured on
+    B200: 2.0-2.3e-3 on 2-layer models, 4.6e-3 worst block at SmolLM2-360M's 32
+    layers (cos 0.99999), 1.6e-2 for bf16 (u = 2^-8). A wrong term in any one
+    backward kernel moves its blocks by 1e-1 or more.
   * Adam: bit-exact against the oracle given the device's own gradient.
 """
 import numpy as np
@@ -70,7 +77,7 @@ def test_p16_grad_one_sequence_matches_oracle(small):
     loss, grad = model.p16_grad(inp[None], tgt[None])
     rloss, rgrad = om.p16_grad(syn.theta, inp, tgt)
     assert abs(loss - rloss) < 1e-3, (loss, rloss)
-    compare_grads(cfg, syn.layout, grad, rgrad, 5e-2, 0.998)
+    compare_grads(cfg, syn.layout, grad, rgrad, 1e-2, 0.9999)
     # the gradient call leaves the parameters untouched
     assert np.array_equal(model.get_trainable().view(np.uint32), syn.theta.view(np.uint32))
 
@@ -85,7 +92,7 @@ def test_p16_grad_batch_is_mean_of_sequences(small):
     rloss = np.mean([r[0] for r in refs])
     rgrad = np.mean([r[1] for r in refs], axis=0).astype(np.float32)
     assert abs(loss - rloss) < 1e-3, (loss, rloss)
-    compare_grads(cfg, syn.layout, grad, rgrad, 5e-2, 0.998)
+    compare_grads(cfg, syn.layout, grad, rgrad, 1e-2, 0.9999)
 
 
 def test_adam_step_bit_exact_against_oracle(small):
@@ -133,7 +140,7 @@ def test_gradient_scale_option_is_transparent(small):
     model.set_option(OPT_GRAD_SCALE_LOG2, 4)
     _, g4 = model.p16_grad(inp[None], tgt[None])
     model.set_option(OPT_GRAD_SCALE_LOG2, 0)
-    compare_grads(cfg, syn.layout, g4, g0, 2e-2, 0.9995)
+    compare_grads(cfg, syn.layout, g4, g0, 5e-3, 0.99999)
 
 
 def test_p16_gqa_autoresearch_shapes(b2p):
@@ -144,7 +151,7 @@ def test_p16_gqa_autoresearch_shapes(b2p):
     loss, grad = model.p16_grad(inp[None], tgt[None])
     rloss, rgrad = om.p16_grad(syn.theta, inp, tgt)
     assert abs(loss - rloss) < 1e-3, (loss, rloss)
-    compare_grads(cfg, syn.layout, grad, rgrad, 5e-2, 0.998)
+    compare_grads(cfg, syn.layout, grad, rgrad, 1e-2, 0.9999)
     model.close()
 
 
@@ -155,7 +162,7 @@ def test_p16_bf16_close(b2p):
     loss, grad = model.p16_grad(inp[None], tgt[None])
     rloss, rgrad = om.p16_grad(syn.theta, inp, tgt)
     assert abs(loss - rloss) < 2e-3, (loss, rloss)
-    compare_grads(cfg, syn.layout, grad, rgrad, 1e-1, 0.99)
+    compare_grads(cfg, syn.layout, grad, rgrad, 5e-2, 0.999)
     model.close()
 
 
@@ -169,7 +176,7 @@ def test_p16_full_smollm2_360m_gradient(b2p):
     print(f"P16 SmolLM2-360M loss gap {abs(loss - rloss):.3e}")
     assert abs(loss - rloss) < 1e-3, (loss, rloss)
     assert 9.0 < loss < 10.5
-    compare_grads(cfg, syn.layout, grad, rgrad, 5e-2, 0.998)
+    compare_grads(cfg, syn.layout, grad, rgrad, 1e-2, 0.9999)
     model.close()
 
 
