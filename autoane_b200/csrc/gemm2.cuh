@@ -410,6 +410,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const int row = m0 + row_in_tile;
       const bool row_ok = row < M;
 
+      // RoPE factors of this row for the tile, loaded while the tile's MMAs run: with head_dim
+      // 64 every chunk of this warp (chunks half, half + 2, ...) covers the same half of the 32
+      // frequencies, ((n0 / 32) + half) % 2 (the tables hold 64 KB, more than the L1 left beside
+      // the pipeline's shared memory, so per-chunk loads would each go to L2)
+      float rcs[16], rsn[16];
+      if (KIND == EPI_QKV_ROPE) {
+        const int pos = (m0 % ep.seq_len) + row_in_tile;
+        const int fh = ((n0 >> 5) + half) & 1;
+        const float4* cs4 = reinterpret_cast<const float4*>(ep.rope_cos + (long long)pos * 32 + 16 * fh);
+        const float4* sn4 = reinterpret_cast<const float4*>(ep.rope_sin + (long long)pos * 32 + 16 * fh);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 c4 = __ldg(cs4 + q), s4 = __ldg(sn4 + q);
+          rcs[4 * q] = c4.x; rcs[4 * q + 1] = c4.y; rcs[4 * q + 2] = c4.z; rcs[4 * q + 3] = c4.w;
+          rsn[4 * q] = s4.x; rsn[4 * q + 1] = s4.y; rsn[4 * q + 2] = s4.z; rsn[4 * q + 3] = s4.w;
+        }
+      }
+
       mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, ep.status, DEV_TIMEOUT_EPILOGUE);
       named_bar_sync(2, 32 * kEpiWarps);
       if (et == 0) *epi_abort = *abort_flag;
@@ -421,13 +439,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       float ce_m = -INFINITY, ce_s = 0.f;
       int tgt = -1;
       if (KIND == EPI_CE && row_ok) tgt = ep.targets[row];
-      const float* rope_cs_row = nullptr;
-      const float* rope_sn_row = nullptr;
-      if (KIND == EPI_QKV_ROPE) {
-        const int pos = (m0 % ep.seq_len) + row_in_tile;
-        rope_cs_row = ep.rope_cos + (long long)pos * 32;
-        rope_sn_row = ep.rope_sin + (long long)pos * 32;
-      }
 
 #pragma unroll 1
       for (int ch = half; ch < nch; ch += 2) {
@@ -473,19 +484,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           continue;
         }
         if (KIND == EPI_QKV_ROPE && col < ep.rope_cols) {
-          const float4* cs4 = reinterpret_cast<const float4*>(rope_cs_row + ((col & 63) >> 1));
-          const float4* sn4 = reinterpret_cast<const float4*>(rope_sn_row + ((col & 63) >> 1));
+          // head_dim 64: the chunk covers frequency indices 16·fh .. 16·fh + 15 of one head
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 c4 = __ldg(cs4 + q), s4 = __ldg(sn4 + q);
-            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = 8 * q + 2 * e;
-              const float v0 = v[c], v1 = v[c + 1];
-              v[c] = v0 * cs[e] - v1 * sn[e];
-              v[c + 1] = v0 * sn[e] + v1 * cs[e];
-            }
+          for (int i = 0; i < 16; ++i) {
+            const float v0 = v[2 * i], v1 = v[2 * i + 1];
+            v[2 * i] = v0 * rcs[i] - v1 * rsn[i];
+            v[2 * i + 1] = v0 * rsn[i] + v1 * rcs[i];
           }
         }
         if (KIND == EPI_RESID) {

@@ -293,10 +293,11 @@ def test_io_shim_call_site_compiles_and_matches(b2p, tmp_path):
     ffn = O.sgemm(h16(w["W2"]), h16(h1 / (1.0 + np.exp(-h1)) * h3))
     # x_cur comes back through the fp16 surface (io_read_dyn, io.h:109-114): every element
     # is the fp16 rounding of x + FFN(x), so it may differ from the rounded oracle value by
-    # at most one fp16 ulp (the FFN itself is checked unrounded above at 1e-3)
+    # one fp16 ulp plus the FFN's own error (gated at 1e-3 of its largest value, as above)
     ref16 = h16(h16(xc) + ffn)
     ulp = np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float32)
-    assert np.all(np.abs(x_io - ref16) <= ulp), np.max(np.abs(x_io - ref16) / ulp)
+    bound = ulp + 1e-3 * np.max(np.abs(ffn))
+    assert np.all(np.abs(x_io - ref16) <= bound), np.max(np.abs(x_io - ref16) / bound)
 
 
 def test_io_shim_dyn_matmul_requests_compile_and_match(b2p, tmp_path):
