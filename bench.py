@@ -176,13 +176,25 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU reference / baseline
-def cpu_reference_rate(max_seconds: float = 20.0, max_steps: int = 6, min_steps: int = 2, weights=None, embed=None):
+def host_cores():
+    """(logical CPUs, physical cores) of this host."""
+    try:
+        import psutil
+        phys = psutil.cpu_count(logical=False)
+    except Exception:
+        phys = None
+    return os.cpu_count() or 1, phys
+
+
+def cpu_reference_rate(max_seconds: float = 20.0, max_steps: int = 6, min_steps: int = 2, weights=None, embed=None,
+                       threads: int | None = None):
     """MeZO-LoRA-split steps/s of the CPU reference path on this host's cores (one step = one seq-step).
 
     Uses the reference's own cpu_ops.h compiled from the AutoANE sources (oracle/_ref) for the
-    forward when that library was built, otherwise the oracle restatement (oracle/liboracle.so)."""
+    forward when that library was built, otherwise the oracle restatement (oracle/liboracle.so).
+    `threads` BLAS threads (default: every logical CPU)."""
     from oracle import oracle as O
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     O.set_threads(threads)
     cfg = O.ModelCfg(dim=DIMS["dim"], hidden=DIMS["hidden"], heads=DIMS["heads"], kv_heads=DIMS["kv_heads"],
                      hd=DIMS["head_dim"], seq=DIMS["seq"], nlayers=DIMS["nlayers"], vocab=DIMS["vocab"],
@@ -488,6 +500,10 @@ def main():
         cpu = None
         if keep_cpu:
             cpu = cpu_reference_rate(weights=cpu_w, embed=embed)
+            one = cpu_reference_rate(max_seconds=25.0, max_steps=3, min_steps=1, weights=cpu_w, embed=embed, threads=1)
+            logical, physical = host_cores()
+            cpu |= {"cores_logical": logical, "cores_physical": physical,
+                    "one_core": {"value": one["value"], "unit": one["unit"], "cores": 1, "sample": one["sample"]}}
         line = {"metric": "MeZO-LoRA steps/s SmolLM2-360M @1/2/4/8 B200; proj-GEMM % of TC peak",
                 "value": round(value, 3), "unit": "seq-steps/s", "n_gpus": world, "steps": K, "warmup": W,
                 "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "weak",
