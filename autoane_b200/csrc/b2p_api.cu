@@ -37,6 +37,11 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
   DeviceCtx* c = nullptr;
   int rc = ctx_get(&c);
   if (rc) return rc;
+  if (splitk_preferred(kind, M, N, K, c->num_sms))
+    return launch_gemm_splitk(kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, static_cast<cudaStream_t>(stream));
+  if (M >= 2 * kBM && pair_supported(kind, M, N, ep))
+    return launch_gemm_pair(kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, nullptr, ep,
+                            static_cast<cudaStream_t>(stream));
   return launch_gemm(pick_bn_rows(M, N, kind, c->num_sms), kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy,
                      nullptr, ep, static_cast<cudaStream_t>(stream));
 }

@@ -108,6 +108,16 @@ bool pair_supported(int kind, int M, int N, const EpiParams& ep);
 int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                      void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
 
+// Plain fp32 / 16-bit output GEMMs of at most 1024 rows whose 128 x 64 tiles fit one wave
+// (gemm_sk.cu): each tile's K loop is split over a cluster of up to 4 CTAs, partial sums
+// added in rank order over distributed shared memory. splitk_applies() tells whether a
+// launch qualifies.
+bool splitk_applies(int kind, int M, int N, int num_sms);
+// Whether the split-K kernel is the faster choice for this shape (measured rule, gemm_sk.cu).
+bool splitk_preferred(int kind, int M, int N, int K, int num_sms);
+int launch_gemm_splitk(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                       void* out, int ldo, cudaStream_t st);
+
 // Pick the tile width for an N-column output (largest width whose padding
 // waste is minimal; SwiGLU and CE need multiples of 64 / any).
 int pick_bn(int N, int kind);

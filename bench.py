@@ -970,7 +970,8 @@ def run_gemm_sweep(args):
             M8 = (M + 7) // 8 * 8
             wc = [torch.cat([w, torch.zeros(M8 - M, K, device=dev, dtype=dt)]) if M8 > M else w for w in ws]
             cs = [torch.empty(T, M8, device=dev, dtype=dt) for _ in range(ncopy)]
-            fn = "b2p_gemm_pair" if T >= 256 else "b2p_gemm"
+            # up to 1024 rows b2p_gemm splits each tile's K loop over a cluster; above, the CTA-pair engine
+            fn = "b2p_gemm" if T <= 1024 else "b2p_gemm_pair"
 
             def ours(i, f32=True):
                 st = torch.cuda.current_stream().cuda_stream

@@ -66,6 +66,11 @@ int b2p_device_status(void* stream);
  * row pitch ldy elements. This is the device-resident form of the reference's
  * cblas_sgemm projection call sites (training/train_mezo.m:1533-1538) in the
  * transposed, token-major layout: X holds tokens as rows, W output channels.
+ * Up to 1024 rows, when the 128 x 64 output tiles fit one wave and the split
+ * pays (at most two ways, or K >= 2048), the K loop of each tile is split over
+ * a cluster of CTAs (partial sums added in a fixed order, so results repeat
+ * bit for bit); otherwise the CTA-pair engine (M >= 256) or the persistent
+ * single-CTA engine runs it.
  * Asynchronous on `stream` (NULL = default stream). */
 int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
              void* stream);

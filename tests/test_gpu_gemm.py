@@ -1,6 +1,8 @@
 """Tile-engine GEMM parity on the B200: Y = X·W^T against a torch fp32 matmul of
 the same 16-bit inputs (tolerance: normwise max|err|/max|ref| < 2e-3 for fp16,
-8e-3 for bf16 outputs stored in 16 bit)."""
+8e-3 for bf16 outputs stored in 16 bit). b2p_gemm runs up to 1024 rows on the
+cluster split-K kernel (gemm_sk.cu), above on the persistent single-CTA engine;
+b2p_gemm_pair on the CTA-pair engine."""
 import pytest
 import torch
 
@@ -11,6 +13,7 @@ pytestmark = pytest.mark.gpu
 SHAPES = [
     (128, 128, 64), (256, 960, 960), (256, 320, 960), (384, 1600, 960), (256, 2560, 960),
     (256, 960, 2560), (200, 1000, 72), (1024, 16893, 960), (8192, 960, 960), (130, 48, 40),
+    (100, 320, 2560), (1000, 2560, 960), (1025, 960, 960),
 ]
 
 
@@ -66,3 +69,17 @@ def test_pair_gemm_matches_fp32(b2p, M, N, K, dt, out_f32):
     err = (y - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
     tol = 2e-3 if (out_f32 or dt == "f16") else 8e-3
     assert err < tol, f"normwise error {err:.3e} (M={M} N={N} K={K} {dt} out_f32={out_f32})"
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 960, 960), (100, 320, 2560), (128, 2560, 960)])
+def test_split_k_is_repeatable(b2p, M, N, K):
+    """The cluster split-K kernel adds its partial sums in a fixed rank order: two calls give
+    the same bits (and so do the fp32 and 16-bit paths after rounding the fp32 result)."""
+    torch.manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda").half()
+    w = (0.02 * torch.randn(N, K, device="cuda")).half()
+    a = run_gemm(x, w, 1, 0)
+    b = run_gemm(x, w, 1, 0)
+    assert torch.equal(a, b)
+    h = run_gemm(x, w, 0, 0)
+    assert torch.equal(h, a.half().float())
