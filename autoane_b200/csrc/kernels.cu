@@ -372,285 +372,370 @@ __global__ void __launch_bounds__(256, 2) norm_lora_mma_kernel(NormLoraArgs a) {
   }
 }
 
-// LoRA-down of a 16-bit input (no norm) with prepared per-variant A rows, as a
-// persistent kernel: every CTA takes a contiguous range of RT-row tiles, keeps the
-// copies of the next STAGES - 1 tiles in flight (cp.async ring) while the current one
-// is multiplied, and splits each tile's K (= dim) over its 8 warps (mma.sync
-// m16n8k16, fp32), summing the warps' partials in a fixed order. A rows are restaged
-// only when the tile's variant changes (a contiguous range crosses few variant groups).
-template <int NP, int RT, int NA, int STAGES>
-struct LdSmem {
-  static constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, MT = RT / 16;
-  static constexpr int kX = RT * XS * 2;            // one x tile (16-bit)
-  static constexpr int kA = NT * 8 * XS * 2;        // A rows (16-bit, zero padded to whole n-tiles)
-  static constexpr int kRed = 8 * RT * NT * 8 * 4;  // per-warp partial U
-  static constexpr int kTotal = STAGES * kX + kA + kRed;
-};
+// ---------------------------------------------------------------------------
+// Persistent LoRA-down kernels with prepared operands. Each CTA takes a
+// contiguous range of 16-row tiles; loader warps fill a ring of 16-bit tiles in
+// shared memory (full/empty mbarriers with bounded waits) and LoRA warps take
+// whole tiles from it in turn, U = X · A^T over the full K with mma.sync
+// m16n8k16 (fp32 accumulation), rounded to 16 bit like the U operand of the
+// LoRA-up tensor-core step that consumes it. No CTA-wide barrier inside the loop.
+//
+// Variant operands: the range meets groups g0 .. g0 + k_last (group = row /
+// group_rows); group g0 + k uses operand slot k % VS. Slots 0 .. VS-1 are staged
+// at the start; at the first tile of a group k >= VS the role that reads a slot
+// meets on its own named barrier (all of its tiles before that group are done,
+// so nobody still reads group k - VS), restages the slot and meets again.
+// ---------------------------------------------------------------------------
 
-template <int NP, typename T, int NA, int RT, int STAGES>
-__global__ void __launch_bounds__(256, 1) lora_down_kernel(NormLoraArgs a) {
-  using S = LdSmem<NP, RT, NA, STAGES>;
-  constexpr int dim = S::dim, XS = S::XS, NT = S::NT, MT = S::MT, KS = dim / 16;
-  extern __shared__ __align__(16) uint8_t smx[];
-  T* s_x = reinterpret_cast<T*>(smx);                              // [STAGES][RT][XS]
-  T* s_a = reinterpret_cast<T*>(smx + STAGES * S::kX);             // [NT*8][XS]
-  float* s_red = reinterpret_cast<float*>(smx + STAGES * S::kX + S::kA);  // [8][RT][NT*8]
-  pdl_enter();
-  const int ntiles = (a.rows + RT - 1) / RT;
-  const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
-  const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
-  if (t_begin >= t_end) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t sx0 = smem_u32(s_x), sab = smem_u32(s_a);
-
-  auto load_x = [&](int tile, int buf) {
-    const int row0 = tile * RT;
-    for (int i = threadIdx.x; i < RT * (dim / 8); i += 256) {
-      const int r = i / (dim / 8), c8 = i - r * (dim / 8);
-      const int row = row0 + r;
-      if (row < a.rows)
-        cp_async16(sx0 + (uint32_t)(((buf * RT + r) * XS + c8 * 8) * 2),
-                   static_cast<const T*>(a.in) + (long long)row * dim + c8 * 8);
-      else
-        *reinterpret_cast<uint4*>(s_x + (buf * RT + r) * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  // prologue: tiles t_begin .. t_begin + STAGES - 2 in flight (one commit group each)
+// One warp's 16 x (8 NT) product over K = 16 KS: X rows at sxb, A rows at sab (16-bit,
+// row pitch XS elements, conflict-free ldmatrix). K-step kk accumulates into chain
+// kk % 4 (four independent mma dependency chains); the chains are added at the end
+// as (c0 + c1) + (c2 + c3).
+template <typename T, int NT, int KS, int XS>
+__device__ __forceinline__ void warp_tile_down(uint32_t sxb, uint32_t sab, int lane, float (&c)[NT][4]) {
+  static_assert(KS % 4 == 0, "K must be a multiple of 64");
+  float acc[4][NT][4];
 #pragma unroll
-  for (int i = 0; i < STAGES - 1; ++i) {
-    if (t_begin + i < t_end) load_x(t_begin + i, i);
-    cp_async_commit();
-  }
-  int cur_var = -1;
-  int next_var = a.pc.group_variant[(t_begin * RT) / a.pc.group_rows];  // loaded one tile ahead
-  for (int tile = t_begin; tile < t_end; ++tile) {
-    const int buf = (tile - t_begin) % STAGES;
-    const int var = next_var;
-    if (tile + 1 < t_end) next_var = a.pc.group_variant[((tile + 1) * RT) / a.pc.group_rows];
-    if (var != cur_var) {
-      __syncthreads();  // every warp is done with the previous A rows
-      const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
-      for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 256) {
-        const int r = i / (dim / 8), c8 = i - r * (dim / 8);
-        if (r < NA)
-          cp_async16(sab + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
-        else
-          *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
-      }
-      cp_async_commit();
-      cp_async_wait<0>();  // (rare) A rows and every tile in flight have landed
-      cur_var = var;
-    }
-    // the buffer of tile + STAGES - 1 was last read by the previous iteration's mma (all
-    // warps passed the barrier before that iteration's reduction since)
-    if (tile + STAGES - 1 < t_end) load_x(tile + STAGES - 1, (tile - t_begin + STAGES - 1) % STAGES);
-    cp_async_commit();
-    cp_async_wait<STAGES - 1>();  // this tile's rows have landed
-    __syncthreads();
-
-    // ---- split-K mma: warp w takes k-steps [w KS/8, (w+1) KS/8) of every (m16, n8) task ----
-    float c[MT][NT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) c[mt][nt][0] = c[mt][nt][1] = c[mt][nt][2] = c[mt][nt][3] = 0.f;
-    const int lm = lane >> 3, lr = lane & 7;
-    const uint32_t sxb = sx0 + (uint32_t)(buf * RT * XS * 2);
-    for (int kk = warp * KS / 8; kk < (warp + 1) * KS / 8; ++kk) {
-      uint32_t bf[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        uint32_t b2, b3;
-        ldsm_x4(sab + (uint32_t)(((nt * 8 + lr) * XS + kk * 16 + (lm & 1) * 8) * 2), bf[nt][0], bf[nt][1], b2, b3);
-      }
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        uint32_t af[4];
-        ldsm_x4(sxb + (uint32_t)(((mt * 16 + (lm & 1) * 8 + lr) * XS + kk * 16 + (lm >> 1) * 8) * 2), af[0], af[1],
-                af[2], af[3]);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816<T>(c[mt][nt], af, bf[nt][0], bf[nt][1]);
-      }
-    }
-    const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int rr = mt * 16 + g + ((e >> 1) << 3), n = nt * 8 + 2 * t4 + (e & 1);
-          s_red[(warp * RT + rr) * (NT * 8) + n] = c[mt][nt][e];
-        }
-    __syncthreads();
-    // ---- partials summed in warp order, rounded to 16 bit like the LoRA-up operand ----
-    for (int i = threadIdx.x; i < RT * NA; i += 256) {
-      const int rr = i / NA, n = i - rr * NA;
-      const int row = tile * RT + rr;
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) v += s_red[(w * RT + rr) * (NT * 8) + n];
-      if (row < a.rows) {
-        const int m = n / a.rank, j = n - m * a.rank;
-        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(v);
-      }
-    }
-  }
-}
-
-// RMSNorm (perturbed weight) + LoRA-down with prepared operands, as a persistent
-// kernel of 16 warps over a contiguous range of 16-row tiles: warp w owns row w of
-// every tile and keeps the fp32 rows of the next two tiles in flight in registers
-// (a three-deep ring) while it normalises the current one (xn to HBM and to a 16-bit
-// smem tile, the same arithmetic and per-lane order as norm_lora_mma_kernel). The
-// tile's LoRA-down then runs as split-K mma.sync over the 16 warps, partials summed
-// in warp order. A rows and the rms weight are restaged when the variant changes.
-template <int NP, int NA>
-struct NdSmem {
-  static constexpr int RT = 16, WARPS = 16, dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8;
-  static constexpr int kX = RT * XS * 2;            // normalised 16-bit tile
-  static constexpr int kA = NT * 8 * XS * 2;        // A rows (16-bit, zero padded to whole n-tiles)
-  static constexpr int kW = dim * 4;
-  static constexpr int kRed = WARPS * RT * NT * 8 * 4;
-  static constexpr int kTotal = kX + kA + kW + kRed;
-};
-
-template <int NP, typename T, int NA>
-__global__ void __launch_bounds__(512, 1) norm_down_kernel(NormLoraArgs a) {
-  using S = NdSmem<NP, NA>;
-  constexpr int RT = S::RT, W = S::WARPS, dim = S::dim, XS = S::XS, NT = S::NT, KS = dim / 16;
-  using HV = typename H2<T>::V;
-  extern __shared__ __align__(16) uint8_t smx[];
-  T* s_x = reinterpret_cast<T*>(smx);                                      // [RT][XS]
-  T* s_a = reinterpret_cast<T*>(smx + S::kX);                              // [NT*8][XS]
-  float* s_w = reinterpret_cast<float*>(smx + S::kX + S::kA);              // [dim]
-  float* s_red = reinterpret_cast<float*>(smx + S::kX + S::kA + S::kW);    // [W][RT][NT*8]
-  pdl_enter();
-  const int ntiles = (a.rows + RT - 1) / RT;
-  const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
-  const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
-  if (t_begin >= t_end) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t sx0 = smem_u32(s_x), sab = smem_u32(s_a), swb = smem_u32(s_w);
-  const float2* in = static_cast<const float2*>(a.in);
-
-  auto load_row = [&](int tile, float2 (&v)[NP]) {
-    const int row = tile * RT + warp;
-    if (tile < t_end && row < a.rows) {
-      const float2* src = in + (long long)row * (dim / 2);
-#pragma unroll
-      for (int k = 0; k < NP; ++k) v[k] = __ldg(src + lane + 32 * k);
-    } else {
-#pragma unroll
-      for (int k = 0; k < NP; ++k) v[k] = make_float2(0.f, 0.f);
-    }
-  };
-
-  int cur_var = -1;
-  // variant of the next tile, loaded one tile ahead (its latency off the tile's path)
-  int next_var = a.pc.group_variant[(t_begin * RT) / a.pc.group_rows];
-  auto process = [&](int tile, const float2 (&v)[NP]) {
-    const int var = next_var;
-    if (tile + 1 < t_end) next_var = a.pc.group_variant[((tile + 1) * RT) / a.pc.group_rows];
-    if (var != cur_var) {  // uniform over the CTA: every warp walks the same tiles
-      __syncthreads();     // every warp is done with the previous operands
-      const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
-      for (int i = threadIdx.x; i < NT * 8 * (dim / 8); i += 32 * W) {
-        const int r = i / (dim / 8), c8 = i - r * (dim / 8);
-        if (r < NA)
-          cp_async16(sab + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
-        else
-          *reinterpret_cast<uint4*>(s_a + r * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
-      }
-      const float* wp = a.w_prep + (long long)var * a.w_prep_vstride;
-      for (int i = threadIdx.x; i < dim / 4; i += 32 * W) cp_async16(swb + 16u * i, wp + 4 * i);
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-      cur_var = var;
-    }
-    // ---- RMSNorm of this warp's row: xn to HBM and to the 16-bit tile ----
-    const int row = tile * RT + warp;
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < NP; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
-    ss = warp_sum(ss);
-    const float m = __fmul_rn(ss, 1.0f / (float)dim);
-    const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
-    HV* sx = reinterpret_cast<HV*>(s_x + warp * XS);
-    HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
-#pragma unroll
-    for (int k = 0; k < NP; ++k) {
-      const int c = 2 * (lane + 32 * k);
-      const HV h = H2<T>::from_f2(__fmul_rn(__fmul_rn(v[k].x, rstd), s_w[c]),
-                                  __fmul_rn(__fmul_rn(v[k].y, rstd), s_w[c + 1]));
-      if (row < a.rows) dst[lane + 32 * k] = h;
-      sx[lane + 32 * k] = h;
-    }
-    __syncthreads();
-    // ---- split-K mma over the normalised tile: warp w takes k-steps [w KS/W, (w+1) KS/W) ----
-    float c[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
-    const int lm = lane >> 3, lr = lane & 7;
-#pragma unroll 1  // 3-4 steps per warp; the next tiles' rows hold 2 NP registers meanwhile
-    for (int kk = warp * KS / W; kk < (warp + 1) * KS / W; ++kk) {
-      uint32_t af[4];
-      ldsm_x4(sx0 + (uint32_t)((((lm & 1) * 8 + lr) * XS + kk * 16 + (lm >> 1) * 8) * 2), af[0], af[1], af[2], af[3]);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(sab + (uint32_t)(((nt * 8 + lr) * XS + kk * 16 + (lm & 1) * 8) * 2), b0, b1, b2, b3);
-        mma16816<T>(c[nt], af, b0, b1);
-      }
-    }
-    const int g = lane >> 2, t4 = lane & 3;
+  for (int q = 0; q < 4; ++q)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rr = g + ((e >> 1) << 3), n = nt * 8 + 2 * t4 + (e & 1);
-        s_red[(warp * RT + rr) * (NT * 8) + n] = c[nt][e];
-      }
-    __syncthreads();  // (also: every warp's reads of s_x are done before the next tile's rows land there)
-    for (int i = threadIdx.x; i < RT * NA; i += 32 * W) {
-      const int rr = i / NA, n = i - rr * NA;
-      const int orow = tile * RT + rr;
-      float sum = 0.f;
+      for (int e = 0; e < 4; ++e) acc[q][nt][e] = 0.f;
+  const int lm = lane >> 3, lr = lane & 7;
+  // A fragment: matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15); B: one x4 load gives
+  // k-steps kk and kk + 1, low and high k halves, of an 8-row n-tile of A
+  const uint32_t a_off = (uint32_t)((((lm & 1) * 8 + lr) * XS + (lm >> 1) * 8) * 2);
+  const uint32_t b_off = (uint32_t)((lr * XS + (lm >> 1) * 16 + (lm & 1) * 8) * 2);
+#pragma unroll 1
+  for (int kk = 0; kk < KS; kk += 4) {
+    uint32_t af[4][4];
 #pragma unroll
-      for (int w = 0; w < W; ++w) sum += s_red[(w * RT + rr) * (NT * 8) + n];
-      if (orow < a.rows) {
-        const int mi = n / a.rank, j = n - mi * a.rank;
-        static_cast<T*>(a.U)[(long long)orow * kUCols + a.u_col + 16 * mi + j] = static_cast<T>(sum);
+    for (int q = 0; q < 4; ++q)
+      ldsm_x4(sxb + a_off + (uint32_t)((kk + q) * 32), af[q][0], af[q][1], af[q][2], af[q][3]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(sab + b_off + (uint32_t)(nt * 8 * XS * 2 + (kk + 2 * h) * 32), b0, b1, b2, b3);
+        mma16816<T>(acc[2 * h][nt], af[2 * h], b0, b1);
+        mma16816<T>(acc[2 * h + 1][nt], af[2 * h + 1], b2, b3);
+      }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[nt][e] = (acc[0][nt][e] + acc[1][nt][e]) + (acc[2][nt][e] + acc[3][nt][e]);
+}
+
+// U[row0 + r, u_col + 16 m + j] for the accumulator fragment of warp_tile_down
+// (column n = m * rank + j < NA), rows past a.rows skipped.
+template <typename T, int NT, int NA>
+__device__ __forceinline__ void store_u_tile(const NormLoraArgs& a, int row0, int lane, const float (&c)[NT][4]) {
+  const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int n = nt * 8 + 2 * t4 + (e & 1), row = row0 + g + ((e >> 1) << 3);
+      if (n < NA && row < a.rows) {
+        const int m = n / a.rank, j = n - m * a.rank;
+        static_cast<T*>(a.U)[(long long)row * kUCols + a.u_col + 16 * m + j] = static_cast<T>(c[nt][e]);
       }
     }
-  };
+}
 
-  // three-deep register ring: tiles t+1 and t+2 in flight while tile t is processed
-  float2 xa[NP], xb[NP], xc[NP];
-  load_row(t_begin, xa);
-  load_row(t_begin + 1, xb);
-  for (int tile = t_begin; tile < t_end; tile += 3) {
-    load_row(tile + 2, xc);
-    process(tile, xa);
-    if (tile + 1 >= t_end) break;
-    load_row(tile + 3, xa);
-    process(tile + 1, xb);
-    if (tile + 2 >= t_end) break;
-    load_row(tile + 4, xb);
-    process(tile + 2, xc);
+// Stage the prepared A rows of `var` (NA rows of dim 16-bit values) into a slot
+// of pitch XS, by `nthr` threads (index tid); waits for its own copies.
+template <typename T, int NA, int dim, int XS>
+__device__ __forceinline__ void stage_a_rows(const NormLoraArgs& a, int var, T* slot, int tid, int nthr) {
+  const T* ap = static_cast<const T*>(a.a_prep) + (long long)var * a.a_prep_vstride;
+  const uint32_t dst = smem_u32(slot);
+  for (int i = tid; i < NA * (dim / 8); i += nthr) {
+    const int r = i / (dim / 8), c8 = i - r * (dim / 8);
+    cp_async16(dst + (uint32_t)((r * XS + c8 * 8) * 2), ap + (long long)r * a.a_prep_ld + c8 * 8);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+}
+
+// Zero the rows NA .. 8 NT - 1 of every A slot (the n-tile padding; never restaged).
+template <typename T, int NA, int NT, int XS, int VS>
+__device__ __forceinline__ void zero_a_padding(T* s_a, int tid, int nthr) {
+  if constexpr (NA < NT * 8) {
+    constexpr int kPer = (NT * 8 - NA) * (XS / 8);  // 16-byte chunks per slot
+    for (int i = tid; i < VS * kPer; i += nthr) {
+      const int sl = i / kPer, rem = i - sl * kPer;
+      const int r = NA + rem / (XS / 8), c8 = rem % (XS / 8);
+      *reinterpret_cast<uint4*>(s_a + (sl * NT * 8 + r) * XS + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
 }
 
+// LoRA-down of a 16-bit input (no norm): one loader warp moves each tile's rows
+// with 1-D bulk copies (one per row, into rows of pitch XS) completing on the
+// tile's full barrier; CW LoRA warps take tiles in turn. Tile i uses slot i % NS
+// with NS a multiple of CW, so each LoRA warp has slots of its own and waits for
+// their phases in order (a warp never waits on a slot whose previous phase, a tile
+// of another warp, may still be pending: bulk copies complete in any order).
+template <int NP, int NA>
+struct LdSmem {
+  static constexpr int RT = 16, CW = NP <= 16 ? 4 : 2, THREADS = 32 * (CW + 1);
+  static constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, KS = dim / 16;
+  static constexpr int kX = RT * XS * 2;      // one 16-bit tile
+  static constexpr int kA = NT * 8 * XS * 2;  // one variant's A rows (zero padded to whole n-tiles)
+  static constexpr int kBudget = 227 * 1024 - 128;
+  static constexpr int VS = 2 * kA + 3 * kX <= kBudget ? 2 : 1;
+  static constexpr int kFit = (kBudget - VS * kA) / kX;
+  static constexpr int NS = (kFit >= 6 ? 6 : kFit) / CW * CW;
+  static constexpr int kAOff = NS * kX, kBarOff = kAOff + VS * kA;
+  static constexpr int kTotal = kBarOff + (2 * NS + 2) * 8;
+};
+
 template <int NP, typename T, int NA>
-static int launch_norm_down(const NormLoraArgs& a, cudaStream_t st) {
+__global__ void __launch_bounds__(LdSmem<NP, NA>::THREADS, 1) lora_down_kernel(NormLoraArgs a, uint32_t* status) {
+  using S = LdSmem<NP, NA>;
+  constexpr int RT = S::RT, CW = S::CW, dim = S::dim, XS = S::XS, NT = S::NT, VS = S::VS, NS = S::NS;
+  extern __shared__ __align__(16) uint8_t smx[];
+  T* s_x = reinterpret_cast<T*>(smx);                 // [NS][RT][XS]
+  T* s_a = reinterpret_cast<T*>(smx + S::kAOff);      // [VS][NT*8][XS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smx + S::kBarOff);
+  uint64_t* empty = full + NS;
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(empty + NS);
+  pdl_enter();
+  const int ntiles = (a.rows + RT - 1) / RT;
+  const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+  if (t_begin >= t_end) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 32);
+    }
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == CW) {
+    // ---- loader ----
+    const T* in = static_cast<const T*>(a.in);
+    int issued = 0;
+    for (int tile = t_begin; tile < t_end; ++tile, ++issued) {
+      const int i = tile - t_begin, slot = i % NS;
+      if (!mbar_wait(&empty[slot], ((i / NS) & 1) ^ 1, abort_flag, status, DEV_TIMEOUT_PRODUCER)) break;
+      const int row0 = tile * RT;
+      const int nr = a.rows - row0 < RT ? a.rows - row0 : RT;
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(nr * dim * 2));
+      __syncwarp();
+      if (lane < nr)
+        bulk_load(s_x + (slot * RT + lane) * XS, in + (long long)(row0 + lane) * dim, dim * 2, &full[slot]);
+    }
+    // copies still in flight when the consumers gave up (abort path) land before the CTA exits
+    for (int i = issued - 1; i >= 0 && i >= issued - NS; --i) mbar_wait_drain(&full[i % NS], (i / NS) & 1);
+    return;
+  }
+
+  // ---- LoRA warps ----
+  const int g0 = (t_begin * RT) / a.pc.group_rows;
+  const int k_last = ((t_end - 1) * RT) / a.pc.group_rows - g0;
+  const int tid = threadIdx.x;  // 0 .. 32 CW - 1
+  zero_a_padding<T, NA, NT, XS, VS>(s_a, tid, 32 * CW);
+  for (int k = 0; k < VS && k <= k_last; ++k)
+    stage_a_rows<T, NA, dim, XS>(a, a.pc.group_variant[g0 + k], s_a + k * NT * 8 * XS, tid, 32 * CW);
+  named_bar_sync(1, 32 * CW);
+  int kdone = VS - 1;
+  auto advance = [&](int k) {
+    while (kdone < k) {
+      ++kdone;
+      named_bar_sync(1, 32 * CW);
+      stage_a_rows<T, NA, dim, XS>(a, a.pc.group_variant[g0 + kdone], s_a + (kdone % VS) * NT * 8 * XS, tid,
+                                   32 * CW);
+      named_bar_sync(1, 32 * CW);
+    }
+  };
+  for (int tile = t_begin + warp; tile < t_end; tile += CW) {
+    const int k = (tile * RT) / a.pc.group_rows - g0;
+    advance(k);
+    const int i = tile - t_begin, slot = i % NS;
+    if (mbar_wait(&full[slot], (i / NS) & 1, abort_flag, status, DEV_TIMEOUT_MMA)) {
+      float c[NT][4];
+      warp_tile_down<T, NT, S::KS, XS>(smem_u32(s_x + slot * RT * XS), smem_u32(s_a + (k % VS) * NT * 8 * XS), lane,
+                                       c);
+      store_u_tile<T, NT, NA>(a, tile * RT, lane, c);
+    }
+    mbar_arrive(&empty[slot]);
+  }
+  advance(k_last);
+}
+
+// RMSNorm (perturbed weight) + LoRA-down: NW norm warps take the rows of the range in
+// turn (row j to warp j % NW), keep their next two rows in flight in registers while
+// they normalise the current one (the same arithmetic and per-lane order as
+// norm_lora_mma_kernel) and write it to HBM (xn) and, as 16 bit, into the tile ring;
+// LW LoRA warps take tiles in turn. 16 warps in all, so that a thread may hold 128
+// registers. The norm warps restage the rms weight slots, the LoRA warps the A slots.
+template <int NP, int NA>
+struct NdSmem {
+  static constexpr int RT = 16, NW = 14, LW = 2, THREADS = 32 * (NW + LW);
+  static constexpr int dim = NP * 64, XS = dim + 8, NT = (NA + 7) / 8, KS = dim / 16, VS = 2;
+  static constexpr int kX = RT * XS * 2, kA = NT * 8 * XS * 2, kW = dim * 4;
+  static constexpr int kFit = (227 * 1024 - 128 - VS * (kA + kW)) / kX;
+  static constexpr int NS = (kFit >= 4 ? 4 : kFit) / LW * LW;  // a multiple of LW, as in LdSmem
+  static_assert(NW <= RT, "every norm warp has a row in every tile");
+  static constexpr int kAOff = NS * kX, kWOff = kAOff + VS * kA, kBarOff = kWOff + VS * kW;
+  static constexpr int kTotal = kBarOff + (2 * NS + 2) * 8;
+};
+
+template <int NP, typename T, int NA>
+__global__ void __launch_bounds__(NdSmem<NP, NA>::THREADS, 1) norm_down_kernel(NormLoraArgs a, uint32_t* status) {
   using S = NdSmem<NP, NA>;
-  static_assert(S::kTotal <= 227 * 1024, "norm/LoRA-down tiles exceed shared memory");
+  constexpr int RT = S::RT, NW = S::NW, LW = S::LW, dim = S::dim, XS = S::XS, NT = S::NT, VS = S::VS,
+                NS = S::NS;
+  using HV = typename H2<T>::V;
+  extern __shared__ __align__(16) uint8_t smx[];
+  T* s_x = reinterpret_cast<T*>(smx);                      // [NS][RT][XS]
+  T* s_a = reinterpret_cast<T*>(smx + S::kAOff);           // [VS][NT*8][XS]
+  float* s_w = reinterpret_cast<float*>(smx + S::kWOff);   // [VS][dim]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smx + S::kBarOff);
+  uint64_t* empty = full + NS;
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(empty + NS);
+  pdl_enter();
+  const int ntiles = (a.rows + RT - 1) / RT;
+  const int t_begin = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+  if (t_begin >= t_end) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 32 * RT);  // every lane of every row of the tile
+      mbar_init(&empty[s], 32);
+    }
+    *abort_flag = 0u;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int g0 = (t_begin * RT) / a.pc.group_rows;
+  const int k_last = ((t_end - 1) * RT) / a.pc.group_rows - g0;
+
+  if (warp < NW) {
+    // ---- norm warps ----
+    const float2* in = static_cast<const float2*>(a.in);
+    const int r_begin = t_begin * RT, nrows = (t_end - t_begin) * RT;  // rows past a.rows normalise zeros
+    auto load_row = [&](int q, float2 (&v)[NP]) {
+      const int j = warp + NW * q, row = r_begin + j;
+      if (j < nrows && row < a.rows) {
+        const float2* src = in + (long long)row * (dim / 2);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) v[k] = __ldg(src + lane + 32 * k);
+      } else {
+#pragma unroll
+        for (int k = 0; k < NP; ++k) v[k] = make_float2(0.f, 0.f);
+      }
+    };
+    auto stage_w = [&](int k) {
+      const float* wp = a.w_prep + (long long)a.pc.group_variant[g0 + k] * a.w_prep_vstride;
+      const uint32_t dst = smem_u32(s_w + (k % VS) * dim);
+      for (int i = threadIdx.x; i < dim / 4; i += 32 * NW) cp_async16(dst + 16u * i, wp + 4 * i);
+      cp_async_commit();
+      cp_async_wait<0>();
+    };
+    float2 xa[NP], xb[NP], xc[NP];
+    load_row(0, xa);
+    load_row(1, xb);
+    for (int k = 0; k < VS && k <= k_last; ++k) stage_w(k);
+    named_bar_sync(1, 32 * NW);
+    int kdone = VS - 1;
+    auto advance = [&](int k) {
+      while (kdone < k) {  // every norm warp is past the rows of group kdone + 1 - VS
+        ++kdone;
+        named_bar_sync(1, 32 * NW);
+        stage_w(kdone);
+        named_bar_sync(1, 32 * NW);
+      }
+    };
+    // normalise range row j = warp + NW q (j < nrows)
+    auto norm_row = [&](int q, const float2 (&v)[NP]) {
+      const int j = warp + NW * q, row = r_begin + j;
+      const int k = (r_begin + (j / RT) * RT) / a.pc.group_rows - g0;  // the tile's group (rows past a.rows too)
+      advance(k);
+      const int i = j / RT, slot = i % NS;
+      mbar_wait(&empty[slot], ((i / NS) & 1) ^ 1, abort_flag, status, DEV_TIMEOUT_PRODUCER);
+      const float* w = s_w + (k % VS) * dim;
+      float ss = 0.f;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) ss += v[p].x * v[p].x + v[p].y * v[p].y;
+      ss = warp_sum(ss);
+      const float m = __fmul_rn(ss, 1.0f / (float)dim);
+      const float rstd = 1.0f / sqrtf(__fadd_rn(m, 1e-5f));
+      HV* sx = reinterpret_cast<HV*>(s_x + (slot * RT + j % RT) * XS);
+      HV* dst = reinterpret_cast<HV*>(static_cast<T*>(a.xn) + (long long)row * dim);
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const int c = 2 * (lane + 32 * p);
+        const HV h = H2<T>::from_f2(__fmul_rn(__fmul_rn(v[p].x, rstd), w[c]),
+                                    __fmul_rn(__fmul_rn(v[p].y, rstd), w[c + 1]));
+        if (row < a.rows) dst[lane + 32 * p] = h;
+        sx[lane + 32 * p] = h;
+      }
+      mbar_arrive(&full[slot]);
+    };
+    const int nq = (nrows - warp + NW - 1) / NW;  // rows of this warp
+    for (int q = 0; q < nq; q += 3) {
+      load_row(q + 2, xc);
+      norm_row(q, xa);
+      if (q + 1 >= nq) break;
+      load_row(q + 3, xa);
+      norm_row(q + 1, xb);
+      if (q + 2 >= nq) break;
+      load_row(q + 4, xb);
+      norm_row(q + 2, xc);
+    }
+    advance(k_last);
+    return;
+  }
+
+  // ---- LoRA warps ----
+  const int lw = warp - NW, tid = threadIdx.x - 32 * NW;
+  zero_a_padding<T, NA, NT, XS, VS>(s_a, tid, 32 * LW);
+  for (int k = 0; k < VS && k <= k_last; ++k)
+    stage_a_rows<T, NA, dim, XS>(a, a.pc.group_variant[g0 + k], s_a + k * NT * 8 * XS, tid, 32 * LW);
+  named_bar_sync(2, 32 * LW);
+  int kdone = VS - 1;
+  auto advance = [&](int k) {
+    while (kdone < k) {
+      ++kdone;
+      named_bar_sync(2, 32 * LW);
+      stage_a_rows<T, NA, dim, XS>(a, a.pc.group_variant[g0 + kdone], s_a + (kdone % VS) * NT * 8 * XS, tid,
+                                   32 * LW);
+      named_bar_sync(2, 32 * LW);
+    }
+  };
+  for (int tile = t_begin + lw; tile < t_end; tile += LW) {
+    const int k = (tile * RT) / a.pc.group_rows - g0;
+    advance(k);
+    const int i = tile - t_begin, slot = i % NS;
+    if (mbar_wait(&full[slot], (i / NS) & 1, abort_flag, status, DEV_TIMEOUT_MMA)) {
+      float c[NT][4];
+      warp_tile_down<T, NT, S::KS, XS>(smem_u32(s_x + slot * RT * XS), smem_u32(s_a + (k % VS) * NT * 8 * XS), lane,
+                                       c);
+      store_u_tile<T, NT, NA>(a, tile * RT, lane, c);
+    }
+    mbar_arrive(&empty[slot]);
+  }
+  advance(k_last);
+}
+
+template <typename S, auto K>  // one instantiation (and shared-memory attribute) per kernel
+static int launch_down(const NormLoraArgs& a, cudaStream_t st) {
+  constexpr auto k = K;
+  static_assert(S::kTotal <= 227 * 1024, "LoRA-down tiles exceed shared memory");
+  static_assert(S::NS >= 2, "LoRA-down needs at least two ring slots");
   B2P_REQUIRE(a.pc.group_rows % S::RT == 0, "variant groups must be multiples of %d rows", S::RT);
   DeviceCtx* c = nullptr;
   int rc = ctx_get(&c);
   if (rc) return rc;
-  auto k = norm_down_kernel<NP, T, NA>;
   static thread_local uint64_t attr_mask = 0;  // one per instantiation
   if (!(attr_mask & (1ull << (c->device & 63)))) {
     B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
@@ -658,31 +743,20 @@ static int launch_norm_down(const NormLoraArgs& a, cudaStream_t st) {
   }
   const int ntiles = (a.rows + S::RT - 1) / S::RT;
   const int grid = ntiles < c->num_sms ? ntiles : c->num_sms;
-  B2P_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(32 * S::WARPS), S::kTotal, st, a));
+  B2P_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(S::THREADS), S::kTotal, st, a, c->status));
   B2P_POST_LAUNCH();
   return B2P_OK;
 }
 
 template <int NP, typename T, int NA>
+static int launch_norm_down(const NormLoraArgs& a, cudaStream_t st) {
+  return launch_down<NdSmem<NP, NA>, norm_down_kernel<NP, T, NA>>(a, st);
+}
+
+template <int NP, typename T, int NA>
 static int launch_lora_down(const NormLoraArgs& a, cudaStream_t st) {
-  constexpr int RT = 16, STAGES = NP * 64 <= 1024 ? 4 : 2;
-  using S = LdSmem<NP, RT, NA, STAGES>;
-  static_assert(S::kTotal <= 227 * 1024, "LoRA-down tiles exceed shared memory");
-  B2P_REQUIRE(a.pc.group_rows % RT == 0, "variant groups must be multiples of %d rows", RT);
-  DeviceCtx* c = nullptr;
-  int rc = ctx_get(&c);
-  if (rc) return rc;
-  auto k = lora_down_kernel<NP, T, NA, RT, STAGES>;
-  static thread_local uint64_t attr_mask = 0;  // one per instantiation
-  if (!(attr_mask & (1ull << (c->device & 63)))) {
-    B2P_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-    attr_mask |= 1ull << (c->device & 63);
-  }
-  const int ntiles = (a.rows + RT - 1) / RT;
-  const int grid = ntiles < c->num_sms ? ntiles : c->num_sms;
-  B2P_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(256), S::kTotal, st, a));
-  B2P_POST_LAUNCH();
-  return B2P_OK;
+  B2P_REQUIRE(((uintptr_t)a.in & 15) == 0, "LoRA-down input must be 16-byte aligned");
+  return launch_down<LdSmem<NP, NA>, lora_down_kernel<NP, T, NA>>(a, st);
 }
 
 template <int NP, typename T, bool NORM, int NA>
@@ -714,7 +788,7 @@ static int launch_nl_na(const NormLoraArgs& a, size_t smem, int blocks, cudaStre
       default: break;
     }
   }
-  if constexpr (NORM && NP <= 15) {  // the three-row register ring fits up to dim 960
+  if constexpr (NORM && NP <= 16) {  // the norm warps' register ring fits up to dim 1024
     if (a.a_prep && a.w_prep) {
       switch (a.n_a * a.rank) {
         case 8: return launch_norm_down<NP, T, 8>(a, st);
