@@ -256,7 +256,9 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           ok = false;
           break;
         }
-        const int u = atomicAdd(a.sched, 1);
+        // the first unit of each CTA is its block index (no counter round trip at start-up); the
+        // rest come from the counter, offset by the grid size
+        const int u = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(a.sched, 1);
         ring[slot] = u;
         mbar_arrive(&u_full[slot]);
         if (u >= total_units) break;
@@ -310,23 +312,12 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       uint64_t t_idle = 0;
       for (uint32_t it = 0;; ++it) {
         bool did = false;
-        if (t_p < t_s && mbar_test_wait(&p_full[t_p & 1], (uint32_t)(t_p >> 1) & 1u)) {
-          const int b = t_p & 1;
-          const uint32_t info = b ? pv_info1 : pv_info0;
-          const int kvs = (int)(info & 1u), nkeys = (int)(info >> 8);
-          tc_fence_after();
-          const uint32_t o_tmem = tmem_base + b * 256 + kAtOCol;
-          const uint32_t p_tmem = tmem_base + b * 256;
-          const uint32_t v_base = smem_u32(sV + kvs * AtSmem::kKV);
-          const int nch = nkeys / 32;  // 16-key steps ks < nch hold side A's P, the rest side B's
-          for (int ks = 0; ks < nkeys / 16; ++ks)
-            umma_f16_ts(o_tmem, p_tmem + ks * 8 + (ks >= nch ? nch * 8 : 0), sw128_mnmajor_desc(v_base + ks * 2048),
-                        idesc_o, ks > 0 ? 1u : 0u);
-          umma_commit(&o_full[b]);
-          if (info & 2u) umma_commit(&kv_empty[kvs]);
-          ++t_p;
-          did = true;
-        }
+        // One head is in softmax at a time: S of head t_s issues when no head is in softmax
+        // (t_s == t_p) or when the one in softmax (t_p) has written its P, and then ahead of that
+        // head's P·V, so the next softmax runs while the tensor core does the P·V. (With S issued as
+        // soon as a buffer frees, both warpgroup pairs ran their softmax at the same time, sharing
+        // the MUFU of each SM sub-partition, and the tensor core idled meanwhile.)
+        const bool p_ready = t_p < t_s && mbar_test_wait(&p_full[t_p & 1], (uint32_t)(t_p >> 1) & 1u);
         if (!done_s && t_s < t_p + 2) {
           if (need_unit) {
             const int slot = k % kAtRing;
@@ -348,7 +339,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               need_kv = false;
               did = true;
             }
-          } else {
+          } else if (t_s == t_p || p_ready) {
             const int b = t_s & 1;
             const uint32_t n = (uint32_t)(t_s >> 1) & 1u;
             if (mbar_test_wait(&q_full[b], n) && mbar_test_wait(&t_empty[b], n ^ 1u)) {
@@ -373,6 +364,23 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               did = true;
             }
           }
+        }
+        if (p_ready) {
+          const int b = t_p & 1;
+          const uint32_t info = b ? pv_info1 : pv_info0;
+          const int kvs = (int)(info & 1u), nkeys = (int)(info >> 8);
+          tc_fence_after();
+          const uint32_t o_tmem = tmem_base + b * 256 + kAtOCol;
+          const uint32_t p_tmem = tmem_base + b * 256;
+          const uint32_t v_base = smem_u32(sV + kvs * AtSmem::kKV);
+          const int nch = nkeys / 32;  // 16-key steps ks < nch hold side A's P, the rest side B's
+          for (int ks = 0; ks < nkeys / 16; ++ks)
+            umma_f16_ts(o_tmem, p_tmem + ks * 8 + (ks >= nch ? nch * 8 : 0), sw128_mnmajor_desc(v_base + ks * 2048),
+                        idesc_o, ks > 0 ? 1u : 0u);
+          umma_commit(&o_full[b]);
+          if (info & 2u) umma_commit(&kv_empty[kvs]);
+          ++t_p;
+          did = true;
         }
         if (done_s && t_p == t_s) break;
         // bounded: give up after the wait budget without progress, or when another role aborted

@@ -46,7 +46,7 @@ def test_gemm_matches_fp32(b2p, M, N, K, dt, out_f32):
 
 
 PAIR_SHAPES = [(256, 960, 960), (512, 1600, 960), (384, 2560, 960), (1024, 16893, 960), (8192, 960, 2560),
-               (300, 100, 64), (16384, 5120, 960)]
+               (300, 100, 64), (16384, 5120, 960), (16384, 960, 2560), (16384, 1600, 960)]
 
 
 @pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
