@@ -27,10 +27,11 @@
 // heads, so the softmax of one head overlaps the MMAs of the next; splitting a
 // head's keys halves the serial softmax path of its rows.
 //
-// Warps: 0 TMEM owner and TMA producer, 1 MMA issuer, 2-9 the pair of buffer 0
-// (2-5 side A, 6-9 side B), 10-17 the pair of buffer 1 (warp % 4 selects the
-// warp's 32-lane TMEM quarter). The MMA issuer polls its barriers and issues
-// whichever of S(next) and P·V(oldest) is ready first.
+// Warps: 0 TMEM owner and TMA producer, 1 and 18 the MMA issuers of buffers 0
+// and 1, 2-9 the pair of buffer 0 (2-5 side A, 6-9 side B), 10-17 the pair of
+// buffer 1 (warp % 4 selects the warp's 32-lane TMEM quarter). Head t's S is
+// issued once head t-1 has its row maxima, so at most one pair is in its exp
+// pass at a time.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -45,7 +46,7 @@ namespace {
 constexpr int kAtRows = 128;   // query rows per tile (UMMA M)
 constexpr int kAtHD = 64;      // head dim
 constexpr int kAtMaxKeys = 256;
-constexpr int kAtThreads = 576;   // 2 + 16 warps
+constexpr int kAtThreads = 608;   // 3 + 16 warps
 constexpr int kAtSoftWarps = 8;    // per buffer: 4 on each half of the keys
 constexpr int kAtOCol = 192;       // O = P·V columns inside a 256-column buffer
 constexpr int kAtRing = 4;     // unit-id ring between the producer and the consumers
@@ -59,7 +60,7 @@ struct AtSmem {
   static constexpr int kKOff = kQOff + 2 * kQ;           // 2 K tiles (unit double buffer)
   static constexpr int kVOff = kKOff + 2 * kKV;          // 2 V tiles
   static constexpr int kBarOff = kVOff + 2 * kKV;
-  static constexpr int kNumBars = 16 + 2 * kAtRing + 1;
+  static constexpr int kNumBars = 18 + 2 * kAtRing + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kRedOff = kMiscOff + 64;           // [buffer][side][128] partial max, then sum
   static constexpr int kTotal = kRedOff + 2 * 2 * 128 * 4 + 1024;  // + 1024-byte alignment slack
@@ -200,9 +201,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   uint64_t* p_full = bars + 10;
   uint64_t* o_full = bars + 12;
   uint64_t* t_empty = bars + 14;
-  uint64_t* u_full = bars + 16;
+  uint64_t* m_full = bars + 16;
+  uint64_t* u_full = bars + 18;
   uint64_t* u_empty = u_full + kAtRing;
-  uint64_t* drain_bar = u_empty + kAtRing;
+  uint64_t* drain_bar = u_empty + kAtRing;  // [2], one per MMA issuer
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + AtSmem::kMiscOff);
   uint32_t* tmem_holder = misc;
   volatile uint32_t* abort_flag = misc + 1;
@@ -218,17 +220,19 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);            // both MMA issuers (each commits after its last use)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kAtSoftWarps);   // one arrive per softmax warp of the buffer
       mbar_init(&o_full[i], 1);
       mbar_init(&t_empty[i], kAtSoftWarps);
+      mbar_init(&m_full[i], kAtSoftWarps);   // the buffer's head has its row maxima
     }
     for (int i = 0; i < kAtRing; ++i) {
       mbar_init(&u_full[i], 1);
-      mbar_init(&u_empty[i], 1 + 2 * kAtSoftWarps);  // MMA thread + one arrive per softmax warp
+      mbar_init(&u_empty[i], 2 + 2 * kAtSoftWarps);  // both MMA threads + one arrive per softmax warp
     }
-    mbar_init(drain_bar, 1);
+    mbar_init(&drain_bar[0], 1);
+    mbar_init(&drain_bar[1], 1);
     *abort_flag = 0;
     wg_abort[0] = wg_abort[1] = 0;
     fence_mbar_init();
@@ -296,115 +300,85 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         // (the abort flag is set: every consumer's bounded wait returns)
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || warp == kAtThreads / 32 - 1) {
+    // ---------------- MMA issuers: warp 1 for TMEM buffer 0 (even heads), the last warp for buffer 1 ----------------
+    // A tcgen05.mma holds its issuing thread for about as long as an N = 256 step takes, whatever its
+    // N (measured: ~105-150 cycles for N = 64 with one issuer), while two issuers' N = 64 streams
+    // overlap on the tensor core. So each buffer has its own issuer: one head's P·V no longer delays
+    // the other buffer's S. Head t's S issues once head t-1 (other buffer) has its row maxima (m_full):
+    // its max pass then overlaps that head's exp pass, and the two pairs' exp passes, which share the
+    // MUFU of each SM sub-partition, follow one another instead of running together.
     if (lane == 0) {
+      const int b = warp == 1 ? 0 : 1;
       const uint32_t idesc_s128 = umma_idesc_f16(BF16, kAtRows, 128);
       const uint32_t idesc_s256 = umma_idesc_f16(BF16, kAtRows, 256);
       const uint32_t idesc_o = umma_idesc_f16(BF16, kAtRows, kAtHD) | (1u << 16);  // B = V, MN-major
-      // S side: next head t_s of unit k (head j of gq); P·V side: oldest head t_p < t_s.
-      int t_s = 0, t_p = 0, k = 0, j = 0;
-      bool need_unit = true, need_kv = false, done_s = false, issued_any = false, ok = true;
-      Unit un{};
-      // per TMEM buffer: K/V stage, key count, last head of its unit (packed: bit 0 stage,
-      // bit 1 last, bits 8+ keys), so the state stays in registers
-      uint32_t pv_info0 = 0, pv_info1 = 0;
-      uint64_t t_idle = 0;
-      for (uint32_t it = 0;; ++it) {
-        bool did = false;
-        // One head is in softmax at a time: S of head t_s issues when no head is in softmax
-        // (t_s == t_p) or when the one in softmax (t_p) has written its P, and then ahead of that
-        // head's P·V, so the next softmax runs while the tensor core does the P·V. (With S issued as
-        // soon as a buffer frees, both warpgroup pairs ran their softmax at the same time, sharing
-        // the MUFU of each SM sub-partition, and the tensor core idled meanwhile.)
-        const bool p_ready = t_p < t_s && mbar_test_wait(&p_full[t_p & 1], (uint32_t)(t_p >> 1) & 1u);
-        if (!done_s && t_s < t_p + 2) {
-          if (need_unit) {
-            const int slot = k % kAtRing;
-            if (mbar_test_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u)) {
-              const int u = ring[slot];
-              mbar_arrive(&u_empty[slot]);
-              if (u >= total_units) {
-                done_s = true;
-              } else {
-                un = decode_unit(u, a);
-                need_unit = false;
-                need_kv = true;
-                j = 0;
-              }
-              did = true;
-            }
-          } else if (need_kv) {
-            if (mbar_test_wait(&kv_full[k & 1], (uint32_t)(k >> 1) & 1u)) {
-              need_kv = false;
-              did = true;
-            }
-          } else if (t_s == t_p || p_ready) {
-            const int b = t_s & 1;
-            const uint32_t n = (uint32_t)(t_s >> 1) & 1u;
-            if (mbar_test_wait(&q_full[b], n) && mbar_test_wait(&t_empty[b], n ^ 1u)) {
-              tc_fence_after();
-              const int kvs = k & 1;
-              const uint32_t q_base = smem_u32(sQ + b * AtSmem::kQ);
-              const uint32_t k_base = smem_u32(sK + kvs * AtSmem::kKV);
-              const uint32_t idesc_s = un.nkeys == 256 ? idesc_s256 : idesc_s128;
-              for (int kk = 0; kk < kAtHD / 16; ++kk)
-                umma_f16_ss(tmem_base + b * 256, sw128_kmajor_desc(q_base + kk * 32),
-                            sw128_kmajor_desc(k_base + kk * 32), idesc_s, kk > 0 ? 1u : 0u);
-              umma_commit(&s_full[b]);
-              umma_commit(&q_empty[b]);
-              issued_any = true;
-              const uint32_t info = (uint32_t)kvs | (j == gq - 1 ? 2u : 0u) | ((uint32_t)un.nkeys << 8);
-              if (b) pv_info1 = info; else pv_info0 = info;
-              ++t_s;
-              if (++j == gq) {
-                ++k;
-                need_unit = true;
-              }
-              did = true;
-            }
-          }
+      bool ok = true, issued_any = false;
+      int t0 = 0;  // global index of the unit's first head
+      for (int k = 0; ok; ++k, t0 += gq) {
+        const int slot = k % kAtRing;
+        if (!mbar_wait(&u_full[slot], (uint32_t)(k / kAtRing) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
         }
-        if (p_ready) {
-          const int b = t_p & 1;
-          const uint32_t info = b ? pv_info1 : pv_info0;
-          const int kvs = (int)(info & 1u), nkeys = (int)(info >> 8);
+        const int u = ring[slot];
+        mbar_arrive(&u_empty[slot]);
+        if (u >= total_units) break;
+        const Unit un = decode_unit(u, a);
+        const int kvs = k & 1;
+        // this issuer's heads of the unit: t0 + j with (t0 + j) % 2 == b
+        const int j_first = ((t0 & 1) == b) ? 0 : 1;
+        int j_last = -1;
+        for (int j = j_first; j < gq; j += 2) j_last = j;
+        // (also without heads here: an arrival on kv_empty before this unit's K/V has landed could be
+        // counted towards the stage's previous unit, whose other issuer may still be reading it)
+        if (!mbar_wait(&kv_full[kvs], (uint32_t)(k >> 1) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        if (j_last < 0) {  // none of this unit's heads: release its K/V stage for this issuer
+          mbar_arrive(&kv_empty[kvs]);
+          continue;
+        }
+        const uint32_t k_base = smem_u32(sK + kvs * AtSmem::kKV);
+        const uint32_t v_base = smem_u32(sV + kvs * AtSmem::kKV);
+        const uint32_t idesc_s = un.nkeys == 256 ? idesc_s256 : idesc_s128;
+        for (int j = j_first; j < gq; j += 2) {
+          const int t = t0 + j;
+          const uint32_t n = (uint32_t)(t >> 1) & 1u;  // phase of buffer b's barriers for head t
+          const int tp = t - 1;                          // previous head, on the other buffer
+          if ((tp >= 0 && !mbar_wait(&m_full[b ^ 1], (uint32_t)(tp >> 1) & 1u, abort_flag, status, DEV_TIMEOUT_MMA)) ||
+              !mbar_wait(&q_full[b], n, abort_flag, status, DEV_TIMEOUT_MMA) ||
+              !mbar_wait(&t_empty[b], n ^ 1u, abort_flag, status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(sQ + b * AtSmem::kQ);
+          for (int kk = 0; kk < kAtHD / 16; ++kk)
+            umma_f16_ss(tmem_base + b * 256, sw128_kmajor_desc(q_base + kk * 32), sw128_kmajor_desc(k_base + kk * 32),
+                        idesc_s, kk > 0 ? 1u : 0u);
+          umma_commit(&s_full[b]);
+          umma_commit(&q_empty[b]);
+          issued_any = true;
+          if (!mbar_wait(&p_full[b], n, abort_flag, status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t o_tmem = tmem_base + b * 256 + kAtOCol;
           const uint32_t p_tmem = tmem_base + b * 256;
-          const uint32_t v_base = smem_u32(sV + kvs * AtSmem::kKV);
-          const int nch = nkeys / 32;  // 16-key steps ks < nch hold side A's P, the rest side B's
-          for (int ks = 0; ks < nkeys / 16; ++ks)
+          const int nch = un.nkeys / 32;  // 16-key steps ks < nch hold side A's P, the rest side B's
+          for (int ks = 0; ks < un.nkeys / 16; ++ks)
             umma_f16_ts(o_tmem, p_tmem + ks * 8 + (ks >= nch ? nch * 8 : 0), sw128_mnmajor_desc(v_base + ks * 2048),
                         idesc_o, ks > 0 ? 1u : 0u);
           umma_commit(&o_full[b]);
-          if (info & 2u) umma_commit(&kv_empty[kvs]);
-          ++t_p;
-          did = true;
-        }
-        if (done_s && t_p == t_s) break;
-        // bounded: give up after the wait budget without progress, or when another role aborted
-        if (did) {
-          t_idle = 0;
-        } else if ((it & 255u) == 0u) {
-          if (*abort_flag) {
-            ok = false;
-            break;
-          }
-          const uint64_t now = sm_cycles();
-          if (t_idle == 0) {
-            t_idle = now;
-          } else if (now - t_idle > kWaitBudgetCycles) {
-            *abort_flag = 1;
-            atomicCAS(status, 0u, (uint32_t)DEV_TIMEOUT_MMA);
-            ok = false;
-            break;
-          }
+          if (j == j_last) umma_commit(&kv_empty[kvs]);
         }
       }
       if (!ok && issued_any) {
-        umma_commit(drain_bar);
-        mbar_wait_drain(drain_bar, 0);
+        umma_commit(&drain_bar[b]);
+        mbar_wait_drain(&drain_bar[b], 0);
       }
     }
   } else {
@@ -461,6 +435,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         red[side * 128 + r] = mx;
         named_bar_sync(bar_id, 256);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&m_full[wg]);  // the next head's S may issue now
         mx = fmaxf(mx, red[(side ^ 1) * 128 + r]);
         // pass 2: P = exp2((s - max)·scale) as 16-bit pairs, chunk c at columns
         // [16c + p_off, +16) (this side's own S columns, read before they are written),
