@@ -62,4 +62,27 @@ int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, in
                           static_cast<cudaStream_t>(stream));
 }
 
+int b2p_gemm_pair_mn(const void* X, int ldx, int x_mn, const void* W, int ldw, int w_mn, void* Y, int M, int N, int K,
+                     int ldy, int dtype, int out_f32, void* stream) {
+  B2P_REQUIRE(X && W && Y, "null operand");
+  B2P_REQUIRE(dtype == B2P_F16 || dtype == B2P_BF16, "dtype must be B2P_F16 or B2P_BF16");
+  B2P_REQUIRE(M >= 2 * kBM, "the CTA-pair engine needs M >= %d (got %d)", 2 * kBM, M);
+  B2P_REQUIRE((x_mn == 0 || x_mn == 1) && (w_mn == 0 || w_mn == 1), "x_mn / w_mn must be 0 or 1");
+  B2P_REQUIRE(ldy >= N, "ldy (%d) < N (%d)", ldy, N);
+  B2P_REQUIRE(out_f32 ? (ldy % 4 == 0) : (ldy % 8 == 0), "ldy must keep 16-byte row alignment");
+  B2P_REQUIRE((reinterpret_cast<uintptr_t>(Y) & 15u) == 0, "Y must be 16-byte aligned");
+  EpiParams ep;
+  std::memset(&ep, 0, sizeof(ep));
+  ep.M = M;
+  ep.N = N;
+  const int kind = out_f32 ? EPI_F32 : EPI_H16;
+  if (!x_mn && !w_mn) {
+    B2P_REQUIRE(ldx >= K && ldw >= K && ldx % 8 == 0 && ldw % 8 == 0, "row pitches must be >= K, multiples of 8");
+    return launch_gemm_pair(kind, dtype == B2P_BF16, X, ldx, W, ldw, M, N, K, Y, ldy, nullptr, ep,
+                            static_cast<cudaStream_t>(stream));
+  }
+  return launch_gemm_pair_mn(kind, (x_mn ? 1 : 0) | (w_mn ? 2 : 0), dtype == B2P_BF16, X, ldx, W, ldw, M, N, K, Y, ldy,
+                             ep, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -105,6 +105,12 @@ int launch_gemm(int bn, int kind, bool bf16, const void* X, int ldx, const void*
 // variant groups of whole 256-row tiles, LoRA only on the fused QKV / residual
 // epilogues); launch_gemm_pair() has the same contract as launch_gemm.
 bool pair_supported(int kind, int M, int N, const EpiParams& ep);
+// MN-major operands on the CTA-pair engine (plain tiles, no LoRA): opm bit 0 = X given as [K][M]
+// rows of pitch ldx, bit 1 = W given as [K][N] rows of pitch ldw. Epilogues: EPI_F32 (opm 2, 3),
+// EPI_H16 (opm 2), EPI_RESID (opm 3). pair_mn_supported() tells whether a launch qualifies.
+bool pair_mn_supported(int kind, int opm, int M, int N, int K, const void* X, int ldx, const void* W, int ldw);
+int launch_gemm_pair_mn(int kind, int opm, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N,
+                        int K, void* out, int ldo, const EpiParams& ep, cudaStream_t st);
 int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                      void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
 

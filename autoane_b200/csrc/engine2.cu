@@ -6,7 +6,7 @@ namespace b2p {
 
 namespace {
 
-template <int BN, int KIND, typename OutT, bool BF16, int NSEG>
+template <int BN, int KIND, typename OutT, bool BF16, int NSEG, int OPM = 0>
 int launch_pair_t(const void* X, int ldx, const void* W, int ldw, int M, int N, int K, void* out, int ldo,
                   const void* u16, const EpiParams& ep, cudaStream_t st) {
   DeviceCtx* c = nullptr;
@@ -15,8 +15,18 @@ int launch_pair_t(const void* X, int ldx, const void* W, int ldw, int M, int N, 
   using S = PairSmem<BN, KIND, NSEG>;
   const TmapType in_t = BF16 ? TM_BF16 : TM_F16;
   CUtensorMap tx, tw, to, tu;
-  if ((rc = make_tmap_2d(&tx, X, in_t, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, 64, kBM, 128))) return rc;
-  if ((rc = make_tmap_2d(&tw, W, in_t, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, 64, BN / 2, 128))) return rc;
+  // K-major: [M][K] / [N][K] rows, one box of 64 K x the tile's rows; MN-major: [K][M] / [K][N] rows,
+  // boxes of 64 M (or N) x 64 K
+  if (OPM & 1) {
+    if ((rc = make_tmap_2d(&tx, X, in_t, (uint64_t)M, (uint64_t)K, (uint64_t)ldx, 64, 64, 128))) return rc;
+  } else {
+    if ((rc = make_tmap_2d(&tx, X, in_t, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, 64, kBM, 128))) return rc;
+  }
+  if (OPM & 2) {
+    if ((rc = make_tmap_2d(&tw, W, in_t, (uint64_t)N, (uint64_t)K, (uint64_t)ldw, 64, 64, 128))) return rc;
+  } else {
+    if ((rc = make_tmap_2d(&tw, W, in_t, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, 64, BN / 2, 128))) return rc;
+  }
   if (S::kStores) {
     const int ncols = KIND == EPI_SWIGLU ? N / 2 : N;
     if (S::kOutF32) {
@@ -32,7 +42,7 @@ int launch_pair_t(const void* X, int ldx, const void* W, int ldw, int M, int N, 
   } else {
     tu = tx;
   }
-  auto kern = gemm_pair_kernel<BN, KIND, OutT, BF16, NSEG>;
+  auto kern = gemm_pair_kernel<BN, KIND, OutT, BF16, NSEG, OPM>;
   static thread_local uint64_t attr_dev_mask = 0;
   if (!(attr_dev_mask & (1ull << (c->device & 63)))) {
     B2P_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
@@ -109,7 +119,48 @@ int dispatch_pair(int kind, const void* X, int ldx, const void* W, int ldw, int 
   return B2P_ERR_UNSUPPORTED;
 }
 
+template <typename H, bool BF16>
+int dispatch_pair_mn(int kind, int opm, const void* X, int ldx, const void* W, int ldw, int M, int N, int K, void* out,
+                     int ldo, const EpiParams& ep, cudaStream_t st) {
+  switch (kind) {
+    case EPI_F32:
+      if (opm == 2) return launch_pair_t<256, EPI_F32, H, BF16, 0, 2>(X, ldx, W, ldw, M, N, K, out, ldo, nullptr, ep, st);
+      if (opm == 3) return launch_pair_t<256, EPI_F32, H, BF16, 0, 3>(X, ldx, W, ldw, M, N, K, out, ldo, nullptr, ep, st);
+      break;
+    case EPI_H16:
+      if (opm == 2) return launch_pair_t<256, EPI_H16, H, BF16, 0, 2>(X, ldx, W, ldw, M, N, K, out, ldo, nullptr, ep, st);
+      break;
+    case EPI_RESID:
+      if (opm == 3)
+        return launch_pair_t<256, EPI_RESID, H, BF16, 0, 3>(X, ldx, W, ldw, M, N, K, out, ldo, nullptr, ep, st);
+      break;
+  }
+  set_error("no MN-major CTA-pair kernel for epilogue %d with operand layout %d", kind, opm);
+  return B2P_ERR_UNSUPPORTED;
+}
+
 }  // namespace
+
+bool pair_mn_supported(int kind, int opm, int M, int N, int K, const void* X, int ldx, const void* W, int ldw) {
+  // MN-major boxes start on 64-element boundaries of the contiguous dimension (16-byte TMA rule);
+  // rows of 16-byte multiples
+  if (M < 2 * kBM || N < 1 || K < 1 || ldx % 8 != 0 || ldw % 8 != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(X) & 15u) != 0 || (reinterpret_cast<uintptr_t>(W) & 15u) != 0) return false;
+  return (kind == EPI_F32 && (opm == 2 || opm == 3)) || (kind == EPI_H16 && opm == 2) ||
+         (kind == EPI_RESID && opm == 3);
+}
+
+int launch_gemm_pair_mn(int kind, int opm, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N,
+                        int K, void* out, int ldo, const EpiParams& ep, cudaStream_t st) {
+  B2P_REQUIRE(M > 0 && N > 0 && K > 0, "empty GEMM (M=%d N=%d K=%d)", M, N, K);
+  B2P_REQUIRE(!ep.has_lora, "MN-major CTA-pair GEMMs take no LoRA segments");
+  B2P_REQUIRE(out != nullptr, "GEMM without an output");
+  B2P_REQUIRE(pair_mn_supported(kind, opm, M, N, K, X, ldx, W, ldw),
+              "MN-major CTA-pair GEMM: epilogue %d / layout %d unsupported, M < 256, or unaligned operands", kind, opm);
+  B2P_REQUIRE((opm & 1 ? ldx >= M : ldx >= K) && (opm & 2 ? ldw >= N : ldw >= K), "operand row pitch too small");
+  if (bf16) return dispatch_pair_mn<__nv_bfloat16, true>(kind, opm, X, ldx, W, ldw, M, N, K, out, ldo, ep, st);
+  return dispatch_pair_mn<__half, false>(kind, opm, X, ldx, W, ldw, M, N, K, out, ldo, ep, st);
+}
 
 bool pair_supported(int kind, int M, int N, const EpiParams& ep) {
   (void)N;

@@ -19,6 +19,13 @@
 //             with both U tiles' bytes + one remote arrive).
 //   lempty[b] both CTAs; committed by the leader's MMA thread.
 //
+// Operand layouts (OPM): bit 0 set, X is given MN-major, as [K][M] rows (the A
+// tile of a K step is two 64-row atoms of 64 K rows each, one TMA box apiece);
+// bit 1 set, W is given MN-major, as [K][N] rows (BN/128 atoms per CTA). The
+// data-gradient GEMMs of the backward multiply by W itself (dX = dY·W, W stored
+// [out][in]) and the weight gradients by dY^T and X (stored [tokens][features]):
+// MN-major operands read them where they lie instead of from transposed copies.
+//
 // LoRA: the correction Σ_s U_s · Bv_s^T runs as one K=16 MMA per segment s
 // (Q, K, V of the fused QKV projection are three segments; Wo is one). A tile
 // may span segments: rows of Bv_s outside segment s are zero.
@@ -107,7 +114,7 @@ __device__ __forceinline__ void pair_tile(const PairTiles& t, int i, int& mt, in
   n0 = nt * BN;
 }
 
-template <int BN, int KIND, typename OutT, bool BF16, int NSEG>
+template <int BN, int KIND, typename OutT, bool BF16, int NSEG, int OPM = 0>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmU, int M, int N,
@@ -119,6 +126,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   constexpr int HB = BN / 2;  // W rows per CTA
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN must be a multiple of 32 in [64, 256]");
   static_assert(KIND != EPI_SWIGLU || BN % 64 == 0, "SwiGLU tiles hold two halves of 32-column chunks");
+  static_assert(OPM == 0 || (NSEG == 0 && BN % 128 == 0), "MN-major operands: plain tiles of 128 or 256 columns");
+  constexpr bool A_MN = (OPM & 1) != 0, B_MN = (OPM & 2) != 0;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -198,8 +207,22 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * S::kStageBytes);
-          tma_load_2d_pair(sA + stage * S::kAStage, &tmX, fb, kb * kBK, mt * 2 * kBM + (int)rank * kBM);
-          tma_load_2d_pair(sB + stage * S::kBStage, &tmW, fb, kb * kBK, n0 + (int)rank * (nw / 2));
+          if (A_MN) {
+#pragma unroll
+            for (int at = 0; at < kBM / 64; ++at)
+              tma_load_2d_pair(sA + stage * S::kAStage + at * 8192, &tmX, fb, mt * 2 * kBM + (int)rank * kBM + at * 64,
+                               kb * kBK);
+          } else {
+            tma_load_2d_pair(sA + stage * S::kAStage, &tmX, fb, kb * kBK, mt * 2 * kBM + (int)rank * kBM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int at = 0; at < HB / 64; ++at)
+              tma_load_2d_pair(sB + stage * S::kBStage + at * 8192, &tmW, fb, n0 + (int)rank * (nw / 2) + at * 64,
+                               kb * kBK);
+          } else {
+            tma_load_2d_pair(sB + stage * S::kBStage, &tmW, fb, kb * kBK, n0 + (int)rank * (nw / 2));
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -236,7 +259,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (tile >= tl.total) break;
         int mt, nt, n0, nw;
         pair_tile<BN>(tl, tile, mt, nt, n0, nw);
-        const uint32_t idesc = umma_idesc_f16(BF16, 2 * kBM, nw);
+        const uint32_t idesc_l = umma_idesc_f16(BF16, 2 * kBM, nw);  // K-major (LoRA step)
+        const uint32_t idesc = idesc_l | (A_MN ? (1u << 15) : 0u) | (B_MN ? (1u << 16) : 0u);
         if (!mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, ep.status, DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
@@ -249,11 +273,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + stage * S::kAStage));
-          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + stage * S::kBStage));
+          // K-major: +32 B per K = 16 step inside the swizzle atom; MN-major: +16 K rows (2048 B)
+          const uint64_t adesc = A_MN ? sw128_mn_desc(smem_u32(sA + stage * S::kAStage), 8192)
+                                      : sw128_kmajor_desc(smem_u32(sA + stage * S::kAStage));
+          const uint64_t bdesc = B_MN ? sw128_mn_desc(smem_u32(sB + stage * S::kBStage), 8192)
+                                      : sw128_kmajor_desc(smem_u32(sB + stage * S::kBStage));
+          constexpr uint64_t a_step = A_MN ? (2048u >> 4) : 2u, b_step = B_MN ? (2048u >> 4) : 2u;
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k)
-            umma_f16_ss_pair(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss_pair(d_tmem, adesc + a_step * k, bdesc + b_step * k, idesc, (kb | k) != 0 ? 1u : 0u);
           issued_any = true;
           const uint32_t eb = smem_u32(&empty_bar[stage]);
           umma_commit_pair(eb);
@@ -274,7 +302,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int s = 0; s < NSEG; ++s)
             umma_f16_ss_pair(d_tmem, sw32_kmajor_desc(smem_u32(buf + s * S::kLoraU)),
-                             sw32_kmajor_desc(smem_u32(buf + NSEG * S::kLoraU + s * S::kLoraB)), idesc, 1u);
+                             sw32_kmajor_desc(smem_u32(buf + NSEG * S::kLoraU + s * S::kLoraB)), idesc_l, 1u);
           const uint32_t le = smem_u32(&lempty_bar[lb]);
           umma_commit_pair(le);
           umma_commit_pair(mapa_shared(le, peer));

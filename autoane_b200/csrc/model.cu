@@ -176,6 +176,30 @@ int gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, 
   return rc;
 }
 
+// gemm() for the MN-major CTA-pair launches of the backward (operands read in the layout they are
+// stored in). Returns B2P_ERR_UNSUPPORTED, launching nothing, when the pair engine does not take the
+// launch (B2P_OPT_PAIR_GEMM 0, fewer than 256 rows, unaligned operands): the caller then uses K-major
+// copies on the engine chosen by gemm().
+int gemm_mn(b2p_model* m, int kind, int opm, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+            void* out, int ldo, const EpiParams& ep) {
+  if (!m->use_pair || ep.has_lora || !pair_mn_supported(kind, opm, M, N, K, X, ldx, W, ldw)) return B2P_ERR_UNSUPPORTED;
+  if (!m->prof) return launch_gemm_pair_mn(kind, opm, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, ep, m->st);
+  while (m->ev_pool.size() < m->ev_used + 2) {
+    cudaEvent_t e;
+    B2P_CHECK_CUDA(cudaEventCreate(&e));
+    m->ev_pool.push_back(e);
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  B2P_CHECK_CUDA(cudaStreamIsCapturing(m->st, &cap));
+  const unsigned flags = cap == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+  B2P_CHECK_CUDA(cudaEventRecordWithFlags(m->ev_pool[m->ev_used], m->st, flags));
+  int rc = launch_gemm_pair_mn(kind, opm, m->bf16, X, ldx, W, ldw, M, N, K, out, ldo, ep, m->st);
+  B2P_CHECK_CUDA(cudaEventRecordWithFlags(m->ev_pool[m->ev_used + 1], m->st, flags));
+  m->ev_used += 2;
+  m->prof_flops.push_back(2.0 * M * (double)N * K);
+  return rc;
+}
+
 // The batched forward over G groups whose inputs are already staged on the device.
 // With `sv`, every activation the backprop-LoRA backward reads is written to its
 // per-layer slab instead of the shared scratch buffers, and the W1/W3 outputs are
@@ -616,6 +640,10 @@ LoraEpi model_lora_epi(const b2p_model* m) { return lora_epi(m); }
 int model_gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                void* out, int ldo, const void* u16, const EpiParams& ep) {
   return gemm(m, bn, kind, X, ldx, W, ldw, M, N, K, out, ldo, ep, u16);
+}
+int model_gemm_mn(b2p_model* m, int kind, int opm, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                  void* out, int ldo, const EpiParams& ep) {
+  return gemm_mn(m, kind, opm, X, ldx, W, ldw, M, N, K, out, ldo, ep);
 }
 int model_run_forward(b2p_model* m, int G, const int32_t* tok, const ForwardSaves* sv) {
   return run_forward(m, G, tok, sv);

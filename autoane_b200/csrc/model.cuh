@@ -116,6 +116,10 @@ PerturbCtx model_pctx(const b2p_model* m);
 LoraEpi model_lora_epi(const b2p_model* m);
 int model_gemm(b2p_model* m, int bn, int kind, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                void* out, int ldo, const void* u16, const EpiParams& ep);
+// model_gemm with MN-major operands on the CTA-pair engine (opm as launch_gemm_pair_mn); returns
+// B2P_ERR_UNSUPPORTED without launching when the pair engine does not take it.
+int model_gemm_mn(b2p_model* m, int kind, int opm, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                  void* out, int ldo, const EpiParams& ep);
 
 // Where the forward writes the activations the backward reads (all null: the
 // plain MeZO forward, which reuses one buffer per activation).

@@ -56,6 +56,9 @@ struct P16State {
   int weights_version = -1;
   int cv_pad = 0;
   void *wqkvT = nullptr, *woT = nullptr, *w13T = nullptr, *w2T = nullptr, *cembedT = nullptr;
+  int kmajor_version = -1;  // weights_version of w13T / w2T / cembedT (built only for the K-major path)
+  int cembedT_pad = 0;
+  bool use_mn = false;      // this step reads W1|W3, W2, the embedding (and dW's operands) MN-major
   ForwardSaves sv;
   void* dlogits = nullptr;  // (full mode also keeps sv.xn2)
   float *dy = nullptr, *dy2 = nullptr, *dxf = nullptr, *dsilu = nullptr;
@@ -1002,8 +1005,6 @@ int ensure_model_state(b2p_model* m) {
   P16_ALLOC(s->wqkvT, L * D * (QKV + kUCols) * e);
   B2P_CHECK_CUDA(cudaMemset(s->wqkvT, 0, L * D * (QKV + kUCols) * e));
   P16_ALLOC(s->woT, L * QD * D * e);
-  P16_ALLOC(s->w13T, L * D * 2 * H * e);
-  P16_ALLOC(s->w2T, L * H * D * e);
   P16_ALLOC(s->a_oT, L * QD * r * 4);
   P16_ALLOC(s->bblk_qkv, L * 64 * QKV * e);
   P16_ALLOC(s->bblk_o, L * 64 * D * e);
@@ -1028,43 +1029,67 @@ int ensure_model_state(b2p_model* m) {
   return B2P_OK;
 }
 
-// Transposed copies of the frozen weights for the data-gradient GEMMs.
+// Transposed copies of the frozen weights for the data-gradient GEMMs that read them K-major: Wqkv
+// (with the LoRA K-extension columns) and Wo, whose GEMMs carry LoRA terms. W1|W3, W2 and the compact
+// embedding are read where they lie, MN-major, on the CTA-pair engine; their transposed copies are
+// built only for steps that cannot use it (ensure_weights_kmajor).
 int ensure_weights(b2p_model* m) {
   P16State* s = m->p16;
   if (s->weights_version == m->weights_version) return B2P_OK;
   const auto& c = m->cfg;
-  const int L = c.nlayers, D = c.dim, H = c.hidden, QD = m->q_dim, QKV = m->qkv_dim;
+  const int L = c.nlayers, D = c.dim, QD = m->q_dim, QKV = m->qkv_dim;
   const size_t e = model_esz(m);
   const int cv_pad = (m->cv + 63) / 64 * 64;
   if (cv_pad != s->cv_pad) {
-    if (s->cembedT) cudaFree(s->cembedT);
-    s->cembedT = nullptr;
-    P16_ALLOC(s->cembedT, (size_t)D * cv_pad * e);
     s->cv_pad = cv_pad;
     s->gen++;
     release_rows(s);  // dlogits rows depend on the padded vocabulary
   }
-  B2P_CHECK_CUDA(cudaMemsetAsync(s->cembedT, 0, (size_t)D * cv_pad * e, m->st));
   int rc;
   const bool bf = m->bf16;
-  for (int l = 0; l < L && true; ++l) {
+  for (int l = 0; l < L; ++l) {
     const char* wqkv = static_cast<const char*>(m->wqkv) + (size_t)l * QKV * D * e;
     const char* wo = static_cast<const char*>(m->wo) + (size_t)l * D * QD * e;
-    const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
-    const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
     if ((rc = transpose16(wqkv, QKV, D, D, static_cast<char*>(s->wqkvT) + (size_t)l * D * (QKV + kUCols) * e,
                           QKV + kUCols, bf, m->st)))
       return rc;
     if ((rc = transpose16(wo, D, QD, QD, static_cast<char*>(s->woT) + (size_t)l * QD * D * e, D, bf, m->st)))
       return rc;
+  }
+  s->weights_version = m->weights_version;
+  return B2P_OK;
+}
+
+// K-major (transposed) copies of W1|W3, W2 and the compact embedding, for steps on the single-CTA
+// engine (fewer than 256 token rows, or B2P_OPT_PAIR_GEMM 0).
+int ensure_weights_kmajor(b2p_model* m) {
+  P16State* s = m->p16;
+  if (s->kmajor_version == m->weights_version && s->cembedT_pad == s->cv_pad) return B2P_OK;
+  const auto& c = m->cfg;
+  const int L = c.nlayers, D = c.dim, H = c.hidden;
+  const size_t e = model_esz(m);
+  if (!s->w13T) P16_ALLOC(s->w13T, (size_t)L * D * 2 * H * e);
+  if (!s->w2T) P16_ALLOC(s->w2T, (size_t)L * H * D * e);
+  if (s->cembedT_pad != s->cv_pad) {
+    if (s->cembedT) cudaFree(s->cembedT);
+    s->cembedT = nullptr;
+    P16_ALLOC(s->cembedT, (size_t)D * s->cv_pad * e);
+    s->cembedT_pad = s->cv_pad;
+  }
+  B2P_CHECK_CUDA(cudaMemsetAsync(s->cembedT, 0, (size_t)D * s->cv_pad * e, m->st));
+  int rc;
+  const bool bf = m->bf16;
+  for (int l = 0; l < L; ++l) {
+    const char* w13 = static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e;
+    const char* w2 = static_cast<const char*>(m->w2) + (size_t)l * D * H * e;
     if ((rc = transpose16(w13, 2 * H, D, D, static_cast<char*>(s->w13T) + (size_t)l * D * 2 * H * e, 2 * H, bf,
                           m->st)))
       return rc;
     if ((rc = transpose16(w2, D, H, H, static_cast<char*>(s->w2T) + (size_t)l * H * D * e, D, bf, m->st)))
       return rc;
   }
-  if ((rc = transpose16(m->cembed, m->cv, D, D, s->cembedT, cv_pad, bf, m->st))) return rc;
-  s->weights_version = m->weights_version;
+  if ((rc = transpose16(m->cembed, m->cv, D, D, s->cembedT, s->cv_pad, bf, m->st))) return rc;
+  s->kmajor_version = m->weights_version;
   return B2P_OK;
 }
 
@@ -1274,6 +1299,8 @@ int p16_grad(b2p_model* m, const int32_t* d_tok, const int32_t* d_tgt, int n_seq
   P16State* s = m->p16;
   if ((rc = ensure_weights(m))) return rc;
   if ((rc = ensure_rows(m, R))) return rc;
+  s->use_mn = m->use_pair && R >= 2 * kBM;
+  if (!s->use_mn && (rc = ensure_weights_kmajor(m))) return rc;
   // group/variant tables and per-row targets (host-staged, outside any graph)
   std::vector<VariantInfo> vars(1, VariantInfo{0, 0, 0.f, 0.f});
   if ((rc = model_stage_groups(m, n_seq, vars, d_tgt))) return rc;
@@ -1378,20 +1405,29 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
   std::memset(&ef, 0, sizeof(ef));
   ef.M = R;
   ef.N = D;
-  if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dlogits, s->cv_pad, s->cembedT, s->cv_pad, R, D, s->cv_pad,
-                       s->dxf, D, nullptr, ef)))
+  // dy = dlogits · E over the CV real vocabulary columns (E stored [CV][D]: MN-major operand)
+  if (s->use_mn) {
+    if ((rc = model_gemm_mn(m, EPI_F32, 2, s->dlogits, s->cv_pad, m->cembed, D, R, D, m->cv, s->dxf, D, ef)))
+      return rc;
+  } else if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dlogits, s->cv_pad, s->cembedT, s->cv_pad, R, D,
+                              s->cv_pad, s->dxf, D, nullptr, ef))) {
     return rc;
+  }
   // full backprop: dW[out, in] += (1/lambda) * dY^T X over the R token rows, as a GEMM of the
   // transposed 16-bit operands (K = R) accumulated into the fp32 gradient by the reduce-add epilogue
   auto wgrad_gemm = [&](const void* dY, int ld_dy, int n_out, const void* X, int ld_x, int n_in, float* out) -> int {
     int rc2;
-    if ((rc2 = transpose16(dY, R, n_out, ld_dy, s->tA, R, bf, m->st))) return rc2;
-    if ((rc2 = transpose16(X, R, n_in, ld_x, s->tB, R, bf, m->st))) return rc2;
     EpiParams ew;
     std::memset(&ew, 0, sizeof(ew));
     ew.M = n_out;
     ew.N = n_in;
     ew.alpha = inv_lambda;
+    // dY and X as stored ([R][features]): both MN-major operands, K = R, no transposes
+    if (s->use_mn && (rc2 = model_gemm_mn(m, EPI_RESID, 3, dY, ld_dy, X, ld_x, n_out, n_in, R, out, n_in, ew)) !=
+                         B2P_ERR_UNSUPPORTED)
+      return rc2;
+    if ((rc2 = transpose16(dY, R, n_out, ld_dy, s->tA, R, bf, m->st))) return rc2;
+    if ((rc2 = transpose16(X, R, n_in, ld_x, s->tB, R, bf, m->st))) return rc2;
     return model_gemm(m, pick_bn(n_in, EPI_RESID), EPI_RESID, s->tA, R, s->tB, R, n_out, n_in, R, out, n_in, nullptr,
                       ew);
   };
@@ -1426,9 +1462,16 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
     std::memset(&p0, 0, sizeof(p0));
     p0.M = R;
     p0.N = H;
-    if ((rc = model_gemm(m, pick_bn(H, EPI_F32), EPI_F32, s->d16, D,
-                         static_cast<char*>(s->w2T) + (size_t)l * H * D * e, D, R, H, D, s->dsilu, H, nullptr, p0)))
+    // W2 stored [D][H]: MN-major operand of dsilu = dffn · W2
+    if (s->use_mn) {
+      if ((rc = model_gemm_mn(m, EPI_F32, 2, s->d16, D, static_cast<const char*>(m->w2) + (size_t)l * D * H * e, H, R,
+                              H, D, s->dsilu, H, p0)))
+        return rc;
+    } else if ((rc = model_gemm(m, pick_bn(H, EPI_F32), EPI_F32, s->d16, D,
+                                static_cast<char*>(s->w2T) + (size_t)l * H * D * e, D, R, H, D, s->dsilu, H, nullptr,
+                                p0))) {
       return rc;
+    }
     if ((rc = swiglu_bwd(s->dsilu, slab(v.h13, l, 2 * H), R, H, s->dh13, bf, m->st))) return rc;
     if (s->full) {
       // dW2 = dffn^T · silu_out and dW1|W3 = [dh1|dh3]^T · x2norm  (train.m:1027-1034)
@@ -1441,10 +1484,16 @@ int p16_kernels(b2p_model* m, const int32_t* d_tok, int n_seq) {
     std::memset(&p1, 0, sizeof(p1));
     p1.M = R;
     p1.N = D;
-    if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dh13, 2 * H,
-                         static_cast<char*>(s->w13T) + (size_t)l * D * 2 * H * e, 2 * H, R, D, 2 * H, s->dxf, D,
-                         nullptr, p1)))
+    // W1|W3 stored [2H][D] (interleaved rows): MN-major operand of dx_ffn = [dh1|dh3] · [W1;W3]
+    if (s->use_mn) {
+      if ((rc = model_gemm_mn(m, EPI_F32, 2, s->dh13, 2 * H, static_cast<const char*>(m->w13) + (size_t)l * 2 * H * D * e,
+                              D, R, D, 2 * H, s->dxf, D, p1)))
+        return rc;
+    } else if ((rc = model_gemm(m, pick_bn(D, EPI_F32), EPI_F32, s->dh13, 2 * H,
+                                static_cast<char*>(s->w13T) + (size_t)l * D * 2 * H * e, 2 * H, R, D, 2 * H, s->dxf,
+                                D, nullptr, p1))) {
       return rc;
+    }
     // RMSNorm2 backward + skip: dx2 = rmsnorm_bwd(dx_ffn) + dy; d16 = alpha dx2
     std::memset(&ra, 0, sizeof(ra));
     ra.g = s->dxf;
@@ -1664,6 +1713,8 @@ int full_grad(b2p_model* m, const uint16_t* tokens, const uint16_t* ctargets, in
   if ((rc = ensure_weights(m))) return rc;
   const int R = n_seq * m->cfg.seq;
   if ((rc = ensure_rows(m, R))) return rc;
+  m->p16->use_mn = m->use_pair && R >= 2 * kBM;
+  if (!m->p16->use_mn && (rc = ensure_weights_kmajor(m))) return rc;
   if ((rc = model_stage_tokens(m, tokens, ctargets, n_seq))) return rc;
   // rows grouped by token, each group in sequence order (deterministic embedding scatter)
   std::vector<int32_t> idx(R);

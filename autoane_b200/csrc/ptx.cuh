@@ -307,6 +307,21 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// MN-major tile with 128-byte swizzle, as TMA writes a box of 64 MN elements x
+// 64 K rows: each 128-byte row holds 64 consecutive M (or N) elements at one K
+// index, groups of 8 K rows sit 1024 B apart (SBO), and further 64-element MN
+// atoms follow `lbo_bytes` apart (LBO). The start address advances by 2048 B
+// (16 K rows) per K = 16 step.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;     // SBO: 8 K rows x 128 B
+  d |= static_cast<uint64_t>(1u) << 46;             // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
+  return d;
+}
+
 // Same for a K-major tile with 32-byte rows (16 16-bit elements = one UMMA K
 // step) and 32-byte swizzle: 8-row core groups 256 B apart, layout 6.
 __device__ __forceinline__ uint64_t sw32_kmajor_desc(uint32_t saddr) {

@@ -80,6 +80,14 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
  * 128 rows of X and half of the W tile. Requires M >= 256. */
 int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
                   void* stream);
+/* b2p_gemm_pair with operands read in either layout, as the backward passes
+ * hold them: X is [M][K] rows (x_mn 0) or [K][M] rows (x_mn 1), pitch ldx;
+ * W is [N][K] rows (w_mn 0) or [K][N] rows (w_mn 1), pitch ldw. Y[M][N] =
+ * X·W^T with X, W read where they lie (MN-major tcgen05 operands, no transposed
+ * copies). Layouts: (0, 1) with fp32 or 16-bit output, (1, 1) with fp32
+ * output, (0, 0) as b2p_gemm_pair. M >= 256; pitches multiples of 8 elements. */
+int b2p_gemm_pair_mn(const void* X, int ldx, int x_mn, const void* W, int ldw, int w_mn, void* Y, int M, int N, int K,
+                     int ldy, int dtype, int out_f32, void* stream);
 
 /* Causal GQA attention on device buffers (cpu_sdpa_forward,
  * training/cpu_ops.h:321-360, with K/V tiled over the query heads by

@@ -83,3 +83,56 @@ def test_split_k_is_repeatable(b2p, M, N, K):
     assert torch.equal(a, b)
     h = run_gemm(x, w, 0, 0)
     assert torch.equal(h, a.half().float())
+
+
+@pytest.mark.parametrize("M,N,K,x_mn", [(256, 960, 960, 0), (8192, 960, 2560, 0), (8192, 2560, 960, 0),
+                                         (4096, 960, 16893, 0), (1024, 960, 1920, 0), (300, 200, 72, 0),
+                                         (512, 512, 4096, 1), (1408, 512, 4096, 1), (16893, 512, 4096, 1),
+                                         (384, 300, 520, 1)])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("out_f32", [1, 0])
+def test_pair_gemm_mn_major_operands(b2p, M, N, K, x_mn, dt, out_f32):
+    """The backward's GEMMs read W as stored ([out][in]: dX = dY·W, W MN-major) and, for weight
+    gradients, dY and X as stored ([tokens][features]: dW = dY^T·X, both MN-major). The same product
+    through K-major copies: within the pair engine's tolerance of the fp32 product, and bit-identical to
+    the K-major launch on the transposed operands (same tiles, same K order)."""
+    if x_mn and not out_f32:
+        pytest.skip("MN-major X is built for fp32 (weight-gradient) outputs")
+    torch.manual_seed(M + 3 * N + 5 * K + x_mn)
+    dtype = torch.float16 if dt == "f16" else torch.bfloat16
+    xk = torch.randn(M, K, device="cuda").to(dtype)            # [M][K]
+    wk = (0.02 * torch.randn(N, K, device="cuda")).to(dtype)   # [N][K]
+    ldw = (N + 7) // 8 * 8
+    wmn = torch.zeros(K, ldw, device="cuda", dtype=dtype)
+    wmn[:, :N] = wk.t()
+    if x_mn:
+        ldx = (M + 7) // 8 * 8
+        xop = torch.zeros(K, ldx, device="cuda", dtype=dtype)
+        xop[:, :M] = xk.t()
+    else:
+        ldx = (K + 7) // 8 * 8
+        xop = torch.zeros(M, ldx, device="cuda", dtype=dtype)
+        xop[:, :K] = xk
+    ldk = (K + 7) // 8 * 8
+    xkp = torch.zeros(M, ldk, device="cuda", dtype=dtype)
+    xkp[:, :K] = xk
+    wkp = torch.zeros(N, ldk, device="cuda", dtype=dtype)
+    wkp[:, :K] = wk
+    ref = xk.float() @ wk.float().t()
+    pad = 4 if out_f32 else 8
+    ldy = (N + pad - 1) // pad * pad
+    code = 0 if dt == "f16" else 1
+    odt = torch.float32 if out_f32 else dtype
+    y_mn = torch.zeros(M, ldy, device="cuda", dtype=odt)
+    y_k = torch.zeros(M, ldy, device="cuda", dtype=odt)
+    _lib.call("b2p_gemm_pair_mn", xop.data_ptr(), ldx, x_mn, wmn.data_ptr(), ldw, 1, y_mn.data_ptr(), M, N, K, ldy, code,
+              out_f32, None)
+    _lib.call("b2p_gemm_pair_mn", xkp.data_ptr(), ldk, 0, wkp.data_ptr(), ldk, 0, y_k.data_ptr(), M, N, K, ldy, code,
+              out_f32, None)
+    torch.cuda.synchronize()
+    _lib.call("b2p_device_status", None)
+    y_mn, y_k = y_mn[:, :N].float(), y_k[:, :N].float()
+    err = (y_mn - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
+    tol = 2e-3 if (out_f32 or dt == "f16") else 8e-3
+    assert err < tol, f"normwise error {err:.3e}"
+    assert torch.equal(y_mn, y_k)
