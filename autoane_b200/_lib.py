@@ -59,6 +59,7 @@ ABI: dict[str, tuple] = {
     "b2p_sign_masks_noalloc": (i32, [C.POINTER(C.c_int64), i32, u64p, i32, vp, vp]),
     "b2p_model_set_option": (i32, [vp, i32, i32]),
     "b2p_gemm_pair": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+    "b2p_gemm_mi": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
     "b2p_gemm_pair_mn": (i32, [vp, i32, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp]),
     "b2p_p16_grad": (i32, [vp, u16p, u16p, i32, fp, vp]),
     "b2p_p16_grad_device": (i32, [vp, vp, vp, i32, vp]),

@@ -37,8 +37,9 @@ int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy
   DeviceCtx* c = nullptr;
   int rc = ctx_get(&c);
   if (rc) return rc;
-  if (splitk_preferred(kind, M, N, K, c->num_sms))
-    return launch_gemm_splitk(kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, static_cast<cudaStream_t>(stream));
+  if (const int route = small_gemm_route(kind, M, N, K, c->num_sms))
+    return launch_gemm_small(route, kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy,
+                             static_cast<cudaStream_t>(stream));
   if (M >= 2 * kBM && pair_supported(kind, M, N, ep))
     return launch_gemm_pair(kind, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy, nullptr, ep,
                             static_cast<cudaStream_t>(stream));
@@ -83,6 +84,17 @@ int b2p_gemm_pair_mn(const void* X, int ldx, int x_mn, const void* W, int ldw, i
   }
   return launch_gemm_pair_mn(kind, (x_mn ? 1 : 0) | (w_mn ? 2 : 0), dtype == B2P_BF16, X, ldx, W, ldw, M, N, K, Y, ldy,
                              ep, static_cast<cudaStream_t>(stream));
+}
+
+int b2p_gemm_mi(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
+                void* stream) {
+  B2P_REQUIRE(X && W && Y, "null operand");
+  B2P_REQUIRE(dtype == B2P_F16 || dtype == B2P_BF16, "dtype must be B2P_F16 or B2P_BF16");
+  B2P_REQUIRE(K % 8 == 0, "K must be a multiple of 8 (16-byte rows)");
+  B2P_REQUIRE(ldy >= N, "ldy (%d) < N (%d)", ldy, N);
+  B2P_REQUIRE((reinterpret_cast<uintptr_t>(Y) & 15u) == 0, "Y must be 16-byte aligned");
+  return launch_gemm_mi(out_f32 ? EPI_F32 : EPI_H16, dtype == B2P_BF16, X, K, W, K, M, N, K, Y, ldy,
+                        static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

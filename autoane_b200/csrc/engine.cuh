@@ -111,6 +111,16 @@ bool pair_supported(int kind, int M, int N, const EpiParams& ep);
 bool pair_mn_supported(int kind, int opm, int M, int N, int K, const void* X, int ldx, const void* W, int ldw);
 int launch_gemm_pair_mn(int kind, int opm, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N,
                         int K, void* out, int ldo, const EpiParams& ep, cudaStream_t st);
+// Plain fp32 / 16-bit output GEMM on 128 x 64 tiles, one CTA per tile, its K-blocks spread over
+// four MMA issuer warps with one TMEM accumulator each (summed in issuer order in the epilogue).
+int launch_gemm_mi(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
+                   void* out, int ldo, cudaStream_t st);
+// Route of a plain fp32 / 16-bit GEMM of at most 1024 rows whose 128 x 64 tiles fit one wave:
+// SMALL_GEMM_NONE (the persistent engines), SMALL_GEMM_SPLITK or SMALL_GEMM_MULTI_ISSUER.
+enum SmallGemmRoute { SMALL_GEMM_NONE = 0, SMALL_GEMM_SPLITK = 1, SMALL_GEMM_MULTI_ISSUER = 2 };
+int small_gemm_route(int kind, int M, int N, int K, int num_sms);
+int launch_gemm_small(int route, int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N,
+                      int K, void* out, int ldo, cudaStream_t st);
 int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                      void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
 
@@ -119,8 +129,6 @@ int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W,
 // added in rank order over distributed shared memory. splitk_applies() tells whether a
 // launch qualifies.
 bool splitk_applies(int kind, int M, int N, int num_sms);
-// Whether the split-K kernel is the faster choice for this shape (measured rule, gemm_sk.cu).
-bool splitk_preferred(int kind, int M, int N, int K, int num_sms);
 int launch_gemm_splitk(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                        void* out, int ldo, cudaStream_t st);
 

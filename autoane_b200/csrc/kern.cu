@@ -355,8 +355,8 @@ int run_projection(b2p_kernel* k, const void* W) {
     DeviceCtx* c = nullptr;
     int rc = ctx_get(&c);
     if (rc) return rc;
-    if (splitk_preferred(EPI_F32, S, k->N, k->K, c->num_sms))
-      return launch_gemm_splitk(EPI_F32, k->bf16, k->x16, k->K, W, k->K, S, k->N, k->K, k->y32, k->N, k->st);
+    if (const int route = small_gemm_route(EPI_F32, S, k->N, k->K, c->num_sms))
+      return launch_gemm_small(route, EPI_F32, k->bf16, k->x16, k->K, W, k->K, S, k->N, k->K, k->y32, k->N, k->st);
     if (S >= 2 * kBM && pair_supported(EPI_F32, S, k->N, ep))
       return launch_gemm_pair(EPI_F32, k->bf16, k->x16, k->K, W, k->K, S, k->N, k->K, k->y32, k->N, nullptr, ep,
                               k->st);

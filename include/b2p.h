@@ -66,11 +66,12 @@ int b2p_device_status(void* stream);
  * row pitch ldy elements. This is the device-resident form of the reference's
  * cblas_sgemm projection call sites (training/train_mezo.m:1533-1538) in the
  * transposed, token-major layout: X holds tokens as rows, W output channels.
- * Up to 1024 rows, when the 128 x 64 output tiles fit one wave and the split
- * pays (at most two ways, or K >= 2048), the K loop of each tile is split over
- * a cluster of CTAs (partial sums added in a fixed order, so results repeat
- * bit for bit); otherwise the CTA-pair engine (M >= 256) or the persistent
- * single-CTA engine runs it.
+ * Up to 1024 rows, when the 128 x 64 output tiles fit one wave, one CTA per
+ * tile spreads its K loop over four MMA issuers (b2p_gemm_mi), or, for a long
+ * K (>= 2048) that a cluster of CTAs can split, the K loop of each tile is
+ * split over the cluster; partial sums are added in a fixed order either way,
+ * so results repeat bit for bit. Otherwise the CTA-pair engine (M >= 256) or
+ * the persistent single-CTA engine runs it.
  * Asynchronous on `stream` (NULL = default stream). */
 int b2p_gemm(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
              void* stream);
@@ -88,6 +89,12 @@ int b2p_gemm_pair(const void* X, const void* W, void* Y, int M, int N, int K, in
  * output, (0, 0) as b2p_gemm_pair. M >= 256; pitches multiples of 8 elements. */
 int b2p_gemm_pair_mn(const void* X, int ldx, int x_mn, const void* W, int ldw, int w_mn, void* Y, int M, int N, int K,
                      int ldy, int dtype, int out_f32, void* stream);
+/* Same contract as b2p_gemm on 128 x 64 output tiles, one CTA per tile, each
+ * tile's K-blocks spread over four tcgen05 MMA issuer warps with an accumulator
+ * each, added in a fixed order (results repeat bit for bit). For GEMMs of few
+ * token rows, where a single issuer's K loop is the critical path. */
+int b2p_gemm_mi(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int out_f32,
+                void* stream);
 
 /* Causal GQA attention on device buffers (cpu_sdpa_forward,
  * training/cpu_ops.h:321-360, with K/V tiled over the query heads by

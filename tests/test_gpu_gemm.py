@@ -136,3 +136,32 @@ def test_pair_gemm_mn_major_operands(b2p, M, N, K, x_mn, dt, out_f32):
     tol = 2e-3 if (out_f32 or dt == "f16") else 8e-3
     assert err < tol, f"normwise error {err:.3e}"
     assert torch.equal(y_mn, y_k)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 960, 960), (256, 320, 960), (1024, 2560, 960), (128, 960, 2560), (100, 200, 72),
+                                   (1000, 960, 24), (300, 5000, 960)])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("out_f32", [1, 0])
+def test_multi_issuer_gemm(b2p, M, N, K, dt, out_f32):
+    """b2p_gemm_mi (128 x 64 tiles, four MMA issuers with an accumulator each, summed in issuer order):
+    within the engines' tolerance of the fp32 product, including ragged M / N / K, K shorter than one
+    64-wide block per issuer and more tiles than SMs; bit-identical on repeat."""
+    torch.manual_seed(M + 7 * N + 3 * K)
+    dtype = torch.float16 if dt == "f16" else torch.bfloat16
+    x = torch.randn(M, K, device="cuda").to(dtype)
+    w = (0.02 * torch.randn(N, K, device="cuda")).to(dtype)
+    ref = x.float() @ w.float().t()
+    pad = 4 if out_f32 else 8
+    ldy = (N + pad - 1) // pad * pad
+    outs = []
+    for _ in range(2):
+        y = torch.zeros(M, ldy, device="cuda", dtype=torch.float32 if out_f32 else dtype)
+        _lib.call("b2p_gemm_mi", x.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K, ldy, 0 if dt == "f16" else 1,
+                  out_f32, None)
+        torch.cuda.synchronize()
+        _lib.call("b2p_device_status", None)
+        outs.append(y[:, :N].float())
+    assert torch.equal(outs[0], outs[1])
+    err = (outs[0] - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
+    tol = 2e-3 if (out_f32 or dt == "f16") else 8e-3
+    assert err < tol, f"normwise error {err:.3e}"
