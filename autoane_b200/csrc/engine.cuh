@@ -125,9 +125,9 @@ int launch_gemm_pair(int kind, bool bf16, const void* X, int ldx, const void* W,
                      void* out, int ldo, const void* u16, const EpiParams& ep, cudaStream_t st);
 
 // Plain fp32 / 16-bit output GEMMs of at most 1024 rows whose 128 x 64 tiles fit one wave
-// (gemm_sk.cu): each tile's K loop is split over a cluster of up to 4 CTAs, partial sums
-// added in rank order over distributed shared memory. splitk_applies() tells whether a
-// launch qualifies.
+// (gemm_sk.cu): each tile's K loop is split over a cluster of up to 4 CTAs (four MMA issuers
+// each), the partial tiles moved by bulk copies into CTA 0 and added in rank order.
+// splitk_applies() tells whether a launch qualifies.
 bool splitk_applies(int kind, int M, int N, int num_sms);
 int launch_gemm_splitk(int kind, bool bf16, const void* X, int ldx, const void* W, int ldw, int M, int N, int K,
                        void* out, int ldo, cudaStream_t st);
