@@ -44,10 +44,7 @@ struct PairSmem {
   static constexpr int kBStage = (BN / 2) * kBK * 2;    // this CTA's BN/2 rows of W
   static constexpr int kStageBytes = kAStage + kBStage;
   static constexpr int kStageOutBytes = kStores ? (kOutF32 ? 4096 : 2048) : 0;
-  // Wo (fp32 residual reduce-add, K = 960): its epilogue is as long as its main loop, so each epilogue
-  // warp stages chunk c + 1 while the TMA still reads chunk c (two boxes per warp)
-  static constexpr int kOutBoxes = (KIND == EPI_RESID && NSEG == 1) ? 2 : 1;
-  static constexpr int kOutBytes = kStageOutBytes * kEpiWarps * kOutBoxes;
+  static constexpr int kOutBytes = kStageOutBytes * kEpiWarps;
   static constexpr int kLoraU = kBM * kMaxRank * 2;           // 4 KB per segment
   static constexpr int kLoraB = (BN / 2) * kMaxRank * 2;      // BN/2 x 32 B per segment
   static constexpr int kLoraBuf = NSEG * (kLoraU + kLoraB);
@@ -426,8 +423,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int half = ew >> 2;
     const int row_in_tile = lg * 32 + lane;
     const int et = threadIdx.x - kFirstEpiWarp * 32;
-    uint8_t* box0 = sOut + ew * S::kStageOutBytes * S::kOutBoxes;
-    int bsel = 0;  // staging box of the next chunk
+    uint8_t* box = sOut + ew * S::kStageOutBytes;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
     int acc = 0;
@@ -528,27 +524,18 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] *= ep.alpha;
         }
-        // with two boxes, the group still allowed in flight is the previous chunk's, on the other box
-        if (lane == 0) {
-          if (S::kOutBoxes == 2)
-            bulk_wait_read1();
-          else
-            bulk_wait_read0();
-        }
+        if (lane == 0) bulk_wait_read0();
         __syncwarp();
-        uint8_t* box = box0 + bsel * S::kStageOutBytes;
         stage_row<S::kOutF32, OutT>(box, lane, v);
         fence_proxy_async_smem();
         __syncwarp();
-        const bool do_store = m0 + lg * 32 < M && col < (KIND == EPI_SWIGLU ? N / 2 : N);  // warp-uniform
-        if (lane == 0 && do_store) {
+        if (lane == 0 && m0 + lg * 32 < M && col < (KIND == EPI_SWIGLU ? N / 2 : N)) {
           if (KIND == EPI_RESID)
             tma_reduce_add_2d(&tmOut, box, col, m0 + lg * 32);
           else
             tma_store_2d(&tmOut, box, col, m0 + lg * 32);
           bulk_commit();
         }
-        if (S::kOutBoxes == 2 && do_store) bsel ^= 1;
       }
       if (KIND == EPI_CE && row_ok)
         ep.ce_part[(long long)row * (2 * ep.n_tiles_n) + 2 * nt + half] = make_float2(ce_m, ce_s);
