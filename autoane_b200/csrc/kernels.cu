@@ -1220,10 +1220,13 @@ __global__ void lora_prep_kernel(LoraPrepArgs a) {
       const long long ii = a2 ? i - n_a : i;
       const long long per = a2 ? per_a2 : per_a;
       const int ld = a2 ? a.hidden : a.ld;
-      const long long lv = ii / per, e = ii - lv * per;
-      const int l = (int)(lv / a.n_var);
-      v = (int)(lv - (long long)l * a.n_var);
-      const int row = (int)(e / ld), c = (int)(e - (long long)row * ld);
+      // 32-bit index arithmetic (the launcher checks that every count fits): 64-bit divisions cost
+      // several times the rest of the element's work
+      const uint32_t ii32 = (uint32_t)ii, per32 = (uint32_t)per;
+      const uint32_t lv = ii32 / per32, e = ii32 - lv * per32;
+      const int l = (int)(lv / (uint32_t)a.n_var);
+      v = (int)(lv - (uint32_t)l * (uint32_t)a.n_var);
+      const int row = (int)(e / (uint32_t)ld), c = (int)(e - (uint32_t)row * (uint32_t)ld);
       const int m = row / r, j = row - m * r;
       int width;
       long long off;
@@ -1254,16 +1257,17 @@ __global__ void lora_prep_kernel(LoraPrepArgs a) {
     float* dst;
     const long long nl = (long long)a.nlayers * a.n_var * per_w;
     if (k < nl) {
-      const long long lv = k / per_w, e = k - lv * per_w;
-      const int l = (int)(lv / a.n_var);
-      v = (int)(lv - (long long)l * a.n_var);
-      const int which = (int)(e / a.dim), c = (int)(e - (long long)which * a.dim);
+      const uint32_t k32 = (uint32_t)k, pw32 = (uint32_t)per_w;
+      const uint32_t lv = k32 / pw32, e = k32 - lv * pw32;
+      const int l = (int)(lv / (uint32_t)a.n_var);
+      v = (int)(lv - (uint32_t)l * (uint32_t)a.n_var);
+      const int which = (int)(e / (uint32_t)a.dim), c = (int)(e - (uint32_t)which * (uint32_t)a.dim);
       p = (long long)l * a.layer_size + (which ? a.oRf : a.oRa) + c;
       dst = a.w_out + k;
     } else {
-      const long long e = k - nl;
-      v = (int)(e / a.dim);
-      p = a.oRfinal + (e - (long long)v * a.dim);
+      const uint32_t e = (uint32_t)(k - nl);
+      v = (int)(e / (uint32_t)a.dim);
+      p = a.oRfinal + (long long)(e - (uint32_t)v * (uint32_t)a.dim);
       dst = a.w_final + e;
     }
     const VariantInfo vi = a.variants[v];
@@ -1277,6 +1281,11 @@ int launch_lora_prep(const LoraPrepArgs& a, bool bf16, cudaStream_t st) {
   B2P_REQUIRE(a.n_var >= 1 && a.rank >= 1 && a.rank <= 8 && a.ld >= a.dim && a.ld >= a.q_dim && a.ld % 8 == 0 &&
                   (a.segs == 4 || a.segs == 6) && (!a.a2_out || a.hidden % 8 == 0),
               "bad LoRA prep shape");
+  {
+    const long long per_a = (long long)a.segs * a.rank * a.ld, per_a2 = a.a2_out ? (long long)a.rank * a.hidden : 0;
+    const long long n = (long long)a.nlayers * a.n_var * (per_a + per_a2 + 2LL * a.dim) + (long long)a.n_var * a.dim;
+    B2P_REQUIRE(n < (1LL << 31), "LoRA prep of %lld elements exceeds the kernel's 32-bit indexing", n);
+  }
   if (bf16)
     lora_prep_kernel<__nv_bfloat16><<<148 * 8, 256, 0, st>>>(a);
   else
